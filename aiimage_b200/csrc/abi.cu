@@ -1,0 +1,460 @@
+// abi.cu -- host side of the libaexis_cuda C ABI (include/aexis_cuda.h):
+// argument validation with the reference's error classes, weight handles,
+// and dispatch to the kernels. No C++ exception crosses the ABI.
+#include <cmath>
+#include <cstdarg>
+#include <cstring>
+#include <algorithm>
+#include <new>
+
+#include "aexis_internal.h"
+
+#define AEXIS_API extern "C" __attribute__((visibility("default")))
+
+namespace {
+thread_local std::string g_create_error;
+}
+
+int aexis_fail(aexis_ctx* ctx, int code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    if (ctx) ctx->err = buf;
+    else g_create_error = buf;
+    return code;
+}
+
+int aexis_cuda_check(aexis_ctx* ctx, cudaError_t e, const char* what) {
+    if (e == cudaSuccess) return AEXIS_OK;
+    return aexis_fail(ctx, AEXIS_E_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+int aexis_scratch(aexis_ctx* ctx, size_t bytes, void** out) {
+    if (bytes > ctx->scratch_bytes) {
+        // The old buffer may still be read by enqueued work: wait before freeing.
+        if (ctx->scratch) {
+            cudaStreamSynchronize(ctx->stream);
+            cudaFree(ctx->scratch);
+            ctx->scratch = nullptr;
+            ctx->scratch_bytes = 0;
+        }
+        size_t sz = std::max<size_t>(bytes, 1 << 20);
+        cudaError_t e = cudaMalloc(&ctx->scratch, sz);
+        if (e != cudaSuccess) return aexis_cuda_check(ctx, e, "scratch cudaMalloc");
+        ctx->scratch_bytes = sz;
+    }
+    *out = ctx->scratch;
+    return AEXIS_OK;
+}
+
+namespace {
+
+int bind(aexis_ctx* ctx) { return aexis_cuda_check(ctx, cudaSetDevice(ctx->device), "cudaSetDevice"); }
+
+bool valid_dtype(int d) { return d == AEXIS_F32 || d == AEXIS_F16; }
+
+int upload(aexis_ctx* ctx, const void* host, size_t bytes, void** dev, const char* what) {
+    cudaError_t e = cudaMalloc(dev, bytes);
+    if (e != cudaSuccess) return aexis_cuda_check(ctx, e, what);
+    e = cudaMemcpy(*dev, host, bytes, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+        cudaFree(*dev);
+        *dev = nullptr;
+        return aexis_cuda_check(ctx, e, what);
+    }
+    return AEXIS_OK;
+}
+
+// Host quantizer shared by the Q8 / Q4 float upload paths
+// (AexisGraphSession.NewInt{8,4}WeightOnlyUpload(float[], ...)).
+int quantize_rows(int bits, const float* data, int out_ch, int per_ch, int contiguous, uint32_t* packed,
+                  float* scales) {
+    if (!data || !packed || !scales) return AEXIS_E_NULL;
+    if (out_ch <= 0) return AEXIS_E_RANGE;
+    if (per_ch <= 0) return AEXIS_E_SHAPE;
+    const long long total = (long long)out_ch * per_ch;
+    const long long words = std::max<long long>(1, (total + (bits == 4 ? 7 : 3)) / (bits == 4 ? 8 : 4));
+    std::memset(packed, 0, sizeof(uint32_t) * words);
+    const float qmax = bits == 4 ? 7.0f : 127.0f;
+    const int lim = bits == 4 ? 7 : 127;
+    for (int oc = 0; oc < out_ch; ++oc) {
+        float max_abs = 0.0f;
+        for (int vi = 0; vi < per_ch; ++vi) {
+            const long long si = contiguous ? (long long)oc * per_ch + vi : (long long)vi * out_ch + oc;
+            max_abs = std::max(max_abs, std::fabs(data[si]));
+        }
+        const float scale = max_abs > 0.0f ? max_abs / qmax : 1.0f;
+        scales[oc] = scale;
+        for (int vi = 0; vi < per_ch; ++vi) {
+            const long long si = contiguous ? (long long)oc * per_ch + vi : (long long)vi * out_ch + oc;
+            int q = (int)std::nearbyintf(data[si] / scale);  // midpoint to even, as Mathf.RoundToInt
+            q = q < -lim ? -lim : (q > lim ? lim : q);
+            if (bits == 4) packed[si >> 3] |= ((uint32_t)q & 0xFu) << ((si & 7) * 4);
+            else packed[si >> 2] |= (uint32_t)(uint8_t)(int8_t)q << ((si & 3) * 8);
+        }
+    }
+    return AEXIS_OK;
+}
+
+size_t dsize(int dtype) { return dtype == AEXIS_F16 ? 2 : 4; }
+
+}  // namespace
+
+// ---------------------------------------------------------------- context
+AEXIS_API int aexis_cuda_abi_version(void) { return AEXIS_CUDA_ABI_VERSION; }
+
+AEXIS_API int aexis_cuda_create(int device, aexis_ctx** out) {
+    if (!out) return aexis_fail(nullptr, AEXIS_E_NULL, "out is null");
+    *out = nullptr;
+    int count = 0;
+    cudaError_t e = cudaGetDeviceCount(&count);
+    if (e != cudaSuccess || count == 0)
+        return aexis_fail(nullptr, AEXIS_E_CUDA, "no CUDA device: %s", cudaGetErrorString(e));
+    if (device < 0 || device >= count)
+        return aexis_fail(nullptr, AEXIS_E_RANGE, "device %d out of range [0, %d)", device, count);
+    cudaDeviceProp prop;
+    e = cudaGetDeviceProperties(&prop, device);
+    if (e != cudaSuccess) return aexis_fail(nullptr, AEXIS_E_CUDA, "cudaGetDeviceProperties: %s", cudaGetErrorString(e));
+    if (prop.major != 10)
+        return aexis_fail(nullptr, AEXIS_E_UNSUPPORTED, "device %d is sm_%d%d; this build targets sm_100a (B200)",
+                          device, prop.major, prop.minor);
+    aexis_ctx* ctx = new (std::nothrow) aexis_ctx();
+    if (!ctx) return aexis_fail(nullptr, AEXIS_E_STATE, "out of host memory");
+    ctx->device = device;
+    ctx->sm_count = prop.multiProcessorCount;
+    e = cudaSetDevice(device);
+    if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&ctx->own_stream, cudaStreamNonBlocking);
+    if (e != cudaSuccess) {
+        delete ctx;
+        return aexis_fail(nullptr, AEXIS_E_CUDA, "stream create: %s", cudaGetErrorString(e));
+    }
+    ctx->stream = ctx->own_stream;
+    *out = ctx;
+    return AEXIS_OK;
+}
+
+AEXIS_API int aexis_cuda_destroy(aexis_ctx* ctx) {
+    if (!ctx) return AEXIS_E_NULL;
+    cudaSetDevice(ctx->device);
+    if (ctx->own_stream) cudaStreamSynchronize(ctx->own_stream);
+    if (ctx->scratch) cudaFree(ctx->scratch);
+    if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
+    delete ctx;
+    return AEXIS_OK;
+}
+
+AEXIS_API const char* aexis_cuda_last_error(const aexis_ctx* ctx) {
+    return ctx ? ctx->err.c_str() : g_create_error.c_str();
+}
+
+AEXIS_API int aexis_cuda_set_stream(aexis_ctx* ctx, void* stream) {
+    if (!ctx) return AEXIS_E_NULL;
+    ctx->stream = stream ? (cudaStream_t)stream : ctx->own_stream;
+    return AEXIS_OK;
+}
+
+AEXIS_API int aexis_cuda_sync(aexis_ctx* ctx) {
+    if (!ctx) return AEXIS_E_NULL;
+    int rc = bind(ctx);
+    if (rc) return rc;
+    return aexis_cuda_check(ctx, cudaStreamSynchronize(ctx->stream), "cudaStreamSynchronize");
+}
+
+// ---------------------------------------------------------------- weights
+AEXIS_API int aexis_quantize_q8_rows(const float* data, int out_ch, int per_ch, int contiguous, uint32_t* packed,
+                                     float* scales) {
+    return quantize_rows(8, data, out_ch, per_ch, contiguous, packed, scales);
+}
+
+AEXIS_API int aexis_quantize_q4_rows(const float* data, int out_ch, int per_ch, int contiguous, uint32_t* packed,
+                                     float* scales) {
+    return quantize_rows(4, data, out_ch, per_ch, contiguous, packed, scales);
+}
+
+static int weights_q(aexis_ctx* ctx, int kind, const uint32_t* packed, const void* scales, int scale_dtype, int n,
+                     int k, int group, aexis_weights** out) {
+    if (!ctx) return AEXIS_E_NULL;
+    if (!out) return aexis_fail(ctx, AEXIS_E_NULL, "out is null");
+    *out = nullptr;
+    if (!packed || !scales)
+        return aexis_fail(ctx, AEXIS_E_NULL, "%s Gemm weights and scales must be configured together.",
+                          kind == WK_Q4 ? "INT4" : "INT8");
+    if (n <= 0 || k <= 0) return aexis_fail(ctx, AEXIS_E_RANGE, "n=%d k=%d must be positive", n, k);
+    if (!valid_dtype(scale_dtype)) return aexis_fail(ctx, AEXIS_E_UNSUPPORTED, "scale dtype %d", scale_dtype);
+    const long long total = (long long)n * k;
+    if (total > (1LL << 40)) return aexis_fail(ctx, AEXIS_E_RANGE, "weight too large");
+    long long nscales;
+    if (kind == WK_Q4) {
+        if (group <= 0 || k % group != 0)
+            return aexis_fail(ctx, AEXIS_E_SHAPE, "Direct Q4 group size must divide the Gemm K dimension.");
+        nscales = total / group;
+    } else {
+        nscales = n;
+    }
+    int rc = bind(ctx);
+    if (rc) return rc;
+    aexis_weights* w = new (std::nothrow) aexis_weights();
+    if (!w) return aexis_fail(ctx, AEXIS_E_STATE, "out of host memory");
+    w->kind = kind;
+    w->n = n;
+    w->k = k;
+    w->group = kind == WK_Q4 ? group : 0;
+    w->scale_dtype = scale_dtype;
+    const long long words = std::max<long long>(1, (total + (kind == WK_Q4 ? 7 : 3)) / (kind == WK_Q4 ? 8 : 4));
+    w->data_bytes = (size_t)words * 4;
+    w->scale_bytes = (size_t)nscales * dsize(scale_dtype);
+    rc = upload(ctx, packed, w->data_bytes, &w->data, "weight upload");
+    if (rc == AEXIS_OK) rc = upload(ctx, scales, w->scale_bytes, &w->scales, "scale upload");
+    if (rc) {
+        if (w->data) cudaFree(w->data);
+        delete w;
+        return rc;
+    }
+    *out = w;
+    return AEXIS_OK;
+}
+
+AEXIS_API int aexis_cuda_weights_q8(aexis_ctx* ctx, const uint32_t* packed, const void* scales, int scale_dtype,
+                                    int n, int k, aexis_weights** out) {
+    return weights_q(ctx, WK_Q8, packed, scales, scale_dtype, n, k, 0, out);
+}
+
+AEXIS_API int aexis_cuda_weights_q4(aexis_ctx* ctx, const uint32_t* packed, const void* scales, int scale_dtype,
+                                    int n, int k, int group, aexis_weights** out) {
+    return weights_q(ctx, WK_Q4, packed, scales, scale_dtype, n, k, group, out);
+}
+
+AEXIS_API int aexis_cuda_weights_dense(aexis_ctx* ctx, const void* data, int dtype, int n, int k,
+                                       aexis_weights** out) {
+    if (!ctx) return AEXIS_E_NULL;
+    if (!out || !data) return aexis_fail(ctx, AEXIS_E_NULL, "data/out is null");
+    *out = nullptr;
+    if (n <= 0 || k <= 0) return aexis_fail(ctx, AEXIS_E_RANGE, "n=%d k=%d must be positive", n, k);
+    if (!valid_dtype(dtype)) return aexis_fail(ctx, AEXIS_E_UNSUPPORTED, "dtype %d", dtype);
+    int rc = bind(ctx);
+    if (rc) return rc;
+    aexis_weights* w = new (std::nothrow) aexis_weights();
+    if (!w) return aexis_fail(ctx, AEXIS_E_STATE, "out of host memory");
+    w->kind = dtype == AEXIS_F16 ? WK_F16 : WK_F32;
+    w->n = n;
+    w->k = k;
+    w->data_bytes = (size_t)n * k * dsize(dtype);
+    rc = upload(ctx, data, w->data_bytes, &w->data, "dense upload");
+    if (rc) {
+        delete w;
+        return rc;
+    }
+    *out = w;
+    return AEXIS_OK;
+}
+
+AEXIS_API int aexis_cuda_weights_free(aexis_ctx* ctx, aexis_weights* w) {
+    if (!ctx || !w) return AEXIS_E_NULL;
+    bind(ctx);
+    cudaStreamSynchronize(ctx->stream);
+    if (w->data) cudaFree(w->data);
+    if (w->scales) cudaFree(w->scales);
+    delete w;
+    return AEXIS_OK;
+}
+
+AEXIS_API int aexis_cuda_weights_dequant(aexis_ctx* ctx, const aexis_weights* w, float* out) {
+    if (!ctx) return AEXIS_E_NULL;
+    if (!w || !out) return aexis_fail(ctx, AEXIS_E_NULL, "weights/out is null");
+    int rc = bind(ctx);
+    if (rc) return rc;
+    return aexis_cuda_check(ctx, launch_dequant(w, out, ctx->stream), "dequant launch");
+}
+
+// ----------------------------------------------------------------- linear
+static int gemm_common(aexis_ctx* ctx, const void* a, int a_dtype, int lda, int m, int k, const aexis_weights* w,
+                       const float* bias, float alpha, float beta, void* y, int y_dtype, int ldy, int n, int epi) {
+    if (!ctx) return AEXIS_E_NULL;
+    if (!a) return aexis_fail(ctx, AEXIS_E_NULL, "a is null");
+    if (!w) return aexis_fail(ctx, AEXIS_E_NULL, "b is null");
+    if (!y) return aexis_fail(ctx, AEXIS_E_NULL, "output is null");
+    if (m <= 0) return aexis_fail(ctx, AEXIS_E_RANGE, "m=%d", m);
+    if (n <= 0) return aexis_fail(ctx, AEXIS_E_RANGE, "n=%d", n);
+    if (k <= 0) return aexis_fail(ctx, AEXIS_E_RANGE, "k=%d", k);
+    if (w->kind != WK_Q4 && w->kind != WK_Q8)
+        return aexis_fail(ctx, AEXIS_E_UNSUPPORTED, "Gemm needs INT4 or INT8 weights");
+    if (w->n != n || w->k != k)
+        return aexis_fail(ctx, AEXIS_E_SHAPE, "weight is [%d, %d], call asks for n=%d k=%d", w->n, w->k, n, k);
+    if (lda < k || ldy < n) return aexis_fail(ctx, AEXIS_E_SHAPE, "lda=%d < k or ldy=%d < n", lda, ldy);
+    if (!valid_dtype(a_dtype) || !valid_dtype(y_dtype))
+        return aexis_fail(ctx, AEXIS_E_UNSUPPORTED, "dtype a=%d y=%d", a_dtype, y_dtype);
+    int rc = bind(ctx);
+    if (rc) return rc;
+    GemvArgs g;
+    g.a_dtype = a_dtype;
+    g.w = w;
+    g.bias = bias;
+    g.alpha = alpha;
+    g.beta = beta;
+    g.y_dtype = y_dtype;
+    g.epilogue = epi;
+    for (int r = 0; r < m; ++r) {
+        g.x = (const char*)a + (size_t)r * lda * dsize(a_dtype);
+        g.y = (char*)y + (size_t)r * ldy * dsize(y_dtype);
+        rc = aexis_cuda_check(ctx, launch_gemv(g, ctx->sm_count, ctx->stream), "gemv launch");
+        if (rc) return rc;
+    }
+    return AEXIS_OK;
+}
+
+AEXIS_API int aexis_cuda_gemm(aexis_ctx* ctx, const void* a, int a_dtype, int lda, int m, int k,
+                              const aexis_weights* w, const float* bias, float alpha, float beta, void* y,
+                              int y_dtype, int ldy, int n) {
+    return gemm_common(ctx, a, a_dtype, lda, m, k, w, bias, alpha, beta, y, y_dtype, ldy, n, EPI_STORE);
+}
+
+AEXIS_API int aexis_cuda_gemm_tiled(aexis_ctx* ctx, const void* a, int a_dtype, int lda, int m, int k,
+                                    const aexis_weights* w, const float* bias, float alpha, float beta, void* y,
+                                    int y_dtype, int ldy, int n) {
+    return gemm_common(ctx, a, a_dtype, lda, m, k, w, bias, alpha, beta, y, y_dtype, ldy, n, EPI_STORE_TILED);
+}
+
+// ------------------------------------------------------- pointwise layers
+AEXIS_API int aexis_cuda_rmsnorm(aexis_ctx* ctx, const void* x, int x_dtype, int rows, int width, int ld,
+                                 const float* gamma, int affine_size, float eps, void* y, int y_dtype) {
+    if (!ctx) return AEXIS_E_NULL;
+    if (!x) return aexis_fail(ctx, AEXIS_E_NULL, "input is null");
+    if (!y) return aexis_fail(ctx, AEXIS_E_NULL, "output is null");
+    if (rows <= 0 || width <= 0 || ld < width)
+        return aexis_fail(ctx, AEXIS_E_STATE, "RmsNormPack4LinearMat requires a one- or two-dimensional logical tensor.");
+    if (!valid_dtype(x_dtype) || !valid_dtype(y_dtype)) return aexis_fail(ctx, AEXIS_E_UNSUPPORTED, "dtype");
+    int rc = bind(ctx);
+    if (rc) return rc;
+    return aexis_cuda_check(ctx, launch_rmsnorm(x, x_dtype, rows, width, ld, gamma, gamma ? affine_size : 0, eps, y,
+                                                y_dtype, ctx->stream), "rmsnorm launch");
+}
+
+AEXIS_API int aexis_cuda_rope(aexis_ctx* ctx, const float* src, int embed_dim, int seq_len, int num_heads,
+                              const float* cos_table, const float* sin_table, int interleaved, float* out) {
+    if (!ctx) return AEXIS_E_NULL;
+    if (!src) return aexis_fail(ctx, AEXIS_E_NULL, "input is null");
+    if (!cos_table) return aexis_fail(ctx, AEXIS_E_NULL, "cos is null");
+    if (!sin_table) return aexis_fail(ctx, AEXIS_E_NULL, "sin is null");
+    if (!out) return aexis_fail(ctx, AEXIS_E_NULL, "output is null");
+    if (embed_dim <= 0 || seq_len <= 0 || num_heads <= 0)
+        return aexis_fail(ctx, AEXIS_E_RANGE, "shape w=%d h=%d c=%d", embed_dim, seq_len, num_heads);
+    if (src == out) return aexis_fail(ctx, AEXIS_E_SHAPE, "in-place RoPE is not supported (pairs are read twice)");
+    int rc = bind(ctx);
+    if (rc) return rc;
+    return aexis_cuda_check(ctx, launch_rope(src, embed_dim, seq_len, num_heads, cos_table, sin_table, interleaved, out,
+                                             ctx->stream), "rope launch");
+}
+
+AEXIS_API int aexis_cuda_kv_append(aexis_ctx* ctx, const float* current, int width, int rows, int slices, int offset,
+                                   float* cache, int cache_rows) {
+    if (!ctx) return AEXIS_E_NULL;
+    if (!current) return aexis_fail(ctx, AEXIS_E_NULL, "current is null");
+    if (!cache) return aexis_fail(ctx, AEXIS_E_NULL, "output is null");
+    if (offset < 0) return aexis_fail(ctx, AEXIS_E_RANGE, "destinationOffset=%d", offset);
+    if (rows <= 0) return aexis_fail(ctx, AEXIS_E_RANGE, "currentHeight=%d", rows);
+    if (width <= 0 || slices <= 0)
+        return aexis_fail(ctx, AEXIS_E_STATE, "AppendSequencePack4Cdhw requires matching width/depth textures.");
+    if (offset + rows > cache_rows)
+        return aexis_fail(ctx, AEXIS_E_STATE, "AppendSequencePack4Cdhw output height is too small.");
+    int rc = bind(ctx);
+    if (rc) return rc;
+    return aexis_cuda_check(ctx, launch_kv_append(current, width, rows, slices, offset, cache, cache_rows, ctx->stream),
+                            "kv append launch");
+}
+
+AEXIS_API int aexis_cuda_kv_concat(aexis_ctx* ctx, const float* past, int past_rows, const float* current, int cur_rows,
+                                   int width, int slices, float* out, int out_rows) {
+    if (!ctx) return AEXIS_E_NULL;
+    if (!past) return aexis_fail(ctx, AEXIS_E_NULL, "a is null");
+    if (!current) return aexis_fail(ctx, AEXIS_E_NULL, "b is null");
+    if (!out) return aexis_fail(ctx, AEXIS_E_NULL, "output is null");
+    if (past_rows <= 0 || cur_rows <= 0) return aexis_fail(ctx, AEXIS_E_RANGE, "aHeight=%d bHeight=%d", past_rows, cur_rows);
+    if (width <= 0 || slices <= 0)
+        return aexis_fail(ctx, AEXIS_E_STATE, "ConcatSequencePack4Cdhw requires matching width/depth textures.");
+    if (out_rows < past_rows + cur_rows)
+        return aexis_fail(ctx, AEXIS_E_STATE, "ConcatSequencePack4Cdhw output height is too small.");
+    int rc = bind(ctx);
+    if (rc) return rc;
+    return aexis_cuda_check(ctx, launch_kv_concat(past, past_rows, current, cur_rows, width, slices, out, out_rows,
+                                                  ctx->stream), "kv concat launch");
+}
+
+AEXIS_API int aexis_cuda_sdpa(aexis_ctx* ctx, const float* q, const float* k, const float* v, int src_len, int dst_len,
+                              int embed_dim, int out_embed_dim, int num_heads, int num_groups, float scale,
+                              const float* mask, int mask_w, int mask_h, int causal, int causal_offset, float* out) {
+    if (!ctx) return AEXIS_E_NULL;
+    if (!q) return aexis_fail(ctx, AEXIS_E_NULL, "query is null");
+    if (!k) return aexis_fail(ctx, AEXIS_E_NULL, "key is null");
+    if (!v) return aexis_fail(ctx, AEXIS_E_NULL, "value is null");
+    if (!out) return aexis_fail(ctx, AEXIS_E_NULL, "output is null");
+    if (src_len <= 0) return aexis_fail(ctx, AEXIS_E_RANGE, "srcLen=%d", src_len);
+    if (dst_len <= 0 || sdpa_smem_bytes(dst_len) > 200 * 1024)
+        return aexis_fail(ctx, AEXIS_E_RANGE, "dstLen=%d (max %d)", dst_len, (int)(200 * 1024 / sizeof(float)));
+    if (embed_dim <= 0) return aexis_fail(ctx, AEXIS_E_RANGE, "embedDim=%d", embed_dim);
+    if (out_embed_dim <= 0) return aexis_fail(ctx, AEXIS_E_RANGE, "outEmbedDim=%d", out_embed_dim);
+    if (num_heads <= 0) return aexis_fail(ctx, AEXIS_E_RANGE, "numHeads=%d", num_heads);
+    if (num_groups <= 0) return aexis_fail(ctx, AEXIS_E_RANGE, "numGroups=%d", num_groups);
+    int rc = bind(ctx);
+    if (rc) return rc;
+    return aexis_cuda_check(ctx, launch_sdpa(q, k, v, src_len, dst_len, embed_dim, out_embed_dim, num_heads,
+                                             num_groups, scale, mask, mask ? mask_w : 0, mask ? mask_h : 0, causal,
+                                             causal_offset, out, ctx->stream), "sdpa launch");
+}
+
+AEXIS_API int aexis_cuda_argmax(aexis_ctx* ctx, const float* logits, int rows, int width, int ld, int32_t* out_idx) {
+    if (!ctx) return AEXIS_E_NULL;
+    if (!logits) return aexis_fail(ctx, AEXIS_E_NULL, "input is null");
+    if (!out_idx) return aexis_fail(ctx, AEXIS_E_NULL, "output is null");
+    if (width <= 0) return aexis_fail(ctx, AEXIS_E_RANGE, "logicalWidth=%d", width);
+    if (rows <= 0) return aexis_fail(ctx, AEXIS_E_RANGE, "logicalHeight=%d", rows);
+    if (ld < width) return aexis_fail(ctx, AEXIS_E_SHAPE, "ld=%d < width", ld);
+    int rc = bind(ctx);
+    if (rc) return rc;
+    void* keys = nullptr;
+    rc = aexis_scratch(ctx, sizeof(unsigned long long) * (size_t)rows, &keys);
+    if (rc) return rc;
+    return aexis_cuda_check(ctx, launch_argmax(logits, rows, width, ld, out_idx, (unsigned long long*)keys,
+                                               ctx->sm_count, ctx->stream), "argmax launch");
+}
+
+AEXIS_API int aexis_cuda_topk(aexis_ctx* ctx, const float* logits, int rows, int width, int ld, int k, float* out_vals,
+                              int32_t* out_idx) {
+    if (!ctx) return AEXIS_E_NULL;
+    if (!logits || !out_vals || !out_idx) return aexis_fail(ctx, AEXIS_E_NULL, "null pointer");
+    if (width <= 0 || rows <= 0) return aexis_fail(ctx, AEXIS_E_RANGE, "rows=%d width=%d", rows, width);
+    if (k < 1 || k > 64) return aexis_fail(ctx, AEXIS_E_RANGE, "k=%d (1..64)", k);
+    if (ld < width) return aexis_fail(ctx, AEXIS_E_SHAPE, "ld=%d < width", ld);
+    int rc = bind(ctx);
+    if (rc) return rc;
+    return aexis_cuda_check(ctx, launch_topk(logits, rows, width, ld, k, out_vals, out_idx, ctx->stream), "topk launch");
+}
+
+AEXIS_API int aexis_cuda_embed(aexis_ctx* ctx, const int32_t* words, int count, const aexis_weights* table,
+                               const float* bias, float* out) {
+    if (!ctx) return AEXIS_E_NULL;
+    if (!words || !table || !out) return aexis_fail(ctx, AEXIS_E_NULL, "null pointer");
+    if (count <= 0) return aexis_fail(ctx, AEXIS_E_RANGE, "count=%d", count);
+    int rc = bind(ctx);
+    if (rc) return rc;
+    return aexis_cuda_check(ctx, launch_embed(words, count, table, bias, out, ctx->stream), "embed launch");
+}
+
+AEXIS_API int aexis_cuda_swish(aexis_ctx* ctx, const float* x, int count, float* y) {
+    if (!ctx) return AEXIS_E_NULL;
+    if (!x || !y) return aexis_fail(ctx, AEXIS_E_NULL, "null pointer");
+    if (count <= 0) return aexis_fail(ctx, AEXIS_E_RANGE, "count=%d", count);
+    int rc = bind(ctx);
+    if (rc) return rc;
+    return aexis_cuda_check(ctx, launch_swish(x, count, y, ctx->stream), "swish launch");
+}
+
+AEXIS_API int aexis_cuda_swiglu(aexis_ctx* ctx, const float* gate, const float* up, int count, float* y) {
+    if (!ctx) return AEXIS_E_NULL;
+    if (!gate || !up || !y) return aexis_fail(ctx, AEXIS_E_NULL, "null pointer");
+    if (count <= 0) return aexis_fail(ctx, AEXIS_E_RANGE, "count=%d", count);
+    int rc = bind(ctx);
+    if (rc) return rc;
+    return aexis_cuda_check(ctx, launch_swiglu(gate, up, count, y, ctx->stream), "swiglu launch");
+}

@@ -1,0 +1,141 @@
+// aexis_internal.h -- shared declarations of libaexis_cuda (not part of the ABI).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <cstdint>
+#include <cstdio>
+#include <string>
+#include <vector>
+
+#include "../../include/aexis_cuda.h"
+
+// Weight storage kinds held by an aexis_weights handle.
+enum aexis_wkind { WK_Q4 = 4, WK_Q8 = 8, WK_F16 = 16, WK_F32 = 32 };
+
+struct aexis_weights {
+    int kind = 0;            // aexis_wkind
+    int n = 0, k = 0;        // [n, k] logical shape
+    int group = 0;           // Q4 scale block along the flat index (divides k)
+    int scale_dtype = AEXIS_F32;
+    void* data = nullptr;    // device: packed words (Q4/Q8) or dense values
+    void* scales = nullptr;  // device: fp32 or fp16 scales (Q4/Q8)
+    size_t data_bytes = 0, scale_bytes = 0;
+};
+
+struct aexis_ctx {
+    int device = 0;
+    int sm_count = 0;
+    cudaStream_t own_stream = nullptr;
+    cudaStream_t stream = nullptr;
+    std::string err;
+    // Grow-only device scratch (split-K attention partials, argmax keys).
+    void* scratch = nullptr;
+    size_t scratch_bytes = 0;
+};
+
+// Records `msg` on the context and returns `code`.
+int aexis_fail(aexis_ctx* ctx, int code, const char* fmt, ...);
+// Checks a CUDA call; on failure records "<what>: <cuda error>" and returns E_CUDA.
+int aexis_cuda_check(aexis_ctx* ctx, cudaError_t e, const char* what);
+// Returns a device buffer of at least `bytes` (grow-only, owned by ctx).
+int aexis_scratch(aexis_ctx* ctx, size_t bytes, void** out);
+
+// ---------------------------------------------------------------- launchers
+// Every launcher enqueues on `stream` and returns the launch's cudaError_t.
+
+// Epilogue of the batch-1 GEMV kernels.
+enum gemv_epilogue {
+    EPI_STORE = 0,      // y[n] = alpha * (beta*bias[n] + acc)      (bias may be null)
+    EPI_STORE_TILED,    // y[n] = beta*bias[n] + alpha * acc
+    EPI_RESIDUAL,       // y[n] (fp32) += acc                        (decoder residual add)
+    EPI_SWIGLU,         // rows (2i, 2i+1) = (gate_i, up_i): y[i] = silu(gate)*up
+    EPI_QKV_ROPE,       // decoder QKV: RoPE on row pairs, q -> fp32, k/v -> fp16 cache
+    EPI_LOGITS_ARGMAX,  // y[n] (fp32) = acc, and the greedy key max-reduced into *argmax_key
+};
+
+struct GemvArgs {
+    const void* x = nullptr;      // activation [k] (a_dtype)
+    int a_dtype = AEXIS_F32;
+    const aexis_weights* w = nullptr;
+    const float* bias = nullptr;
+    float alpha = 1.0f, beta = 1.0f;
+    void* y = nullptr;
+    int y_dtype = AEXIS_F32;
+    int epilogue = EPI_STORE;
+    // Optional RMSNorm prologue on x (decoder): x <- x*rsqrt(max(mean(x^2)+eps,1e-20))*gamma.
+    const float* norm_gamma = nullptr;
+    float norm_eps = 0.0f;
+    // EPI_QKV_ROPE extras.
+    const float* rope_cos = nullptr;   // [rot_dim/2] row of this position
+    const float* rope_sin = nullptr;
+    const int* rope_map = nullptr;     // per internal row: packed destination descriptor
+    __half* k_cache = nullptr;         // [kv_heads][cap][head_dim] of this layer
+    __half* v_cache = nullptr;
+    int head_dim = 0, kv_cap = 0, q_rows = 0, kv_rows = 0, rot_dim = 0;
+    const int* pos_ptr = nullptr;      // device position (decoder graph)
+    unsigned long long* argmax_key = nullptr;  // EPI_LOGITS_ARGMAX target
+    bool pdl = false;                  // launch with programmatic dependent launch
+};
+
+// y = W x for one activation row; picks the fast streaming kernel when the
+// weight layout allows it, else the exact generic kernel.
+cudaError_t launch_gemv(const GemvArgs& a, int sm_count, cudaStream_t stream);
+// Reports which kernel launch_gemv would use ("q4_fast", "q8_fast", "generic").
+const char* gemv_kernel_name(const aexis_weights* w);
+
+cudaError_t launch_dequant(const aexis_weights* w, float* out, cudaStream_t s);
+cudaError_t launch_rmsnorm(const void* x, int x_dtype, int rows, int width, int ld,
+                           const float* gamma, int affine_size, float eps, void* y, int y_dtype,
+                           cudaStream_t s);
+cudaError_t launch_rope(const float* src, int embed_dim, int seq_len, int num_heads,
+                        const float* cosv, const float* sinv, int interleaved, float* out,
+                        cudaStream_t s);
+cudaError_t launch_kv_append(const float* cur, int width, int rows, int slices, int offset,
+                             float* cache, int cache_rows, cudaStream_t s);
+cudaError_t launch_kv_concat(const float* a, int a_rows, const float* b, int b_rows, int width,
+                             int slices, float* out, int out_rows, cudaStream_t s);
+cudaError_t launch_sdpa(const float* q, const float* k, const float* v, int src_len, int dst_len,
+                        int embed_dim, int out_embed_dim, int num_heads, int num_groups,
+                        float scale, const float* mask, int mask_w, int mask_h, int causal,
+                        int causal_offset, float* out, cudaStream_t s);
+size_t sdpa_smem_bytes(int dst_len);
+cudaError_t launch_argmax(const float* logits, int rows, int width, int ld, int32_t* out,
+                          unsigned long long* keys, int sm_count, cudaStream_t s);
+cudaError_t launch_topk(const float* logits, int rows, int width, int ld, int k, float* vals,
+                        int32_t* idx, cudaStream_t s);
+cudaError_t launch_embed(const int32_t* words, int count, const aexis_weights* table,
+                         const float* bias, float* out, cudaStream_t s);
+cudaError_t launch_swish(const float* x, int count, float* y, cudaStream_t s);
+cudaError_t launch_swiglu(const float* g, const float* u, int count, float* y, cudaStream_t s);
+
+// Device helpers shared by kernels.
+#ifdef __CUDACC__
+__device__ __forceinline__ float aexis_load_act(const void* p, int dtype, long long i) {
+    return dtype == AEXIS_F16 ? __half2float(reinterpret_cast<const __half*>(p)[i])
+                              : reinterpret_cast<const float*>(p)[i];
+}
+__device__ __forceinline__ void aexis_store_out(void* p, int dtype, long long i, float v) {
+    if (dtype == AEXIS_F16) reinterpret_cast<__half*>(p)[i] = __float2half_rn(v);
+    else reinterpret_cast<float*>(p)[i] = v;
+}
+// Order-preserving map of an fp32 value to uint32 (larger float -> larger key).
+__device__ __forceinline__ unsigned int aexis_orderable(float v) {
+    unsigned int b = __float_as_uint(v);
+    return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+// Greedy-selection key: orderable value in the high word, (~index) in the low
+// word, so the maximum key is the largest value at the lowest index -- the
+// strict > scan of AexisArgMaxPack4LinearMat (HLSL Pack4Matmul:645-686). -0
+// counts as +0; a NaN never wins unless it is at index 0 (where it wins, as in
+// the scan).
+__device__ __forceinline__ unsigned long long aexis_argmax_key(float v, int idx) {
+    unsigned int hi;
+    if (v != v) hi = idx == 0 ? 0xFFFFFFFFu : 0u;
+    else hi = aexis_orderable(v == 0.0f ? 0.0f : v);
+    return ((unsigned long long)hi << 32) | (unsigned long long)(0xFFFFFFFFu - (unsigned int)idx);
+}
+__device__ __forceinline__ int aexis_argmax_index(unsigned long long key) {
+    return key == 0ull ? 0 : (int)(0xFFFFFFFFu - (unsigned int)(key & 0xFFFFFFFFull));
+}
+#endif

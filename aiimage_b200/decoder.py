@@ -1,0 +1,113 @@
+"""DecoderSession: the host mirror of Qwen35DecoderSession's greedy decode
+(Packages/com.aexis/Samples/AIImageApplicationExample/Runtime/Scripts/
+Qwen35DecoderSession.cs: Generate :1160-1237, DecodeCore :469-585,
+SelectNextToken :734-809) over libaexis_cuda's fused decoder.
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import numpy as np
+
+from . import errors
+from .native import F16, F32, DecoderConfig, check, lib
+from .ops import AexisOps
+from .synth import DecoderCfg
+
+
+def _np(a):
+    return a.ctypes.data_as(C.c_void_p)
+
+
+class DecoderSession:
+    def __init__(self, ops: AexisOps, cfg: DecoderCfg, scale_dtype: int = F16):
+        self.ops, self.cfg = ops, cfg
+        c = cfg
+        self._cfg = DecoderConfig(c.n_layers, c.hidden, c.n_heads, c.n_kv_heads, c.head_dim, c.ffn, c.vocab,
+                                  c.kv_capacity, c.rot_dim, c.bits, c.group, c.lm_bits, c.lm_group, scale_dtype,
+                                  c.rope_theta, c.eps)
+        self.h = C.c_void_p()
+        check(lib().aexis_cuda_decoder_create(ops.ctx, C.byref(self._cfg), C.byref(self.h)), ops.ctx)
+        self._scale_dtype = scale_dtype
+
+    def close(self):
+        if self.h:
+            lib().aexis_cuda_decoder_destroy(self.h)
+            self.h = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def _check(self, st):
+        check(st, self.ops.ctx)
+
+    # -- loading (AexisGemmLayer / AexisRMSNormLayer / AexisEmbedLayer LoadLayer)
+    def set_linear(self, layer: int, which: int, packed: np.ndarray, scales: np.ndarray):
+        p = np.ascontiguousarray(packed, dtype=np.uint32)
+        s = np.ascontiguousarray(scales, dtype=np.float16 if self._scale_dtype == F16 else np.float32)
+        self._check(lib().aexis_cuda_decoder_set_linear(self.h, layer, which, _np(p), _np(s), self._scale_dtype))
+
+    def set_norm(self, layer: int, which: int, gamma: np.ndarray):
+        g = np.ascontiguousarray(gamma)
+        dt = F16 if g.dtype == np.float16 else F32
+        g = g.astype(np.float16 if dt == F16 else np.float32, copy=False)
+        self._check(lib().aexis_cuda_decoder_set_norm(self.h, layer, which, _np(g), dt))
+
+    def set_embedding(self, table: np.ndarray):
+        t = np.ascontiguousarray(table)
+        dt = F16 if t.dtype == np.float16 else F32
+        t = t.astype(np.float16 if dt == F16 else np.float32, copy=False)
+        self._check(lib().aexis_cuda_decoder_set_embedding(self.h, _np(t), dt))
+
+    def load(self, model) -> "DecoderSession":
+        """Upload every weight of a SyntheticDecoder (or any object with the
+        same linear/norm/embedding accessors)."""
+        c = self.cfg
+        for layer in range(c.n_layers):
+            for which in range(7):
+                self.set_linear(layer, which, *model.linear(layer, which))
+            for which in range(2):
+                self.set_norm(layer, which, model.norm(layer, which))
+        self.set_linear(-1, 7, *model.linear(-1, 7))
+        self.set_norm(-1, 0, model.norm(-1, 0))
+        self.set_embedding(model.embedding)
+        return self
+
+    # -- decoding -----------------------------------------------------------
+    def reset(self):
+        self._check(lib().aexis_cuda_decoder_reset(self.h))
+
+    @property
+    def position(self) -> int:
+        v = C.c_int32()
+        self._check(lib().aexis_cuda_decoder_position(self.h, C.byref(v)))
+        return v.value
+
+    def prefill(self, tokens) -> int:
+        t = np.ascontiguousarray(tokens, dtype=np.int32)
+        out = np.zeros(1, dtype=np.int32)
+        self._check(lib().aexis_cuda_decoder_prefill(self.h, _np(t), t.size, _np(out)))
+        return int(out[0])
+
+    def step(self, token: int) -> int:
+        out = np.zeros(1, dtype=np.int32)
+        self._check(lib().aexis_cuda_decoder_step(self.h, int(token), _np(out)))
+        return int(out[0])
+
+    def generate(self, prompt, max_new: int) -> list[int]:
+        """Greedy: prefill `prompt`, return max_new generated token ids."""
+        p = np.ascontiguousarray(prompt, dtype=np.int32)
+        out = np.zeros(max_new, dtype=np.int32)
+        self._check(lib().aexis_cuda_decoder_generate(self.h, _np(p), p.size, max_new, _np(out)))
+        return [int(x) for x in out]
+
+    def logits(self) -> np.ndarray:
+        out = np.empty(self.cfg.vocab, dtype=np.float32)
+        self._check(lib().aexis_cuda_decoder_logits(self.h, _np(out)))
+        return out
+
+
+__all__ = ["DecoderSession", "errors"]

@@ -1,0 +1,245 @@
+"""Host-side mirror of the reference's AexisOps operator surface for the
+quantized-decoder hot path, over the libaexis_cuda C ABI.
+
+Method names follow Packages/com.aexis/Runtime/Execution/Graph/AexisOps.cs in
+snake_case, with the same argument meaning and the same error classes
+(aiimage_b200.errors). Tensors are torch CUDA tensors used only as device
+memory; every computation runs in libaexis_cuda's kernels on the tensor's
+device. Work is enqueued on torch's current stream.
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import numpy as np
+
+from . import errors
+from .native import F16, F32, check, lib
+
+
+def _ptr(t):
+    return None if t is None else C.c_void_p(t.data_ptr())
+
+
+def _dtype_code(t) -> int:
+    import torch
+    if t.dtype == torch.float32:
+        return F32
+    if t.dtype == torch.float16:
+        return F16
+    raise errors.NotSupportedError(f"dtype {t.dtype} (float32 or float16)")
+
+
+def _np_ptr(a: np.ndarray):
+    return a.ctypes.data_as(C.c_void_p)
+
+
+class Weights:
+    """An uploaded weight (InnerProductPack / Int{4,8}WeightOnlyUpload)."""
+
+    def __init__(self, ops: "AexisOps", handle, kind: str, n: int, k: int, group: int = 0):
+        self._ops, self.handle, self.kind, self.n, self.k, self.group = ops, handle, kind, n, k, group
+
+    def free(self):
+        if self.handle:
+            lib().aexis_cuda_weights_free(self._ops.ctx, self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            if self._ops.ctx:
+                self.free()
+        except Exception:
+            pass
+
+
+def quantize_rows(bits: int, data: np.ndarray, out_ch: int, per_ch: int, contiguous: bool = True):
+    """AexisGraphSession.NewInt{8,4}WeightOnlyUpload(float[], ...) host quantizer
+    (AexisGraphSession.cs:12834-12964): returns (packed uint32, scales fp32)."""
+    d = np.ascontiguousarray(data, dtype=np.float32).reshape(-1)
+    if d.size != out_ch * per_ch:
+        raise errors.ArgumentError("weight layout must contain exactly outputChannels * valuesPerOutputChannel values")
+    per_word = 8 if bits == 4 else 4
+    packed = np.zeros(max(1, (d.size + per_word - 1) // per_word), dtype=np.uint32)
+    scales = np.zeros(out_ch, dtype=np.float32)
+    fn = lib().aexis_quantize_q4_rows if bits == 4 else lib().aexis_quantize_q8_rows
+    check(fn(_np_ptr(d), out_ch, per_ch, int(contiguous), _np_ptr(packed), _np_ptr(scales)))
+    return packed, scales
+
+
+class AexisOps:
+    """One libaexis_cuda context on one GPU (new AexisOps(), AexisOps.cs)."""
+
+    def __init__(self, device: int = 0, use_torch_stream: bool = True):
+        self.ctx = C.c_void_p()
+        self.device = device
+        st = lib().aexis_cuda_create(device, C.byref(self.ctx))
+        if st != 0:
+            msg = lib().aexis_cuda_last_error(None)
+            raise errors.BY_STATUS.get(st, errors.AexisError)(msg.decode() if msg else "create failed")
+        self._use_torch_stream = use_torch_stream
+        self._int8 = None
+        self._int4 = None
+
+    # -- context ---------------------------------------------------------
+    def close(self):
+        if self.ctx:
+            lib().aexis_cuda_destroy(self.ctx)
+            self.ctx = C.c_void_p()
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def _bind_stream(self):
+        if self._use_torch_stream:
+            import torch
+            s = torch.cuda.current_stream(self.device).cuda_stream
+            lib().aexis_cuda_set_stream(self.ctx, C.c_void_p(s))
+
+    def _call(self, fn, *args):
+        self._bind_stream()
+        check(fn(self.ctx, *args), self.ctx)
+
+    def sync(self):
+        check(lib().aexis_cuda_sync(self.ctx), self.ctx)
+
+    # -- weights ----------------------------------------------------------
+    def new_int8_weight_only_upload(self, packed: np.ndarray, scales: np.ndarray, n: int, k: int) -> Weights:
+        """AexisGraphSession.NewInt8WeightOnlyUpload(AexisQuantizedTensor, n) (:12887-12910)."""
+        p = np.ascontiguousarray(packed, dtype=np.uint32)
+        s = np.ascontiguousarray(scales)
+        sd = F16 if s.dtype == np.float16 else F32
+        s = s.astype(np.float16 if sd == F16 else np.float32, copy=False)
+        if s.size != n:
+            raise errors.ArgumentError("Direct Q8 upload must contain one scale per output channel.")
+        if p.size != max(1, (n * k + 3) // 4):
+            raise errors.ArgumentError("Direct Q8 packed payload size mismatch.")
+        h = C.c_void_p()
+        check(lib().aexis_cuda_weights_q8(self.ctx, _np_ptr(p), _np_ptr(s), sd, n, k, C.byref(h)), self.ctx)
+        return Weights(self, h, "q8", n, k)
+
+    def new_int4_weight_only_upload(self, packed: np.ndarray, scales: np.ndarray, n: int, k: int,
+                                    group: int) -> Weights:
+        """AexisGraphSession.NewInt4WeightOnlyUpload(AexisQuantizedTensor, n, k) (:12966-12998)."""
+        p = np.ascontiguousarray(packed, dtype=np.uint32)
+        s = np.ascontiguousarray(scales)
+        sd = F16 if s.dtype == np.float16 else F32
+        s = s.astype(np.float16 if sd == F16 else np.float32, copy=False)
+        if group <= 0 or k % group != 0:
+            raise errors.ArgumentError("Direct Q4 group size must divide the Gemm K dimension.")
+        if s.size != n * k // group:
+            raise errors.ArgumentError("Direct Q4 upload scale count does not match its group size.")
+        if p.size != max(1, (n * k + 7) // 8):
+            raise errors.ArgumentError("Direct Q4 packed payload size mismatch.")
+        h = C.c_void_p()
+        check(lib().aexis_cuda_weights_q4(self.ctx, _np_ptr(p), _np_ptr(s), sd, n, k, group, C.byref(h)), self.ctx)
+        return Weights(self, h, "q4", n, k, group)
+
+    def new_dense_weights(self, data: np.ndarray) -> Weights:
+        a = np.ascontiguousarray(data)
+        dt = F16 if a.dtype == np.float16 else F32
+        a = a.astype(np.float16 if dt == F16 else np.float32, copy=False)
+        n, k = a.shape
+        h = C.c_void_p()
+        check(lib().aexis_cuda_weights_dense(self.ctx, _np_ptr(a), dt, n, k, C.byref(h)), self.ctx)
+        return Weights(self, h, "f16" if dt == F16 else "f32", n, k)
+
+    def set_int8_gemm_weights(self, w: Weights | None):
+        """AexisOps.SetInt8GemmWeights (:706-712)."""
+        self._int8 = w
+
+    def set_int4_gemm_weights(self, w: Weights | None):
+        """AexisOps.SetInt4GemmWeights (:730-739)."""
+        self._int4 = w
+
+    def dequant(self, w: Weights, out):
+        self._call(lib().aexis_cuda_weights_dequant, w.handle, _ptr(out))
+
+    # -- linear -----------------------------------------------------------
+    def _gemm(self, fn, a, c, m, n, k, trans_b, alpha, beta, use_c, broadcast_type_c, output):
+        if a is None:
+            raise errors.ArgumentNullError("a")
+        if output is None:
+            raise errors.ArgumentNullError("output")
+        if use_c and c is None:
+            raise errors.ArgumentNullError("c")
+        w = self._int4 or self._int8
+        if w is None:
+            raise errors.NotSupportedError("only INT4/INT8 weight-only Gemm weights are implemented by this backend")
+        if not trans_b:
+            raise errors.NotSupportedError("quantized Gemm weights are stored transB (output-channel major)")
+        if use_c and broadcast_type_c != 4:
+            raise errors.NotSupportedError("bias broadcast type 4 (per output column) only")
+        lda = a.stride(0) if a.dim() == 2 else k
+        ldy = output.stride(0) if output.dim() == 2 else n
+        self._call(fn, _ptr(a), _dtype_code(a), lda, m, k, w.handle, _ptr(c) if use_c else None, alpha, beta,
+                   _ptr(output), _dtype_code(output), ldy, n)
+
+    def gemm2d_pack4_linear_texture_a(self, a, c, m, n, k, trans_b=True, alpha=1.0, beta=1.0, use_c=False,
+                                      broadcast_type_c=4, output=None):
+        """AexisOps.Gemm2DPack4LinearTextureA (:3649-3683)."""
+        self._gemm(lib().aexis_cuda_gemm, a, c, m, n, k, trans_b, alpha, beta, use_c, broadcast_type_c, output)
+
+    def gemm2d_pack4_tiled_texture_a(self, a, c, m, n, k, trans_b=True, alpha=1.0, beta=1.0, use_c=False,
+                                     broadcast_type_c=4, output=None):
+        """AexisOps.Gemm2DPack4TiledTextureAFromLinear (:3722-3752); output row stride = its tiled width."""
+        self._gemm(lib().aexis_cuda_gemm_tiled, a, c, m, n, k, trans_b, alpha, beta, use_c, broadcast_type_c,
+                   output)
+
+    # -- pointwise --------------------------------------------------------
+    def rms_norm_pack4_linear_mat(self, x, rows, width, gamma, affine_size, affine, eps, output):
+        """AexisOps.RmsNormPack4LinearMat (:8267-8283)."""
+        if x is None:
+            raise errors.ArgumentNullError("input")
+        if output is None:
+            raise errors.ArgumentNullError("output")
+        ld = x.stride(0) if x.dim() == 2 else width
+        g = gamma if affine else None
+        self._call(lib().aexis_cuda_rmsnorm, _ptr(x), _dtype_code(x), rows, width, ld, _ptr(g),
+                   affine_size if affine else 0, eps, _ptr(output), _dtype_code(output))
+
+    def rotary_embed_pack4(self, x, embed_dim, seq_len, num_heads, cos, sin, interleaved, output):
+        """AexisOps.RotaryEmbedPack4 (:8514-8540); Pack4 CDHW fp32."""
+        self._call(lib().aexis_cuda_rope, _ptr(x), embed_dim, seq_len, num_heads, _ptr(cos), _ptr(sin),
+                   int(interleaved), _ptr(output))
+
+    def append_sequence_pack4_cdhw(self, current, destination_offset, current_height, cache, width, slices,
+                                   cache_rows):
+        """AexisOps.AppendSequencePack4Cdhw (:6384-6400)."""
+        self._call(lib().aexis_cuda_kv_append, _ptr(current), width, current_height, slices, destination_offset,
+                   _ptr(cache), cache_rows)
+
+    def concat_sequence_pack4_cdhw(self, a, b, a_height, b_height, output, width, slices, out_rows):
+        """AexisOps.ConcatSequencePack4Cdhw (:6336-6360)."""
+        self._call(lib().aexis_cuda_kv_concat, _ptr(a), a_height, _ptr(b), b_height, width, slices, _ptr(output),
+                   out_rows)
+
+    def sdpa_attention_pack4_cdhw(self, q, k, v, src_len, dst_len, embed_dim, out_embed_dim, num_heads,
+                                  num_groups, scale, output, mask=None, mask_w=0, mask_h=0, causal=False,
+                                  causal_query_offset=0):
+        """AexisOps.SdpaAttentionPack4Cdhw (:10147-10200)."""
+        self._call(lib().aexis_cuda_sdpa, _ptr(q), _ptr(k), _ptr(v), src_len, dst_len, embed_dim, out_embed_dim,
+                   num_heads, num_groups, scale, _ptr(mask), mask_w, mask_h, int(causal), causal_query_offset,
+                   _ptr(output))
+
+    def arg_max_pack4_linear_mat(self, logits, logical_width, logical_height, output, ld=None):
+        """AexisOps.ArgMaxPack4LinearMat (:9982-10003); output int32 [rows]."""
+        ld = ld if ld is not None else (logits.stride(0) if logits.dim() == 2 else logical_width)
+        self._call(lib().aexis_cuda_argmax, _ptr(logits), logical_height, logical_width, ld, _ptr(output))
+
+    def top_k(self, logits, width, rows, k, out_vals, out_idx, ld=None):
+        ld = ld if ld is not None else (logits.stride(0) if logits.dim() == 2 else width)
+        self._call(lib().aexis_cuda_topk, _ptr(logits), rows, width, ld, k, _ptr(out_vals), _ptr(out_idx))
+
+    def embed_texture(self, words, count, table: Weights, bias, output):
+        """AexisOps.EmbedTexture (:10764-10810)."""
+        self._call(lib().aexis_cuda_embed, _ptr(words), count, table.handle, _ptr(bias), _ptr(output))
+
+    def swish(self, x, count, y):
+        self._call(lib().aexis_cuda_swish, _ptr(x), count, _ptr(y))
+
+    def swiglu(self, gate, up, count, y):
+        self._call(lib().aexis_cuda_swiglu, _ptr(gate), _ptr(up), count, _ptr(y))

@@ -1,0 +1,298 @@
+/*
+ * aexis_cuda.h -- C ABI of libaexis_cuda, the B200 (sm_100a) backend for the
+ * Aexis quantized-decoder hot path.
+ *
+ * Each entry point replaces one AexisOps / AexisGraphSession method of the
+ * reference (paths relative to Packages/com.aexis/Runtime/ in newzjh/AIImage;
+ * "Ops" = Execution/Graph/AexisOps.cs, "Session" = Execution/Graph/
+ * AexisGraphSession.cs). Argument meaning and validation follow the cited
+ * method; where the reference throws, the call returns the matching status:
+ *   ArgumentNullException        -> AEXIS_E_NULL
+ *   ArgumentOutOfRangeException  -> AEXIS_E_RANGE
+ *   ArgumentException            -> AEXIS_E_SHAPE
+ *   NotSupportedException        -> AEXIS_E_UNSUPPORTED
+ *   InvalidOperationException    -> AEXIS_E_STATE
+ * and aexis_cuda_last_error(ctx) holds the message. No C++ exception crosses
+ * this boundary.
+ *
+ * Memory: "device" pointers are CUDA device memory owned by the caller;
+ * "host" pointers are host memory the call copies from or to before it
+ * returns. Tensors keep the reference's logical Pack4 layouts:
+ *   - a 2-D [rows, W] matrix is row-major with a caller-given row stride
+ *     (Pack4 linear storage uses stride ceil(W/4)*4);
+ *   - a CDHW tensor [W, H, 1, C] stores element (x, y, c) at
+ *     ((c/4 * H + y) * W + x) * 4 + (c & 3).
+ * All device work is enqueued on the context's stream and is asynchronous;
+ * aexis_cuda_sync() waits for it. A context is not thread-safe; use one per
+ * GPU (and per host thread).
+ */
+#ifndef AEXIS_CUDA_H_
+#define AEXIS_CUDA_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define AEXIS_CUDA_ABI_VERSION 1
+
+typedef enum aexis_status {
+    AEXIS_OK = 0,
+    AEXIS_E_NULL = 1,
+    AEXIS_E_RANGE = 2,
+    AEXIS_E_SHAPE = 3,
+    AEXIS_E_UNSUPPORTED = 4,
+    AEXIS_E_STATE = 5,
+    AEXIS_E_CUDA = 6,
+    AEXIS_E_TIMEOUT = 7
+} aexis_status;
+
+typedef enum aexis_dtype {
+    AEXIS_F32 = 0,
+    AEXIS_F16 = 1
+} aexis_dtype;
+
+typedef struct aexis_ctx aexis_ctx;
+typedef struct aexis_weights aexis_weights;
+typedef struct aexis_decoder aexis_decoder;
+
+/* ------------------------------------------------------------------ context */
+
+/* ABI version of the loaded library (AEXIS_CUDA_ABI_VERSION). No reference
+ * counterpart; lets a binding check it loaded a matching library. */
+int aexis_cuda_abi_version(void);
+
+/* new AexisOps() (Ops constructor): binds `device` and creates the context's
+ * stream. Checks that the device is sm_100. */
+int aexis_cuda_create(int device, aexis_ctx** out);
+
+/* AexisOps.Dispose (Ops): frees the context's stream and scratch. */
+int aexis_cuda_destroy(aexis_ctx* ctx);
+
+/* Last error message of the context ("" when none). A NULL ctx returns the
+ * message of the last failed aexis_cuda_create on this thread. */
+const char* aexis_cuda_last_error(const aexis_ctx* ctx);
+
+/* Enqueue subsequent work on a caller-owned cudaStream_t (NULL restores the
+ * context's own stream). The reference records into a CommandBuffer
+ * (Ops Gemm2DPack4LinearTextureA(CommandBuffer, ...) overloads, Ops:3685). */
+int aexis_cuda_set_stream(aexis_ctx* ctx, void* cuda_stream);
+
+/* Graphics.ExecuteCommandBuffer + readback fence: wait for enqueued work. */
+int aexis_cuda_sync(aexis_ctx* ctx);
+
+/* ------------------------------------------------------------------ weights */
+
+/* Session.NewInt8WeightOnlyUpload(AexisQuantizedTensor, n) (Session:12887-
+ * 12910) followed by Ops.SetInt8GemmWeights (Ops:706-712).
+ * packed: host, ceil(n*k/4) uint32, element (row, col) = byte (idx & 3) of word
+ * idx >> 2 with idx = row*k + col, two's complement. scales: host, one per
+ * output row, fp32 or fp16 (scale_dtype). The library keeps its own device copy.
+ * Errors: NULL arrays -> E_NULL; n, k <= 0 -> E_RANGE. */
+int aexis_cuda_weights_q8(aexis_ctx* ctx, const uint32_t* packed, const void* scales,
+                          int scale_dtype, int n, int k, aexis_weights** out);
+
+/* Session.NewInt4WeightOnlyUpload(AexisQuantizedTensor, n, k) (Session:12966-
+ * 12998) followed by Ops.SetInt4GemmWeights (Ops:730-739).
+ * packed: host, ceil(n*k/8) uint32, nibble (idx & 7) of word idx >> 3 (low
+ * nibble first), two's complement [-8, 7]. scales: host, n*k/group values;
+ * element idx uses scale idx / group. group must divide k (E_SHAPE otherwise,
+ * as the reference's "group size must divide the Gemm K dimension"). */
+int aexis_cuda_weights_q4(aexis_ctx* ctx, const uint32_t* packed, const void* scales,
+                          int scale_dtype, int n, int k, int group, aexis_weights** out);
+
+/* Plain fp16 or fp32 [n, k] table (Ops.SetFp16GemmWeights / the _EmbedW
+ * buffer of Ops.EmbedTexture, Ops:10764-10810). Used by aexis_cuda_embed. */
+int aexis_cuda_weights_dense(aexis_ctx* ctx, const void* data, int dtype, int n, int k,
+                             aexis_weights** out);
+
+/* InnerProductPack.Dispose (Session:357-367): release a weight handle. */
+int aexis_cuda_weights_free(aexis_ctx* ctx, aexis_weights* w);
+
+/* Dequantize the whole weight to fp32 [n, k] (device `out`), one
+ * AexisGemm2DReadB (HLSL Pack4Matmul:707-734) per element. Used to prove
+ * bit-exact unpacking and indexing. */
+int aexis_cuda_weights_dequant(aexis_ctx* ctx, const aexis_weights* w, float* out);
+
+/* Host-side quantizers of the float upload paths: Session.NewInt8Weight-
+ * OnlyUpload(float[], ...) (Session:12834-12885) and NewInt4WeightOnlyUpload
+ * (float[], ...) (Session:12912-12964): per output channel scale maxAbs/127
+ * (or /7), values RoundToInt (midpoint to even) and clamped to [-127, 127]
+ * (or [-7, 7]). `packed` (ceil(n*k/4) or /8 words) and `scales` (out_ch
+ * floats) are host arrays the call fills. For Q4 the effective scale block is
+ * per_ch when outputs are contiguous (scaleBlockSize, Session:12956). */
+int aexis_quantize_q8_rows(const float* data, int out_ch, int per_ch, int contiguous,
+                           uint32_t* packed, float* scales);
+int aexis_quantize_q4_rows(const float* data, int out_ch, int per_ch, int contiguous,
+                           uint32_t* packed, float* scales);
+
+/* ------------------------------------------------------------------- linear */
+
+/* Ops.Gemm2DPack4LinearTextureA(a, inputPacked, b, c, m, n, k, transB=true,
+ * alpha, beta, useC, broadcastTypeC=4, output) (Ops:3649-3683), kernel
+ * AexisGemm2DPack4LinearTextureAFromLinear (HLSL Pack4Matmul:1038-1104):
+ *   y[r, c] = alpha * (beta * bias[c] + sum_k a[r, k] * W(c, k))
+ * a: device [m, lda] of a_dtype; bias: device fp32 [n] or NULL (useC=false);
+ * y: device [m, ldy] of y_dtype. Accumulation is fp32.
+ * Errors: a/w/y NULL -> E_NULL; m, n, k <= 0 -> E_RANGE; n or k not the
+ * weight's shape, lda < k or ldy < n -> E_SHAPE. */
+int aexis_cuda_gemm(aexis_ctx* ctx, const void* a, int a_dtype, int lda, int m, int k,
+                    const aexis_weights* w, const float* bias, float alpha, float beta,
+                    void* y, int y_dtype, int ldy, int n);
+
+/* Ops.Gemm2DPack4TiledTextureAFromLinear (Ops:3722-3752), the lm_head
+ * variant (HLSL Pack4Matmul:2245-2300): bias is added after the sum,
+ *   y[r, c] = beta * bias[c] + alpha * sum_k a[r, k] * W(c, k).
+ * A tiled Pack4 output texture is row-major with row stride ldy (its
+ * tileRowsPerMatrix * width * 4 floats). */
+int aexis_cuda_gemm_tiled(aexis_ctx* ctx, const void* a, int a_dtype, int lda, int m, int k,
+                          const aexis_weights* w, const float* bias, float alpha, float beta,
+                          void* y, int y_dtype, int ldy, int n);
+
+/* --------------------------------------------------------- pointwise layers */
+
+/* Ops.RmsNormPack4LinearMat(input, shape, gamma, affineSize, affine, eps,
+ * output) (Ops:8267-8283; COMMON AexisRmsNormPack4LinearMat:4531-4563), per row:
+ *   y = x * rsqrt(max(mean(x^2) + eps, 1e-20)) * gamma[clamp(i, 0, affine_size-1)]
+ * gamma NULL (or affine_size 0) means no affine. x, y device; ld is the row
+ * stride of both. */
+int aexis_cuda_rmsnorm(aexis_ctx* ctx, const void* x, int x_dtype, int rows, int width, int ld,
+                       const float* gamma, int affine_size, float eps, void* y, int y_dtype);
+
+/* Ops.RotaryEmbedPack4(input, shape[w=embed, h=seq, c=heads], cos, sin,
+ * interleaved, output) (Ops:8514-8540; HLSL Pack4PointwiseNorm:414-473).
+ * src/out: device fp32 Pack4 CDHW [embed_dim, seq_len, 1, num_heads];
+ * cos/sin: device fp32 [seq_len, embed_dim/2]. Rotate-half unless interleaved. */
+int aexis_cuda_rope(aexis_ctx* ctx, const float* src, int embed_dim, int seq_len, int num_heads,
+                    const float* cos_table, const float* sin_table, int interleaved, float* out);
+
+/* Ops.AppendSequencePack4Cdhw(current, offset, rows, cache) (Ops:6384-6400;
+ * HLSL Pack4Elementwise:84-98): copy `rows` rows of `current` (Pack4 CDHW,
+ * width texels x rows x slices) into rows offset.. of `cache` (cache_rows
+ * rows). Rows beyond the cache are dropped. offset < 0 -> E_RANGE. */
+int aexis_cuda_kv_append(aexis_ctx* ctx, const float* current, int width, int rows, int slices,
+                         int offset, float* cache, int cache_rows);
+
+/* Ops.ConcatSequencePack4Cdhw(a, b, aHeight, bHeight, output) (Ops:6336-6360;
+ * HLSL Pack4Elementwise:64-81); rows past a_rows + b_rows are zeroed. */
+int aexis_cuda_kv_concat(aexis_ctx* ctx, const float* past, int past_rows, const float* current,
+                         int cur_rows, int width, int slices, float* out, int out_rows);
+
+/* Ops.SdpaAttentionPack4Cdhw(q, k, v, srcLen, dstLen, embedDim, outEmbedDim,
+ * numHeads, numGroups, scale, output, mask, causal, causalQueryOffset)
+ * (Ops:10147-10200; HLSL Pack4Matmul:420-557). q/out: Pack4 CDHW [embed,
+ * src_len, 1, num_heads]; k: [embed, dst_len, 1, num_groups]; v: [out_embed,
+ * dst_len, 1, num_groups]; mask: NULL or single-channel Pack4 [mask_w, mask_h]
+ * (value in lane 0 of each texel). GQA kv head = head / (num_heads/num_groups).
+ * The reference rejects dst_len > 4096; this backend accepts any dst_len. */
+int aexis_cuda_sdpa(aexis_ctx* ctx, const float* q, const float* k, const float* v, int src_len,
+                    int dst_len, int embed_dim, int out_embed_dim, int num_heads, int num_groups,
+                    float scale, const float* mask, int mask_w, int mask_h, int causal,
+                    int causal_offset, float* out);
+
+/* Ops.ArgMaxPack4LinearMat(logits, logicalWidth, logicalHeight, tileRows,
+ * output) (Ops:9982-10003; HLSL Pack4Matmul:645-686): per row the first index
+ * of the maximum (strict >, so ties go to the lowest index; a NaN is never
+ * chosen unless it is at index 0). logits: device fp32 [rows, ld];
+ * out_idx: device int32 [rows]. */
+int aexis_cuda_argmax(aexis_ctx* ctx, const float* logits, int rows, int width, int ld,
+                      int32_t* out_idx);
+
+/* Top-k per row for the sampler (Qwen35Sampler, Samples/.../Qwen35Decoder-
+ * Session.cs:1823-1900 sorts the full vocabulary on the CPU): the k largest
+ * logits in descending order, equal values by ascending index.
+ * out_vals/out_idx: device [rows, k]. 1 <= k <= 64. */
+int aexis_cuda_topk(aexis_ctx* ctx, const float* logits, int rows, int width, int ld, int k,
+                    float* out_vals, int32_t* out_idx);
+
+/* Ops.EmbedTexture (Ops:10764-10810; HLSL BufferTensor AexisEmbedValue:37-62):
+ * out[q, p] = W(clamp(words[q], 0, vocab-1), p) (+ bias[p]) for a Q4 (group
+ * scales), Q8 (per-token scales) or dense table. words: device int32 [count];
+ * bias: device fp32 [dim] or NULL; out: device fp32 [count, dim]. */
+int aexis_cuda_embed(aexis_ctx* ctx, const int32_t* words, int count, const aexis_weights* table,
+                     const float* bias, float* out);
+
+/* AexisSwishLinearMat (HLSL Pack4Matmul:91-94,205-218): y = x / (1 + exp(-x)). */
+int aexis_cuda_swish(aexis_ctx* ctx, const float* x, int count, float* y);
+
+/* Swish on the gate then BinaryOp multiply by the up projection, as one pass
+ * (HLSL Pack4Matmul:91-94,118-128): y = silu(gate) * up. */
+int aexis_cuda_swiglu(aexis_ctx* ctx, const float* gate, const float* up, int count, float* y);
+
+/* ------------------------------------------------------------------ decoder */
+
+/* Shape of the full-attention decoder stack driven by Qwen35DecoderSession
+ * (Samples/.../Qwen35DecoderSession.cs:167-172 for the reference constants). */
+typedef struct aexis_decoder_config {
+    int32_t n_layers;
+    int32_t hidden;
+    int32_t n_heads;
+    int32_t n_kv_heads;
+    int32_t head_dim;
+    int32_t ffn;
+    int32_t vocab;
+    int32_t kv_capacity;   /* KV cache length (positions) */
+    int32_t rot_dim;       /* rotated dims per head (rotate-half), even, <= head_dim */
+    int32_t bits;          /* 4 or 8: decoder linear weights */
+    int32_t group;         /* Q4 group along K (divides hidden and ffn) */
+    int32_t lm_bits;       /* 4 or 8: lm_head */
+    int32_t lm_group;      /* Q4 group of the lm_head */
+    int32_t scale_dtype;   /* AEXIS_F16 or AEXIS_F32: dtype of every weight scale */
+    float rope_theta;
+    float eps;             /* RMSNorm eps */
+} aexis_decoder_config;
+
+/* Qwen35DecoderSession constructor (Qwen35DecoderSession.cs:1748-1766):
+ * allocates the weights, fp16 KV cache and the per-step CUDA graph. */
+int aexis_cuda_decoder_create(aexis_ctx* ctx, const aexis_decoder_config* cfg,
+                              aexis_decoder** out);
+int aexis_cuda_decoder_destroy(aexis_decoder* dec);
+
+/* Weight loading (AexisGemmLayer.LoadLayer -> NewInt{4,8}WeightOnlyUpload,
+ * AexisGemmLayer.cs:15-160). layer in [0, n_layers) with which: 0 q_proj,
+ * 1 k_proj, 2 v_proj, 3 o_proj, 4 gate_proj, 5 up_proj, 6 down_proj; or
+ * layer -1, which 7 for the lm_head. Arrays are host arrays in the same
+ * packed format as aexis_cuda_weights_q4 / _q8. */
+int aexis_cuda_decoder_set_linear(aexis_decoder* dec, int layer, int which, const uint32_t* packed,
+                                  const void* scales, int scale_dtype);
+
+/* RMSNorm gammas (AexisRMSNormLayer.LoadLayer, AexisRMSNormLayer.cs:16-45):
+ * which 0 = input norm, 1 = post-attention norm; layer -1 = final norm.
+ * gamma: host [hidden] of dtype. */
+int aexis_cuda_decoder_set_norm(aexis_decoder* dec, int layer, int which, const void* gamma,
+                                int dtype);
+
+/* Token embedding table (AexisEmbedLayer, AexisEmbedLayer.cs:40-180): host
+ * [vocab, hidden] of dtype. */
+int aexis_cuda_decoder_set_embedding(aexis_decoder* dec, const void* table, int dtype);
+
+/* Qwen35DecoderSession.CreateInitialState (:376-400): position back to 0. */
+int aexis_cuda_decoder_reset(aexis_decoder* dec);
+int aexis_cuda_decoder_position(const aexis_decoder* dec, int32_t* out_position);
+
+/* RunTokens for a prompt (Qwen35DecoderSession.cs:1254-1269): appends
+ * `count` host token ids at the current position and writes the greedy next
+ * token (host) after the last one. */
+int aexis_cuda_decoder_prefill(aexis_decoder* dec, const int32_t* tokens, int count,
+                               int32_t* next_token);
+
+/* One decode step (DecodeCore :469-585 + SelectNextToken :734-809, greedy):
+ * host token id in, host greedy token out (the reference's per-token argmax
+ * readback). E_RANGE when the KV cache is full. */
+int aexis_cuda_decoder_step(aexis_decoder* dec, int32_t token, int32_t* next_token);
+
+/* Qwen35DecoderSession.Generate (:1160-1237), greedy, no EOS stop: prefill
+ * `prompt`, then produce max_new tokens into out_tokens (host). */
+int aexis_cuda_decoder_generate(aexis_decoder* dec, const int32_t* prompt, int n_prompt,
+                                int max_new, int32_t* out_tokens);
+
+/* The fp32 logits of the last step (host [vocab]), for sampling outside the
+ * greedy path (Qwen35DecoderSession.ProjectLogits :715-733). */
+int aexis_cuda_decoder_logits(aexis_decoder* dec, float* out_logits);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* AEXIS_CUDA_H_ */
