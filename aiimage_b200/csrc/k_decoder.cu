@@ -159,17 +159,19 @@ __global__ void __launch_bounds__(kAttnThreads) dec_attn_kernel(
     if (tid == 0) counters[g] = 0u;
 }
 
-// token = argmax(key); out_tokens[*step] = token (when given); position += 1.
+// token = argmax(key); out_tokens[*step] = token while *step < max_out;
+// position += 1.
 __global__ void dec_finish_kernel(const unsigned long long* key, int* token, int* pos, int* out_tokens,
-                                  int* step, int emit) {
+                                  int* step, int emit, int max_out) {
     griddep_wait();
     griddep_launch();
     if (threadIdx.x == 0 && blockIdx.x == 0) {
         if (emit) {
             const int t = aexis_argmax_index(*key);
             *token = t;
-            if (out_tokens) out_tokens[*step] = t;
-            *step += 1;
+            const int s = *step;
+            if (out_tokens && s >= 0 && s < max_out) out_tokens[s] = t;
+            *step = s + 1;
         }
         *pos += 1;
     }
@@ -378,7 +380,8 @@ cudaError_t enqueue_step(aexis_decoder* d, cudaStream_t s, int emit) {
         const unsigned long long* key = d->key;
         int* outs = d->ints + 3;
         int em = emit;
-        void* args[] = {(void*)&key, &token, &pos, &outs, &step, &em};
+        int mo = d->max_out;
+        void* args[] = {(void*)&key, &token, &pos, &outs, &step, &em, &mo};
         e = launch_pdl((const void*)dec_finish_kernel, dim3(1), dim3(32), 0, s, args);
     }
     return e;

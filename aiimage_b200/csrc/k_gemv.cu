@@ -402,7 +402,9 @@ __global__ void __launch_bounds__(kThreads) gemv_generic_kernel(
 template <int BITS, typename ST, int SMODE, int R>
 cudaError_t launch_fast_t(const FastParams& fp, int sm_count, bool pdl, cudaStream_t stream) {
     auto kern = gemv_fast_kernel<BITS, ST, SMODE, R>;
-    const size_t smem = (size_t)fp.k * sizeof(float);
+    // The swizzle permutes 16-byte units inside groups of eight: pad the
+    // buffer to whole groups so every swizzled unit is inside it.
+    const size_t smem = (size_t)((fp.k + 31) / 32 * 32) * sizeof(float);
     static int occ = -1;  // resident CTAs per SM for this instantiation (queried once)
     static size_t occ_smem = 0;
     if (occ < 0 || occ_smem != smem) {

@@ -1,0 +1,508 @@
+#!/usr/bin/env python
+"""Benchmark of the quantized-decoder hot path on B200 (libaexis_cuda).
+
+Headline: the batch-1 Q4 group-32 dequant-GEMV sweep over
+(K, N) = (1024,3072), (1024,512), (1024,3584), (3584,1024), (1024,151936), in
+algorithmic HBM GB/s. One step = one pass over the five GEMVs (fp16 x and y,
+fp16 scales, fp32 accumulation). Weight sets are rotated among copies whose
+total is > 4x L2, so no step finds its weights in L2. Steps are replayed from
+CUDA graphs (programmatic dependent launch between the GEMVs).
+
+Also reported: config 1 (Q8 GEMV) and config 3 (the 24-layer synthetic Q4
+decoder: 512-token prompt, 64 greedy tokens, tokens/s), the dominant kernel's
+roofline, the CPU oracle baseline, clocks during the timed region, and the
+end-to-end number through the C ABI with host buffers.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+
+N > 1 runs under torchrun: the sweep does not shard (a GEMV has no exchange),
+so every rank runs the same workload as an independent replica; value is the
+aggregate over ranks, timed as the max over ranks.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+from aiimage_b200 import synth  # noqa: E402
+
+SWEEP = synth.Q4_SWEEP
+GROUP = 32
+SWEEP_BYTES = [synth.gemv_bytes(4, n, k, GROUP) for (k, n) in SWEEP]
+STEP_BYTES = sum(SWEEP_BYTES)
+L2_BYTES = 126 * 1024 * 1024
+DOMINANT = 4  # (1024, 151936): the lm_head-sized GEMV, 93% of a step's bytes
+
+
+def measured_peak():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def profile_traffic(name: str):
+    """DRAM bytes per launch from a committed ncu summary (profiles/<name>),
+    line 'traffic_bytes_per_launch: <int>'; None when absent."""
+    path = os.path.join(ROOT, "profiles", name)
+    try:
+        for line in open(path):
+            if line.strip().startswith("traffic_bytes_per_launch:"):
+                return int(line.split(":", 1)[1].strip().split()[0])
+    except OSError:
+        pass
+    return None
+
+
+class ClockSampler:
+    """Samples SM clock and throttle reasons through NVML while running."""
+
+    REASONS = {"gpu_idle": 0x1, "applications_clocks_setting": 0x2, "sw_power_cap": 0x4, "hw_slowdown": 0x8,
+               "sync_boost": 0x10, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
+               "hw_power_brake_slowdown": 0x80, "display_clock_setting": 0x100}
+
+    def __init__(self, index: int, period_s: float = 0.005):
+        self.index, self.period = index, period_s
+        self.samples, self.reasons = [], set()
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._t = None
+
+    def __enter__(self):
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self._nv = pynvml
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(self.index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+        except Exception as e:  # NVML missing: report no samples
+            self.error = str(e)
+        return self
+
+    def _run(self):
+        nv = self._nv
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM))
+                try:
+                    r = nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+                except AttributeError:
+                    r = nv.nvmlDeviceGetCurrentClocksThrottleReasons(self._h)
+                for name, bit in self.REASONS.items():
+                    if r & bit and name != "gpu_idle":
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            time.sleep(self.period)
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._t:
+            self._t.join()
+
+    def summary(self):
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None,
+                "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+def dist_setup(n_gpus: int):
+    import torch
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world: int):
+    import torch
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+class Sweep:
+    """The config-2 weight sets, uploaded `copies` times, and per-copy graphs."""
+
+    def __init__(self, ops, seed: int = 1):
+        import torch
+        self.ops = ops
+        self.copies = max(2, -(-4 * L2_BYTES // STEP_BYTES))  # total > 4x L2
+        host = [synth.q4_weights(n, k, GROUP, seed, tag=(k, n)) for (k, n) in SWEEP]
+        self.w = [[ops.new_int4_weight_only_upload(p, s, n, k, GROUP) for (p, s), (k, n) in zip(host, SWEEP)]
+                  for _ in range(self.copies)]
+        self.x_host = [synth.activations(k, seed, tag=(k, n)) for (k, n) in SWEEP]
+        self.x = [torch.from_numpy(x).cuda() for x in self.x_host]
+        self.y = [torch.zeros((1, n), dtype=torch.float16, device="cuda") for (k, n) in SWEEP]
+        self.x_pin = [torch.from_numpy(x).pin_memory() for x in self.x_host]
+        self.y_pin = [torch.zeros((1, n), dtype=torch.float16).pin_memory() for (k, n) in SWEEP]
+
+    def gemv(self, copy: int, i: int):
+        k, n = SWEEP[i]
+        self.ops.set_int8_gemm_weights(None)
+        self.ops.set_int4_gemm_weights(self.w[copy][i])
+        self.ops.gemm2d_pack4_linear_texture_a(self.x[i], None, 1, n, k, True, 1.0, 1.0, False, 4, self.y[i])
+
+    def step(self, copy: int):
+        for i in range(len(SWEEP)):
+            self.gemv(copy, i)
+
+    def graph(self, fn, reps: int):
+        """Capture `reps` rotations of fn(copy) over all copies into one graph."""
+        import torch
+        g = torch.cuda.CUDAGraph()
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            with torch.cuda.graph(g, stream=s):
+                for _ in range(reps):
+                    for c in range(self.copies):
+                        fn(c)
+        torch.cuda.current_stream().wait_stream(s)
+        return g
+
+
+def time_graph_steps(graph_big, steps_per_big, graphs_single, copies, steps, warmup, world):
+    """Replay graphs for exactly `steps` steps after `warmup`; CUDA-event time."""
+    import torch
+
+    def run(n):
+        done = 0
+        while n - done >= steps_per_big:
+            graph_big.replay()
+            done += steps_per_big
+        while done < n:
+            graphs_single[done % copies].replay()
+            done += 1
+
+    run(warmup)
+    barrier(world)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    run(steps)
+    end.record()
+    end.synchronize()
+    barrier(world)
+    return start.elapsed_time(end) / 1e3
+
+
+def run_gpu(args):
+    import torch
+    world, rank, local = dist_setup(args.gpus)
+    from aiimage_b200.ops import AexisOps
+    from aiimage_b200 import native
+    native.lib()  # fails loudly when the CUDA library is missing
+    ops = AexisOps(local)
+    sw = Sweep(ops)
+    copies = sw.copies
+    for c in range(copies):  # first calls outside capture (kernel attributes, occupancy)
+        sw.step(c)
+    torch.cuda.synchronize()
+    singles = [sw.graph(lambda c, cc=cc: sw.step(cc) if c == 0 else None, 1) for cc in range(copies)]
+    reps = max(1, 60 // copies)
+    big = sw.graph(sw.step, reps)
+    steps_per_big = reps * copies
+
+    with ClockSampler(local) as clk:
+        secs = time_graph_steps(big, steps_per_big, singles, copies, args.steps, args.warmup, world)
+    secs = max_over_ranks(secs, world)
+    value = world * args.steps * STEP_BYTES / secs / 1e9
+
+    # Dominant kernel alone: back-to-back launches over rotating copies.
+    def dom(c):
+        sw.gemv(c, DOMINANT)
+    dom_reps = max(1, 120 // copies)
+    g_dom = sw.graph(dom, dom_reps)
+    g_dom.replay()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n_rep = 5
+    ev0.record()
+    for _ in range(n_rep):
+        g_dom.replay()
+    ev1.record()
+    ev1.synchronize()
+    dom_launches = n_rep * dom_reps * copies
+    dom_s = ev0.elapsed_time(ev1) / 1e3 / dom_launches
+    peak, peak_kind = measured_peak()
+    achieved = SWEEP_BYTES[DOMINANT] / dom_s / 1e9
+    traffic = profile_traffic("q4_gemv_1024x151936.md")
+
+    # Per-shape throughput (each GEMV alone, same method), config 1 Q8 GEMV.
+    per_shape = {}
+    for i, (k, n) in enumerate(SWEEP):
+        g = sw.graph(lambda c, i=i: sw.gemv(c, i), max(1, 120 // copies))
+        g.replay()
+        torch.cuda.synchronize()
+        ev0.record()
+        g.replay()
+        ev1.record()
+        ev1.synchronize()
+        t = ev0.elapsed_time(ev1) / 1e3 / (max(1, 120 // copies) * copies)
+        per_shape[f"{k}x{n}"] = {"us": round(t * 1e6, 3), "GB/s": round(SWEEP_BYTES[i] / t / 1e9, 1),
+                                 "frac": round(SWEEP_BYTES[i] / t / 1e9 / peak, 3)}
+    q8 = bench_q8(ops, peak)
+
+    # End to end through the C ABI with host buffers: per step, H2D of the five
+    # activations from pinned memory, the five gemm calls, D2H of the outputs.
+    stream = torch.cuda.current_stream()
+
+    def e2e_step(c):
+        for i in range(len(SWEEP)):
+            sw.x[i].copy_(sw.x_pin[i], non_blocking=True)
+        sw.step(c)
+        for i in range(len(SWEEP)):
+            sw.y_pin[i].copy_(sw.y[i], non_blocking=True)
+        stream.synchronize()
+
+    e2e_steps = max(1, min(args.steps, 200))
+    for c in range(min(args.warmup, copies)):
+        e2e_step(c)
+    barrier(world)
+    ev0.record()
+    for i in range(e2e_steps):
+        e2e_step(i % copies)
+    ev1.record()
+    ev1.synchronize()
+    e2e_s = max_over_ranks(ev0.elapsed_time(ev1) / 1e3, world)
+    h2d = sum(k * 2 for k, n in SWEEP)
+    d2h = sum(n * 2 for k, n in SWEEP)
+
+    decoder = None
+    if not args.skip_decoder:
+        try:
+            decoder = bench_decoder(ops, peak)
+        except Exception as e:  # reported, never silently replaced
+            decoder = {"error": f"{type(e).__name__}: {e}"}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.skip_cpu:
+        cpu = cpu_baseline(args.cpu_seconds)
+
+    if rank == 0:
+        line = {
+            "metric": "Q4 g32 dequant-GEMV sweep, algorithmic HBM GB/s (batch 1)",
+            "value": round(value, 1),
+            "unit": "GB/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(secs / args.steps * 1e3, 5),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "int4 weights, fp16 act/scales, fp32 accumulate",
+            "data": "synthetic (seeded PCG64; BASELINE config 2 shapes and distributions)",
+            "config": {"workload": "config2_q4_g32_gemv_sweep_m1", "shapes_KxN": [list(s) for s in SWEEP],
+                       "bytes_per_step": STEP_BYTES, "weight_copies": copies,
+                       "l2": f"weights rotated over {copies} copies ({copies * STEP_BYTES / 2**20:.0f} MiB > 4x L2)",
+                       "parallelism": f"replicas x{world}"},
+            "roofline": {"bound": "hbm", "kernel": "gemv_fast q4 (1024x151936)",
+                         "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "traffic": traffic,
+                         "algorithmic_bytes_per_launch": SWEEP_BYTES[DOMINANT],
+                         "us_per_launch": round(dom_s * 1e6, 3), "peak_source": peak_kind + " (MEASURED_PEAKS.json hbm_gbs)"},
+            "per_shape": per_shape,
+            "config1_q8": q8,
+            "decoder": decoder,
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(e2e_steps * STEP_BYTES * world / e2e_s / 1e9, 2), "unit": "GB/s",
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "path": "aexis_cuda_gemm via ctypes, pinned host x/y, sync per step"},
+            "gpu_launches": args.steps * len(SWEEP),
+            "clocks": clk.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    ops.close()
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+def bench_q8(ops, peak):
+    """Q8 K=1024 N=3584 GEMV (rotated copies, graph)."""
+    import torch
+    k, n = 1024, 3584
+    p, s = synth.q8_weights(n, k, seed=0)
+    b = synth.gemv_bytes(8, n, k)
+    copies = max(2, -(-4 * L2_BYTES // b))
+    ws = [ops.new_int8_weight_only_upload(p, s, n, k) for _ in range(copies)]
+    x = torch.from_numpy(synth.activations(k, seed=0)).cuda()
+    y = torch.zeros((1, n), dtype=torch.float16, device="cuda")
+
+    def call(c):
+        ops.set_int4_gemm_weights(None)
+        ops.set_int8_gemm_weights(ws[c])
+        ops.gemm2d_pack4_linear_texture_a(x, None, 1, n, k, True, 1.0, 1.0, False, 4, y)
+
+    call(0)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    st = torch.cuda.Stream()
+    st.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(st):
+        with torch.cuda.graph(g, stream=st):
+            for c in range(copies):
+                call(c)
+    torch.cuda.current_stream().wait_stream(st)
+    g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(3):
+        g.replay()
+    e1.record()
+    e1.synchronize()
+    t = e0.elapsed_time(e1) / 1e3 / (3 * copies)
+    return {"shape_KxN": [k, n], "bytes": b, "us": round(t * 1e6, 3), "GB/s": round(b / t / 1e9, 1),
+            "frac": round(b / t / 1e9 / peak, 3)}
+
+
+def bench_decoder(ops, peak):
+    """24-layer synthetic Q4 decoder, 512-token prompt, then
+    64 greedy tokens. Device tokens/s from the graph-chained generate call
+    (one H2D token in, one D2H of the 64 ids out), and the per-token host
+    round-trip rate (aexis_cuda_decoder_step: id in, greedy id out)."""
+    import torch
+    from aiimage_b200.decoder import DecoderSession
+    cfg = synth.QWEN35_08B_Q4
+    model = synth.SyntheticDecoder(cfg, seed=3)
+    prompt = model.prompt(512, seed=30)
+    sess = DecoderSession(ops, cfg).load(model)
+    sess.prefill(prompt[:-1])
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    toks = sess.generate(prompt[-1:], 64)  # 64 decode steps, positions 511..574
+    gen_s = time.perf_counter() - t0
+    sess.reset()
+    sess.prefill(prompt[:-1])
+    nxt = int(prompt[-1])
+    t0 = time.perf_counter()
+    for _ in range(64):
+        nxt = sess.step(nxt)
+    step_s = time.perf_counter() - t0
+    kv_mean = cfg.n_layers * 2 * cfg.n_kv_heads * cfg.head_dim * 2 * (511 + 32)
+    bytes_tok = model.weight_bytes_per_token() + kv_mean
+    sess.close()
+    return {"workload": "config3_q4_decoder_prompt512_greedy64", "tokens_per_s": round(64 / gen_s, 1),
+            "ms_per_token": round(gen_s / 64 * 1e3, 4), "e2e_tokens_per_s_host_roundtrip": round(64 / step_s, 1),
+            "bytes_per_token": bytes_tok, "GB/s": round(bytes_tok * 64 / gen_s / 1e9, 1),
+            "frac": round(bytes_tok * 64 / gen_s / 1e9 / peak, 3), "first_tokens": toks[:8],
+            "kernels_per_token": 2 + 5 * cfg.n_layers + 1}
+
+
+def cpu_baseline(budget_s: float = 12.0):
+    """The CPU oracle (restated reference path) on the same sweep, all host
+    threads, bounded to ~budget_s of work."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    O.build()
+    host = [synth.q4_weights(n, k, GROUP, 1, tag=(k, n)) for (k, n) in SWEEP]
+    xs = [synth.activations(k, 1, tag=(k, n)).astype(np.float32) for (k, n) in SWEEP]
+    scales = [s.astype(np.float32) for _, s in host]
+    passes, t0 = 0, time.perf_counter()
+    while True:
+        for (p, _), s, x, (k, n) in zip(host, scales, xs, SWEEP):
+            O.gemm(x, 4, p, s, GROUP, n)
+        passes += 1
+        el = time.perf_counter() - t0
+        if el >= budget_s or passes >= 50:
+            break
+    return {"value": round(passes * STEP_BYTES / el / 1e9, 3), "unit": "GB/s", "cores": O.num_threads(),
+            "kind": "port", "sample": f"{passes} full sweep pass(es) of config 2 through the C++ oracle "
+                                      f"(sequential fp32 per output, OpenMP over outputs), {el:.1f} s"}
+
+
+def run_reference(args):
+    """--impl reference: the reference's CPU path for this workload (the C++
+    oracle restating AexisGemm2DPack4LinearTextureA / AexisGemm2DReadB) on all
+    host threads. Under torchrun only rank 0 runs."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    O.build()
+    host = [synth.q4_weights(n, k, GROUP, 1, tag=(k, n)) for (k, n) in SWEEP]
+    xs = [synth.activations(k, 1, tag=(k, n)).astype(np.float32) for (k, n) in SWEEP]
+    scales = [s.astype(np.float32) for _, s in host]
+
+    def step():
+        for (p, _), s, x, (k, n) in zip(host, scales, xs, SWEEP):
+            O.gemm(x, 4, p, s, GROUP, n)
+
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    el = time.perf_counter() - t0
+    value = args.steps * STEP_BYTES / el / 1e9
+    line = {"impl": "reference", "metric": "Q4 g32 dequant-GEMV sweep, algorithmic HBM GB/s (batch 1)",
+            "value": round(value, 3), "unit": "GB/s", "n_gpus": int(os.environ.get("WORLD_SIZE", "1")),
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(el / args.steps * 1e3, 3),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "int4 weights, fp32 compute", "data": "synthetic (same seeded inputs as the GPU arm)",
+            "config": {"workload": "config2_q4_g32_gemv_sweep_m1", "shapes_KxN": [list(s) for s in SWEEP]},
+            "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": O.num_threads(), "kind": "port",
+                             "sample": f"{args.steps} full sweep passes through the C++ oracle"},
+            "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=3000)
+    ap.add_argument("--warmup", type=int, default=30)
+    ap.add_argument("--impl", choices=["aexis", "reference"], default="aexis")
+    ap.add_argument("--skip-decoder", action="store_true", help="omit the config-3 decoder measurement")
+    ap.add_argument("--skip-cpu", action="store_true", help="omit the CPU oracle baseline")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    if args.impl == "reference":
+        if args.steps > 20:
+            args.steps = 20  # each reference step is a full CPU pass (~0.5 s); bound the run
+        run_reference(args)
+    else:
+        run_gpu(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -297,14 +297,16 @@ class OracleDecoder:
         return nxt, logits, float(margin[0])
 
     def generate(self, prompt, max_new: int):
-        """Qwen35DecoderSession.Generate, greedy: returns (tokens, margins)."""
+        """Qwen35DecoderSession.Generate, greedy: returns (tokens, margins);
+        the logits of the last step are kept in self.last_logits."""
         prompt = [int(t) for t in prompt]
         for t in prompt[:-1]:
             self.step(t, want_logits=False)
-        tok, _, margin = self.step(prompt[-1])
+        tok, logits, margin = self.step(prompt[-1])
         out, margins = [tok], [margin]
         while len(out) < max_new:
-            tok, _, margin = self.step(tok)
+            tok, logits, margin = self.step(tok)
             out.append(tok)
             margins.append(margin)
+        self.last_logits = logits
         return out, margins

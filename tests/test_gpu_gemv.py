@@ -1,0 +1,187 @@
+"""GPU parity of the dequant GEMV (libaexis_cuda) against the CPU oracle.
+
+Tolerance (the north-star bar for fp16/fp32 accumulation): every output within
+1e-2 relative, |gpu - ref| <= 1e-2 * |ref| + 1e-3 * max|ref|, plus a norm-wise
+relative error <= 2e-3. Unpacking and indexing are checked bit-exact through
+aexis_cuda_weights_dequant.
+"""
+import numpy as np
+import pytest
+
+from aiimage_b200 import errors, synth
+
+pytestmark = pytest.mark.gpu
+
+RTOL, ATOL_REL, NORM_TOL = 1e-2, 1e-3, 2e-3
+
+
+def assert_gemv_close(got, ref):
+    got = np.asarray(got, dtype=np.float64)
+    ref = np.asarray(ref, dtype=np.float64)
+    scale = np.abs(ref).max()
+    err = np.abs(got - ref)
+    bad = err > RTOL * np.abs(ref) + ATOL_REL * scale
+    assert not bad.any(), f"{bad.sum()} outputs off; worst {err.max():.3g} at {int(err.argmax())} (scale {scale:.3g})"
+    assert np.linalg.norm(got - ref) <= NORM_TOL * np.linalg.norm(ref)
+
+
+def run_gemv(ops, w, x16, n, dtype_out, bias=None, alpha=1.0, beta=1.0, tiled=False, x_f32=False):
+    import torch
+    x = torch.from_numpy(x16.astype(np.float32) if x_f32 else x16).cuda()
+    m = x.shape[0]
+    y = torch.zeros((m, n), dtype=dtype_out, device="cuda")
+    b = None if bias is None else torch.from_numpy(bias).cuda()
+    ops.set_int4_gemm_weights(w if w.kind == "q4" else None)
+    ops.set_int8_gemm_weights(w if w.kind == "q8" else None)
+    fn = ops.gemm2d_pack4_tiled_texture_a if tiled else ops.gemm2d_pack4_linear_texture_a
+    fn(x, b, m, n, w.k, True, alpha, beta, b is not None, 4, y)
+    torch.cuda.synchronize()
+    return y.float().cpu().numpy()
+
+
+def test_config1_q8_gemv(ops, oracle):
+    """Q8 K=1024 N=3584, fp16 per-row scales, fp16 x and y, seed 0."""
+    k, n = 1024, 3584
+    p, s = synth.q8_weights(n, k, seed=0)
+    x = synth.activations(k, seed=0)
+    w = ops.new_int8_weight_only_upload(p, s, n, k)
+    import torch
+    got = run_gemv(ops, w, x, n, torch.float16)
+    ref = oracle.gemm(x.astype(np.float32), 8, p, s.astype(np.float32), 0, n)
+    assert_gemv_close(got, ref)
+
+
+@pytest.mark.parametrize("k,n", synth.Q4_SWEEP)
+def test_config2_q4_sweep(ops, oracle, k, n):
+    """Q4 group 32, fp16 scales, every sweep shape."""
+    import torch
+    p, s = synth.q4_weights(n, k, 32, seed=1, tag=(k, n))
+    x = synth.activations(k, seed=1, tag=(k, n))
+    w = ops.new_int4_weight_only_upload(p, s, n, k, 32)
+    got = run_gemv(ops, w, x, n, torch.float16)
+    ref = oracle.gemm(x.astype(np.float32), 4, p, s.astype(np.float32), 32, n)
+    assert_gemv_close(got, ref)
+
+
+@pytest.mark.parametrize("bits,k,n,group,sdt", [
+    (4, 1024, 256, 16, np.float32),   # reference-native mobile Q4: group 16, fp32 scales
+    (4, 2048, 96, 64, np.float16),    # group 64 (scale per two chunks)
+    (4, 1024, 72, 1024, np.float32),  # per-row Q4 (float upload path, scaleBlockSize = K)
+    (4, 3584, 40, 3584, np.float16),  # per-row, K not a power of two
+    (8, 3584, 128, 0, np.float32),    # Q8, K spans several tiles
+    (8, 4096, 24, 0, np.float16),
+])
+def test_fast_kernel_formats(ops, oracle, bits, k, n, group, sdt):
+    import torch
+    if bits == 4:
+        p, s = synth.q4_weights(n, k, group, seed=2, tag=(k, n, group))
+        s = s.astype(sdt)
+        w = ops.new_int4_weight_only_upload(p, s, n, k, group)
+    else:
+        p, s = synth.q8_weights(n, k, seed=2, tag=(k, n))
+        s = s.astype(sdt)
+        w = ops.new_int8_weight_only_upload(p, s, n, k)
+    x = synth.activations(k, seed=2, tag=(k,))
+    got = run_gemv(ops, w, x, n, torch.float32)
+    ref = oracle.gemm(x.astype(np.float32), bits, p, s.astype(np.float32), group, n)
+    assert_gemv_close(got, ref)
+
+
+@pytest.mark.parametrize("bits,k,n,group", [(4, 100, 37, 10), (4, 48, 33, 16), (8, 40, 19, 0), (8, 7, 5, 0),
+                                            (4, 5, 3, 5)])
+def test_generic_kernel_odd_shapes(ops, oracle, bits, k, n, group):
+    """Shapes the streaming kernel cannot take (rows not 16-byte aligned, odd K)
+    go through the exact flat-index kernel."""
+    import torch
+    r = np.random.default_rng(k * 131 + n)
+    words = (n * k + (7 if bits == 4 else 3)) // (8 if bits == 4 else 4)
+    p = r.integers(0, 2 ** 32, size=words, dtype=np.uint64).astype(np.uint32)
+    s = r.uniform(0.002, 0.02, size=(n * k // group) if bits == 4 else n).astype(np.float32)
+    w = (ops.new_int4_weight_only_upload(p, s, n, k, group) if bits == 4
+         else ops.new_int8_weight_only_upload(p, s, n, k))
+    x = synth.activations(k, seed=3, tag=(k,))
+    got = run_gemv(ops, w, x, n, torch.float32)
+    ref = oracle.gemm(x.astype(np.float32), bits, p, s, group, n)
+    assert_gemv_close(got, ref)
+
+
+@pytest.mark.parametrize("bits,k,n,group,sdt", [(4, 1024, 512, 32, np.float16), (4, 1024, 64, 16, np.float32),
+                                                (8, 1024, 300, 0, np.float16), (4, 100, 37, 10, np.float32),
+                                                (8, 7, 5, 0, np.float32)])
+def test_dequant_bit_exact(ops, oracle, bits, k, n, group, sdt):
+    """Every element of AexisGemm2DReadB, bit for bit."""
+    import torch
+    r = np.random.default_rng(n)
+    words = (n * k + (7 if bits == 4 else 3)) // (8 if bits == 4 else 4)
+    p = r.integers(0, 2 ** 32, size=words, dtype=np.uint64).astype(np.uint32)
+    s = r.uniform(0.002, 0.02, size=(n * k // group) if bits == 4 else n).astype(sdt)
+    w = (ops.new_int4_weight_only_upload(p, s, n, k, group) if bits == 4
+         else ops.new_int8_weight_only_upload(p, s, n, k))
+    out = torch.empty(n * k, dtype=torch.float32, device="cuda")
+    ops.dequant(w, out)
+    got = out.cpu().numpy().reshape(n, k)
+    ref = oracle.dequant(bits, p, s.astype(np.float32), group, n, k)
+    assert np.array_equal(got.view(np.uint32), ref.view(np.uint32))
+
+
+@pytest.mark.parametrize("tiled", [False, True])
+def test_bias_alpha_beta_rows_and_strides(ops, oracle, tiled):
+    """m > 1 with Pack4 row strides, fp32 in/out, bias seeded (linear) or added
+    after (tiled), alpha/beta."""
+    import torch
+    k, n, m = 1024, 250, 3
+    p, s = synth.q4_weights(n, k, 32, seed=4)
+    w = ops.new_int4_weight_only_upload(p, s, n, k, 32)
+    x = synth.activations(k, seed=4, m=m).astype(np.float32)
+    bias = np.random.default_rng(4).standard_normal(n).astype(np.float32)
+    ld = (n + 3) // 4 * 4 + 4
+    xa = torch.zeros((m, k + 12), dtype=torch.float32, device="cuda")
+    xa[:, :k] = torch.from_numpy(x).cuda()
+    y = torch.zeros((m, ld), dtype=torch.float32, device="cuda")
+    b = torch.from_numpy(bias).cuda()
+    ops.set_int8_gemm_weights(None)
+    ops.set_int4_gemm_weights(w)
+    fn = ops.gemm2d_pack4_tiled_texture_a if tiled else ops.gemm2d_pack4_linear_texture_a
+    fn(xa, b, m, n, k, True, 0.5, 2.0, True, 4, y)
+    torch.cuda.synchronize()
+    got = y[:, :n].cpu().numpy()
+    ref = oracle.gemm(x, 4, p, s.astype(np.float32), 32, n, bias=bias, alpha=0.5, beta=2.0, tiled=tiled)
+    assert_gemv_close(got, ref)
+    assert torch.count_nonzero(y[:, n:]).item() == 0  # padding lanes untouched
+
+
+def test_reference_gemm_known_answer_on_gpu(ops):
+    """NcnnInt8WeightOnlyGpuTests.AssertGemmKernel through the GPU path (1e-5)."""
+    import torch
+    from aiimage_b200.ops import quantize_rows
+    inp = np.array([1, -1, 0.5, 2], dtype=np.float32)
+    wts = np.array([1, -0.5, 0.25, 2, 0.5, 1, -1, 0.25], dtype=np.float32)
+    bias = np.array([0.1, -0.2], dtype=np.float32)
+    p, s = quantize_rows(8, wts, 2, 4)
+    w = ops.new_int8_weight_only_upload(p, s, 2, 4)
+    got = run_gemv(ops, w, inp.reshape(1, 4), 2, torch.float32, bias=bias, x_f32=True)[0]
+    f = np.float32
+    for oc in range(2):
+        q = np.clip(np.rint(wts[oc * 4:oc * 4 + 4] / s[oc]), -127, 127)
+        exp = f(bias[oc]) + f(np.sum(inp * q.astype(np.float32) * s[oc], dtype=np.float32))
+        assert abs(got[oc] - exp) <= 1e-5
+
+
+def test_argument_errors(ops):
+    import torch
+    p, s = synth.q4_weights(64, 64, 32, seed=5)
+    w = ops.new_int4_weight_only_upload(p, s, 64, 64, 32)
+    ops.set_int8_gemm_weights(None)
+    ops.set_int4_gemm_weights(w)
+    x = torch.zeros((1, 64), dtype=torch.float16, device="cuda")
+    y = torch.zeros((1, 64), dtype=torch.float16, device="cuda")
+    with pytest.raises(errors.ArgumentError):
+        ops.gemm2d_pack4_linear_texture_a(x, None, 1, 32, 64, output=y)  # n differs from the weight
+    with pytest.raises(errors.ArgumentOutOfRangeError):
+        ops.gemm2d_pack4_linear_texture_a(x, None, 0, 64, 64, output=y)
+    with pytest.raises(errors.ArgumentNullError):
+        ops.gemm2d_pack4_linear_texture_a(x, None, 1, 64, 64, use_c=True, output=y)
+    with pytest.raises(errors.ArgumentError):
+        ops.new_int4_weight_only_upload(p, s, 64, 64, 48)  # group does not divide K
+    with pytest.raises(errors.ArgumentError):
+        ops.new_int8_weight_only_upload(p, s[:10], 64, 64)

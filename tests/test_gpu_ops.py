@@ -1,0 +1,211 @@
+"""GPU parity of the pointwise / attention / selection kernels against the oracle
+and the reference's own golden cases (Pack4 layouts at the ABI)."""
+import math
+
+import numpy as np
+import pytest
+
+from test_oracle_pins import create_values, pack4_to_planar, planar_to_pack4, reference_sdpa_with_cache
+
+pytestmark = pytest.mark.gpu
+
+
+def cuda(a):
+    import torch
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def host(t):
+    import torch
+    torch.cuda.synchronize()
+    return t.cpu().numpy()
+
+
+@pytest.mark.parametrize("dtype", ["f32", "f16"])
+def test_rmsnorm(ops, oracle, dtype):
+    import torch
+    x = np.random.default_rng(1).standard_normal((3, 1024)).astype(np.float32)
+    if dtype == "f16":
+        x = x.astype(np.float16).astype(np.float32)
+    g = np.random.default_rng(2).standard_normal(1024).astype(np.float32) * 0.02
+    xt = cuda(x.astype(np.float16) if dtype == "f16" else x)
+    y = torch.zeros((3, 1024), dtype=torch.float32, device="cuda")
+    ops.rms_norm_pack4_linear_mat(xt, 3, 1024, cuda(g), 1024, True, 1e-6, y)
+    assert np.allclose(host(y), oracle.rmsnorm(x, g, eps=1e-6), rtol=2e-6, atol=1e-9)
+    ops.rms_norm_pack4_linear_mat(xt, 3, 1024, cuda(g), 1, True, 1e-6, y)
+    assert np.allclose(host(y), oracle.rmsnorm(x, g, eps=1e-6, affine_size=1), rtol=2e-6, atol=1e-9)
+    ops.rms_norm_pack4_linear_mat(xt, 3, 1024, None, 0, False, 1e-6, y)
+    assert np.allclose(host(y), oracle.rmsnorm(x, None, eps=1e-6), rtol=2e-6, atol=1e-9)
+
+
+@pytest.mark.parametrize("interleaved", [False, True])
+def test_rope(ops, oracle, interleaved):
+    import torch
+    E, L, H = 128, 3, 10
+    src = np.random.default_rng(3).standard_normal(((H + 3) // 4) * L * E * 4).astype(np.float32)
+    cos, sin = oracle.rope_tables(L, E, 1e6)
+    out = torch.zeros(src.size, dtype=torch.float32, device="cuda")
+    ops.rotary_embed_pack4(cuda(src), E, L, H, cuda(cos), cuda(sin), interleaved, out)
+    ref = oracle.rope(src, E, L, H, cos, sin, interleaved)
+    got = host(out)
+    valid = pack4_to_planar(ref, E, L, H)
+    assert np.array_equal(pack4_to_planar(got, E, L, H), valid)
+
+
+def test_kv_append_and_concat_bit_exact(ops, oracle):
+    import torch
+    W, slices, cap = 128, 1, 16
+    cur = np.random.default_rng(4).standard_normal(slices * 2 * W * 4).astype(np.float32)
+    cache0 = np.random.default_rng(5).standard_normal(slices * cap * W * 4).astype(np.float32)
+    cache = cuda(cache0.copy())
+    ops.append_sequence_pack4_cdhw(cuda(cur), 5, 2, cache, W, slices, cap)
+    assert np.array_equal(host(cache), oracle.append_sequence(cur, W, 2, slices, 5, cache0, cap))
+    a = np.random.default_rng(6).standard_normal(2 * 3 * W * 4).astype(np.float32)
+    b = np.random.default_rng(7).standard_normal(2 * 2 * W * 4).astype(np.float32)
+    out = torch.full((2 * 7 * W * 4,), 9.0, dtype=torch.float32, device="cuda")
+    ops.concat_sequence_pack4_cdhw(cuda(a), cuda(b), 3, 2, out, W, 2, 7)
+    assert np.array_equal(host(out), oracle.concat_sequence(a, 3, b, 2, W, 2, 7))
+    from aiimage_b200 import errors
+    with pytest.raises(errors.InvalidOperationError):
+        ops.append_sequence_pack4_cdhw(cuda(cur), 15, 2, cache, W, slices, cap)
+    with pytest.raises(errors.ArgumentOutOfRangeError):
+        ops.append_sequence_pack4_cdhw(cuda(cur), -1, 2, cache, W, slices, cap)
+
+
+def test_sdpa_reference_golden_cases(ops):
+    """The two SDPA golden tests of NcnnLinearCmdPack4GoldenTests (3e-4)."""
+    import torch
+    seq, embed, heads = 3, 3, 2
+    q = create_values(heads * seq * embed, 0.07, 3)
+    k = create_values(heads * seq * embed, 0.05, 5)
+    v = create_values(heads * seq * embed, 0.11, 7)
+    mask = np.array([0, -0.25, -1.5, 0, 0, -0.5, 0.1, 0, 0], dtype=np.float32)
+    scale = 1.0 / math.sqrt(embed)
+    exp = reference_sdpa_with_cache(q, k, v, seq, seq, embed, heads, scale, True, 0, mask)
+    out = torch.zeros(seq * embed * 4, dtype=torch.float32, device="cuda")
+    ops.sdpa_attention_pack4_cdhw(cuda(planar_to_pack4(q, embed, seq, heads)), cuda(planar_to_pack4(k, embed, seq, heads)),
+                                  cuda(planar_to_pack4(v, embed, seq, heads)), seq, seq, embed, embed, heads, heads,
+                                  scale, out, mask=cuda(planar_to_pack4(mask, seq, seq, 1)), mask_w=seq, mask_h=seq,
+                                  causal=True)
+    assert np.max(np.abs(pack4_to_planar(host(out), embed, seq, heads) - exp)) <= 3e-4
+
+    past, cur, heads = 3, 2, 5
+    total = past + cur
+    q = create_values(heads * cur * embed, 0.07, 3)
+    pk = create_values(heads * past * embed, 0.05, 5)
+    ck = create_values(heads * cur * embed, 0.04, 11)
+    pv = create_values(heads * past * embed, 0.11, 7)
+    cv = create_values(heads * cur * embed, 0.09, 13)
+    sl = (heads + 3) // 4
+    kc = torch.zeros(sl * total * embed * 4, dtype=torch.float32, device="cuda")
+    vc = torch.zeros_like(kc)
+    ops.concat_sequence_pack4_cdhw(cuda(planar_to_pack4(pk, embed, past, heads)), cuda(planar_to_pack4(ck, embed, cur, heads)),
+                                   past, cur, kc, embed, sl, total)
+    ops.concat_sequence_pack4_cdhw(cuda(planar_to_pack4(pv, embed, past, heads)), cuda(planar_to_pack4(cv, embed, cur, heads)),
+                                   past, cur, vc, embed, sl, total)
+    out = torch.zeros(sl * cur * embed * 4, dtype=torch.float32, device="cuda")
+    ops.sdpa_attention_pack4_cdhw(cuda(planar_to_pack4(q, embed, cur, heads)), kc, vc, cur, total, embed, embed, heads,
+                                  heads, scale, out, causal=True, causal_query_offset=past)
+
+    def cat(a, b):
+        x = np.concatenate([a.reshape(heads, past, embed), b.reshape(heads, cur, embed)], 1)
+        return x.reshape(-1)
+
+    ek, ev = cat(pk, ck), cat(pv, cv)
+    assert np.max(np.abs(pack4_to_planar(host(kc), embed, total, heads) - ek)) <= 1e-5
+    exp = reference_sdpa_with_cache(q, ek, ev, cur, total, embed, heads, scale, True, past)
+    assert np.max(np.abs(pack4_to_planar(host(out), embed, cur, heads) - exp)) <= 3e-4
+
+
+def test_sdpa_gqa_beyond_reference_cap(ops, oracle):
+    """GQA 8/2 heads, head_dim 128, 5000 keys (past the reference's 4096 cap)."""
+    import torch
+    src, dst, E, H, G = 2, 5000, 128, 8, 2
+    r = np.random.default_rng(8)
+    q = r.standard_normal(2 * src * E * 4).astype(np.float32)
+    k = r.standard_normal(1 * dst * E * 4).astype(np.float32)
+    v = r.standard_normal(1 * dst * E * 4).astype(np.float32)
+    out = torch.zeros(2 * src * E * 4, dtype=torch.float32, device="cuda")
+    scale = 1 / math.sqrt(E)
+    ops.sdpa_attention_pack4_cdhw(cuda(q), cuda(k), cuda(v), src, dst, E, E, H, G, scale, out, causal=True,
+                                  causal_query_offset=dst - src)
+    ref = oracle.sdpa(q, k, v, src, dst, E, E, H, G, scale, causal=True, causal_offset=dst - src)
+    got = pack4_to_planar(host(out), E, src, H)
+    exp = pack4_to_planar(ref, E, src, H)
+    assert np.allclose(got, exp, rtol=1e-4, atol=1e-5)
+
+
+def test_argmax_known_answers_and_ties(ops, oracle):
+    import torch
+    out = torch.zeros(8, dtype=torch.int32, device="cuda")
+    v = -np.arange(17, dtype=np.float32)
+    v[13] = 100
+    ops.arg_max_pack4_linear_mat(cuda(v), 17, 1, out)
+    assert host(out)[0] == 13
+    packs = 10
+    tiled = np.zeros(packs * 4, dtype=np.float32)
+    for p in range(packs):
+        tiled[p * 4:p * 4 + 4] = [-(p * 4 + 1), -(p * 4 + 2), -(p * 4 + 3), -(p * 4 + 4)]
+    tiled[34] = 100
+    ops.arg_max_pack4_linear_mat(cuda(tiled), 37, 1, out, ld=40)
+    assert host(out)[0] == 34
+    cases = [np.array([1, 3, 3, 2, 3], np.float32), np.array([np.nan, 5, 6], np.float32),
+             np.array([1, np.nan, 6], np.float32), np.array([-0.0, 0.0, -1], np.float32),
+             np.array([-np.inf, -np.inf], np.float32)]
+    for c in cases:
+        ops.arg_max_pack4_linear_mat(cuda(c), c.size, 1, out)
+        assert host(out)[0] == oracle.argmax(c)[0], c
+    r = np.random.default_rng(9)
+    big = r.standard_normal((4, 151936)).astype(np.float32)
+    big[1, 1000] = big[1, 77] = big[1].max() + 1  # tie -> lowest index
+    ops.arg_max_pack4_linear_mat(cuda(big), 151936, 4, out)
+    assert np.array_equal(host(out)[:4], oracle.argmax(big))
+
+
+def test_topk(ops, oracle):
+    import torch
+    r = np.random.default_rng(10)
+    x = r.standard_normal((3, 20000)).astype(np.float32)
+    x[0, 50:60] = 9.0  # ties ordered by index
+    k = 50
+    vals = torch.zeros((3, k), dtype=torch.float32, device="cuda")
+    idx = torch.zeros((3, k), dtype=torch.int32, device="cuda")
+    ops.top_k(cuda(x), 20000, 3, k, vals, idx)
+    rv, ri = oracle.topk(x, k)
+    assert np.array_equal(host(idx), ri)
+    assert np.array_equal(host(vals), rv)
+
+
+@pytest.mark.parametrize("kind", ["q4", "q8", "f16", "f32"])
+def test_embed(ops, oracle, kind):
+    import torch
+    from aiimage_b200 import synth
+    V, Dm = 300, 64
+    words = np.array([0, 5, 299, 400, -3, 17], dtype=np.int32)  # out-of-range ids clamp
+    bias = np.random.default_rng(11).standard_normal(Dm).astype(np.float32)
+    out = torch.zeros((words.size, Dm), dtype=torch.float32, device="cuda")
+    if kind == "q4":
+        p, s = synth.q4_weights(V, Dm, 16, seed=12)
+        t = ops.new_int4_weight_only_upload(p, s, V, Dm, 16)
+        ref = oracle.embed(words, 4, Dm, V, packed=p, scales=s.astype(np.float32), blk=16, bias=bias)
+    elif kind == "q8":
+        p, s = synth.q8_weights(V, Dm, seed=12)
+        t = ops.new_int8_weight_only_upload(p, s, V, Dm)
+        ref = oracle.embed(words, 8, Dm, V, packed=p, scales=s.astype(np.float32), bias=bias)
+    else:
+        tab = np.random.default_rng(13).standard_normal((V, Dm)).astype(np.float16 if kind == "f16" else np.float32)
+        t = ops.new_dense_weights(tab)
+        ref = oracle.embed(words, 32, Dm, V, table=tab.astype(np.float32), bias=bias)
+    ops.embed_texture(cuda(words), words.size, t, cuda(bias), out)
+    assert np.array_equal(host(out), ref)
+
+
+def test_swish_and_swiglu(ops, oracle):
+    import torch
+    x = (np.random.default_rng(14).standard_normal(4096) * 4).astype(np.float32)
+    u = np.random.default_rng(15).standard_normal(4096).astype(np.float32)
+    y = torch.zeros(4096, dtype=torch.float32, device="cuda")
+    ops.swish(cuda(x), 4096, y)
+    assert np.allclose(host(y), oracle.swish(x), rtol=2e-6, atol=1e-7)
+    ops.swiglu(cuda(x), cuda(u), 4096, y)
+    assert np.allclose(host(y), oracle.swiglu(x, u), rtol=2e-6, atol=1e-7)
