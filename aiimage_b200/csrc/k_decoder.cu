@@ -435,12 +435,11 @@ int upload_f32(aexis_decoder* d, float* dst, const void* src, int dtype, size_t 
                             "norm upload");
 }
 
-// Runs `count` steps from the host (prompt tokens already on the device when
-// tokens == nullptr). Returns the last greedy token when want_token.
-int run_steps(aexis_decoder* d, int emit_last, int count) {
+// Replays `count` decode steps; emit = 1 uses the full step graph (lm_head,
+// greedy token fed back on the device), emit = 0 the prompt-token graph.
+int run_steps(aexis_decoder* d, int emit, int count) {
     cudaStream_t s = d->ctx->stream;
     for (int i = 0; i < count; ++i) {
-        const bool emit = emit_last && i == count - 1;
         cudaError_t e = cudaGraphLaunch(emit ? d->step_exec : d->prefill_exec, s);
         if (e != cudaSuccess) return aexis_cuda_check(d->ctx, e, "graph launch");
     }

@@ -29,11 +29,14 @@ class DecoderSession:
         self.h = C.c_void_p()
         check(lib().aexis_cuda_decoder_create(ops.ctx, C.byref(self._cfg), C.byref(self.h)), ops.ctx)
         self._scale_dtype = scale_dtype
+        ops._register(self)
 
     def close(self):
-        if self.h:
+        # A decoder lives inside its context: destroy it first (AexisOps.close
+        # closes its decoders before the context goes away).
+        if self.h and self.ops.ctx:
             lib().aexis_cuda_decoder_destroy(self.h)
-            self.h = C.c_void_p()
+        self.h = C.c_void_p()
 
     def __del__(self):
         try:

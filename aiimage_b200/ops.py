@@ -10,6 +10,7 @@ device. Work is enqueued on torch's current stream.
 from __future__ import annotations
 
 import ctypes as C
+import weakref
 
 import numpy as np
 
@@ -80,10 +81,17 @@ class AexisOps:
         self._use_torch_stream = use_torch_stream
         self._int8 = None
         self._int4 = None
+        self._children = weakref.WeakSet()
 
     # -- context ---------------------------------------------------------
+    def _register(self, child):
+        """Objects owning device state of this context (closed before it)."""
+        self._children.add(child)
+
     def close(self):
         if self.ctx:
+            for child in list(self._children):
+                child.close()
             lib().aexis_cuda_destroy(self.ctx)
             self.ctx = C.c_void_p()
 

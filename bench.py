@@ -392,7 +392,7 @@ def bench_q8(ops, peak):
             "frac": round(b / t / 1e9 / peak, 3)}
 
 
-def bench_decoder(ops, peak):
+def bench_decoder(ops, peak, prompt_len: int = 512, new_tokens: int = 64):
     """24-layer synthetic Q4 decoder, 512-token prompt, then
     64 greedy tokens. Device tokens/s from the graph-chained generate call
     (one H2D token in, one D2H of the 64 ids out), and the per-token host
@@ -401,27 +401,28 @@ def bench_decoder(ops, peak):
     from aiimage_b200.decoder import DecoderSession
     cfg = synth.QWEN35_08B_Q4
     model = synth.SyntheticDecoder(cfg, seed=3)
-    prompt = model.prompt(512, seed=30)
+    prompt = model.prompt(prompt_len, seed=30)
     sess = DecoderSession(ops, cfg).load(model)
     sess.prefill(prompt[:-1])
     torch.cuda.synchronize()
     t0 = time.perf_counter()
-    toks = sess.generate(prompt[-1:], 64)  # 64 decode steps, positions 511..574
+    toks = sess.generate(prompt[-1:], new_tokens)  # decode steps at positions prompt_len-1 ..
     gen_s = time.perf_counter() - t0
     sess.reset()
     sess.prefill(prompt[:-1])
     nxt = int(prompt[-1])
     t0 = time.perf_counter()
-    for _ in range(64):
+    for _ in range(new_tokens):
         nxt = sess.step(nxt)
     step_s = time.perf_counter() - t0
-    kv_mean = cfg.n_layers * 2 * cfg.n_kv_heads * cfg.head_dim * 2 * (511 + 32)
+    kv_mean = cfg.n_layers * 2 * cfg.n_kv_heads * cfg.head_dim * 2 * (prompt_len - 1 + new_tokens // 2)
     bytes_tok = model.weight_bytes_per_token() + kv_mean
     sess.close()
-    return {"workload": "config3_q4_decoder_prompt512_greedy64", "tokens_per_s": round(64 / gen_s, 1),
-            "ms_per_token": round(gen_s / 64 * 1e3, 4), "e2e_tokens_per_s_host_roundtrip": round(64 / step_s, 1),
-            "bytes_per_token": bytes_tok, "GB/s": round(bytes_tok * 64 / gen_s / 1e9, 1),
-            "frac": round(bytes_tok * 64 / gen_s / 1e9 / peak, 3), "first_tokens": toks[:8],
+    n = new_tokens
+    return {"workload": f"config3_q4_decoder_prompt{prompt_len}_greedy{n}", "tokens_per_s": round(n / gen_s, 1),
+            "ms_per_token": round(gen_s / n * 1e3, 4), "e2e_tokens_per_s_host_roundtrip": round(n / step_s, 1),
+            "bytes_per_token": bytes_tok, "GB/s": round(bytes_tok * n / gen_s / 1e9, 1),
+            "frac": round(bytes_tok * n / gen_s / 1e9 / peak, 3), "first_tokens": toks[:8],
             "kernels_per_token": 2 + 5 * cfg.n_layers + 1}
 
 
@@ -445,6 +446,40 @@ def cpu_baseline(budget_s: float = 12.0):
     return {"value": round(passes * STEP_BYTES / el / 1e9, 3), "unit": "GB/s", "cores": O.num_threads(),
             "kind": "port", "sample": f"{passes} full sweep pass(es) of config 2 through the C++ oracle "
                                       f"(sequential fp32 per output, OpenMP over outputs), {el:.1f} s"}
+
+
+def run_only(args):
+    """Single-kernel / single-path modes for profiling (not the bench contract):
+    --only dominant   W + K launches of the (1024, 151936) Q4 GEMV, rotating
+                      over copies larger than L2, no graphs
+    --only decoder    the config-3 decoder with --prompt-len / --new-tokens"""
+    import torch
+    torch.cuda.set_device(0)
+    from aiimage_b200.ops import AexisOps
+    ops = AexisOps(0)
+    peak, _ = measured_peak()
+    if args.only == "decoder":
+        out = bench_decoder(ops, peak, args.prompt_len, args.new_tokens)
+    else:
+        k, n = SWEEP[DOMINANT]
+        p, s = synth.q4_weights(n, k, GROUP, 1, tag=(k, n))
+        copies = max(2, -(-2 * L2_BYTES // SWEEP_BYTES[DOMINANT]))
+        ws = [ops.new_int4_weight_only_upload(p, s, n, k, GROUP) for _ in range(copies)]
+        x = torch.from_numpy(synth.activations(k, 1, tag=(k, n))).cuda()
+        y = torch.zeros((1, n), dtype=torch.float16, device="cuda")
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        for i in range(args.warmup + args.steps):
+            if i == args.warmup:
+                e0.record()
+            ops.set_int4_gemm_weights(ws[i % copies])
+            ops.gemm2d_pack4_linear_texture_a(x, None, 1, n, k, True, 1.0, 1.0, False, 4, y)
+        e1.record()
+        e1.synchronize()
+        t = e0.elapsed_time(e1) / 1e3 / max(1, args.steps)
+        out = {"kernel": "gemv q4 1024x151936", "launches": args.warmup + args.steps, "copies": copies,
+               "us_per_launch_incl_host_gaps": round(t * 1e6, 2)}
+    print(json.dumps({"only": args.only, **out}), flush=True)
+    ops.close()
 
 
 def run_reference(args):
@@ -493,10 +528,15 @@ def main():
     ap.add_argument("--skip-decoder", action="store_true", help="omit the config-3 decoder measurement")
     ap.add_argument("--skip-cpu", action="store_true", help="omit the CPU oracle baseline")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--only", choices=["dominant", "decoder"], help="profiling mode (see run_only)")
+    ap.add_argument("--prompt-len", type=int, default=512)
+    ap.add_argument("--new-tokens", type=int, default=64)
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
-    if args.impl == "reference":
+    if args.only:
+        run_only(args)
+    elif args.impl == "reference":
         if args.steps > 20:
             args.steps = 20  # each reference step is a full CPU pass (~0.5 s); bound the run
         run_reference(args)
