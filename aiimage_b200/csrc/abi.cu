@@ -31,6 +31,15 @@ int aexis_cuda_check(aexis_ctx* ctx, cudaError_t e, const char* what) {
     return aexis_fail(ctx, AEXIS_E_CUDA, "%s: %s", what, cudaGetErrorString(e));
 }
 
+int aexis_check_status(aexis_ctx* ctx) {
+    int st = 0;
+    cudaError_t e = cudaMemcpy(&st, ctx->status, sizeof(int), cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return aexis_cuda_check(ctx, e, "status readback");
+    if (st == 0) return AEXIS_OK;
+    cudaMemset(ctx->status, 0, sizeof(int));
+    return aexis_fail(ctx, st, "a kernel gave up on a bounded wait (status %d); the context stays usable", st);
+}
+
 int aexis_scratch(aexis_ctx* ctx, size_t bytes, void** out) {
     if (bytes > ctx->scratch_bytes) {
         // The old buffer may still be read by enqueued work: wait before freeing.
@@ -56,7 +65,8 @@ int bind(aexis_ctx* ctx) { return aexis_cuda_check(ctx, cudaSetDevice(ctx->devic
 bool valid_dtype(int d) { return d == AEXIS_F32 || d == AEXIS_F16; }
 
 int upload(aexis_ctx* ctx, const void* host, size_t bytes, void** dev, const char* what) {
-    cudaError_t e = cudaMalloc(dev, bytes);
+    cudaError_t e = cudaMalloc(dev, bytes + kWeightPad);
+    if (e == cudaSuccess) e = cudaMemset((char*)*dev + bytes, 0, kWeightPad);
     if (e != cudaSuccess) return aexis_cuda_check(ctx, e, what);
     e = cudaMemcpy(*dev, host, bytes, cudaMemcpyHostToDevice);
     if (e != cudaSuccess) {
@@ -131,6 +141,13 @@ AEXIS_API int aexis_cuda_create(int device, aexis_ctx** out) {
         return aexis_fail(nullptr, AEXIS_E_CUDA, "stream create: %s", cudaGetErrorString(e));
     }
     ctx->stream = ctx->own_stream;
+    e = cudaMalloc(&ctx->status, sizeof(int));
+    if (e == cudaSuccess) e = cudaMemset(ctx->status, 0, sizeof(int));
+    if (e != cudaSuccess) {
+        cudaStreamDestroy(ctx->own_stream);
+        delete ctx;
+        return aexis_fail(nullptr, AEXIS_E_CUDA, "status alloc: %s", cudaGetErrorString(e));
+    }
     *out = ctx;
     return AEXIS_OK;
 }
@@ -140,6 +157,7 @@ AEXIS_API int aexis_cuda_destroy(aexis_ctx* ctx) {
     cudaSetDevice(ctx->device);
     if (ctx->own_stream) cudaStreamSynchronize(ctx->own_stream);
     if (ctx->scratch) cudaFree(ctx->scratch);
+    if (ctx->status) cudaFree(ctx->status);
     if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
     delete ctx;
     return AEXIS_OK;
@@ -159,7 +177,9 @@ AEXIS_API int aexis_cuda_sync(aexis_ctx* ctx) {
     if (!ctx) return AEXIS_E_NULL;
     int rc = bind(ctx);
     if (rc) return rc;
-    return aexis_cuda_check(ctx, cudaStreamSynchronize(ctx->stream), "cudaStreamSynchronize");
+    rc = aexis_cuda_check(ctx, cudaStreamSynchronize(ctx->stream), "cudaStreamSynchronize");
+    if (rc) return rc;
+    return aexis_check_status(ctx);
 }
 
 // ---------------------------------------------------------------- weights
@@ -288,6 +308,7 @@ static int gemm_common(aexis_ctx* ctx, const void* a, int a_dtype, int lda, int 
     int rc = bind(ctx);
     if (rc) return rc;
     GemvArgs g;
+    g.status = ctx->status;
     g.a_dtype = a_dtype;
     g.w = w;
     g.bias = bias;

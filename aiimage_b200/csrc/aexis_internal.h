@@ -32,6 +32,9 @@ struct aexis_ctx {
     // Grow-only device scratch (split-K attention partials, argmax keys).
     void* scratch = nullptr;
     size_t scratch_bytes = 0;
+    // Device status word: kernels whose bounded waits run out record
+    // AEXIS_E_TIMEOUT here; aexis_cuda_sync reports and clears it.
+    int* status = nullptr;
 };
 
 // Records `msg` on the context and returns `code`.
@@ -40,6 +43,9 @@ int aexis_fail(aexis_ctx* ctx, int code, const char* fmt, ...);
 int aexis_cuda_check(aexis_ctx* ctx, cudaError_t e, const char* what);
 // Returns a device buffer of at least `bytes` (grow-only, owned by ctx).
 int aexis_scratch(aexis_ctx* ctx, size_t bytes, void** out);
+// Reads (and clears) the context status word after a synchronize: returns
+// the recorded error (AEXIS_E_TIMEOUT) or AEXIS_OK.
+int aexis_check_status(aexis_ctx* ctx);
 
 // ---------------------------------------------------------------- launchers
 // Every launcher enqueues on `stream` and returns the launch's cudaError_t.
@@ -75,14 +81,22 @@ struct GemvArgs {
     int head_dim = 0, kv_cap = 0, q_rows = 0, kv_rows = 0, rot_dim = 0;
     const int* pos_ptr = nullptr;      // device position (decoder graph)
     unsigned long long* argmax_key = nullptr;  // EPI_LOGITS_ARGMAX target
+    int* status = nullptr;             // context status word (bounded-wait timeouts)
     bool pdl = false;                  // launch with programmatic dependent launch
 };
 
 // y = W x for one activation row; picks the fast streaming kernel when the
 // weight layout allows it, else the exact generic kernel.
 cudaError_t launch_gemv(const GemvArgs& a, int sm_count, cudaStream_t stream);
-// Reports which kernel launch_gemv would use ("q4_fast", "q8_fast", "generic").
+// Reports which kernel launch_gemv would use.
 const char* gemv_kernel_name(const aexis_weights* w);
+// The bulk-copy streaming GEMV (k_gemv_stream.cu): whether it takes `w`, and
+// its launch.
+bool gemv_stream_supported(const aexis_weights* w);
+cudaError_t launch_gemv_stream(const GemvArgs& a, int sm_count, int* status, cudaStream_t stream);
+// Bytes of padding after every weight and scale allocation: bulk copies of a
+// partial last tile round their size up to 16 bytes.
+constexpr size_t kWeightPad = 256;
 
 cudaError_t launch_dequant(const aexis_weights* w, float* out, cudaStream_t s);
 cudaError_t launch_rmsnorm(const void* x, int x_dtype, int rows, int width, int ld,

@@ -230,8 +230,8 @@ int alloc_weights(aexis_decoder* d, aexis_weights& w, int bits, int group, int s
     w.data_bytes = (size_t)n * k / (bits == 4 ? 2 : 1);
     const size_t nscales = bits == 4 ? (size_t)n * (k / group) : (size_t)n;
     w.scale_bytes = nscales * (scale_dtype == AEXIS_F16 ? 2 : 4);
-    int rc = alloc(d, &w.data, w.data_bytes, "decoder weight alloc");
-    if (rc == AEXIS_OK) rc = alloc(d, &w.scales, w.scale_bytes, "decoder scale alloc");
+    int rc = alloc(d, &w.data, w.data_bytes + kWeightPad, "decoder weight alloc");
+    if (rc == AEXIS_OK) rc = alloc(d, &w.scales, w.scale_bytes + kWeightPad, "decoder scale alloc");
     return rc;
 }
 
@@ -309,6 +309,7 @@ cudaError_t enqueue_step(aexis_decoder* d, cudaStream_t s, int emit) {
         __half* kc = d->kcache + (size_t)l * c.n_kv_heads * c.kv_capacity * D;
         __half* vc = d->vcache + (size_t)l * c.n_kv_heads * c.kv_capacity * D;
         GemvArgs g;
+        g.status = d->ctx->status;
         g.pdl = true;
         g.x = d->h;
         g.w = &L.qkv;
@@ -341,6 +342,7 @@ cudaError_t enqueue_step(aexis_decoder* d, cudaStream_t s, int emit) {
             if (e != cudaSuccess) return e;
         }
         GemvArgs o;
+        o.status = d->ctx->status;
         o.pdl = true;
         o.x = d->attn;
         o.w = &L.o;
@@ -348,6 +350,7 @@ cudaError_t enqueue_step(aexis_decoder* d, cudaStream_t s, int emit) {
         o.epilogue = EPI_RESIDUAL;
         if ((e = launch_gemv(o, d->ctx->sm_count, s)) != cudaSuccess) return e;
         GemvArgs f1;
+        f1.status = d->ctx->status;
         f1.pdl = true;
         f1.x = d->h;
         f1.w = &L.gateup;
@@ -357,6 +360,7 @@ cudaError_t enqueue_step(aexis_decoder* d, cudaStream_t s, int emit) {
         f1.norm_eps = c.eps;
         if ((e = launch_gemv(f1, d->ctx->sm_count, s)) != cudaSuccess) return e;
         GemvArgs f2;
+        f2.status = d->ctx->status;
         f2.pdl = true;
         f2.x = d->act;
         f2.w = &L.down;
@@ -366,6 +370,7 @@ cudaError_t enqueue_step(aexis_decoder* d, cudaStream_t s, int emit) {
     }
     if (emit) {
         GemvArgs lm;
+        lm.status = d->ctx->status;
         lm.pdl = true;
         lm.x = d->h;
         lm.w = &d->lm;
@@ -694,6 +699,7 @@ AEXIS_API int aexis_cuda_decoder_prefill(aexis_decoder* d, const int32_t* tokens
     d->host_pos += count;
     rc = aexis_cuda_check(d->ctx, cudaMemcpyAsync(next_token, d->ints, sizeof(int), cudaMemcpyDeviceToHost, s), "readback");
     if (!rc) rc = aexis_cuda_check(d->ctx, cudaStreamSynchronize(s), "sync");
+    if (!rc) rc = aexis_check_status(d->ctx);
     return rc;
 }
 
@@ -732,6 +738,7 @@ AEXIS_API int aexis_cuda_decoder_generate(aexis_decoder* d, const int32_t* promp
     rc = aexis_cuda_check(d->ctx, cudaMemcpyAsync(out_tokens, d->ints + 3, sizeof(int) * max_new, cudaMemcpyDeviceToHost, s),
                           "readback");
     if (!rc) rc = aexis_cuda_check(d->ctx, cudaStreamSynchronize(s), "sync");
+    if (!rc) rc = aexis_check_status(d->ctx);
     return rc;
 }
 

@@ -25,92 +25,14 @@
 //
 // The generic kernel covers every other layout (odd k, groups that are not
 // multiples of 16, ...) with the reference's exact flat indexing.
-#include "aexis_internal.h"
+#include "gemv_dev.cuh"
 
 namespace {
 
+using namespace aexis_dev;
+
 constexpr int kWarps = 8;
 constexpr int kThreads = kWarps * 32;
-
-__device__ __forceinline__ uint4 ldg_stream(const uint4* p) {
-    uint4 r;
-    asm("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
-        : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
-        : "l"(p));
-    return r;
-}
-
-__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
-__device__ __forceinline__ void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;"); }
-
-// acc.{x,y} += (as_float(f0) + m0, as_float(f1) + m1) * (a0, a1), with packed
-// fp32x2 add and FMA (each lane rounds exactly as the scalar op would).
-__device__ __forceinline__ void mac2(unsigned long long& acc, uint32_t f0, uint32_t f1, float m0,
-                                     float m1, float a0, float a1) {
-    asm("{\n\t.reg .b64 f, m, a, d;\n\t"
-        "mov.b64 f, {%1, %2};\n\t"
-        "mov.b64 m, {%3, %4};\n\t"
-        "mov.b64 a, {%5, %6};\n\t"
-        "add.rn.f32x2 d, f, m;\n\t"
-        "fma.rn.f32x2 %0, d, a, %0;\n\t}"
-        : "+l"(acc)
-        : "r"(f0), "r"(f1), "f"(m0), "f"(m1), "f"(a0), "f"(a1));
-}
-
-__device__ __forceinline__ float sum2(unsigned long long acc) {
-    return __uint_as_float((uint32_t)acc) + __uint_as_float((uint32_t)(acc >> 32));
-}
-
-// Int4 magic constants: (nibble-field ^ 8<<4j') | 0x4B000000 read as fp32 is
-// 2^23 + (u ^ 8) * 16^j'; subtracting 2^23 + 8 * 16^j' leaves q * 16^j'.
-constexpr uint32_t kQ4X0 = 0x4B000008u, kQ4X1 = 0x4B000080u, kQ4X2 = 0x4B000800u,
-                   kQ4X3 = 0x4B008000u, kQ4X4 = 0x4B080000u;
-#define Q4M(x) (-__uint_as_float(x))
-
-// 32 int4 products of one 16-byte chunk against 32 pre-scaled activations.
-__device__ __forceinline__ unsigned long long dot_q4_chunk(const uint4 w, const float4* a) {
-    unsigned long long acc = 0ull;
-    const uint32_t words[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const uint32_t v = words[i];
-        const uint32_t vh = v >> 12;
-        const float4 a0 = a[2 * i], a1 = a[2 * i + 1];
-        mac2(acc, (v & 0xFu) ^ kQ4X0, (v & 0xF0u) ^ kQ4X1, Q4M(kQ4X0), Q4M(kQ4X1), a0.x, a0.y);
-        mac2(acc, (v & 0xF00u) ^ kQ4X2, (v & 0xF000u) ^ kQ4X3, Q4M(kQ4X2), Q4M(kQ4X3), a0.z, a0.w);
-        mac2(acc, (v & 0xF0000u) ^ kQ4X4, (vh & 0xF00u) ^ kQ4X2, Q4M(kQ4X4), Q4M(kQ4X2), a1.x, a1.y);
-        mac2(acc, (vh & 0xF000u) ^ kQ4X3, (vh & 0xF0000u) ^ kQ4X4, Q4M(kQ4X3), Q4M(kQ4X4), a1.z, a1.w);
-    }
-    return acc;
-}
-
-// 16 int8 products of one 16-byte chunk. Bytes are biased by 128 (XOR), moved
-// under the 2^23 exponent with PRMT, and the 2^23 + 128 bias is subtracted.
-__device__ __forceinline__ void dot_q8_chunk(unsigned long long& acc, const uint4 w, const float4* a) {
-    const uint32_t words[4] = {w.x, w.y, w.z, w.w};
-    const float m = -__uint_as_float(0x4B000080u);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const uint32_t v = words[i] ^ 0x80808080u;
-        const float4 av = a[i];
-        mac2(acc, __byte_perm(v, 0x4B000000u, 0x7650), __byte_perm(v, 0x4B000000u, 0x7651), m, m,
-             av.x, av.y);
-        mac2(acc, __byte_perm(v, 0x4B000000u, 0x7652), __byte_perm(v, 0x4B000000u, 0x7653), m, m,
-             av.z, av.w);
-    }
-}
-
-// Physical 16-byte unit of logical unit u in the swizzled activation buffer.
-__device__ __forceinline__ int swz(int u) { return u ^ ((u >> 3) & 7); }
-
-template <typename ST>
-__device__ __forceinline__ float load_scale(const ST* s, long long i);
-template <>
-__device__ __forceinline__ float load_scale<float>(const float* s, long long i) { return __ldg(s + i); }
-template <>
-__device__ __forceinline__ float load_scale<__half>(const __half* s, long long i) {
-    return __half2float(__ldg(s + i));
-}
 
 struct FastParams {
     const uint4* W;        // [n][row_u4] 16-byte chunks
@@ -473,6 +395,7 @@ int fast_scale_mode(const aexis_weights* w, int* gshift) {
 }  // namespace
 
 const char* gemv_kernel_name(const aexis_weights* w) {
+    if (gemv_stream_supported(w)) return w->kind == WK_Q4 ? "q4_stream" : "q8_stream";
     int gs;
     if (fast_scale_mode(w, &gs) < 0) return "generic";
     return w->kind == WK_Q4 ? "q4_fast" : "q8_fast";
@@ -480,6 +403,7 @@ const char* gemv_kernel_name(const aexis_weights* w) {
 
 cudaError_t launch_gemv(const GemvArgs& a, int sm_count, cudaStream_t stream) {
     const aexis_weights* w = a.w;
+    if (gemv_stream_supported(w)) return launch_gemv_stream(a, sm_count, a.status, stream);
     int gshift = 0;
     const int smode = fast_scale_mode(w, &gshift);
     const bool pair_epi = a.epilogue == EPI_SWIGLU || a.epilogue == EPI_QKV_ROPE;
