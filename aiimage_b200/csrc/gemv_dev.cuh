@@ -96,28 +96,46 @@ __device__ __forceinline__ float load_scale<__half>(const __half* s, long long i
 // (see act_pair_index) and pre-scaled by the field's 16^-j' (int4) or
 // 256^-j' (int8) so every product is exact before its single rounding.
 //
-// acc += ((x & m) ^ c) as fp32x2 + b) * a
-__device__ __forceinline__ void mac_pair(unsigned long long& acc, unsigned long long x, unsigned long long m,
-                                         unsigned long long c, unsigned long long b, unsigned long long a) {
-    asm("{\n\t.reg .b64 t;\n\t"
-        "and.b64 t, %1, %2;\n\t"
-        "xor.b64 t, t, %3;\n\t"
+// acc += (((x & m) ^ c) as fp32x2 + b) * a, with one three-input LOP3
+// (truth table 0x6A = (a & b) ^ c) per 32-bit half. m and c arrive in
+// registers (PairConsts) so the assembler keeps each isolate as one LOP3.
+__device__ __forceinline__ void mac_pair(unsigned long long& acc, unsigned long long x, uint32_t m, uint32_t c,
+                                         unsigned long long b, unsigned long long a) {
+    asm("{\n\t.reg .b32 xl, xh, tl, th;\n\t.reg .b64 t;\n\t"
+        "mov.b64 {xl, xh}, %1;\n\t"
+        "lop3.b32 tl, xl, %2, %3, 0x6A;\n\t"
+        "lop3.b32 th, xh, %2, %3, 0x6A;\n\t"
+        "mov.b64 t, {tl, th};\n\t"
         "add.rn.f32x2 t, t, %4;\n\t"
         "fma.rn.f32x2 %0, t, %5, %0;\n\t}"
         : "+l"(acc)
-        : "l"(x), "l"(m), "l"(c), "l"(b), "l"(a));
+        : "l"(x), "r"(m), "r"(c), "l"(b), "l"(a));
 }
 
 __device__ __forceinline__ unsigned long long dup64(uint32_t v) {
     return ((unsigned long long)v << 32) | v;
 }
 
-// Int4 field j' (0..4) at bits 4j'..4j'+3: mask, XOR (sign flip + 2^23
-// exponent) and the negated magic 2^23 + 8 * 16^j' as fp32 bits.
-__device__ __forceinline__ unsigned long long q4_mask(int jp) { return dup64(0xFu << (4 * jp)); }
-__device__ __forceinline__ unsigned long long q4_xor(int jp) { return dup64(0x4B000000u | (8u << (4 * jp))); }
-__device__ __forceinline__ unsigned long long q4_bias(int jp) {
-    return dup64(__float_as_uint(-__uint_as_float(0x4B000000u | (8u << (4 * jp)))));
+// Field constants of the int4 / int8 decode: for field j' the mask, the XOR
+// (sign flip + 2^23 exponent) and the negated magic (2^23 + bias * 2^(w*j'))
+// as fp32x2 bits. Built from a runtime zero so they stay in registers.
+struct PairConsts {
+    uint32_t m[5], c[5];
+    unsigned long long b[5];
+};
+
+template <int BITS>
+__device__ __forceinline__ PairConsts make_pair_consts(uint32_t zero) {
+    PairConsts k;
+#pragma unroll
+    for (int j = 0; j < 5; ++j) {
+        const uint32_t mask = BITS == 4 ? (0xFu << (4 * j)) : (j < 2 ? 0xFFu << (8 * j) : 0u);
+        const uint32_t x = BITS == 4 ? (0x4B000000u | (8u << (4 * j))) : (0x4B000000u | (j < 2 ? 0x80u << (8 * j) : 0u));
+        k.m[j] = mask | zero;
+        k.c[j] = x | zero;
+        k.b[j] = dup64(__float_as_uint(-__uint_as_float(x))) | zero;
+    }
+    return k;
 }
 
 // One int4 chunk: x01 = {w0, w1}, x23 = {w2, w3}; a[0..7] pairs of words
@@ -125,37 +143,28 @@ __device__ __forceinline__ unsigned long long q4_bias(int jp) {
 // from the halves shifted right by 12 (the 64-bit shift only pollutes bits
 // 20..31 of the low word, which no mask selects).
 __device__ __forceinline__ void dot_q4_pairs(unsigned long long x01, unsigned long long x23,
-                                             const unsigned long long* a, unsigned long long& acc01,
-                                             unsigned long long& acc23) {
+                                             const unsigned long long* a, const PairConsts& k,
+                                             unsigned long long& acc01, unsigned long long& acc23) {
     const unsigned long long h01 = x01 >> 12, h23 = x23 >> 12;
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
         const int jp = j < 5 ? j : j - 3;
-        const unsigned long long m = q4_mask(jp), c = q4_xor(jp), b = q4_bias(jp);
-        mac_pair(acc01, j < 5 ? x01 : h01, m, c, b, a[j]);
-        mac_pair(acc23, j < 5 ? x23 : h23, m, c, b, a[8 + j]);
+        mac_pair(acc01, j < 5 ? x01 : h01, k.m[jp], k.c[jp], k.b[jp], a[j]);
+        mac_pair(acc23, j < 5 ? x23 : h23, k.m[jp], k.c[jp], k.b[jp], a[8 + j]);
     }
 }
 
-// Int8 field j' (0..1) at bits 8j'..8j'+7 (bytes 2, 3 from the halves shifted
-// right by 16): sign flip by XOR 0x80 << 8j', magic 2^23 + 128 * 256^j'.
-__device__ __forceinline__ unsigned long long q8_mask(int jp) { return dup64(0xFFu << (8 * jp)); }
-__device__ __forceinline__ unsigned long long q8_xor(int jp) { return dup64(0x4B000000u | (0x80u << (8 * jp))); }
-__device__ __forceinline__ unsigned long long q8_bias(int jp) {
-    return dup64(__float_as_uint(-__uint_as_float(0x4B000000u | (0x80u << (8 * jp)))));
-}
-
-// One int8 chunk (16 values): a[0..3] pairs of words (0,1), a[4..7] of (2,3).
+// One int8 chunk (16 values): a[0..3] pairs of words (0,1), a[4..7] of (2,3);
+// bytes 2, 3 come from the halves shifted right by 16.
 __device__ __forceinline__ void dot_q8_pairs(unsigned long long x01, unsigned long long x23,
-                                             const unsigned long long* a, unsigned long long& acc01,
-                                             unsigned long long& acc23) {
+                                             const unsigned long long* a, const PairConsts& k,
+                                             unsigned long long& acc01, unsigned long long& acc23) {
     const unsigned long long h01 = x01 >> 16, h23 = x23 >> 16;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
         const int jp = j & 1;
-        const unsigned long long m = q8_mask(jp), c = q8_xor(jp), b = q8_bias(jp);
-        mac_pair(acc01, j < 2 ? x01 : h01, m, c, b, a[j]);
-        mac_pair(acc23, j < 2 ? x23 : h23, m, c, b, a[4 + j]);
+        mac_pair(acc01, j < 2 ? x01 : h01, k.m[jp], k.c[jp], k.b[jp], a[j]);
+        mac_pair(acc23, j < 2 ? x23 : h23, k.m[jp], k.c[jp], k.b[jp], a[4 + j]);
     }
 }
 

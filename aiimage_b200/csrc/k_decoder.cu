@@ -33,6 +33,8 @@ constexpr int kAttnSplits = 64;   // context splits per KV head (fixed at captur
 constexpr int kAttnThreads = 128;
 constexpr int kMaxHeadDim = 256;
 constexpr int kMaxGroup = 8;      // query heads per KV head
+constexpr int kMinChunk = 32;     // fewest context positions per split
+constexpr int kMaxChunk = 64;     // chunk bound at the largest supported capacity
 
 // h = E[token], key = 0. token_src[token_idx ? *token_idx : 0].
 __global__ void dec_embed_kernel(const __half* table, int vocab, int hidden, const int* token,
@@ -49,39 +51,51 @@ __global__ void dec_embed_kernel(const __half* table, int vocab, int hidden, con
 
 // Split-K decode attention for one KV head and one context split.
 // q: fp32 [n_heads][D] (RoPE applied); caches: fp16 [kv_heads][cap][D].
+// Context positions are cut into `active` splits of `chunk` positions
+// (chunk = max(32, ceil(ctx / kAttnSplits))); CTAs past the active count exit.
 // Scores s = (q . k) * scale; each split keeps (max m, sum l, o = sum e*v);
-// the last CTA of a KV head merges the splits: out = sum_s o_s e^(m_s-M) /
-// sum_s l_s e^(m_s-M). Mathematically the reference's two-pass softmax
-// (HLSL Pack4Matmul:485-547); no context cap.
+// the last CTA of a KV head merges the splits with weights
+// w_s = e^(m_s - M) / sum_s l_s e^(m_s - M), computed once in shared memory,
+// then out = sum_s w_s o_s with independent loads. Mathematically the
+// reference's two-pass softmax (HLSL Pack4Matmul:485-547); no context cap
+// beyond the cache capacity.
 __global__ void __launch_bounds__(kAttnThreads) dec_attn_kernel(
     const float* q, const __half* kc, const __half* vc, int cap, int D, int n_heads, int n_kv,
     float scale, const int* pos_ptr, float* part, unsigned int* counters, float* out) {
     __shared__ float qs[kMaxGroup][kMaxHeadDim];
-    __shared__ float sc[kMaxGroup][64];
+    __shared__ float sc[kMaxGroup][kMaxChunk];
     __shared__ float stat[kMaxGroup][2];
+    __shared__ float wsm[kMaxGroup][kAttnSplits];
     __shared__ bool last;
     griddep_wait();
     griddep_launch();
     const int g = blockIdx.x, split = blockIdx.y;
     const int hpg = n_heads / n_kv;
     const int ctx = *pos_ptr + 1;
-    const int chunk = (ctx + kAttnSplits - 1) / kAttnSplits;
+    int chunk = (ctx + kAttnSplits - 1) / kAttnSplits;
+    chunk = chunk < kMinChunk ? kMinChunk : chunk;
+    const int active = (ctx + chunk - 1) / chunk;
+    if (split >= active) return;
     const int p0 = split * chunk, p1 = min(ctx, p0 + chunk);
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     for (int i = tid; i < hpg * D; i += kAttnThreads) qs[i / D][i % D] = q[(g * hpg + i / D) * D + i % D];
     __syncthreads();
     const __half* kb = kc + (long long)g * cap * D;
     const __half* vb = vc + (long long)g * cap * D;
-    // Scores: one warp per position, lanes across D.
+    // Scores: one warp per position, each lane four consecutive dims.
     for (int p = p0 + warp; p < p1; p += kAttnThreads / 32) {
         float acc[kMaxGroup];
 #pragma unroll
         for (int h = 0; h < kMaxGroup; ++h) acc[h] = 0.0f;
-        for (int d = lane; d < D; d += 32) {
-            const float kv = __half2float(kb[(long long)p * D + d]);
+        for (int d = lane * 4; d < D; d += 128) {
+            const uint2 raw = *reinterpret_cast<const uint2*>(kb + (long long)p * D + d);
+            const float2 k01 = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
+            const float2 k23 = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
 #pragma unroll
             for (int h = 0; h < kMaxGroup; ++h)
-                if (h < hpg) acc[h] = fmaf(qs[h][d], kv, acc[h]);
+                if (h < hpg)
+                    acc[h] = fmaf(qs[h][d + 3], k23.y, fmaf(qs[h][d + 2], k23.x,
+                             fmaf(qs[h][d + 1], k01.y, fmaf(qs[h][d], k01.x, acc[h]))));
         }
 #pragma unroll
         for (int h = 0; h < kMaxGroup; ++h) {
@@ -127,34 +141,43 @@ __global__ void __launch_bounds__(kAttnThreads) dec_attn_kernel(
     }
     if (tid < hpg) {
         float* st = part + ((long long)(g * hpg + tid) * kAttnSplits + split) * stride + D;
-        st[0] = p1 > p0 ? stat[tid][0] : -INFINITY;
-        st[1] = p1 > p0 ? stat[tid][1] : 0.0f;
+        st[0] = stat[tid][0];
+        st[1] = stat[tid][1];
     }
     // Last CTA of this KV head merges the splits (threadfence reduction).
     __threadfence();
     __syncthreads();
-    if (tid == 0) last = atomicAdd(counters + g, 1u) == (unsigned)(kAttnSplits - 1);
+    if (tid == 0) last = atomicAdd(counters + g, 1u) == (unsigned)(active - 1);
     __syncthreads();
     if (!last) return;
     __threadfence();
-    for (int h = 0; h < hpg; ++h) {
-        const float* base = part + (long long)(g * hpg + h) * kAttnSplits * stride;
+    for (int i = tid; i < hpg * active; i += kAttnThreads) {
+        const int h = i / active, s = i % active;
+        const float* st = part + ((long long)(g * hpg + h) * kAttnSplits + s) * stride + D;
+        wsm[h][s] = st[0];
+        sc[h][s] = st[1];
+    }
+    __syncthreads();
+    if (tid < hpg) {
         float M = -INFINITY;
-        for (int s = 0; s < kAttnSplits; ++s) M = fmaxf(M, base[s * stride + D]);
+        for (int s = 0; s < active; ++s) M = fmaxf(M, wsm[tid][s]);
         float L = 0.0f;
-        for (int s = 0; s < kAttnSplits; ++s) {
-            const float l = base[s * stride + D + 1];
-            if (l > 0.0f) L += l * expf(base[s * stride + D] - M);
+        for (int s = 0; s < active; ++s) {
+            const float e = expf(wsm[tid][s] - M);
+            wsm[tid][s] = e;
+            L += sc[tid][s] * e;
         }
         const float inv = 1.0f / fmaxf(L, 1e-20f);
-        for (int d = tid; d < D; d += kAttnThreads) {
-            float acc = 0.0f;
-            for (int s = 0; s < kAttnSplits; ++s) {
-                const float l = base[s * stride + D + 1];
-                if (l > 0.0f) acc = fmaf(base[s * stride + d], expf(base[s * stride + D] - M), acc);
-            }
-            out[(g * hpg + h) * D + d] = acc * inv;
-        }
+        for (int s = 0; s < active; ++s) wsm[tid][s] *= inv;
+    }
+    __syncthreads();
+    for (int i = tid; i < hpg * D; i += kAttnThreads) {
+        const int h = i / D, d = i % D;
+        const float* base = part + (long long)(g * hpg + h) * kAttnSplits * stride + d;
+        float acc = 0.0f;
+#pragma unroll 8
+        for (int s = 0; s < active; ++s) acc = fmaf(wsm[h][s], base[(long long)s * stride], acc);
+        out[(g * hpg + h) * D + d] = acc;
     }
     if (tid == 0) counters[g] = 0u;
 }

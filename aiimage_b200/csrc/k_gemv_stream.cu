@@ -52,6 +52,7 @@ struct StreamParams {
     const int* pos_ptr;
     unsigned long long* argmax_key;
     int* status;
+    uint32_t zero;   // 0, opaque to the compiler (keeps decode constants in registers)
 };
 
 
@@ -113,7 +114,7 @@ __global__ void __launch_bounds__(kStreamThreads, A == 1 ? 2 : 1) gemv_stream_ke
     constexpr int TR = RG * RPG;
     constexpr int EPC = BITS == 4 ? 32 : 16;  // elements per 16-byte chunk
     constexpr int NCT = 32 * WPG;
-    constexpr int LR = RPG == 4 ? 2 : 1;
+    constexpr int LR = RPG == 8 ? 3 : (RPG == 4 ? 2 : 1);
 
     const int S = p.stages;
     uint64_t* full = reinterpret_cast<uint64_t*>(smem);
@@ -210,6 +211,7 @@ __global__ void __launch_bounds__(kStreamThreads, A == 1 ? 2 : 1) gemv_stream_ke
         for (int q = 0; q < NP; ++q)
             a[ai][q] = c < p.nchunks ? reinterpret_cast<const unsigned long long*>(act_s)[c * NP + q] : 0ull;
     }
+    const PairConsts kc = make_pair_consts<BITS>(p.zero);
     unsigned long long best_key = 0ull;
     // Set by any consumer warp whose bounded wait ran out; with WPG > 1 all
     // warps meet at the per-tile barrier and leave together.
@@ -243,10 +245,10 @@ __global__ void __launch_bounds__(kStreamThreads, A == 1 ? 2 : 1) gemv_stream_ke
                     const ST* srow = reinterpret_cast<const ST*>(st + (size_t)tr * p.srow_bytes);
                     if constexpr (BITS == 4) {
                         if constexpr (SMODE == 0) {
-                            dot_q4_pairs(w.x, w.y, a[ai], r01[r], r23[r]);
+                            dot_q4_pairs(w.x, w.y, a[ai], kc, r01[r], r23[r]);
                         } else {
                             unsigned long long c01 = 0ull, c23 = 0ull;
-                            dot_q4_pairs(w.x, w.y, a[ai], c01, c23);
+                            dot_q4_pairs(w.x, w.y, a[ai], kc, c01, c23);
                             if constexpr (SMODE == 1) {
                                 tot[r] = fmaf(sum2u(c01) + sum2u(c23), to_float(srow[c >> p.gshift]), tot[r]);
                             } else {
@@ -255,7 +257,7 @@ __global__ void __launch_bounds__(kStreamThreads, A == 1 ? 2 : 1) gemv_stream_ke
                             }
                         }
                     } else {
-                        dot_q8_pairs(w.x, w.y, a[ai], r01[r], r23[r]);
+                        dot_q8_pairs(w.x, w.y, a[ai], kc, r01[r], r23[r]);
                     }
                 }
             }
@@ -357,6 +359,7 @@ cudaError_t dispatch_geom(const StreamParams& sp, const StreamPlan& pl, int grid
 #define AEXIS_STREAM_CASE(A_, W_, R_)                                                   \
     if (pl.a == A_ && pl.wpg == W_ && pl.rpg == R_)                                     \
         return launch_stream_t<BITS, ST, SMODE, A_, W_, R_>(sp, grid, pl.smem, pdl, s);
+    AEXIS_STREAM_CASE(1, 1, 8)
     AEXIS_STREAM_CASE(1, 1, 4)
     AEXIS_STREAM_CASE(1, 1, 2)
     AEXIS_STREAM_CASE(2, 1, 4)
@@ -391,11 +394,14 @@ static int plan_stream(const aexis_weights* w, int sm_count, StreamPlan* pl, int
     if (64 * wpg < nchunks) return 0;                 // K beyond two chunks per lane of 4 warps
     const int a = nchunks > 32 * wpg ? 2 : 1;
     const int rg = 8 / wpg;
-    int rpg = 4;
     const int row_bytes = w->k * bits / 8;
     const int sdt = w->scale_dtype == AEXIS_F16 ? 2 : 4;
     const int srow_bytes = smode == 0 ? sdt : (w->k / w->group) * sdt;
-    if (wpg == 1 && (w->n + rg * 4 - 1) / (rg * 4) < sm_count) rpg = 2;  // small N: more tiles
+    // Rows per warp per tile: 8 when there are tiles for two CTAs per SM
+    // (amortises the per-tile reduction), else 4, else 2 (small N: more tiles).
+    int rpg = 4;
+    if (wpg == 1 && a == 1 && (w->n + rg * 8 - 1) / (rg * 8) >= 2 * sm_count) rpg = 8;
+    else if (wpg == 1 && (w->n + rg * 4 - 1) / (rg * 4) < sm_count) rpg = 2;
     const int tr = rg * rpg;
     const int w_tile = tr * row_bytes;
     const int s_tile = (tr * srow_bytes + 15) & ~15;
@@ -467,7 +473,11 @@ cudaError_t launch_gemv_stream(const GemvArgs& a, int sm_count, int* status, cud
     sp.pos_ptr = a.pos_ptr;
     sp.argmax_key = a.argmax_key;
     sp.status = status;
-    const int grid = pl.ntiles < sm_count ? pl.ntiles : sm_count;
+    sp.zero = 0;
+    // Large matrices run two CTAs per SM; smaller ones one, which leaves room
+    // for the next kernel's CTA to start streaming under programmatic launch.
+    const int per_sm = (pl.rpg == 8 && 2 * pl.smem <= 220 * 1024) ? 2 : 1;
+    const int grid = pl.ntiles < per_sm * sm_count ? pl.ntiles : per_sm * sm_count;
     if (bits == 8) {
         if (w->scale_dtype == AEXIS_F16) return dispatch_geom<8, __half, 0>(sp, pl, grid, a.pdl, stream);
         return dispatch_geom<8, float, 0>(sp, pl, grid, a.pdl, stream);
