@@ -199,6 +199,29 @@ int aexis_cuda_sdpa(aexis_ctx* ctx, const float* q, const float* k, const float*
 int aexis_cuda_argmax(aexis_ctx* ctx, const float* logits, int rows, int width, int ld,
                       int32_t* out_idx);
 
+/* Rows that aexis_cuda_argmax_static accepts in one call (the size of its
+ * fixed key array: 4096 x 8 bytes, held on every GPU that loads the library). */
+#define AEXIS_ARGMAX_STATIC_MAX_ROWS 4096
+
+/* The greedy argmax of aexis_cuda_argmax, for callers that cannot allocate
+ * device memory. No counterpart in the reference: it exists for hosts that
+ * own all device memory through their own allocator (a game engine's
+ * graphics-interop path, for instance) or that call from a per-frame callback
+ * which must never block, where cudaMalloc / cudaFree may synchronise the
+ * device. It needs no context and allocates nothing: its per-row keys live in
+ * a fixed array inside the library. The caller passes the logits, the output
+ * and a cudaStream_t (NULL = the legacy default stream) of the current device.
+ *   - rows must be <= AEXIS_ARGMAX_STATIC_MAX_ROWS, else AEXIS_E_RANGE.
+ *   - The first call on a device looks up the array's device address (a
+ *     cudaGetSymbolAddress with that device current). Make that first call
+ *     before any stream capture.
+ *   - Every call on a device shares the one array: calls that overlap on the
+ *     GPU (different streams, no ordering between them) race and may return
+ *     wrong indices. Calls on one stream are ordered and safe.
+ * Same result and tie rule as aexis_cuda_argmax. */
+int aexis_cuda_argmax_static(const float* logits, int rows, int width, int ld, int32_t* out_idx,
+                             void* cuda_stream);
+
 /* Top-k per row for the sampler (Qwen35Sampler, Samples/.../Qwen35Decoder-
  * Session.cs:1823-1900 sorts the full vocabulary on the CPU): the k largest
  * logits in descending order, equal values by ascending index.
