@@ -110,6 +110,10 @@ int quantize_rows(int bits, const float* data, int out_ch, int per_ch, int conti
 
 size_t dsize(int dtype) { return dtype == AEXIS_F16 ? 2 : 4; }
 
+// Rows from which a Q8 Gemm takes the tensor-core path (one weight pass)
+// instead of one streaming GEMV per row.
+constexpr int kTcMinRows = 4;
+
 }  // namespace
 
 // ---------------------------------------------------------------- context
@@ -276,6 +280,7 @@ AEXIS_API int aexis_cuda_weights_free(aexis_ctx* ctx, aexis_weights* w) {
     cudaStreamSynchronize(ctx->stream);
     if (w->data) cudaFree(w->data);
     if (w->scales) cudaFree(w->scales);
+    if (w->tc_tiled) cudaFree(w->tc_tiled);
     delete w;
     return AEXIS_OK;
 }
@@ -307,6 +312,22 @@ static int gemm_common(aexis_ctx* ctx, const void* a, int a_dtype, int lda, int 
         return aexis_fail(ctx, AEXIS_E_UNSUPPORTED, "dtype a=%d y=%d", a_dtype, y_dtype);
     int rc = bind(ctx);
     if (rc) return rc;
+    // Batched Q8: one pass over the weights on the tensor cores.
+    if (m >= kTcMinRows && gemm_tc_supported(w, m, a_dtype) && (a_dtype == AEXIS_F16 || y_dtype == AEXIS_F32)) {
+        aexis_weights* wm = const_cast<aexis_weights*>(w);
+        if (!wm->tc_tiled) {
+            cudaError_t e = cudaMalloc(&wm->tc_tiled, gemm_tc_tiled_bytes(w));
+            if (e != cudaSuccess) return aexis_cuda_check(ctx, e, "tensor-core weight tiles");
+            rc = aexis_cuda_check(ctx, launch_repack_q8(w, wm->tc_tiled, ctx->stream), "weight repack");
+            if (rc) return rc;
+        }
+        void* xt = nullptr;
+        rc = aexis_scratch(ctx, gemm_tc_xt_bytes(m, k, a_dtype), &xt);
+        if (rc) return rc;
+        return aexis_cuda_check(ctx, launch_gemm_tc(w, wm->tc_tiled, a, a_dtype, lda, m, xt, bias, alpha, beta, y,
+                                                    y_dtype, ldy, epi == EPI_STORE_TILED, ctx->sm_count, ctx->status,
+                                                    ctx->stream), "tensor-core gemm launch");
+    }
     GemvArgs g;
     g.status = ctx->status;
     g.a_dtype = a_dtype;

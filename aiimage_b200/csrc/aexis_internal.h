@@ -21,6 +21,9 @@ struct aexis_weights {
     void* data = nullptr;    // device: packed words (Q4/Q8) or dense values
     void* scales = nullptr;  // device: fp32 or fp16 scales (Q4/Q8)
     size_t data_bytes = 0, scale_bytes = 0;
+    // Q8 weights repacked into 128-row x 64-k blocks for the tensor-core
+    // batched GEMM, built on the first batched call.
+    void* tc_tiled = nullptr;
 };
 
 struct aexis_ctx {
@@ -97,6 +100,15 @@ cudaError_t launch_gemv_stream(const GemvArgs& a, int sm_count, int* status, cud
 // Bytes of padding after every weight and scale allocation: bulk copies of a
 // partial last tile round their size up to 16 bytes.
 constexpr size_t kWeightPad = 256;
+
+// Batched Q8 GEMM on tcgen05 (k_gemm_tc.cu).
+bool gemm_tc_supported(const aexis_weights* w, int m, int a_dtype);
+size_t gemm_tc_tiled_bytes(const aexis_weights* w);
+size_t gemm_tc_xt_bytes(int m, int k, int a_dtype);
+cudaError_t launch_repack_q8(const aexis_weights* w, void* tiled, cudaStream_t s);
+cudaError_t launch_gemm_tc(const aexis_weights* w, const void* tiled, const void* x, int a_dtype, int lda, int m,
+                           void* xt, const float* bias, float alpha, float beta, void* y, int y_dtype, int ldy,
+                           int tiled_epi, int sm_count, int* status, cudaStream_t s);
 
 cudaError_t launch_dequant(const aexis_weights* w, float* out, cudaStream_t s);
 cudaError_t launch_rmsnorm(const void* x, int x_dtype, int rows, int width, int ld,

@@ -1,0 +1,445 @@
+// k_gemm_tc.cu -- batched Q8 weight-only GEMM on the 5th-generation tensor
+// cores (tcgen05, TMEM accumulators, bulk-copy staging), dequantising in
+// shared memory.
+//
+//   y[b, n] = s_n * sum_k x[b, k] * q[n, k]      (+ bias / alpha / beta epilogue)
+//
+// the batched form of AexisGemm2DPack4LinearTextureAFromLinear with INT8
+// weights and per-output-row scales (HLSL Pack4Matmul:1038-1104, weight read
+// AexisGemm2DReadB :707-734). The per-row scale is constant along K, so the
+// tensor cores multiply the exact int8 values (as fp16) and the scale is
+// applied once per output in the epilogue.
+//
+// Layout:
+//   * weights, repacked once per handle: [N/128][K/64] blocks of 128 rows x 64
+//     int8 (8 KB contiguous), so one k-block of a 128-row slab is one bulk copy;
+//   * activations, prepared per call: [K/64][NB rows][64] fp16 in the 128-byte
+//     swizzled K-major layout the MMA descriptors describe (8-row atoms of
+//     1024 bytes). fp32 activations are split into fp16 hi and lo rows
+//     (x = hi + lo to about 22 bits) that ride in the same MMA as extra
+//     columns, so fp32 inputs keep fp32-class accuracy.
+// Per CTA (persistent, one per SM): a 256-row weight tile (two M=128 MMAs
+// sharing the activation tile) over all K. Warp roles: 0 bulk-copy producer,
+// 1 MMA issuer and TMEM owner, 2-5 dequantise int8 -> fp16 into the swizzled
+// A tiles and run the epilogue from TMEM. Every barrier wait is bounded.
+#include "gemv_dev.cuh"
+
+namespace {
+
+using namespace aexis_dev;
+
+constexpr int kTcThreads = 192;          // 6 warps
+constexpr int kTM = 128;                 // rows per MMA (M)
+constexpr int kTile = 256;               // weight rows per CTA tile (two MMAs)
+constexpr int kKB = 64;                  // K per stage (one 128-byte swizzle atom of fp16)
+constexpr int kStages = 2;
+
+struct TcParams {
+    const uint8_t* wt;        // tiled int8 weights
+    const void* scales;       // per row
+    int scale_f16;
+    const uint8_t* xt;        // prepared activations [K/64][nb][128 B]
+    int n, k, m, nb, split;   // nb = MMA N (rows of xt), split: hi rows [0,m), lo rows [m,2m)
+    int n_tiles;              // ceil(n / 256)
+    const float* bias;
+    float alpha, beta;
+    void* y;
+    int y_f16, ldy;
+    int tiled;                // 1: beta*bias + alpha*acc (lm_head form)
+    int* status;
+};
+
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t smem_addr) {
+    // K-major, 128-byte swizzle: 8-row atoms 1024 bytes apart (SBO), LBO 1,
+    // version 1 (sm_100), layout type 2.
+    uint64_t d = 0;
+    d |= (uint64_t)((smem_addr >> 4) & 0x3FFF);
+    d |= (uint64_t)1 << 16;                      // LBO (unused for swizzled K-major)
+    d |= (uint64_t)(1024 >> 4) << 32;            // SBO
+    d |= (uint64_t)1 << 46;                      // version
+    d |= (uint64_t)2 << 61;                      // SWIZZLE_128B
+    return d;
+}
+
+__device__ __forceinline__ uint32_t idesc_f16_f32(int m, int n) {
+    // c_format F32 (bit 4), a/b F16, both K-major, N >> 3 at bit 17, M >> 4 at bit 24.
+    return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, int accum) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}"
+        ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accum), "r"(0), "r"(0), "r"(0), "r"(0));
+}
+
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+                 ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// int8 x4 (one word) -> two fp16x2 of the exact values: bytes biased by 128
+// (XOR) and placed under the fp16 exponent of 1024 with PRMT, then 1024+128
+// subtracted (exact in fp16).
+__device__ __forceinline__ void i8x4_to_h2x2(uint32_t v, uint32_t& lo, uint32_t& hi) {
+    const uint32_t u = v ^ 0x80808080u;
+    uint32_t a = __byte_perm(u, 0x64646464u, 0x4140);
+    uint32_t b = __byte_perm(u, 0x64646464u, 0x4342);
+    const __half2 bias = __halves2half2(__ushort_as_half(0x6480), __ushort_as_half(0x6480));
+    __half2 ha = __hsub2(*reinterpret_cast<__half2*>(&a), bias);
+    __half2 hb = __hsub2(*reinterpret_cast<__half2*>(&b), bias);
+    lo = *reinterpret_cast<uint32_t*>(&ha);
+    hi = *reinterpret_cast<uint32_t*>(&hb);
+}
+
+__global__ void __launch_bounds__(kTcThreads, 1) gemm_q8_tc_kernel(TcParams p) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    // 1024-aligned carve-up: per stage int8 [256][64], A fp16 2 x [128 x 64], B [nb x 64] fp16.
+    uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const int b_bytes = p.nb * 128;
+    const int stage_bytes = kTile * kKB + 2 * kTM * 128 + ((b_bytes + 1023) & ~1023);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(base + kStages * stage_bytes);
+    uint64_t* full = bars;                   // producer tx
+    uint64_t* a_ready = bars + kStages;      // 4 dequant warps
+    uint64_t* empty = bars + 2 * kStages;    // MMA commit
+    uint64_t* acc_full = bars + 3 * kStages; // MMA commit after a tile
+    uint64_t* acc_empty = acc_full + 1;      // 4 epilogue warps
+    uint64_t* drain = acc_empty + 1;         // final MMA commit before TMEM is freed
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nkb = p.k / kKB;
+    const int my_tiles = (int)blockIdx.x < p.n_tiles ? (p.n_tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+    const uint32_t tmem_cols = (uint32_t)(2 * p.nb <= 32 ? 32 : (2 * p.nb <= 64 ? 64 : (2 * p.nb <= 128 ? 128 :
+                                          (2 * p.nb <= 256 ? 256 : 512))));
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(full + s, 1);
+            mbar_init(a_ready + s, 4);
+            mbar_init(empty + s, 1);
+        }
+        mbar_init(acc_full, 1);
+        mbar_init(acc_empty, 4);
+        mbar_init(drain, 1);
+        *abort_flag = 0;
+        fence_barrier_init();
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+                     ::"r"(smem_u32(tmem_slot)), "r"(tmem_cols) : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    griddep_wait();
+
+    if (warp == 0) {
+        // ----------------------------------------------------------- producer
+        if (lane == 0) {
+            const uint64_t pol = policy_evict_first();
+            int it = 0, issued = 0;
+            for (int t = 0; t < my_tiles && !*abort_flag; ++t) {
+                const int tile = (int)blockIdx.x + t * (int)gridDim.x;
+                for (int kb = 0; kb < nkb; ++kb, ++it) {
+                    const int s = it % kStages;
+                    if (it >= kStages && !mbar_wait(empty + s, ((it / kStages) & 1) ^ 1)) {
+                        report_timeout(p.status);
+                        *abort_flag = 1;
+                        break;
+                    }
+                    uint8_t* st = base + (size_t)s * stage_bytes;
+                    const uint32_t slab = (uint32_t)kTM * kKB;  // 8 KB
+                    mbar_arrive_expect_tx(full + s, 2 * slab + (uint32_t)b_bytes);
+                    for (int j = 0; j < 2; ++j) {
+                        const size_t sub = (size_t)tile * 2 + j;  // 128-row slab index
+                        bulk_g2s(st + j * slab, p.wt + (sub * nkb + kb) * slab, slab, full + s, pol);
+                    }
+                    bulk_g2s_plain(st + kTile * kKB + 2 * kTM * 128, p.xt + (size_t)kb * b_bytes,
+                                   (uint32_t)b_bytes, full + s);
+                    issued = it + 1;
+                }
+            }
+            // No bulk copy may still be landing when the CTA exits (the
+            // consumers wait for every stage on the normal path).
+            for (int i = issued - kStages < 0 ? 0 : issued - kStages; i < issued; ++i)
+                if (!mbar_wait(full + i % kStages, (i / kStages) & 1)) { report_timeout(p.status); break; }
+        }
+    } else if (warp == 1) {
+        // ---------------------------------------------------------- MMA issuer
+        if (lane == 0) {
+            const uint32_t idesc = idesc_f16_f32(kTM, p.nb);
+            int it = 0;
+            for (int t = 0; t < my_tiles && !*abort_flag; ++t) {
+                if (t > 0 && !mbar_wait(acc_empty, (t - 1) & 1)) {
+                    report_timeout(p.status);
+                    *abort_flag = 1;
+                    break;
+                }
+                tc_fence_after();
+                for (int kb = 0; kb < nkb; ++kb, ++it) {
+                    const int s = it % kStages;
+                    if (!mbar_wait(a_ready + s, (it / kStages) & 1)) {
+                        report_timeout(p.status);
+                        *abort_flag = 1;
+                        break;
+                    }
+                    tc_fence_after();
+                    uint8_t* st = base + (size_t)s * stage_bytes;
+                    const uint32_t a0 = smem_u32(st + kTile * kKB);
+                    const uint32_t b0 = smem_u32(st + kTile * kKB + 2 * kTM * 128);
+#pragma unroll
+                    for (int j = 0; j < 2; ++j)
+#pragma unroll
+                        for (int kk = 0; kk < kKB / 16; ++kk)
+                            mma_f16(tmem + (uint32_t)(j * p.nb), sw128_desc(a0 + j * kTM * 128 + kk * 32),
+                                    sw128_desc(b0 + kk * 32), idesc, (kb > 0 || kk > 0) ? 1 : 0);
+                    mma_commit(empty + s);
+                }
+                if (*abort_flag) break;
+                mma_commit(acc_full);
+            }
+            // Every MMA this thread issued has completed before TMEM is freed.
+            mma_commit(drain);
+            if (!mbar_wait(drain, 0)) report_timeout(p.status);
+        }
+    } else {
+        // ----------------------------------------- dequantise + epilogue (2..5)
+        const int dw = warp - 2;              // 0..3
+        const int dt = dw * 32 + lane;        // 0..127
+        const int quad = warp & 3;            // TMEM lane quadrant this warp may access
+        int it = 0;
+        for (int t = 0; t < my_tiles && !*abort_flag; ++t) {
+            const int tile = (int)blockIdx.x + t * (int)gridDim.x;
+            for (int kb = 0; kb < nkb; ++kb, ++it) {
+                const int s = it % kStages;
+                if (!mbar_wait(full + s, (it / kStages) & 1)) {
+                    report_timeout(p.status);
+                    *abort_flag = 1;
+                    break;
+                }
+                uint8_t* st = base + (size_t)s * stage_bytes;
+                uint8_t* a_t = st + kTile * kKB;
+                // Thread dt converts 16 int8 (chunk dt & 3 of row dt >> 2) of
+                // each 32-row group: conflict-free reads and swizzled writes.
+#pragma unroll 2
+                for (int g = 0; g < kTile / 32; ++g) {
+                    const int row = g * 32 + (dt >> 2);          // 0..255
+                    const int ch = dt & 3;                       // 16-byte chunk of the 64 int8
+                    const uint4 q = *reinterpret_cast<const uint4*>(st + row * kKB + ch * 16);
+                    uint32_t h[8];
+                    i8x4_to_h2x2(q.x, h[0], h[1]);
+                    i8x4_to_h2x2(q.y, h[2], h[3]);
+                    i8x4_to_h2x2(q.z, h[4], h[5]);
+                    i8x4_to_h2x2(q.w, h[6], h[7]);
+                    const int j = row >> 7, r = row & 127;
+                    uint8_t* arow = a_t + j * kTM * 128 + (r >> 3) * 1024 + (r & 7) * 128;
+                    const int c0 = 2 * ch, c1 = 2 * ch + 1;     // fp16 16-byte chunks
+                    *reinterpret_cast<uint4*>(arow + ((c0 ^ (r & 7)) << 4)) = make_uint4(h[0], h[1], h[2], h[3]);
+                    *reinterpret_cast<uint4*>(arow + ((c1 ^ (r & 7)) << 4)) = make_uint4(h[4], h[5], h[6], h[7]);
+                }
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(a_ready + s);
+            }
+            if (*abort_flag) break;
+            // Epilogue: wait for the tile's accumulators, then each thread owns
+            // one weight row (TMEM lane) of each 128-row half.
+            if (!mbar_wait(acc_full, t & 1)) {
+                report_timeout(p.status);
+                *abort_flag = 1;
+                break;
+            }
+            tc_fence_after();
+            for (int j = 0; j < 2; ++j) {
+                const int n = tile * kTile + j * kTM + quad * 32 + lane;
+                float sc = 0.0f, bb = 0.0f;
+                if (n < p.n) {
+                    sc = p.scale_f16 ? __half2float(reinterpret_cast<const __half*>(p.scales)[n])
+                                     : reinterpret_cast<const float*>(p.scales)[n];
+                    bb = p.bias ? p.beta * p.bias[n] : 0.0f;
+                }
+                const uint32_t lane_addr = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(j * p.nb);
+                const int mrows = p.m;
+                for (int c0 = 0; c0 < p.nb; c0 += 16) {
+                    float v[16];
+                    tmem_ld16(lane_addr + (uint32_t)c0, v);
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                        const int b = c0 + i;
+                        if (n >= p.n) continue;
+                        if (!p.split) {
+                            if (b < mrows) {
+                                const float out = p.tiled ? bb + p.alpha * (v[i] * sc) : p.alpha * (bb + v[i] * sc);
+                                if (p.y_f16) reinterpret_cast<__half*>(p.y)[(size_t)b * p.ldy + n] = __float2half_rn(out);
+                                else reinterpret_cast<float*>(p.y)[(size_t)b * p.ldy + n] = out;
+                            }
+                        } else if (b < mrows) {
+                            // hi part: stored now, lo part added when its column arrives.
+                            reinterpret_cast<float*>(p.y)[(size_t)b * p.ldy + n] = v[i];
+                        } else if (b < 2 * mrows) {
+                            const int bh = b - mrows;
+                            float* yp = reinterpret_cast<float*>(p.y) + (size_t)bh * p.ldy + n;
+                            const float acc = (*yp + v[i]) * sc;
+                            const float out = p.tiled ? bb + p.alpha * acc : p.alpha * (bb + acc);
+                            *yp = out;
+                        }
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(acc_empty);
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(tmem_cols) : "memory");
+    }
+}
+
+// x [m][lda] (fp16 or fp32) -> xt [K/64][nb][64] fp16, 128-byte swizzled rows.
+// fp32 rows are split: hi = fp16(x) in row b, lo = fp16(x - hi) in row m + b.
+__global__ void prep_x_kernel(const void* x, int a_f16, int lda, int m, int k, int nb, int split, uint8_t* xt) {
+    const long long total = (long long)(k / kKB) * nb * 8;  // 16-byte chunks
+    for (long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x; t < total;
+         t += (long long)gridDim.x * blockDim.x) {
+        const int c = (int)(t & 7);
+        const int row = (int)((t >> 3) % nb);
+        const int kb = (int)(t / (8LL * nb));
+        __half h[8];
+        const int src = split && row >= m ? row - m : row;
+        const bool lo = split && row >= m;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            const int kk = kb * kKB + c * 8 + e;
+            float v = 0.0f;
+            if (src < m) v = aexis_load_act(x, a_f16 ? AEXIS_F16 : AEXIS_F32, (long long)src * lda + kk);
+            const __half hi = __float2half_rn(v);
+            h[e] = lo ? __float2half_rn(v - __half2float(hi)) : hi;
+        }
+        uint8_t* dst = xt + ((size_t)kb * nb + row) * 128 + ((c ^ (row & 7)) << 4);
+        *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<uint4*>(h);
+    }
+}
+
+// Row-major Q8 [n][k] -> [ceil(n/256)*2][k/64][128][64] (rows past n zero;
+// the slab count is even so a 256-row CTA tile never reads past the buffer).
+__global__ void repack_q8_kernel(const uint8_t* src, int n, int k, uint8_t* dst) {
+    const int nkb = k / kKB;
+    const long long total = (long long)((n + kTile - 1) / kTile) * kTile * nkb * 4;  // 16-byte chunks
+    for (long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x; t < total;
+         t += (long long)gridDim.x * blockDim.x) {
+        const int ch = (int)(t & 3);
+        const long long rowblk = t >> 2;                 // (slab, kb, r)
+        const int r = (int)(rowblk % kTM);
+        const long long sk = rowblk / kTM;
+        const int kb = (int)(sk % nkb);
+        const long long slab = sk / nkb;
+        const long long row = slab * kTM + r;
+        uint4 v = make_uint4(0u, 0u, 0u, 0u);
+        if (row < n) v = *reinterpret_cast<const uint4*>(src + row * k + kb * kKB + ch * 16);
+        *reinterpret_cast<uint4*>(dst + ((slab * nkb + kb) * kTM + r) * kKB + ch * 16) = v;
+    }
+}
+
+}  // namespace
+
+size_t gemm_tc_smem_bytes(int nb) {
+    const int b_bytes = nb * 128;
+    const int stage = kTile * kKB + 2 * kTM * 128 + ((b_bytes + 1023) & ~1023);
+    return 1024 + (size_t)kStages * stage + 256;  // alignment slack + barriers
+}
+
+bool gemm_tc_supported(const aexis_weights* w, int m, int a_dtype) {
+    if (w->kind != WK_Q8 || w->k % kKB != 0 || m < 1) return false;
+    const int rows = a_dtype == AEXIS_F32 ? 2 * m : m;
+    const int nb = (rows + 15) / 16 * 16;
+    return nb <= 256 && gemm_tc_smem_bytes(nb) <= 227 * 1024;
+}
+
+size_t gemm_tc_tiled_bytes(const aexis_weights* w) {
+    return (size_t)((w->n + kTile - 1) / kTile) * kTile * w->k;
+}
+
+cudaError_t launch_repack_q8(const aexis_weights* w, void* tiled, cudaStream_t s) {
+    repack_q8_kernel<<<148 * 8, 256, 0, s>>>(reinterpret_cast<const uint8_t*>(w->data), w->n, w->k,
+                                              reinterpret_cast<uint8_t*>(tiled));
+    return cudaGetLastError();
+}
+
+size_t gemm_tc_xt_bytes(int m, int k, int a_dtype) {
+    const int rows = a_dtype == AEXIS_F32 ? 2 * m : m;
+    const int nb = (rows + 15) / 16 * 16;
+    return (size_t)k * nb * 2;
+}
+
+cudaError_t launch_gemm_tc(const aexis_weights* w, const void* tiled, const void* x, int a_dtype, int lda, int m,
+                           void* xt, const float* bias, float alpha, float beta, void* y, int y_dtype, int ldy,
+                           int tiled_epi, int sm_count, int* status, cudaStream_t s) {
+    const int split = a_dtype == AEXIS_F32;
+    const int nb = ((split ? 2 * m : m) + 15) / 16 * 16;
+    const long long chunks = (long long)(w->k / kKB) * nb * 8;
+    int pb = (int)((chunks + 255) / 256);
+    pb = pb > 148 * 8 ? 148 * 8 : (pb < 1 ? 1 : pb);
+    prep_x_kernel<<<pb, 256, 0, s>>>(x, a_dtype == AEXIS_F16, lda, m, w->k, nb, split, reinterpret_cast<uint8_t*>(xt));
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    if (split && y_dtype != AEXIS_F32) return cudaErrorNotSupported;  // hi is staged in y
+    TcParams p = {};
+    p.wt = reinterpret_cast<const uint8_t*>(tiled);
+    p.scales = w->scales;
+    p.scale_f16 = w->scale_dtype == AEXIS_F16;
+    p.xt = reinterpret_cast<const uint8_t*>(xt);
+    p.n = w->n;
+    p.k = w->k;
+    p.m = m;
+    p.nb = nb;
+    p.split = split;
+    p.n_tiles = (w->n + kTile - 1) / kTile;
+    p.bias = bias;
+    p.alpha = alpha;
+    p.beta = beta;
+    p.y = y;
+    p.y_f16 = y_dtype == AEXIS_F16;
+    p.ldy = ldy;
+    p.tiled = tiled_epi;
+    p.status = status;
+    const size_t smem = gemm_tc_smem_bytes(nb);
+    static size_t configured = 0;
+    if (smem > configured) {
+        e = cudaFuncSetAttribute(gemm_q8_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+        configured = smem;
+    }
+    const int grid = p.n_tiles < sm_count ? p.n_tiles : sm_count;
+    gemm_q8_tc_kernel<<<grid, kTcThreads, smem, s>>>(p);
+    return cudaGetLastError();
+}
