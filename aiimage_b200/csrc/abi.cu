@@ -461,6 +461,21 @@ AEXIS_API int aexis_cuda_argmax(aexis_ctx* ctx, const float* logits, int rows, i
                                                ctx->sm_count, ctx->stream), "argmax launch");
 }
 
+AEXIS_API int aexis_cuda_argmax_keys(aexis_ctx* ctx, const float* logits, int rows, int width, int ld,
+                                     int64_t index_offset, uint64_t* keys) {
+    if (!ctx) return AEXIS_E_NULL;
+    if (!logits || !keys) return aexis_fail(ctx, AEXIS_E_NULL, "null pointer");
+    if (width <= 0 || rows <= 0) return aexis_fail(ctx, AEXIS_E_RANGE, "rows=%d width=%d", rows, width);
+    if (ld < width) return aexis_fail(ctx, AEXIS_E_SHAPE, "ld=%d < width", ld);
+    if (index_offset < 0 || index_offset + width > 0xFFFFFFFFLL)
+        return aexis_fail(ctx, AEXIS_E_RANGE, "index_offset=%lld", (long long)index_offset);
+    int rc = bind(ctx);
+    if (rc) return rc;
+    return aexis_cuda_check(ctx, launch_argmax_keys(logits, rows, width, ld, index_offset,
+                                                    (unsigned long long*)keys, ctx->sm_count, ctx->stream),
+                            "argmax keys launch");
+}
+
 AEXIS_API int aexis_cuda_topk(aexis_ctx* ctx, const float* logits, int rows, int width, int ld, int k, float* out_vals,
                               int32_t* out_idx) {
     if (!ctx) return AEXIS_E_NULL;

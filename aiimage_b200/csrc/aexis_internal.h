@@ -128,6 +128,8 @@ cudaError_t launch_sdpa(const float* q, const float* k, const float* v, int src_
 size_t sdpa_smem_bytes(int dst_len);
 cudaError_t launch_argmax(const float* logits, int rows, int width, int ld, int32_t* out,
                           unsigned long long* keys, int sm_count, cudaStream_t s);
+cudaError_t launch_argmax_keys(const float* logits, int rows, int width, int ld, long long offset,
+                               unsigned long long* keys, int sm_count, cudaStream_t s);
 cudaError_t launch_topk(const float* logits, int rows, int width, int ld, int k, float* vals,
                         int32_t* idx, cudaStream_t s);
 cudaError_t launch_embed(const int32_t* words, int count, const aexis_weights* table,

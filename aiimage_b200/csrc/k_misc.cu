@@ -194,12 +194,13 @@ __global__ void sdpa_kernel(const float* q, const float* k, const float* v, int 
 // max-reduced with atomicMax, then decoded.
 __device__ __forceinline__ unsigned long long argmax_key(float v, int idx) { return aexis_argmax_key(v, idx); }
 
-__global__ void argmax_partial_kernel(const float* logits, int width, int ld, unsigned long long* keys) {
+__global__ void argmax_partial_kernel(const float* logits, int width, int ld, unsigned long long* keys,
+                                      long long offset = 0) {
     const int row = blockIdx.y;
     const float* x = logits + (long long)row * ld;
     unsigned long long best = 0ull;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < width; i += gridDim.x * blockDim.x) {
-        const unsigned long long kk = argmax_key(x[i], i);
+        const unsigned long long kk = argmax_key(x[i], (int)(offset + i));
         best = kk > best ? kk : best;
     }
 #pragma unroll
@@ -389,6 +390,18 @@ cudaError_t launch_argmax(const float* logits, int rows, int width, int ld, int3
     if (bx < 1) bx = 1;
     argmax_partial_kernel<<<dim3(bx, rows), kT, 0, s>>>(logits, width, ld, keys);
     argmax_finish_kernel<<<(rows + kT - 1) / kT, kT, 0, s>>>(keys, rows, out);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_argmax_keys(const float* logits, int rows, int width, int ld, long long offset,
+                               unsigned long long* keys, int sm_count, cudaStream_t s) {
+    cudaError_t e = cudaMemsetAsync(keys, 0, sizeof(unsigned long long) * rows, s);
+    if (e != cudaSuccess) return e;
+    int bx = (width + kT * 8 - 1) / (kT * 8);
+    const int cap = (sm_count * 8 + rows - 1) / rows;
+    if (bx > cap) bx = cap;
+    if (bx < 1) bx = 1;
+    argmax_partial_kernel<<<dim3(bx, rows), kT, 0, s>>>(logits, width, ld, keys, offset);
     return cudaGetLastError();
 }
 

@@ -238,6 +238,11 @@ class AexisOps:
         ld = ld if ld is not None else (logits.stride(0) if logits.dim() == 2 else logical_width)
         self._call(lib().aexis_cuda_argmax, _ptr(logits), logical_height, logical_width, ld, _ptr(output))
 
+    def argmax_keys(self, logits, width, rows, index_offset, keys, ld=None):
+        """Per-row 64-bit argmax keys of one vocabulary shard (global indices)."""
+        ld = ld if ld is not None else (logits.stride(0) if logits.dim() == 2 else width)
+        self._call(lib().aexis_cuda_argmax_keys, _ptr(logits), rows, width, ld, index_offset, _ptr(keys))
+
     def top_k(self, logits, width, rows, k, out_vals, out_idx, ld=None):
         ld = ld if ld is not None else (logits.stride(0) if logits.dim() == 2 else width)
         self._call(lib().aexis_cuda_topk, _ptr(logits), rows, width, ld, k, _ptr(out_vals), _ptr(out_idx))

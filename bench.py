@@ -54,6 +54,16 @@ def measured_peak():
         return 6650.0, "fallback"
 
 
+def measured_tflops():
+    """Dense fp16/bf16 tensor peak for a kernel timed alone (burst figure)."""
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            return float(json.load(f)["bf16_tflops"]), "measured"
+    except Exception:
+        return 1590.0, "fallback"
+
+
 def profile_traffic(name: str):
     """DRAM bytes per launch from a committed ncu summary (profiles/<name>),
     line 'traffic_bytes_per_launch: <int>'; None when absent."""
@@ -309,6 +319,13 @@ def run_gpu(args):
         except Exception as e:  # reported, never silently replaced
             decoder = {"error": f"{type(e).__name__}: {e}"}
 
+    config5 = None
+    if not args.skip_config5:
+        try:
+            config5 = bench_config5(ops, world, rank)
+        except Exception as e:
+            config5 = {"error": f"{type(e).__name__}: {e}"}
+
     cpu = None
     if rank == 0 and world == 1 and not args.skip_cpu:
         cpu = cpu_baseline(args.cpu_seconds)
@@ -339,6 +356,7 @@ def run_gpu(args):
             "per_shape": per_shape,
             "config1_q8": q8,
             "decoder": decoder,
+            "config5": config5,
             "cpu_baseline": cpu,
             "e2e": {"value": round(e2e_steps * STEP_BYTES * world / e2e_s / 1e9, 2), "unit": "GB/s",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
@@ -424,6 +442,55 @@ def bench_decoder(ops, peak, prompt_len: int = 512, new_tokens: int = 64):
             "bytes_per_token": bytes_tok, "GB/s": round(bytes_tok * n / gen_s / 1e9, 1),
             "frac": round(bytes_tok * n / gen_s / 1e9 / peak, 3), "first_tokens": toks[:8],
             "kernels_per_token": 2 + 5 * cfg.n_layers + 1}
+
+
+def bench_config5(ops, world: int, rank: int, reps: int = 10):
+    """lm_head 151936 x 1024 Q8 per row, batch 256 fp16
+    hidden states, greedy argmax + top-50 per row. G > 1: vocab shards with
+    the NCCL exchange (aiimage_b200.sharded); rank 0 checks the ids against a
+    single-GPU run of the whole vocabulary."""
+    import torch
+    from aiimage_b200.sharded import ShardedLmHead
+    vocab, hidden, m, k = 151936, 1024, 256, 50
+    p, s = synth.q8_weights(vocab, hidden, seed=5, tag=(vocab, hidden))
+    x = torch.from_numpy(synth.activations(hidden, seed=5, tag=(m, hidden), m=m)).cuda()
+    head = ShardedLmHead(ops, p, s, vocab, hidden, world, rank)
+    logits = torch.empty((m, head.n), dtype=torch.float32, device="cuda")
+    for _ in range(3):
+        ids, vals, idx = head.forward(x, k, logits)
+    torch.cuda.synchronize()
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        ids, vals, idx = head.forward(x, k, logits)
+    e1.record()
+    e1.synchronize()
+    call_s = max_over_ranks(e0.elapsed_time(e1) / 1e3 / reps, world)
+    # GEMM alone (the dominant kernel of the call), this rank's shard.
+    e0.record()
+    for _ in range(reps):
+        head.shard_logits(x, logits)
+    e1.record()
+    e1.synchronize()
+    gemm_s = e0.elapsed_time(e1) / 1e3 / reps
+    flops = 2.0 * m * vocab * hidden
+    peak, kind = measured_tflops()
+    out = {"workload": "config5_lm_head_q8_151936x1024_batch256_argmax_top50", "gpus": world,
+           "ms_per_call": round(call_s * 1e3, 4), "TFLOP/s": round(flops / call_s / 1e12, 1),
+           "gemm_rank_ms": round(gemm_s * 1e3, 4),
+           "gemm_rank_TFLOP/s": round(2.0 * m * head.n * hidden / gemm_s / 1e12, 1),
+           "gemm_frac_of_tensor_peak": round(2.0 * m * head.n * hidden / gemm_s / 1e12 / peak, 3),
+           "tensor_peak": f"{peak} TFLOP/s ({kind}, MEASURED_PEAKS.json bf16_tflops)",
+           "first_ids": ids[:6].tolist()}
+    if world > 1 and rank == 0:
+        full = ShardedLmHead(ops, p, s, vocab, hidden, 1, 0)
+        ids1, _, idx1 = full.forward(x, k)
+        out["ids_match_single_gpu"] = bool(torch.equal(ids1, ids))
+        out["top50_match_single_gpu"] = bool(torch.equal(idx1, idx))
+        full.w.free()
+    head.w.free()
+    return out
 
 
 def cpu_baseline(budget_s: float = 12.0):
@@ -527,6 +594,7 @@ def main():
     ap.add_argument("--impl", choices=["aexis", "reference"], default="aexis")
     ap.add_argument("--skip-decoder", action="store_true", help="omit the config-3 decoder measurement")
     ap.add_argument("--skip-cpu", action="store_true", help="omit the CPU oracle baseline")
+    ap.add_argument("--skip-config5", action="store_true", help="omit the config-5 lm_head measurement")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--only", choices=["dominant", "decoder"], help="profiling mode (see run_only)")
     ap.add_argument("--prompt-len", type=int, default=512)

@@ -199,6 +199,15 @@ int aexis_cuda_sdpa(aexis_ctx* ctx, const float* q, const float* k, const float*
 int aexis_cuda_argmax(aexis_ctx* ctx, const float* logits, int rows, int width, int ld,
                       int32_t* out_idx);
 
+/* The argmax of one vocabulary shard as 64-bit keys, for a cross-GPU max
+ * reduction (the vocab-sharded lm_head; no single reference counterpart:
+ * AexisArgMaxPack4LinearMat, HLSL Pack4Matmul:645-686, split by columns).
+ * keys[r] = (orderable(max value) << 32) | (0xFFFFFFFF - (index_offset + i)),
+ * so the maximum key over all shards is the first global index of the
+ * maximum, as the single-device scan picks it. keys: device uint64 [rows]. */
+int aexis_cuda_argmax_keys(aexis_ctx* ctx, const float* logits, int rows, int width, int ld,
+                           int64_t index_offset, uint64_t* keys);
+
 /* Rows that aexis_cuda_argmax_static accepts in one call (the size of its
  * fixed key array: 4096 x 8 bytes, held on every GPU that loads the library). */
 #define AEXIS_ARGMAX_STATIC_MAX_ROWS 4096
