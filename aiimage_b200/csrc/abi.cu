@@ -173,7 +173,9 @@ AEXIS_API const char* aexis_cuda_last_error(const aexis_ctx* ctx) {
 
 AEXIS_API int aexis_cuda_set_stream(aexis_ctx* ctx, void* stream) {
     if (!ctx) return AEXIS_E_NULL;
-    ctx->stream = stream ? (cudaStream_t)stream : ctx->own_stream;
+    // NULL is the CUDA legacy default stream, as everywhere in CUDA (torch's
+    // default stream handle is 0): work then orders with that stream.
+    ctx->stream = (cudaStream_t)stream;
     return AEXIS_OK;
 }
 

@@ -74,8 +74,9 @@ int aexis_cuda_destroy(aexis_ctx* ctx);
  * message of the last failed aexis_cuda_create on this thread. */
 const char* aexis_cuda_last_error(const aexis_ctx* ctx);
 
-/* Enqueue subsequent work on a caller-owned cudaStream_t (NULL restores the
- * context's own stream). The reference records into a CommandBuffer
+/* Enqueue subsequent work on a caller-owned cudaStream_t; NULL is the CUDA
+ * legacy default stream. Until the first call the context uses a stream of
+ * its own. The reference records into a CommandBuffer
  * (Ops Gemm2DPack4LinearTextureA(CommandBuffer, ...) overloads, Ops:3685). */
 int aexis_cuda_set_stream(aexis_ctx* ctx, void* cuda_stream);
 
