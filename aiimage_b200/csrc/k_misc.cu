@@ -218,62 +218,6 @@ __global__ void argmax_finish_kernel(const unsigned long long* keys, int rows, i
     }
 }
 
-// -------------------------------------------------------------------- top-k
-// One CTA per row. Each thread keeps its own descending top-k list of keys in
-// shared memory; the lists are merged by k rounds of a block-wide max.
-constexpr int kTopkThreads = 128;
-
-__global__ void __launch_bounds__(kTopkThreads) topk_kernel(const float* logits, int width, int ld,
-                                                            int k, float* vals, int32_t* idx) {
-    extern __shared__ unsigned long long lists[];  // [kTopkThreads][k]
-    __shared__ unsigned long long red[kTopkThreads / 32];
-    __shared__ int redw[kTopkThreads / 32];
-    const int row = blockIdx.x, t = threadIdx.x;
-    const float* x = logits + (long long)row * ld;
-    unsigned long long* mine = lists + (long long)t * k;
-    int cnt = 0;
-    for (int i = t; i < width; i += kTopkThreads) {
-        float v = x[i];
-        if (v != v) continue;  // NaN never enters the top-k
-        const unsigned long long key = argmax_key(v, i);
-        if (cnt == k && key <= mine[k - 1]) continue;
-        int j = cnt < k ? cnt++ : k - 1;
-        while (j > 0 && mine[j - 1] < key) { mine[j] = mine[j - 1]; --j; }
-        mine[j] = key;
-    }
-    int head = 0;
-    for (int r = 0; r < k; ++r) {
-        unsigned long long cand = head < cnt ? mine[head] : 0ull;
-        int who = t;
-#pragma unroll
-        for (int o = 16; o >= 1; o >>= 1) {
-            const unsigned long long oc = __shfl_xor_sync(0xffffffffu, cand, o);
-            const int ow = __shfl_xor_sync(0xffffffffu, who, o);
-            if (oc > cand || (oc == cand && ow < who)) { cand = oc; who = ow; }
-        }
-        if ((t & 31) == 0) { red[t >> 5] = cand; redw[t >> 5] = who; }
-        __syncthreads();
-        unsigned long long best = red[0];
-        int bw = redw[0];
-#pragma unroll
-        for (int w = 1; w < kTopkThreads / 32; ++w)
-            if (red[w] > best) { best = red[w]; bw = redw[w]; }
-        if (t == bw && best != 0ull) ++head;
-        if (t == 0) {
-            if (best == 0ull) {
-                vals[(long long)row * k + r] = -INFINITY;
-                idx[(long long)row * k + r] = -1;
-            } else {
-                const unsigned int hi = (unsigned int)(best >> 32);
-                const unsigned int b = (hi & 0x80000000u) ? (hi & 0x7FFFFFFFu) : ~hi;
-                vals[(long long)row * k + r] = __uint_as_float(b);
-                idx[(long long)row * k + r] = (int32_t)(0xFFFFFFFFu - (unsigned int)(best & 0xFFFFFFFFull));
-            }
-        }
-        __syncthreads();
-    }
-}
-
 // -------------------------------------------------------------------- embed
 // AexisEmbedValue (HLSL BufferTensor:37-62) for every (word, p).
 template <typename ST>
@@ -402,17 +346,6 @@ cudaError_t launch_argmax_keys(const float* logits, int rows, int width, int ld,
     if (bx > cap) bx = cap;
     if (bx < 1) bx = 1;
     argmax_partial_kernel<<<dim3(bx, rows), kT, 0, s>>>(logits, width, ld, keys, offset);
-    return cudaGetLastError();
-}
-
-cudaError_t launch_topk(const float* logits, int rows, int width, int ld, int k, float* vals, int32_t* idx,
-                        cudaStream_t s) {
-    const size_t smem = (size_t)kTopkThreads * k * sizeof(unsigned long long);
-    if (smem > 48 * 1024) {
-        cudaError_t e = cudaFuncSetAttribute(topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (e != cudaSuccess) return e;
-    }
-    topk_kernel<<<rows, kTopkThreads, smem, s>>>(logits, width, ld, k, vals, idx);
     return cudaGetLastError();
 }
 

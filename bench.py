@@ -519,7 +519,8 @@ def run_only(args):
     """Single-kernel / single-path modes for profiling (not the bench contract):
     --only dominant   W + K launches of the (1024, 151936) Q4 GEMV, rotating
                       over copies larger than L2, no graphs
-    --only decoder    the config-3 decoder with --prompt-len / --new-tokens"""
+    --only decoder    the config-3 decoder with --prompt-len / --new-tokens
+    --only tcgemm     the config-5 lm_head GEMM alone (M=256, tensor cores)"""
     import torch
     torch.cuda.set_device(0)
     from aiimage_b200.ops import AexisOps
@@ -527,6 +528,23 @@ def run_only(args):
     peak, _ = measured_peak()
     if args.only == "decoder":
         out = bench_decoder(ops, peak, args.prompt_len, args.new_tokens)
+    elif args.only == "tcgemm":
+        vocab, hidden, m = 151936, 1024, 256
+        p, s = synth.q8_weights(vocab, hidden, seed=5, tag=(vocab, hidden))
+        w = ops.new_int8_weight_only_upload(p, s, vocab, hidden)
+        x = torch.from_numpy(synth.activations(hidden, seed=5, tag=(m, hidden), m=m)).cuda()
+        y = torch.empty((m, vocab), dtype=torch.float32, device="cuda")
+        ops.set_int8_gemm_weights(w)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        for i in range(args.warmup + args.steps):
+            if i == args.warmup:
+                e0.record()
+            ops.gemm2d_pack4_tiled_texture_a(x, None, m, vocab, hidden, True, 1.0, 1.0, False, 4, y)
+        e1.record()
+        e1.synchronize()
+        t = e0.elapsed_time(e1) / 1e3 / max(1, args.steps)
+        out = {"kernel": "gemm_q8_tc 256x151936x1024", "us": round(t * 1e6, 2),
+               "TFLOP/s": round(2.0 * m * vocab * hidden / t / 1e12, 1)}
     else:
         k, n = SWEEP[DOMINANT]
         p, s = synth.q4_weights(n, k, GROUP, 1, tag=(k, n))
@@ -596,7 +614,7 @@ def main():
     ap.add_argument("--skip-cpu", action="store_true", help="omit the CPU oracle baseline")
     ap.add_argument("--skip-config5", action="store_true", help="omit the config-5 lm_head measurement")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
-    ap.add_argument("--only", choices=["dominant", "decoder"], help="profiling mode (see run_only)")
+    ap.add_argument("--only", choices=["dominant", "decoder", "tcgemm"], help="profiling mode (see run_only)")
     ap.add_argument("--prompt-len", type=int, default=512)
     ap.add_argument("--new-tokens", type=int, default=64)
     args = ap.parse_args()

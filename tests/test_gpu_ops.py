@@ -165,15 +165,36 @@ def test_argmax_known_answers_and_ties(ops, oracle):
 def test_topk(ops, oracle):
     import torch
     r = np.random.default_rng(10)
-    x = r.standard_normal((3, 20000)).astype(np.float32)
-    x[0, 50:60] = 9.0  # ties ordered by index
+    x = r.standard_normal((5, 20000)).astype(np.float32)
+    x[0, 50:60] = 9.0     # ties ordered by index
+    x[1, :] = 1.0         # one plateau far larger than the candidate buffer
+    x[2, ::2] = -0.0      # signed zeros count as equal
+    x[3, 7000:] = 3.0     # a plateau of 13000 ranked after nothing
+    x[4] *= 1e-30         # tiny values (one exponent bin)
     k = 50
-    vals = torch.zeros((3, k), dtype=torch.float32, device="cuda")
-    idx = torch.zeros((3, k), dtype=torch.int32, device="cuda")
-    ops.top_k(cuda(x), 20000, 3, k, vals, idx)
+    vals = torch.zeros((5, k), dtype=torch.float32, device="cuda")
+    idx = torch.zeros((5, k), dtype=torch.int32, device="cuda")
+    ops.top_k(cuda(x), 20000, 5, k, vals, idx)
     rv, ri = oracle.topk(x, k)
     assert np.array_equal(host(idx), ri)
     assert np.array_equal(host(vals), rv)
+    # Fewer values than k: the rest is padded with (-inf, -1).
+    small = r.standard_normal((2, 30)).astype(np.float32)
+    ops.top_k(cuda(small), 30, 2, k, vals[:2], idx[:2], ld=30)
+    sv, si = oracle.topk(small, 30)
+    assert np.array_equal(host(idx)[:2, :30], si) and np.all(host(idx)[:2, 30:] == -1)
+    assert np.all(np.isneginf(host(vals)[:2, 30:]))
+
+
+def test_topk_config5_shape(ops, oracle):
+    """256 rows x 151936 logits, k = 50 (the config-5 sampler input)."""
+    import torch
+    x = np.random.default_rng(11).standard_normal((256, 151936)).astype(np.float32)
+    vals = torch.zeros((256, 50), dtype=torch.float32, device="cuda")
+    idx = torch.zeros((256, 50), dtype=torch.int32, device="cuda")
+    ops.top_k(cuda(x), 151936, 256, 50, vals, idx)
+    rv, ri = oracle.topk(x, 50)
+    assert np.array_equal(host(idx), ri)
 
 
 @pytest.mark.parametrize("kind", ["q4", "q8", "f16", "f32"])
