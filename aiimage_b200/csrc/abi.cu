@@ -315,7 +315,7 @@ static int gemm_common(aexis_ctx* ctx, const void* a, int a_dtype, int lda, int 
     int rc = bind(ctx);
     if (rc) return rc;
     // Batched Q8: one pass over the weights on the tensor cores.
-    if (m >= kTcMinRows && gemm_tc_supported(w, m, a_dtype) && (a_dtype == AEXIS_F16 || y_dtype == AEXIS_F32)) {
+    if (m >= kTcMinRows && gemm_tc_supported(w, m, a_dtype)) {
         aexis_weights* wm = const_cast<aexis_weights*>(w);
         if (!wm->tc_tiled) {
             cudaError_t e = cudaMalloc(&wm->tc_tiled, gemm_tc_tiled_bytes(w));

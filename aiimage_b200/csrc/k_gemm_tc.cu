@@ -18,36 +18,76 @@
 //     1024 bytes). fp32 activations are split into fp16 hi and lo rows
 //     (x = hi + lo to about 22 bits) that ride in the same MMA as extra
 //     columns, so fp32 inputs keep fp32-class accuracy.
-// Per CTA (persistent, one per SM): a 256-row weight tile (two M=128 MMAs
-// sharing the activation tile) over all K. Warp roles: 0 bulk-copy producer,
-// 1 MMA issuer and TMEM owner, 2-5 dequantise int8 -> fp16 into the swizzled
-// A tiles and run the epilogue from TMEM. Every barrier wait is bounded.
+// Per CTA (persistent, one per SM): a contiguous range of 128-row slabs, two
+// slabs per accumulator tile (two M=128 MMAs sharing the activation tile),
+// each over all K. Three shared-memory rings decouple the latencies: int8
+// weights (up to 8 k-blocks deep, freed as soon as they are dequantised),
+// fp16 A tiles (2 deep, freed by the MMA commit) and activations (3-4 deep,
+// freed by the MMA commit). Warp roles: 0 int8 bulk-copy producer, 1 MMA
+// issuer and TMEM owner, 2-5 dequantise int8 -> fp16 into the swizzled A
+// tiles and run the epilogue from TMEM, 6 activation bulk-copy producer.
+// Every barrier wait is bounded.
 #include "gemv_dev.cuh"
 
 namespace {
 
 using namespace aexis_dev;
 
-constexpr int kTcThreads = 192;          // 6 warps
-constexpr int kTM = 128;                 // rows per MMA (M)
-constexpr int kTile = 256;               // weight rows per CTA tile (two MMAs)
+constexpr int kTcThreads = 224;          // 7 warps
+constexpr int kTM = 128;                 // rows per MMA (M) = rows per slab
+constexpr int kTile = 256;               // at most two slabs per accumulator tile
 constexpr int kKB = 64;                  // K per stage (one 128-byte swizzle atom of fp16)
-constexpr int kStages = 2;
+constexpr int kSlabBytes = kTM * kKB;    // int8 bytes of one slab k-block (8 KB)
+constexpr int kATileBytes = kTM * 128;   // fp16 bytes of one slab k-block (16 KB)
+constexpr int kADepth = 2;               // fp16 A ring
+constexpr int kMaxDepth = 8;             // int8 and activation rings
+constexpr int kSmemBudget = 227 * 1024;
 
 struct TcParams {
     const uint8_t* wt;        // tiled int8 weights
     const void* scales;       // per row
     int scale_f16;
     const uint8_t* xt;        // prepared activations [K/64][nb][128 B]
-    int n, k, m, nb, split;   // nb = MMA N (rows of xt), split: hi rows [0,m), lo rows [m,2m)
-    int n_tiles;              // ceil(n / 256)
+    int n, k, m, nb, split;   // nb = MMA N (rows of xt), split: hi rows [0,m), lo rows [nb/2, nb/2+m)
+    int n_slabs;              // ceil(n / 128)
+    int raw_depth, b_depth;   // ring depths (int8 weights, activations)
     const float* bias;
     float alpha, beta;
     void* y;
     int y_f16, ldy;
     int tiled;                // 1: beta*bias + alpha*acc (lm_head form)
+    int bulk_out;             // y and its row stride 16-byte aligned: staged row stores
     int* status;
 };
+
+// Shared-memory carve-up (offsets from a 1024-aligned base): the fp16 A ring
+// (kADepth x two slabs), the activation ring, the int8 ring, the barriers.
+struct TcLayout {
+    int b_bytes, b_stage, a_off, b_off, raw_off, bar_off, total;
+};
+
+__host__ __device__ inline TcLayout tc_layout(int nb, int raw_depth, int b_depth) {
+    TcLayout L;
+    L.b_bytes = nb * 128;
+    L.b_stage = (L.b_bytes + 1023) & ~1023;
+    L.a_off = 0;
+    L.b_off = kADepth * 2 * kATileBytes;
+    L.raw_off = L.b_off + b_depth * L.b_stage;
+    L.bar_off = L.raw_off + raw_depth * 2 * kSlabBytes;
+    L.total = L.bar_off + 512;
+    return L;
+}
+
+// Ring depths for MMA width nb: activations 3 deep at nb >= 192, else 4; the
+// int8 ring takes what is left, up to 8. False when fewer than 2 fit.
+bool tc_depths(int nb, int& raw_depth, int& b_depth) {
+    const int b_stage = (nb * 128 + 1023) & ~1023;
+    b_depth = nb >= 192 ? 3 : 4;
+    const int avail = kSmemBudget - 1024 - 512 - kADepth * 2 * kATileBytes - b_depth * b_stage;
+    raw_depth = avail / (2 * kSlabBytes);
+    if (raw_depth > kMaxDepth) raw_depth = kMaxDepth;
+    return raw_depth >= 2;
+}
 
 __device__ __forceinline__ uint64_t sw128_desc(uint32_t smem_addr) {
     // K-major, 128-byte swizzle: 8-row atoms 1024 bytes apart (SBO), LBO 1,
@@ -86,17 +126,17 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
-    uint32_t r[16];
+// 16 consecutive TMEM columns of this thread's lane; complete after tmem_wait().
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t* r) {
     asm volatile(
         "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
         : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
           "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
         : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
+
+__device__ __forceinline__ void tmem_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
 
 // int8 x4 (one word) -> two fp16x2 of the exact values: bytes biased by 128
 // (XOR) and placed under the fp16 exponent of 1024 with PRMT, then 1024+128
@@ -114,35 +154,52 @@ __device__ __forceinline__ void i8x4_to_h2x2(uint32_t v, uint32_t& lo, uint32_t&
 
 __global__ void __launch_bounds__(kTcThreads, 1) gemm_q8_tc_kernel(TcParams p) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
-    // 1024-aligned carve-up: per stage int8 [256][64], A fp16 2 x [128 x 64], B [nb x 64] fp16.
     uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    const int b_bytes = p.nb * 128;
-    const int stage_bytes = kTile * kKB + 2 * kTM * 128 + ((b_bytes + 1023) & ~1023);
-    uint64_t* bars = reinterpret_cast<uint64_t*>(base + kStages * stage_bytes);
-    uint64_t* full = bars;                   // producer tx
-    uint64_t* a_ready = bars + kStages;      // 4 dequant warps
-    uint64_t* empty = bars + 2 * kStages;    // MMA commit
-    uint64_t* acc_full = bars + 3 * kStages; // MMA commit after a tile
-    uint64_t* acc_empty = acc_full + 1;      // 4 epilogue warps
-    uint64_t* drain = acc_empty + 1;         // final MMA commit before TMEM is freed
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+    const TcLayout L = tc_layout(p.nb, p.raw_depth, p.b_depth);
+    const int RD = p.raw_depth, BD = p.b_depth;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(base + L.bar_off);
+    uint64_t* raw_full = bars;                    // int8 producer tx
+    uint64_t* raw_empty = bars + kMaxDepth;       // 4 dequant warps
+    uint64_t* b_full = bars + 2 * kMaxDepth;      // activation producer tx
+    uint64_t* b_empty = bars + 3 * kMaxDepth;     // MMA commit
+    uint64_t* a_ready = bars + 4 * kMaxDepth;     // 4 dequant warps
+    uint64_t* a_empty = a_ready + kADepth;        // MMA commit
+    uint64_t* acc_full = a_empty + kADepth;       // MMA commit after a tile
+    uint64_t* acc_empty = acc_full + 1;           // 4 epilogue warps
+    uint64_t* drain = acc_empty + 1;              // final MMA commit before TMEM is freed
+    uint64_t* stg_full = drain + 1;               // 4 epilogue staging buffers: 128 writers
+    uint64_t* stg_free = stg_full + 4;            // 128 readers done with the buffer
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(stg_free + 4);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nkb = p.k / kKB;
-    const int my_tiles = (int)blockIdx.x < p.n_tiles ? (p.n_tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+    // A contiguous range of 128-row slabs per CTA (counts differ by at most
+    // one), taken two slabs per accumulator tile.
+    const int s_lo = (int)((long long)blockIdx.x * p.n_slabs / gridDim.x);
+    const int s_hi = (int)((long long)(blockIdx.x + 1) * p.n_slabs / gridDim.x);
+    const int my_tiles = (s_hi - s_lo + 1) / 2;
     const uint32_t tmem_cols = (uint32_t)(2 * p.nb <= 32 ? 32 : (2 * p.nb <= 64 ? 64 : (2 * p.nb <= 128 ? 128 :
                                           (2 * p.nb <= 256 ? 256 : 512))));
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kStages; ++s) {
-            mbar_init(full + s, 1);
+        for (int s = 0; s < kMaxDepth; ++s) {
+            mbar_init(raw_full + s, 1);
+            mbar_init(raw_empty + s, 4);
+            mbar_init(b_full + s, 1);
+            mbar_init(b_empty + s, 1);
+        }
+        for (int s = 0; s < kADepth; ++s) {
             mbar_init(a_ready + s, 4);
-            mbar_init(empty + s, 1);
+            mbar_init(a_empty + s, 1);
         }
         mbar_init(acc_full, 1);
         mbar_init(acc_empty, 4);
         mbar_init(drain, 1);
+        for (int s = 0; s < 4; ++s) {
+            mbar_init(stg_full + s, 128);
+            mbar_init(stg_free + s, 128);
+        }
         *abort_flag = 0;
         fence_barrier_init();
     }
@@ -159,35 +216,53 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_q8_tc_kernel(TcParams p) {
     griddep_wait();
 
     if (warp == 0) {
-        // ----------------------------------------------------------- producer
+        // ------------------------------------------------- int8 weight producer
         if (lane == 0) {
             const uint64_t pol = policy_evict_first();
             int it = 0, issued = 0;
             for (int t = 0; t < my_tiles && !*abort_flag; ++t) {
-                const int tile = (int)blockIdx.x + t * (int)gridDim.x;
+                const int slab0 = s_lo + 2 * t;
+                const int ns = s_hi - slab0 < 2 ? 1 : 2;
                 for (int kb = 0; kb < nkb; ++kb, ++it) {
-                    const int s = it % kStages;
-                    if (it >= kStages && !mbar_wait(empty + s, ((it / kStages) & 1) ^ 1)) {
+                    const int s = it % RD;
+                    if (it >= RD && !mbar_wait(raw_empty + s, ((it / RD) & 1) ^ 1)) {
                         report_timeout(p.status);
                         *abort_flag = 1;
                         break;
                     }
-                    uint8_t* st = base + (size_t)s * stage_bytes;
-                    const uint32_t slab = (uint32_t)kTM * kKB;  // 8 KB
-                    mbar_arrive_expect_tx(full + s, 2 * slab + (uint32_t)b_bytes);
-                    for (int j = 0; j < 2; ++j) {
-                        const size_t sub = (size_t)tile * 2 + j;  // 128-row slab index
-                        bulk_g2s(st + j * slab, p.wt + (sub * nkb + kb) * slab, slab, full + s, pol);
-                    }
-                    bulk_g2s_plain(st + kTile * kKB + 2 * kTM * 128, p.xt + (size_t)kb * b_bytes,
-                                   (uint32_t)b_bytes, full + s);
+                    if (*abort_flag) break;
+                    uint8_t* st = base + L.raw_off + s * 2 * kSlabBytes;
+                    mbar_arrive_expect_tx(raw_full + s, (uint32_t)(ns * kSlabBytes));
+                    for (int j = 0; j < ns; ++j)
+                        bulk_g2s(st + j * kSlabBytes, p.wt + ((size_t)(slab0 + j) * nkb + kb) * kSlabBytes,
+                                 (uint32_t)kSlabBytes, raw_full + s, pol);
                     issued = it + 1;
                 }
             }
             // No bulk copy may still be landing when the CTA exits (the
             // consumers wait for every stage on the normal path).
-            for (int i = issued - kStages < 0 ? 0 : issued - kStages; i < issued; ++i)
-                if (!mbar_wait(full + i % kStages, (i / kStages) & 1)) { report_timeout(p.status); break; }
+            for (int i = issued - RD < 0 ? 0 : issued - RD; i < issued; ++i)
+                if (!mbar_wait(raw_full + i % RD, (i / RD) & 1)) { report_timeout(p.status); break; }
+        }
+    } else if (warp == 6) {
+        // ---------------------------------------------- activation producer
+        if (lane == 0) {
+            const int total = my_tiles * nkb;
+            int issued = 0;
+            for (int it = 0; it < total && !*abort_flag; ++it) {
+                const int s = it % BD;
+                if (it >= BD && !mbar_wait(b_empty + s, ((it / BD) & 1) ^ 1)) {
+                    report_timeout(p.status);
+                    *abort_flag = 1;
+                    break;
+                }
+                mbar_arrive_expect_tx(b_full + s, (uint32_t)L.b_bytes);
+                bulk_g2s_plain(base + L.b_off + s * L.b_stage, p.xt + (size_t)(it % nkb) * L.b_bytes,
+                               (uint32_t)L.b_bytes, b_full + s);
+                issued = it + 1;
+            }
+            for (int i = issued - BD < 0 ? 0 : issued - BD; i < issued; ++i)
+                if (!mbar_wait(b_full + i % BD, (i / BD) & 1)) { report_timeout(p.status); break; }
         }
     } else if (warp == 1) {
         // ---------------------------------------------------------- MMA issuer
@@ -195,6 +270,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_q8_tc_kernel(TcParams p) {
             const uint32_t idesc = idesc_f16_f32(kTM, p.nb);
             int it = 0;
             for (int t = 0; t < my_tiles && !*abort_flag; ++t) {
+                const int ns = s_hi - (s_lo + 2 * t) < 2 ? 1 : 2;
                 if (t > 0 && !mbar_wait(acc_empty, (t - 1) & 1)) {
                     report_timeout(p.status);
                     *abort_flag = 1;
@@ -202,23 +278,26 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_q8_tc_kernel(TcParams p) {
                 }
                 tc_fence_after();
                 for (int kb = 0; kb < nkb; ++kb, ++it) {
-                    const int s = it % kStages;
-                    if (!mbar_wait(a_ready + s, (it / kStages) & 1)) {
+                    const int sa = it % kADepth, sb = it % BD;
+                    if (!mbar_wait(a_ready + sa, (it / kADepth) & 1) || !mbar_wait(b_full + sb, (it / BD) & 1)) {
                         report_timeout(p.status);
                         *abort_flag = 1;
                         break;
                     }
                     tc_fence_after();
-                    uint8_t* st = base + (size_t)s * stage_bytes;
-                    const uint32_t a0 = smem_u32(st + kTile * kKB);
-                    const uint32_t b0 = smem_u32(st + kTile * kKB + 2 * kTM * 128);
+                    const uint32_t a0 = smem_u32(base + L.a_off + sa * 2 * kATileBytes);
+                    const uint32_t b0 = smem_u32(base + L.b_off + sb * L.b_stage);
 #pragma unroll
-                    for (int j = 0; j < 2; ++j)
+                    for (int j = 0; j < 2; ++j) {
+                        if (j < ns) {
 #pragma unroll
-                        for (int kk = 0; kk < kKB / 16; ++kk)
-                            mma_f16(tmem + (uint32_t)(j * p.nb), sw128_desc(a0 + j * kTM * 128 + kk * 32),
-                                    sw128_desc(b0 + kk * 32), idesc, (kb > 0 || kk > 0) ? 1 : 0);
-                    mma_commit(empty + s);
+                            for (int kk = 0; kk < kKB / 16; ++kk)
+                                mma_f16(tmem + (uint32_t)(j * p.nb), sw128_desc(a0 + j * kATileBytes + kk * 32),
+                                        sw128_desc(b0 + kk * 32), idesc, (kb > 0 || kk > 0) ? 1 : 0);
+                        }
+                    }
+                    mma_commit(a_empty + sa);
+                    mma_commit(b_empty + sb);
                 }
                 if (*abort_flag) break;
                 mma_commit(acc_full);
@@ -233,21 +312,24 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_q8_tc_kernel(TcParams p) {
         const int dt = dw * 32 + lane;        // 0..127
         const int quad = warp & 3;            // TMEM lane quadrant this warp may access
         int it = 0;
+        int chunk = 0;                        // staged epilogue chunks so far (all tiles)
         for (int t = 0; t < my_tiles && !*abort_flag; ++t) {
-            const int tile = (int)blockIdx.x + t * (int)gridDim.x;
+            const int slab0 = s_lo + 2 * t;
+            const int ns = s_hi - slab0 < 2 ? 1 : 2;
             for (int kb = 0; kb < nkb; ++kb, ++it) {
-                const int s = it % kStages;
-                if (!mbar_wait(full + s, (it / kStages) & 1)) {
+                const int sr = it % RD, sa = it % kADepth;
+                if (!mbar_wait(raw_full + sr, (it / RD) & 1) ||
+                    (it >= kADepth && !mbar_wait(a_empty + sa, ((it / kADepth) & 1) ^ 1))) {
                     report_timeout(p.status);
                     *abort_flag = 1;
                     break;
                 }
-                uint8_t* st = base + (size_t)s * stage_bytes;
-                uint8_t* a_t = st + kTile * kKB;
+                const uint8_t* st = base + L.raw_off + sr * 2 * kSlabBytes;
+                uint8_t* a_t = base + L.a_off + sa * 2 * kATileBytes;
                 // Thread dt converts 16 int8 (chunk dt & 3 of row dt >> 2) of
                 // each 32-row group: conflict-free reads and swizzled writes.
 #pragma unroll 2
-                for (int g = 0; g < kTile / 32; ++g) {
+                for (int g = 0; g < ns * (kTM / 32); ++g) {
                     const int row = g * 32 + (dt >> 2);          // 0..255
                     const int ch = dt & 3;                       // 16-byte chunk of the 64 int8
                     const uint4 q = *reinterpret_cast<const uint4*>(st + row * kKB + ch * 16);
@@ -264,52 +346,124 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_q8_tc_kernel(TcParams p) {
                 }
                 fence_proxy_async_smem();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(a_ready + s);
+                if (lane == 0) {
+                    mbar_arrive(raw_empty + sr);
+                    mbar_arrive(a_ready + sa);
+                }
             }
             if (*abort_flag) break;
             // Epilogue: wait for the tile's accumulators, then each thread owns
-            // one weight row (TMEM lane) of each 128-row half.
+            // one weight row (TMEM lane) of each 128-row slab.
             if (!mbar_wait(acc_full, t & 1)) {
                 report_timeout(p.status);
                 *abort_flag = 1;
                 break;
             }
             tc_fence_after();
-            for (int j = 0; j < 2; ++j) {
-                const int n = tile * kTile + j * kTM + quad * 32 + lane;
+            // Column b < m of the accumulator is output row b; with split
+            // activations its lo part sits in column hi_cols + b, so both
+            // halves of a chunk load side by side and nothing is re-read.
+            const int mrows = p.m;
+            const int hi_cols = p.split ? p.nb >> 1 : p.nb;
+            const size_t ldy = (size_t)p.ldy;
+            const int esz = p.y_f16 ? 2 : 4;
+            for (int j = 0; j < ns; ++j) {
+                const int slab = slab0 + j;
+                const int n = slab * kTM + quad * 32 + lane;
+                const bool nvalid = n < p.n;
                 float sc = 0.0f, bb = 0.0f;
-                if (n < p.n) {
+                if (nvalid) {
                     sc = p.scale_f16 ? __half2float(reinterpret_cast<const __half*>(p.scales)[n])
                                      : reinterpret_cast<const float*>(p.scales)[n];
                     bb = p.bias ? p.beta * p.bias[n] : 0.0f;
                 }
                 const uint32_t lane_addr = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(j * p.nb);
-                const int mrows = p.m;
-                for (int c0 = 0; c0 < p.nb; c0 += 16) {
-                    float v[16];
-                    tmem_ld16(lane_addr + (uint32_t)c0, v);
+                const int cnt = p.n - slab * kTM < kTM ? p.n - slab * kTM : kTM;  // valid outputs of the slab
+                if (p.bulk_out && ((cnt * esz) & 15) == 0) {
+                    // Staged path: 32 output rows at a time are transposed
+                    // through shared memory (the idle fp16 A ring: the tile's
+                    // MMAs have retired and the next tile's dequantisation
+                    // has not started), then each warp writes whole 128-output
+                    // row segments with 16-byte (8-byte for fp16) stores: a
+                    // quarter of the store instructions of the lane-per-output
+                    // layout TMEM delivers. Four 16 KB buffers rotate.
+                    for (int c0 = 0; c0 < mrows && !*abort_flag; c0 += 32, ++chunk) {
+                        const int nrows = mrows - c0 < 32 ? mrows - c0 : 32;
+                        const int buf = chunk & 3;
+                        const uint32_t use = (uint32_t)(chunk >> 2);
+                        if (chunk >= 4 && !mbar_wait(stg_free + buf, (use - 1) & 1)) {
+                            report_timeout(p.status);
+                            *abort_flag = 1;
+                            break;
+                        }
+                        uint32_t r[32], q[32];
+                        tmem_ld16(lane_addr + (uint32_t)c0, r);
+                        if (nrows > 16) tmem_ld16(lane_addr + (uint32_t)(c0 + 16), r + 16);
+                        if (p.split) {
+                            tmem_ld16(lane_addr + (uint32_t)(hi_cols + c0), q);
+                            if (nrows > 16) tmem_ld16(lane_addr + (uint32_t)(hi_cols + c0 + 16), q + 16);
+                        }
+                        tmem_wait();
+                        float* stg = reinterpret_cast<float*>(base + L.a_off + buf * (32 * kTM * 4));
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) {
+                            float acc = __uint_as_float(r[i]);
+                            if (p.split) acc += __uint_as_float(q[i]);
+                            const float out = p.tiled ? bb + p.alpha * (acc * sc) : p.alpha * (bb + acc * sc);
+                            if (i < nrows) stg[i * kTM + quad * 32 + lane] = out;
+                        }
+                        mbar_arrive(stg_full + buf);
+                        if (!mbar_wait(stg_full + buf, use & 1)) {
+                            report_timeout(p.status);
+                            *abort_flag = 1;
+                            break;
+                        }
+                        // Warp dw writes rows dw, dw + 4, ...: lane covers outputs 4 lane .. 4 lane + 3.
+                        for (int i = dw; i < nrows; i += 4) {
+                            const float4 v = *reinterpret_cast<const float4*>(stg + i * kTM + lane * 4);
+                            if (lane * 4 < cnt) {
+                                const size_t off = (size_t)(c0 + i) * ldy + (size_t)slab * kTM + lane * 4;
+                                if (p.y_f16) {
+                                    const __half2 h0 = __floats2half2_rn(v.x, v.y), h1 = __floats2half2_rn(v.z, v.w);
+                                    uint2 u;
+                                    u.x = *reinterpret_cast<const uint32_t*>(&h0);
+                                    u.y = *reinterpret_cast<const uint32_t*>(&h1);
+                                    *reinterpret_cast<uint2*>(reinterpret_cast<__half*>(p.y) + off) = u;
+                                } else {
+                                    *reinterpret_cast<float4*>(reinterpret_cast<float*>(p.y) + off) = v;
+                                }
+                            }
+                        }
+                        mbar_arrive(stg_free + buf);
+                    }
+                    continue;
+                }
+                float* yf = reinterpret_cast<float*>(p.y) + n;
+                __half* yh = reinterpret_cast<__half*>(p.y) + n;
+                for (int c0 = 0; c0 < mrows; c0 += 16) {
+                    uint32_t r[16], q[16];
+                    tmem_ld16(lane_addr + (uint32_t)c0, r);
+                    if (p.split) tmem_ld16(lane_addr + (uint32_t)(hi_cols + c0), q);
+                    tmem_wait();
+                    if (!nvalid) continue;
+                    const int lim = mrows - c0;
 #pragma unroll
                     for (int i = 0; i < 16; ++i) {
-                        const int b = c0 + i;
-                        if (n >= p.n) continue;
-                        if (!p.split) {
-                            if (b < mrows) {
-                                const float out = p.tiled ? bb + p.alpha * (v[i] * sc) : p.alpha * (bb + v[i] * sc);
-                                if (p.y_f16) reinterpret_cast<__half*>(p.y)[(size_t)b * p.ldy + n] = __float2half_rn(out);
-                                else reinterpret_cast<float*>(p.y)[(size_t)b * p.ldy + n] = out;
-                            }
-                        } else if (b < mrows) {
-                            // hi part: stored now, lo part added when its column arrives.
-                            reinterpret_cast<float*>(p.y)[(size_t)b * p.ldy + n] = v[i];
-                        } else if (b < 2 * mrows) {
-                            const int bh = b - mrows;
-                            float* yp = reinterpret_cast<float*>(p.y) + (size_t)bh * p.ldy + n;
-                            const float acc = (*yp + v[i]) * sc;
-                            const float out = p.tiled ? bb + p.alpha * acc : p.alpha * (bb + acc);
-                            *yp = out;
+                        float acc = __uint_as_float(r[i]);
+                        if (p.split) acc += __uint_as_float(q[i]);
+                        const float out = p.tiled ? bb + p.alpha * (acc * sc) : p.alpha * (bb + acc * sc);
+                        if (i < lim) {
+                            if (p.y_f16) yh[(size_t)(c0 + i) * ldy] = __float2half_rn(out);
+                            else yf[(size_t)(c0 + i) * ldy] = out;
                         }
                     }
                 }
+            }
+            // The staging buffers alias the A ring: every copy must have read
+            // them before this tile's dequantisation of the next one starts.
+            if (chunk > 0 && !mbar_wait(stg_free + ((chunk - 1) & 3), (uint32_t)((chunk - 1) >> 2) & 1)) {
+                report_timeout(p.status);
+                *abort_flag = 1;
             }
             tc_fence_before();
             __syncwarp();
@@ -326,7 +480,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_q8_tc_kernel(TcParams p) {
 }
 
 // x [m][lda] (fp16 or fp32) -> xt [K/64][nb][64] fp16, 128-byte swizzled rows.
-// fp32 rows are split: hi = fp16(x) in row b, lo = fp16(x - hi) in row m + b.
+// fp32 rows are split: hi = fp16(x) in row b, lo = fp16(x - hi) in row
+// nb/2 + b (nb/2 = m rounded up to 16); padding rows are zero.
 __global__ void prep_x_kernel(const void* x, int a_f16, int lda, int m, int k, int nb, int split, uint8_t* xt) {
     const long long total = (long long)(k / kKB) * nb * 8;  // 16-byte chunks
     for (long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x; t < total;
@@ -335,8 +490,9 @@ __global__ void prep_x_kernel(const void* x, int a_f16, int lda, int m, int k, i
         const int row = (int)((t >> 3) % nb);
         const int kb = (int)(t / (8LL * nb));
         __half h[8];
-        const int src = split && row >= m ? row - m : row;
-        const bool lo = split && row >= m;
+        const int half = nb >> 1;
+        const int src = split && row >= half ? row - half : row;
+        const bool lo = split && row >= half;
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
             const int kk = kb * kKB + c * 8 + e;
@@ -372,17 +528,23 @@ __global__ void repack_q8_kernel(const uint8_t* src, int n, int k, uint8_t* dst)
 
 }  // namespace
 
+// MMA width (rows of the prepared activations): m rounded up to 16, twice
+// that for split fp32 activations.
+int tc_width(int m, int a_dtype) {
+    const int mp = (m + 15) / 16 * 16;
+    return a_dtype == AEXIS_F32 ? 2 * mp : mp;
+}
+
 size_t gemm_tc_smem_bytes(int nb) {
-    const int b_bytes = nb * 128;
-    const int stage = kTile * kKB + 2 * kTM * 128 + ((b_bytes + 1023) & ~1023);
-    return 1024 + (size_t)kStages * stage + 256;  // alignment slack + barriers
+    int rd = 0, bd = 0;
+    if (!tc_depths(nb, rd, bd)) return (size_t)1 << 30;
+    return 1024 + (size_t)tc_layout(nb, rd, bd).total;  // + alignment slack
 }
 
 bool gemm_tc_supported(const aexis_weights* w, int m, int a_dtype) {
     if (w->kind != WK_Q8 || w->k % kKB != 0 || m < 1) return false;
-    const int rows = a_dtype == AEXIS_F32 ? 2 * m : m;
-    const int nb = (rows + 15) / 16 * 16;
-    return nb <= 256 && gemm_tc_smem_bytes(nb) <= 227 * 1024;
+    const int nb = tc_width(m, a_dtype);
+    return nb <= 256 && gemm_tc_smem_bytes(nb) <= (size_t)kSmemBudget;
 }
 
 size_t gemm_tc_tiled_bytes(const aexis_weights* w) {
@@ -396,23 +558,20 @@ cudaError_t launch_repack_q8(const aexis_weights* w, void* tiled, cudaStream_t s
 }
 
 size_t gemm_tc_xt_bytes(int m, int k, int a_dtype) {
-    const int rows = a_dtype == AEXIS_F32 ? 2 * m : m;
-    const int nb = (rows + 15) / 16 * 16;
-    return (size_t)k * nb * 2;
+    return (size_t)k * tc_width(m, a_dtype) * 2;
 }
 
 cudaError_t launch_gemm_tc(const aexis_weights* w, const void* tiled, const void* x, int a_dtype, int lda, int m,
                            void* xt, const float* bias, float alpha, float beta, void* y, int y_dtype, int ldy,
                            int tiled_epi, int sm_count, int* status, cudaStream_t s) {
     const int split = a_dtype == AEXIS_F32;
-    const int nb = ((split ? 2 * m : m) + 15) / 16 * 16;
+    const int nb = tc_width(m, a_dtype);
     const long long chunks = (long long)(w->k / kKB) * nb * 8;
     int pb = (int)((chunks + 255) / 256);
     pb = pb > 148 * 8 ? 148 * 8 : (pb < 1 ? 1 : pb);
     prep_x_kernel<<<pb, 256, 0, s>>>(x, a_dtype == AEXIS_F16, lda, m, w->k, nb, split, reinterpret_cast<uint8_t*>(xt));
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
-    if (split && y_dtype != AEXIS_F32) return cudaErrorNotSupported;  // hi is staged in y
     TcParams p = {};
     p.wt = reinterpret_cast<const uint8_t*>(tiled);
     p.scales = w->scales;
@@ -423,7 +582,8 @@ cudaError_t launch_gemm_tc(const aexis_weights* w, const void* tiled, const void
     p.m = m;
     p.nb = nb;
     p.split = split;
-    p.n_tiles = (w->n + kTile - 1) / kTile;
+    p.n_slabs = (w->n + kTM - 1) / kTM;
+    if (!tc_depths(nb, p.raw_depth, p.b_depth)) return cudaErrorNotSupported;
     p.bias = bias;
     p.alpha = alpha;
     p.beta = beta;
@@ -431,6 +591,8 @@ cudaError_t launch_gemm_tc(const aexis_weights* w, const void* tiled, const void
     p.y_f16 = y_dtype == AEXIS_F16;
     p.ldy = ldy;
     p.tiled = tiled_epi;
+    const int esz = y_dtype == AEXIS_F16 ? 2 : 4;
+    p.bulk_out = (reinterpret_cast<uintptr_t>(y) & 15) == 0 && (((size_t)ldy * esz) & 15) == 0;
     p.status = status;
     const size_t smem = gemm_tc_smem_bytes(nb);
     static size_t configured = 0;
@@ -439,7 +601,7 @@ cudaError_t launch_gemm_tc(const aexis_weights* w, const void* tiled, const void
         if (e != cudaSuccess) return e;
         configured = smem;
     }
-    const int grid = p.n_tiles < sm_count ? p.n_tiles : sm_count;
+    const int grid = p.n_slabs < sm_count ? p.n_slabs : sm_count;
     gemm_q8_tc_kernel<<<grid, kTcThreads, smem, s>>>(p);
     return cudaGetLastError();
 }

@@ -35,6 +35,10 @@ def run_batched(ops, w, x, n, out_dtype, bias=None, alpha=1.0, beta=1.0, tiled=F
     (256, 4096, 1024, "f16"),  # config 5 batch with a smaller vocabulary slice
     (5, 1000, 3584, "f32"),    # ragged N (partial tile), long K
     (100, 640, 128, "f16"),
+    (256, 38000, 1024, "f16"),  # 297 slabs over the SMs: 2-3 per CTA, single-slab tail tiles
+    (128, 384, 256, "f32"),     # hi/lo split at the full MMA width (nb = 256)
+    (7, 1001, 128, "f16"),      # odd row stride: direct stores instead of staged bulk copies
+    (40, 1003, 192, "f32"),
 ])
 def test_tc_gemm_matches_oracle(ops, oracle, m, n, k, act):
     import torch
@@ -48,13 +52,15 @@ def test_tc_gemm_matches_oracle(ops, oracle, m, n, k, act):
     assert_gemv_close(got, ref)
 
 
-@pytest.mark.parametrize("tiled", [False, True])
-def test_tc_gemm_bias_alpha_beta_f16_out(ops, oracle, tiled):
+@pytest.mark.parametrize("tiled,act", [(False, "f16"), (True, "f16"), (False, "f32"), (True, "f32")])
+def test_tc_gemm_bias_alpha_beta_f16_out(ops, oracle, tiled, act):
     import torch
     m, n, k = 16, 768, 256
     p, s = synth.q8_weights(n, k, seed=8)
     w = ops.new_int8_weight_only_upload(p, s.astype(np.float32), n, k)
     x = synth.activations(k, seed=8, m=m)
+    if act == "f32":
+        x = (x.astype(np.float32) * 0.37).astype(np.float32)
     bias = np.random.default_rng(8).standard_normal(n).astype(np.float32)
     got = run_batched(ops, w, x, n, torch.float16, bias=bias, alpha=0.75, beta=1.5, tiled=tiled)
     ref = oracle.gemm(x.astype(np.float32), 8, p, s.astype(np.float32), 0, n, bias=bias, alpha=0.75, beta=1.5,
