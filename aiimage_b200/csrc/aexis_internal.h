@@ -109,6 +109,31 @@ cudaError_t launch_repack_q8(const aexis_weights* w, void* tiled, cudaStream_t s
 cudaError_t launch_gemm_tc(const aexis_weights* w, const void* tiled, const void* x, int a_dtype, int lda, int m,
                            void* xt, const float* bias, float alpha, float beta, void* y, int y_dtype, int ldy,
                            int tiled_epi, int sm_count, int* status, cudaStream_t s);
+// MMA width (rows of the prepared activations) for m rows; fp32 (split) doubles it.
+int tc_width(int m, int a_dtype);
+// Prepare activations for the tensor-core GEMM: op 0 copy, 1 RMSNorm with
+// gamma, 2 SwiGLU of interleaved gate/up pairs; split = fp16 hi + lo rows.
+// Optionally zeroes zero[m][zero_n] (row stride zero_ld). pdl: launched as a
+// programmatic dependent of the previous kernel on the stream.
+cudaError_t launch_tc_prep(int op, const void* x, int x_f16, int lda, int m, int k, const float* gamma, float eps,
+                           int split, void* xt, float* zero, int zero_ld, int zero_n, bool pdl, cudaStream_t s);
+struct TcLaunch {
+    const aexis_weights* w = nullptr;
+    const void* tiled = nullptr;  // launch_repack_q8 layout of w
+    const void* xt = nullptr;     // launch_tc_prep output
+    int m = 0, split = 0;
+    const float* bias = nullptr;
+    float alpha = 1.0f, beta = 1.0f;
+    void* y = nullptr;
+    int y_dtype = AEXIS_F32, ldy = 0;
+    int tiled_epi = 0;
+    int accumulate = 0;  // y += result (fp32 atomics); allows splitting K over CTAs
+    int k_splits = 0;    // 0: automatic
+    int sm_count = 148;
+    int* status = nullptr;
+    bool pdl = false;
+};
+cudaError_t launch_gemm_tc_prepared(const TcLaunch& a, cudaStream_t s);
 
 cudaError_t launch_dequant(const aexis_weights* w, float* out, cudaStream_t s);
 cudaError_t launch_rmsnorm(const void* x, int x_dtype, int rows, int width, int ld,

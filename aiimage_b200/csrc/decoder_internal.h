@@ -1,0 +1,40 @@
+// decoder_internal.h -- the decoder object shared by the batch-1 step graph
+// (k_decoder.cu) and the batched decode path (k_batch.cu).
+#pragma once
+#include <vector>
+
+#include "aexis_internal.h"
+
+struct aexis_decoder {
+    aexis_ctx* ctx = nullptr;
+    aexis_decoder_config cfg = {};
+    struct Layer {
+        aexis_weights qkv, o, gateup, down;
+        float* norm[2] = {nullptr, nullptr};
+        int set_mask = 0;  // bit w set once linear w was loaded; bits 7,8 the norms
+    };
+    std::vector<Layer> layers;
+    aexis_weights lm;
+    int lm_set = 0;
+    float* final_norm = nullptr;
+    __half* embed = nullptr;
+    int embed_set = 0, final_set = 0;
+    int* rope_map = nullptr;        // [qkv rows]
+    float* rope_cos = nullptr;      // [cap][rot/2]
+    float* rope_sin = nullptr;
+    __half* kcache = nullptr;       // [layers][kv][cap][D]
+    __half* vcache = nullptr;
+    float *h = nullptr, *q = nullptr, *attn = nullptr, *act = nullptr, *logits = nullptr, *part = nullptr;
+    unsigned int* counters = nullptr;
+    unsigned long long* key = nullptr;
+    int* ints = nullptr;            // [0] token, [1] pos, [2] step, [3..] out tokens
+    int max_out = 0;
+    int host_pos = 0;
+    cudaGraphExec_t step_exec = nullptr, prefill_exec = nullptr;
+    std::vector<int> qkv_perm;      // internal row -> logical (kind, head, dim)
+};
+
+// cos/sin tables [cap][rot/2] of Qwen35DecoderSession.CreateRopeTextures
+// (Qwen35DecoderSession.cs:1660-1687): inv = 1 / theta^(j * 2/rot) in fp32,
+// angle = pos * inv in fp32, cos/sin evaluated in double and rounded.
+void decoder_rope_tables(int cap, int rot_dim, float theta, std::vector<float>& cs, std::vector<float>& sn);

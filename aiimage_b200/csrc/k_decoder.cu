@@ -20,7 +20,7 @@
 #include <cstring>
 #include <new>
 
-#include "aexis_internal.h"
+#include "decoder_internal.h"
 
 #define AEXIS_API extern "C" __attribute__((visibility("default")))
 
@@ -203,34 +203,7 @@ __global__ void dec_finish_kernel(const unsigned long long* key, int* token, int
 }  // namespace
 
 // ------------------------------------------------------------------ host side
-struct aexis_decoder {
-    aexis_ctx* ctx = nullptr;
-    aexis_decoder_config cfg = {};
-    struct Layer {
-        aexis_weights qkv, o, gateup, down;
-        float* norm[2] = {nullptr, nullptr};
-        int set_mask = 0;  // bit w set once linear w was loaded; bits 7,8 the norms
-    };
-    std::vector<Layer> layers;
-    aexis_weights lm;
-    int lm_set = 0;
-    float* final_norm = nullptr;
-    __half* embed = nullptr;
-    int embed_set = 0, final_set = 0;
-    int* rope_map = nullptr;        // [qkv rows]
-    float* rope_cos = nullptr;      // [cap][rot/2]
-    float* rope_sin = nullptr;
-    __half* kcache = nullptr;       // [layers][kv][cap][D]
-    __half* vcache = nullptr;
-    float *h = nullptr, *q = nullptr, *attn = nullptr, *act = nullptr, *logits = nullptr, *part = nullptr;
-    unsigned int* counters = nullptr;
-    unsigned long long* key = nullptr;
-    int* ints = nullptr;            // [0] token, [1] pos, [2] step, [3..] out tokens
-    int max_out = 0;
-    int host_pos = 0;
-    cudaGraphExec_t step_exec = nullptr, prefill_exec = nullptr;
-    std::vector<int> qkv_perm;      // internal row -> logical (kind, head, dim)
-};
+
 
 namespace {
 
@@ -476,6 +449,19 @@ int run_steps(aexis_decoder* d, int emit, int count) {
 
 }  // namespace
 
+void decoder_rope_tables(int cap, int rot_dim, float theta, std::vector<float>& cs, std::vector<float>& sn) {
+    const int half = rot_dim / 2;
+    cs.assign((size_t)cap * half, 0.0f);
+    sn.assign((size_t)cap * half, 0.0f);
+    for (int p = 0; p < cap; ++p)
+        for (int j = 0; j < half; ++j) {
+            const float inv = 1.0f / (float)std::pow((double)theta, (double)((float)j * (2.0f / (float)rot_dim)));
+            const float ang = (float)p * inv;
+            cs[(size_t)p * half + j] = (float)std::cos((double)ang);
+            sn[(size_t)p * half + j] = (float)std::sin((double)ang);
+        }
+}
+
 AEXIS_API int aexis_cuda_decoder_create(aexis_ctx* ctx, const aexis_decoder_config* cfg, aexis_decoder** out) {
     if (!ctx) return AEXIS_E_NULL;
     if (!cfg || !out) return aexis_fail(ctx, AEXIS_E_NULL, "cfg/out is null");
@@ -562,15 +548,8 @@ AEXIS_API int aexis_cuda_decoder_create(aexis_ctx* ctx, const aexis_decoder_conf
     }
     // RoPE tables (Qwen35DecoderSession.CreateRopeTextures, :1660-1687).
     if (!rc && c.rot_dim > 0) {
-        const int half = c.rot_dim / 2;
-        std::vector<float> cs((size_t)c.kv_capacity * half), sn((size_t)c.kv_capacity * half);
-        for (int p = 0; p < c.kv_capacity; ++p)
-            for (int j = 0; j < half; ++j) {
-                const float inv = 1.0f / (float)std::pow((double)c.rope_theta, (double)((float)j * (2.0f / (float)c.rot_dim)));
-                const float ang = (float)p * inv;
-                cs[(size_t)p * half + j] = (float)std::cos((double)ang);
-                sn[(size_t)p * half + j] = (float)std::sin((double)ang);
-            }
+        std::vector<float> cs, sn;
+        decoder_rope_tables(c.kv_capacity, c.rot_dim, c.rope_theta, cs, sn);
         rc = alloc(d, (void**)&d->rope_cos, sizeof(float) * cs.size(), "alloc");
         if (!rc) rc = alloc(d, (void**)&d->rope_sin, sizeof(float) * sn.size(), "alloc");
         if (!rc) rc = aexis_cuda_check(ctx, cudaMemcpy(d->rope_cos, cs.data(), sizeof(float) * cs.size(), cudaMemcpyHostToDevice), "rope upload");

@@ -57,8 +57,34 @@ struct TcParams {
     int y_f16, ldy;
     int tiled;                // 1: beta*bias + alpha*acc (lm_head form)
     int bulk_out;             // y and its row stride 16-byte aligned: staged row stores
+    int k_splits;             // > 1: work units are (slab, K range), one slab per tile
+    int accumulate;           // 1: y += result with fp32 atomics (bias from the first K range)
     int* status;
 };
+
+// Tile t of a CTA's work range [lo, hi): slabs [slab0, slab0 + ns) over
+// k-blocks [kb0, kb1); `first` when the tile starts at k-block 0.
+struct TcTile {
+    int slab0, ns, kb0, kb1, first;
+};
+
+__device__ __forceinline__ TcTile tc_tile(const TcParams& p, int lo, int hi, int t, int nkb) {
+    TcTile T;
+    if (p.k_splits <= 1) {
+        T.slab0 = lo + 2 * t;
+        T.ns = hi - T.slab0 < 2 ? 1 : 2;
+        T.kb0 = 0;
+        T.kb1 = nkb;
+    } else {
+        const int u = lo + t, ks = u % p.k_splits;
+        T.slab0 = u / p.k_splits;
+        T.ns = 1;
+        T.kb0 = ks * nkb / p.k_splits;
+        T.kb1 = (ks + 1) * nkb / p.k_splits;
+    }
+    T.first = T.kb0 == 0;
+    return T;
+}
 
 // Shared-memory carve-up (offsets from a 1024-aligned base): the fp16 A ring
 // (kADepth x two slabs), the activation ring, the int8 ring, the barriers.
@@ -174,11 +200,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_q8_tc_kernel(TcParams p) {
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nkb = p.k / kKB;
-    // A contiguous range of 128-row slabs per CTA (counts differ by at most
-    // one), taken two slabs per accumulator tile.
-    const int s_lo = (int)((long long)blockIdx.x * p.n_slabs / gridDim.x);
-    const int s_hi = (int)((long long)(blockIdx.x + 1) * p.n_slabs / gridDim.x);
-    const int my_tiles = (s_hi - s_lo + 1) / 2;
+    // A contiguous range of work per CTA (counts differ by at most one):
+    // 128-row slabs taken two per accumulator tile, or with k_splits > 1
+    // (slab, K range) units taken one per tile.
+    const int units = p.k_splits > 1 ? p.n_slabs * p.k_splits : p.n_slabs;
+    const int s_lo = (int)((long long)blockIdx.x * units / gridDim.x);
+    const int s_hi = (int)((long long)(blockIdx.x + 1) * units / gridDim.x);
+    const int my_tiles = p.k_splits > 1 ? s_hi - s_lo : (s_hi - s_lo + 1) / 2;
     const uint32_t tmem_cols = (uint32_t)(2 * p.nb <= 32 ? 32 : (2 * p.nb <= 64 ? 64 : (2 * p.nb <= 128 ? 128 :
                                           (2 * p.nb <= 256 ? 256 : 512))));
 
@@ -214,6 +242,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_q8_tc_kernel(TcParams p) {
     const uint32_t tmem = *tmem_slot;
 
     griddep_wait();
+    griddep_launch();  // every CTA is resident (grid <= SMs): dependents may start their prologue
 
     if (warp == 0) {
         // ------------------------------------------------- int8 weight producer
@@ -221,9 +250,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_q8_tc_kernel(TcParams p) {
             const uint64_t pol = policy_evict_first();
             int it = 0, issued = 0;
             for (int t = 0; t < my_tiles && !*abort_flag; ++t) {
-                const int slab0 = s_lo + 2 * t;
-                const int ns = s_hi - slab0 < 2 ? 1 : 2;
-                for (int kb = 0; kb < nkb; ++kb, ++it) {
+                const TcTile T = tc_tile(p, s_lo, s_hi, t, nkb);
+                const int slab0 = T.slab0, ns = T.ns;
+                for (int kb = T.kb0; kb < T.kb1; ++kb, ++it) {
                     const int s = it % RD;
                     if (it >= RD && !mbar_wait(raw_empty + s, ((it / RD) & 1) ^ 1)) {
                         report_timeout(p.status);
@@ -247,19 +276,22 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_q8_tc_kernel(TcParams p) {
     } else if (warp == 6) {
         // ---------------------------------------------- activation producer
         if (lane == 0) {
-            const int total = my_tiles * nkb;
-            int issued = 0;
-            for (int it = 0; it < total && !*abort_flag; ++it) {
-                const int s = it % BD;
-                if (it >= BD && !mbar_wait(b_empty + s, ((it / BD) & 1) ^ 1)) {
-                    report_timeout(p.status);
-                    *abort_flag = 1;
-                    break;
+            int it = 0, issued = 0;
+            for (int t = 0; t < my_tiles && !*abort_flag; ++t) {
+                const TcTile T = tc_tile(p, s_lo, s_hi, t, nkb);
+                for (int kb = T.kb0; kb < T.kb1; ++kb, ++it) {
+                    const int s = it % BD;
+                    if (it >= BD && !mbar_wait(b_empty + s, ((it / BD) & 1) ^ 1)) {
+                        report_timeout(p.status);
+                        *abort_flag = 1;
+                        break;
+                    }
+                    if (*abort_flag) break;
+                    mbar_arrive_expect_tx(b_full + s, (uint32_t)L.b_bytes);
+                    bulk_g2s_plain(base + L.b_off + s * L.b_stage, p.xt + (size_t)kb * L.b_bytes,
+                                   (uint32_t)L.b_bytes, b_full + s);
+                    issued = it + 1;
                 }
-                mbar_arrive_expect_tx(b_full + s, (uint32_t)L.b_bytes);
-                bulk_g2s_plain(base + L.b_off + s * L.b_stage, p.xt + (size_t)(it % nkb) * L.b_bytes,
-                               (uint32_t)L.b_bytes, b_full + s);
-                issued = it + 1;
             }
             for (int i = issued - BD < 0 ? 0 : issued - BD; i < issued; ++i)
                 if (!mbar_wait(b_full + i % BD, (i / BD) & 1)) { report_timeout(p.status); break; }
@@ -270,14 +302,15 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_q8_tc_kernel(TcParams p) {
             const uint32_t idesc = idesc_f16_f32(kTM, p.nb);
             int it = 0;
             for (int t = 0; t < my_tiles && !*abort_flag; ++t) {
-                const int ns = s_hi - (s_lo + 2 * t) < 2 ? 1 : 2;
+                const TcTile T = tc_tile(p, s_lo, s_hi, t, nkb);
+                const int ns = T.ns;
                 if (t > 0 && !mbar_wait(acc_empty, (t - 1) & 1)) {
                     report_timeout(p.status);
                     *abort_flag = 1;
                     break;
                 }
                 tc_fence_after();
-                for (int kb = 0; kb < nkb; ++kb, ++it) {
+                for (int kb = T.kb0; kb < T.kb1; ++kb, ++it) {
                     const int sa = it % kADepth, sb = it % BD;
                     if (!mbar_wait(a_ready + sa, (it / kADepth) & 1) || !mbar_wait(b_full + sb, (it / BD) & 1)) {
                         report_timeout(p.status);
@@ -293,7 +326,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_q8_tc_kernel(TcParams p) {
 #pragma unroll
                             for (int kk = 0; kk < kKB / 16; ++kk)
                                 mma_f16(tmem + (uint32_t)(j * p.nb), sw128_desc(a0 + j * kATileBytes + kk * 32),
-                                        sw128_desc(b0 + kk * 32), idesc, (kb > 0 || kk > 0) ? 1 : 0);
+                                        sw128_desc(b0 + kk * 32), idesc, (kb > T.kb0 || kk > 0) ? 1 : 0);
                         }
                     }
                     mma_commit(a_empty + sa);
@@ -314,9 +347,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_q8_tc_kernel(TcParams p) {
         int it = 0;
         int chunk = 0;                        // staged epilogue chunks so far (all tiles)
         for (int t = 0; t < my_tiles && !*abort_flag; ++t) {
-            const int slab0 = s_lo + 2 * t;
-            const int ns = s_hi - slab0 < 2 ? 1 : 2;
-            for (int kb = 0; kb < nkb; ++kb, ++it) {
+            const TcTile T = tc_tile(p, s_lo, s_hi, t, nkb);
+            const int slab0 = T.slab0, ns = T.ns;
+            for (int kb = T.kb0; kb < T.kb1; ++kb, ++it) {
                 const int sr = it % RD, sa = it % kADepth;
                 if (!mbar_wait(raw_full + sr, (it / RD) & 1) ||
                     (it >= kADepth && !mbar_wait(a_empty + sa, ((it / kADepth) & 1) ^ 1))) {
@@ -375,7 +408,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_q8_tc_kernel(TcParams p) {
                 if (nvalid) {
                     sc = p.scale_f16 ? __half2float(reinterpret_cast<const __half*>(p.scales)[n])
                                      : reinterpret_cast<const float*>(p.scales)[n];
-                    bb = p.bias ? p.beta * p.bias[n] : 0.0f;
+                    bb = p.bias && T.first ? p.beta * p.bias[n] : 0.0f;
                 }
                 const uint32_t lane_addr = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(j * p.nb);
                 const int cnt = p.n - slab * kTM < kTM ? p.n - slab * kTM : kTM;  // valid outputs of the slab
@@ -430,7 +463,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_q8_tc_kernel(TcParams p) {
                                     u.y = *reinterpret_cast<const uint32_t*>(&h1);
                                     *reinterpret_cast<uint2*>(reinterpret_cast<__half*>(p.y) + off) = u;
                                 } else {
-                                    *reinterpret_cast<float4*>(reinterpret_cast<float*>(p.y) + off) = v;
+                                    float4* dst = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.y) + off);
+                                    if (p.accumulate) atomicAdd(dst, v);
+                                    else *dst = v;
                                 }
                             }
                         }
@@ -454,6 +489,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_q8_tc_kernel(TcParams p) {
                         const float out = p.tiled ? bb + p.alpha * (acc * sc) : p.alpha * (bb + acc * sc);
                         if (i < lim) {
                             if (p.y_f16) yh[(size_t)(c0 + i) * ldy] = __float2half_rn(out);
+                            else if (p.accumulate) atomicAdd(yf + (size_t)(c0 + i) * ldy, out);
                             else yf[(size_t)(c0 + i) * ldy] = out;
                         }
                     }
@@ -479,31 +515,69 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_q8_tc_kernel(TcParams p) {
     }
 }
 
-// x [m][lda] (fp16 or fp32) -> xt [K/64][nb][64] fp16, 128-byte swizzled rows.
-// fp32 rows are split: hi = fp16(x) in row b, lo = fp16(x - hi) in row
-// nb/2 + b (nb/2 = m rounded up to 16); padding rows are zero.
-__global__ void prep_x_kernel(const void* x, int a_f16, int lda, int m, int k, int nb, int split, uint8_t* xt) {
-    const long long total = (long long)(k / kKB) * nb * 8;  // 16-byte chunks
-    for (long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x; t < total;
-         t += (long long)gridDim.x * blockDim.x) {
-        const int c = (int)(t & 7);
-        const int row = (int)((t >> 3) % nb);
-        const int kb = (int)(t / (8LL * nb));
-        __half h[8];
-        const int half = nb >> 1;
-        const int src = split && row >= half ? row - half : row;
-        const bool lo = split && row >= half;
+// Activations -> xt [K/64][nb][64] fp16, 128-byte swizzled rows, one CTA per
+// output row b < nb/(split ? 2 : 1): hi = fp16(v) in row b and, with split,
+// lo = fp16(v - hi) in row nb/2 + b; rows b >= m are zero. The value v is
+//   op 0: x[b][k] (fp16 or fp32);
+//   op 1: RMSNorm, x[b][k] * rsqrt(max(mean(x[b]^2) + eps, 1e-20)) * gamma[k]
+//         (AexisRmsNormPack4LinearMat, AexisCommon.compute:4531-4563; x fp32);
+//   op 2: SwiGLU of interleaved pairs, silu(x[b][2k]) * x[b][2k+1]
+//         (HLSL Pack4Matmul:91-94, 118-128; x fp32).
+// With `zero`, the CTA of row b also clears zero[b][0, zero_n) (the output
+// of a following accumulating GEMM). Waits for the previous grid (PDL).
+__global__ void __launch_bounds__(256) tc_prep_kernel(const void* x, int x_f16, int lda, int m, int k, int op,
+                                                      const float* gamma, float eps, int nb, int split, uint8_t* xt,
+                                                      float* zero, int zero_ld, int zero_n) {
+    __shared__ float red[8];
+    griddep_wait();
+    const int b = blockIdx.x;
+    const int half = split ? nb >> 1 : nb;
+    const float* xf = reinterpret_cast<const float*>(x);
+    const long long row = (long long)b * lda;
+    float inv = 1.0f;
+    if (op == 1 && b < m) {
+        float ss = 0.0f;
+        for (int i = threadIdx.x; i < k; i += 256) ss = fmaf(xf[row + i], xf[row + i], ss);
+#pragma unroll
+        for (int o = 16; o >= 1; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+        __syncthreads();
+        float tot = 0.0f;
+#pragma unroll
+        for (int w = 0; w < 8; ++w) tot += red[w];
+        inv = 1.0f / sqrtf(fmaxf(tot / (float)k + eps, 1e-20f));
+    }
+    for (int c8 = threadIdx.x; c8 < k / 8; c8 += 256) {
+        __half hi[8], lo[8];
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
-            const int kk = kb * kKB + c * 8 + e;
+            const int kk = c8 * 8 + e;
             float v = 0.0f;
-            if (src < m) v = aexis_load_act(x, a_f16 ? AEXIS_F16 : AEXIS_F32, (long long)src * lda + kk);
-            const __half hi = __float2half_rn(v);
-            h[e] = lo ? __float2half_rn(v - __half2float(hi)) : hi;
+            if (b < m) {
+                if (op == 0) {
+                    v = aexis_load_act(x, x_f16 ? AEXIS_F16 : AEXIS_F32, row + kk);
+                } else if (op == 1) {
+                    v = xf[row + kk] * inv * gamma[kk];
+                } else {
+                    const float g = xf[row + 2 * kk], u = xf[row + 2 * kk + 1];
+                    v = __fmul_rn(g / (1.0f + expf(-g)), u);
+                }
+            }
+            hi[e] = __float2half_rn(v);
+            lo[e] = __float2half_rn(v - __half2float(hi[e]));
         }
-        uint8_t* dst = xt + ((size_t)kb * nb + row) * 128 + ((c ^ (row & 7)) << 4);
-        *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<uint4*>(h);
+        const int kb = c8 >> 3, c = c8 & 7;
+        *reinterpret_cast<uint4*>(xt + ((size_t)kb * nb + b) * 128 + ((c ^ (b & 7)) << 4)) =
+            *reinterpret_cast<const uint4*>(hi);
+        if (split) {
+            const int r = half + b;
+            *reinterpret_cast<uint4*>(xt + ((size_t)kb * nb + r) * 128 + ((c ^ (r & 7)) << 4)) =
+                *reinterpret_cast<const uint4*>(lo);
+        }
     }
+    if (zero && b < m)
+        for (int i = threadIdx.x; i < zero_n; i += 256) zero[(long long)b * zero_ld + i] = 0.0f;
+    griddep_launch();
 }
 
 // Row-major Q8 [n][k] -> [ceil(n/256)*2][k/64][128][64] (rows past n zero;
@@ -561,47 +635,107 @@ size_t gemm_tc_xt_bytes(int m, int k, int a_dtype) {
     return (size_t)k * tc_width(m, a_dtype) * 2;
 }
 
+namespace {
+
+cudaError_t launch_maybe_pdl(const void* fn, dim3 grid, dim3 block, size_t smem, bool pdl, cudaStream_t s,
+                             void** args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelExC(&cfg, fn, args);
+}
+
+}  // namespace
+
+cudaError_t launch_tc_prep(int op, const void* x, int x_f16, int lda, int m, int k, const float* gamma, float eps,
+                           int split, void* xt, float* zero, int zero_ld, int zero_n, bool pdl, cudaStream_t s) {
+    const int nb = tc_width(m, split ? AEXIS_F32 : AEXIS_F16);
+    const int rows = split ? nb / 2 : nb;
+    uint8_t* xtp = reinterpret_cast<uint8_t*>(xt);
+    void* args[] = {(void*)&x, &x_f16, &lda, &m, &k, &op, (void*)&gamma, &eps, (void*)&nb, &split, &xtp,
+                    &zero, &zero_ld, &zero_n};
+    return launch_maybe_pdl((const void*)tc_prep_kernel, dim3(rows), dim3(256), 0, pdl, s, args);
+}
+
+cudaError_t launch_gemm_tc_prepared(const TcLaunch& a, cudaStream_t s) {
+    const aexis_weights* w = a.w;
+    const int nb = tc_width(a.m, a.split ? AEXIS_F32 : AEXIS_F16);
+    if (a.accumulate && a.y_dtype != AEXIS_F32) return cudaErrorNotSupported;
+    TcParams p = {};
+    p.wt = reinterpret_cast<const uint8_t*>(a.tiled);
+    p.scales = w->scales;
+    p.scale_f16 = w->scale_dtype == AEXIS_F16;
+    p.xt = reinterpret_cast<const uint8_t*>(a.xt);
+    p.n = w->n;
+    p.k = w->k;
+    p.m = a.m;
+    p.nb = nb;
+    p.split = a.split;
+    p.n_slabs = (w->n + kTM - 1) / kTM;
+    if (!tc_depths(nb, p.raw_depth, p.b_depth)) return cudaErrorNotSupported;
+    p.bias = a.bias;
+    p.alpha = a.alpha;
+    p.beta = a.beta;
+    p.y = a.y;
+    p.y_f16 = a.y_dtype == AEXIS_F16;
+    p.ldy = a.ldy;
+    p.tiled = a.tiled_epi;
+    const int esz = p.y_f16 ? 2 : 4;
+    p.bulk_out = (reinterpret_cast<uintptr_t>(a.y) & 15) == 0 && (((size_t)a.ldy * esz) & 15) == 0;
+    p.accumulate = a.accumulate;
+    // Split K only when accumulating and the slabs alone would leave SMs idle.
+    const int nkb = w->k / kKB;
+    int ks = 1;
+    if (a.accumulate && p.n_slabs < a.sm_count) {
+        ks = a.k_splits > 0 ? a.k_splits : a.sm_count / p.n_slabs;
+        ks = ks > nkb ? nkb : (ks < 1 ? 1 : ks);
+    }
+    p.k_splits = ks;
+    p.status = a.status;
+    const size_t smem = gemm_tc_smem_bytes(nb);
+    int dev = 0;
+    cudaGetDevice(&dev);
+    static size_t configured[64] = {};
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    if (smem > configured[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(gemm_q8_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+        configured[dev] = smem;
+    }
+    const int units = ks > 1 ? p.n_slabs * ks : p.n_slabs;
+    const int grid = units < a.sm_count ? units : a.sm_count;
+    void* args[] = {&p};
+    return launch_maybe_pdl((const void*)gemm_q8_tc_kernel, dim3(grid), dim3(kTcThreads), smem, a.pdl, s, args);
+}
+
 cudaError_t launch_gemm_tc(const aexis_weights* w, const void* tiled, const void* x, int a_dtype, int lda, int m,
                            void* xt, const float* bias, float alpha, float beta, void* y, int y_dtype, int ldy,
                            int tiled_epi, int sm_count, int* status, cudaStream_t s) {
     const int split = a_dtype == AEXIS_F32;
-    const int nb = tc_width(m, a_dtype);
-    const long long chunks = (long long)(w->k / kKB) * nb * 8;
-    int pb = (int)((chunks + 255) / 256);
-    pb = pb > 148 * 8 ? 148 * 8 : (pb < 1 ? 1 : pb);
-    prep_x_kernel<<<pb, 256, 0, s>>>(x, a_dtype == AEXIS_F16, lda, m, w->k, nb, split, reinterpret_cast<uint8_t*>(xt));
-    cudaError_t e = cudaGetLastError();
+    cudaError_t e = launch_tc_prep(0, x, a_dtype == AEXIS_F16, lda, m, w->k, nullptr, 0.0f, split, xt, nullptr, 0, 0,
+                                   false, s);
     if (e != cudaSuccess) return e;
-    TcParams p = {};
-    p.wt = reinterpret_cast<const uint8_t*>(tiled);
-    p.scales = w->scales;
-    p.scale_f16 = w->scale_dtype == AEXIS_F16;
-    p.xt = reinterpret_cast<const uint8_t*>(xt);
-    p.n = w->n;
-    p.k = w->k;
-    p.m = m;
-    p.nb = nb;
-    p.split = split;
-    p.n_slabs = (w->n + kTM - 1) / kTM;
-    if (!tc_depths(nb, p.raw_depth, p.b_depth)) return cudaErrorNotSupported;
-    p.bias = bias;
-    p.alpha = alpha;
-    p.beta = beta;
-    p.y = y;
-    p.y_f16 = y_dtype == AEXIS_F16;
-    p.ldy = ldy;
-    p.tiled = tiled_epi;
-    const int esz = y_dtype == AEXIS_F16 ? 2 : 4;
-    p.bulk_out = (reinterpret_cast<uintptr_t>(y) & 15) == 0 && (((size_t)ldy * esz) & 15) == 0;
-    p.status = status;
-    const size_t smem = gemm_tc_smem_bytes(nb);
-    static size_t configured = 0;
-    if (smem > configured) {
-        e = cudaFuncSetAttribute(gemm_q8_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (e != cudaSuccess) return e;
-        configured = smem;
-    }
-    const int grid = p.n_slabs < sm_count ? p.n_slabs : sm_count;
-    gemm_q8_tc_kernel<<<grid, kTcThreads, smem, s>>>(p);
-    return cudaGetLastError();
+    TcLaunch a;
+    a.w = w;
+    a.tiled = tiled;
+    a.xt = xt;
+    a.m = m;
+    a.split = split;
+    a.bias = bias;
+    a.alpha = alpha;
+    a.beta = beta;
+    a.y = y;
+    a.y_dtype = y_dtype;
+    a.ldy = ldy;
+    a.tiled_epi = tiled_epi;
+    a.sm_count = sm_count;
+    a.status = status;
+    return launch_gemm_tc_prepared(a, s);
 }

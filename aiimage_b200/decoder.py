@@ -6,6 +6,7 @@ SelectNextToken :734-809) over libaexis_cuda's fused decoder.
 from __future__ import annotations
 
 import ctypes as C
+import weakref
 
 import numpy as np
 
@@ -29,11 +30,15 @@ class DecoderSession:
         self.h = C.c_void_p()
         check(lib().aexis_cuda_decoder_create(ops.ctx, C.byref(self._cfg), C.byref(self.h)), ops.ctx)
         self._scale_dtype = scale_dtype
+        self._batches = weakref.WeakSet()
         ops._register(self)
 
     def close(self):
         # A decoder lives inside its context: destroy it first (AexisOps.close
-        # closes its decoders before the context goes away).
+        # closes its decoders before the context goes away); its batches go
+        # before it.
+        for b in list(self._batches):
+            b.close()
         if self.h and self.ops.ctx:
             lib().aexis_cuda_decoder_destroy(self.h)
         self.h = C.c_void_p()
@@ -113,4 +118,65 @@ class DecoderSession:
         return out
 
 
-__all__ = ["DecoderSession", "errors"]
+class BatchSession:
+    """Batched greedy decoding of B independent sequences over one
+    DecoderSession's Q8 weights (aexis_cuda_batch_*): what a host serving B
+    Qwen35DecoderSession instances would run, one step for all of them.
+    Create it after the decoder's weights are loaded."""
+
+    def __init__(self, dec: DecoderSession, max_batch: int, kv_capacity: int, max_steps: int):
+        self.dec = dec
+        self.h = C.c_void_p()
+        check(lib().aexis_cuda_batch_create(dec.h, max_batch, kv_capacity, max_steps, C.byref(self.h)), dec.ops.ctx)
+        self.n = 0
+        dec._batches.add(self)
+
+    def close(self):
+        if self.h and self.dec.h and self.dec.ops.ctx:
+            lib().aexis_cuda_batch_destroy(self.h)
+        self.h = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def _check(self, st):
+        check(st, self.dec.ops.ctx)
+
+    def fill_context(self, ctx_lens, seed: int, first_seq_id: int = 0):
+        """Sequences i < len(ctx_lens) get synthetic contexts of ctx_lens[i]
+        positions (the values of oracle_decoder_fill_context)."""
+        c = np.ascontiguousarray(ctx_lens, dtype=np.int32)
+        self._check(lib().aexis_cuda_batch_fill_context(self.h, c.size, _np(c), int(seed) & (2**64 - 1),
+                                                        int(first_seq_id)))
+        self.n = int(c.size)
+
+    def generate(self, first_tokens, steps: int) -> np.ndarray:
+        """Greedy tokens [steps][n]."""
+        t = np.ascontiguousarray(first_tokens, dtype=np.int32)
+        if self.n and t.size != self.n:  # with no context the library reports the state error
+            raise errors.ArgumentOutOfRangeError(f"{t.size} first tokens for {self.n} sequences")
+        out = np.zeros((max(steps, 0), max(self.n, 1)), dtype=np.int32)
+        self._check(lib().aexis_cuda_batch_generate(self.h, _np(t), int(steps), _np(out)))
+        return out
+
+    def generate_device(self, first_tokens, steps: int):
+        """As generate, without copying the tokens back (timing runs)."""
+        t = np.ascontiguousarray(first_tokens, dtype=np.int32)
+        self._check(lib().aexis_cuda_batch_generate(self.h, _np(t), int(steps), None))
+
+    @property
+    def positions(self) -> np.ndarray:
+        out = np.zeros(self.n, dtype=np.int32)
+        self._check(lib().aexis_cuda_batch_positions(self.h, _np(out)))
+        return out
+
+    def logits(self) -> np.ndarray:
+        out = np.empty((self.n, self.dec.cfg.vocab), dtype=np.float32)
+        self._check(lib().aexis_cuda_batch_logits(self.h, _np(out)))
+        return out
+
+
+__all__ = ["DecoderSession", "BatchSession", "errors"]

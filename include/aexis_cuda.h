@@ -324,6 +324,47 @@ int aexis_cuda_decoder_generate(aexis_decoder* dec, const int32_t* prompt, int n
  * greedy path (Qwen35DecoderSession.ProjectLogits :715-733). */
 int aexis_cuda_decoder_logits(aexis_decoder* dec, float* out_logits);
 
+/* ---- batched greedy decoding ------------------------------------------------
+ * B independent sequences decoded together on one GPU: Qwen35DecoderSession's
+ * DecodeCore + SelectNextToken (Qwen35DecoderSession.cs:469-585, 734-809) run
+ * for B sequences at once, each with its own context length and KV cache.
+ * The reference decodes one sequence per session; a host that serves B
+ * sessions replaces B DecodeCore calls per token with one batch step. Every
+ * linear reads its weights once per step for all B rows (tensor cores).
+ * Requires a Q8 decoder (bits = lm_bits = 8) whose weights are all set: the
+ * batch repacks them at creation, so later aexis_cuda_decoder_set_* calls do
+ * not reach an existing batch. KV caches are fp16, [layers][B][kv][cap][D]. */
+typedef struct aexis_batch aexis_batch;
+
+/* max_batch 1..128 sequences, kv_capacity 1..8192 positions per sequence,
+ * max_steps = most tokens one aexis_cuda_batch_generate call may produce. */
+int aexis_cuda_batch_create(aexis_decoder* dec, int max_batch, int kv_capacity, int max_steps, aexis_batch** out);
+int aexis_cuda_batch_destroy(aexis_batch* batch);
+
+/* Sets `batch` sequences with contexts ctx_lens[i] (host, 0 <= len < capacity)
+ * already in their caches: position p < len of layer l holds, for K (kind 0)
+ * and V (kind 1) of head h and dim d, the fp16 rounding of
+ *   u = (mix64(key ^ idx) >> 40) * 2^-24 - 0.5,
+ *   key = mix64(seed ^ mix64(first_seq_id + i)),
+ *   idx = ((((l * 2 + kind) * 256 + h) * 65536 + p) * 256 + d),
+ * mix64 the splitmix64 finaliser. This stands in for the prefill of a real
+ * prompt (synthetic contexts of a serving benchmark); the CPU oracle fills
+ * its cache with the same values. Each sequence's next position is len. */
+int aexis_cuda_batch_fill_context(aexis_batch* batch, int n, const int32_t* ctx_lens, uint64_t seed,
+                                  int64_t first_seq_id);
+
+/* Greedy decoding of `steps` tokens for every sequence: first_tokens[i]
+ * (host) is the input of sequence i at its current position; out_tokens
+ * (host, may be NULL) receives [steps][n] step-major. Synchronous. E_RANGE
+ * when a sequence would pass its capacity. */
+int aexis_cuda_batch_generate(aexis_batch* batch, const int32_t* first_tokens, int steps, int32_t* out_tokens);
+
+/* Next position of each sequence (host [n]). */
+int aexis_cuda_batch_positions(const aexis_batch* batch, int32_t* out);
+
+/* fp32 logits of the last step, host [n][vocab]. */
+int aexis_cuda_batch_logits(aexis_batch* batch, float* out_logits);
+
 #ifdef __cplusplus
 }
 #endif

@@ -542,6 +542,45 @@ ORACLE_API void* oracle_decoder_create(const OracleDecoderCfg* cfg) {
 }
 
 ORACLE_API void oracle_decoder_destroy(void* h) { delete (ODecoder*)h; }
+
+namespace {
+// splitmix64 finaliser (Steele, Lea and Flood, OOPSLA 2014).
+uint64_t mix64(uint64_t z) {
+    z += 0x9E3779B97F4A7C15ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+}  // namespace
+
+// Synthetic context of a batched-decoding benchmark sequence (no reference
+// counterpart: the reference fills its cache by running a prompt). Positions
+// [0, ctx) of every layer's K (kind 0) and V (kind 1) cache hold the fp16
+// rounding of u = (mix64(key ^ idx) >> 40) * 2^-24 - 0.5 with
+// key = mix64(seed ^ mix64(seq_id)), idx = ((((l*2 + kind)*256 + h)*65536 + p)*256 + d);
+// the next position becomes ctx. Returns -2 when ctx >= capacity.
+ORACLE_API int oracle_decoder_fill_context(void* h, int ctx, uint64_t seed, int64_t seq_id) {
+    ODecoder* d = (ODecoder*)h;
+    const auto& c = d->c;
+    if (ctx < 0 || ctx >= c.kv_capacity) return -2;
+    const uint64_t key = mix64(seed ^ mix64((uint64_t)seq_id));
+    const int D = c.head_dim, KVH = c.n_kv_heads;
+    for (int l = 0; l < c.n_layers; ++l)
+        for (int kind = 0; kind < 2; ++kind) {
+            float* cache = (kind == 0 ? d->kcache : d->vcache).data() + (size_t)l * KVH * c.kv_capacity * D;
+            for (int hh = 0; hh < KVH; ++hh)
+                for (int p = 0; p < ctx; ++p)
+                    for (int i = 0; i < D; ++i) {
+                        const uint64_t idx =
+                            ((((uint64_t)l * 2 + kind) * 256 + hh) * 65536 + (uint64_t)p) * 256 + (uint64_t)i;
+                        const uint64_t r = mix64(key ^ idx);
+                        const float u = (float)(r >> 40) * (1.0f / 16777216.0f) - 0.5f;
+                        cache[((size_t)hh * c.kv_capacity + p) * D + i] = oracle_round_f16(u);
+                    }
+        }
+    d->pos = ctx;
+    return 0;
+}
 ORACLE_API void oracle_decoder_reset(void* h) { ((ODecoder*)h)->pos = 0; }
 ORACLE_API int oracle_decoder_position(void* h) { return ((ODecoder*)h)->pos; }
 

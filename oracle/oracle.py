@@ -68,6 +68,8 @@ def lib():
         L.oracle_decoder_set_norm.argtypes = [vp, C.c_int, C.c_int, F32P]
         L.oracle_decoder_set_embedding.argtypes = [vp, F32P]
         L.oracle_decoder_step.argtypes = [vp, C.c_int, C.c_int, vp, vp]
+        L.oracle_decoder_fill_context.argtypes = [vp, C.c_int, C.c_uint64, C.c_int64]
+        L.oracle_decoder_fill_context.restype = C.c_int
         L.oracle_num_threads.restype = C.c_int
         _lib = L
     return _lib
@@ -287,6 +289,13 @@ class OracleDecoder:
     @property
     def position(self) -> int:
         return int(lib().oracle_decoder_position(self._h))
+
+    def fill_context(self, ctx: int, seed: int, seq_id: int):
+        """Synthetic context of a batched-decoding sequence (the same values
+        aexis_cuda_batch_fill_context writes): positions [0, ctx) filled,
+        next position ctx."""
+        if lib().oracle_decoder_fill_context(self._h, int(ctx), int(seed) & (2**64 - 1), int(seq_id)) != 0:
+            raise ValueError("context must be in [0, kv_capacity)")
 
     def step(self, token: int, want_logits: bool = True):
         logits = np.empty(self._c.vocab, dtype=np.float32) if want_logits else None
