@@ -38,7 +38,6 @@ constexpr int kBatThreads = 256;
 constexpr int kBatChunk = 128;        // context positions per attention CTA
 constexpr int kBatMaxGroup = 8;       // query heads per KV head
 constexpr int kBatMaxHeadDim = 256;
-constexpr int kBatMaxQ = 1024;        // query values per KV head (group x head_dim)
 constexpr int kBatMaxCap = 8192;      // positions per sequence
 constexpr int kBatMaxSplits = kBatMaxCap / kBatChunk;
 
@@ -134,32 +133,40 @@ __global__ void bat_rope_kernel(const float* qkv, int rows, const int* rope_map,
 }
 
 // Split attention for sequence b, KV head g, context positions
-// [split * kBatChunk, ...) of ctx = pos[b] + 1: K and V of the chunk arrive by
-// two bulk copies; scores (q . k) * scale, per-split max m, sum l and
-// o = sum e * v; the last CTA of (b, g) merges the splits with weights
-// e^(m_s - M) / sum_s l_s e^(m_s - M). Mathematically the reference's
-// two-pass softmax (HLSL Pack4Matmul:485-547) with GQA kv = h / (H / Hkv).
+// [split * kBatChunk, ...) of ctx = pos[b] + 1, for the HPG query heads of
+// that KV head: K and V of the chunk arrive by two bulk copies; scores
+// (q . k) * scale, per-split max m, sum l and o = sum e * v; the last CTA of
+// (b, g) merges the splits with weights e^(m_s - M) / sum_s l_s e^(m_s - M).
+// Mathematically the reference's two-pass softmax (HLSL Pack4Matmul:485-547)
+// with GQA kv = h / (H / Hkv).
+//   scores: TPP = D / DPT threads per position, DPT = 64 / HPG dims each
+//           (16-byte chunks interleaved so a position's threads read one
+//           contiguous run), the HPG x DPT query values held in registers,
+//           partial dots added by shuffles within the TPP lanes;
+//   values: each thread owns two dims of every head over every VG-th
+//           position; the VG partial sums are added through shared memory.
 // Dynamic shared memory: K and V chunks (2 x kBatChunk x D fp16).
-__global__ void __launch_bounds__(kBatThreads) bat_attn_kernel(const float* q, const __half* kc, const __half* vc,
+template <int HPG>
+__global__ void __launch_bounds__(kBatThreads, 3) bat_attn_kernel(const float* q, const __half* kc, const __half* vc,
                                                                int cap, int D, int n_heads, int kvh, float scale,
                                                                const int* pos, float* part, unsigned int* counters,
                                                                float* out, int* status) {
+    constexpr int DPT = 64 / HPG;
+    constexpr int CH = DPT / 8;  // 16-byte K chunks per thread and position
     extern __shared__ __align__(128) uint8_t smem[];
-    __shared__ float qs[kBatMaxQ];   // [hpg][D]
-    __shared__ float sc[kBatMaxGroup][kBatChunk];
-    __shared__ float stat[kBatMaxGroup][2];
-    __shared__ float wsm[kBatMaxGroup][kBatMaxSplits];
+    __shared__ __align__(16) float sc[kBatChunk][HPG];  // scores, then e = exp(s - m), [p][h]
+    __shared__ float stat[HPG][2];
+    __shared__ float wsm[HPG][kBatMaxSplits];
     __shared__ __align__(8) uint64_t bar;
     __shared__ bool last, ok;
     griddep_wait();
     griddep_launch();
     const int split = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
-    const int hpg = n_heads / kvh;
     const int ctx = pos[b] + 1;
     const int active = (ctx + kBatChunk - 1) / kBatChunk;
     if (split >= active) return;
     const int p0 = split * kBatChunk, p1 = min(ctx, p0 + kBatChunk), np = p1 - p0;
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int tid = threadIdx.x, warp = tid >> 5;
     __half* ks = reinterpret_cast<__half*>(smem);
     __half* vs = ks + (size_t)kBatChunk * D;
     const size_t head_off = ((size_t)b * kvh + g) * cap;
@@ -174,8 +181,20 @@ __global__ void __launch_bounds__(kBatThreads) bat_attn_kernel(const float* q, c
         aexis_dev::bulk_g2s_plain(ks, kc + (head_off + p0) * D, bytes, &bar);
         aexis_dev::bulk_g2s_plain(vs, vc + (head_off + p0) * D, bytes, &bar);
     }
-    for (int i = tid; i < hpg * D; i += kBatThreads)
-        qs[i] = q[((long long)b * n_heads + g * hpg) * D + i];
+    // This thread's query slice: chunks s, s + TPP, ... (8 dims each) of every head.
+    const int tpp = D / DPT;
+    const int slot = tid % tpp;
+    const float* qb = q + ((long long)b * n_heads + g * HPG) * D;
+    float qr[HPG][DPT];
+#pragma unroll
+    for (int h = 0; h < HPG; ++h)
+#pragma unroll
+        for (int j = 0; j < CH; ++j) {
+            const float4 a0 = *reinterpret_cast<const float4*>(qb + h * D + (slot + j * tpp) * 8);
+            const float4 a1 = *reinterpret_cast<const float4*>(qb + h * D + (slot + j * tpp) * 8 + 4);
+            qr[h][j * 8 + 0] = a0.x; qr[h][j * 8 + 1] = a0.y; qr[h][j * 8 + 2] = a0.z; qr[h][j * 8 + 3] = a0.w;
+            qr[h][j * 8 + 4] = a1.x; qr[h][j * 8 + 5] = a1.y; qr[h][j * 8 + 6] = a1.z; qr[h][j * 8 + 7] = a1.w;
+        }
     if (tid == 0) {
         ok = aexis_dev::mbar_wait(&bar, 0);
         if (!ok) aexis_dev::report_timeout(status);  // the copies never completed: nothing is merged
@@ -183,40 +202,46 @@ __global__ void __launch_bounds__(kBatThreads) bat_attn_kernel(const float* q, c
     __syncthreads();
     if (!ok) return;
     aexis_dev::mbar_try_wait(&bar, 0);  // completed phase: acquire the copied bytes in every thread
-    // Scores: one warp per position, each lane four consecutive dims.
-    for (int p = warp; p < np; p += kBatThreads / 32) {
-        float acc[kBatMaxGroup];
+    // Scores. Every lane runs every pass (the shuffles need the whole warp).
+    const int ppp = kBatThreads / tpp;
+    for (int base = 0; base < np; base += ppp) {
+        const int pp = base + tid / tpp;
+        const bool valid = pp < np;
+        float acc[HPG];
 #pragma unroll
-        for (int h = 0; h < kBatMaxGroup; ++h) acc[h] = 0.0f;
-        for (int d = lane * 4; d < D; d += 128) {
-            const uint2 raw = *reinterpret_cast<const uint2*>(ks + (size_t)p * D + d);
-            const float2 k01 = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
-            const float2 k23 = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
+        for (int h = 0; h < HPG; ++h) acc[h] = 0.0f;
 #pragma unroll
-            for (int h = 0; h < kBatMaxGroup; ++h)
-                if (h < hpg)
-                    acc[h] = fmaf(qs[h * D + d + 3], k23.y, fmaf(qs[h * D + d + 2], k23.x,
-                             fmaf(qs[h * D + d + 1], k01.y, fmaf(qs[h * D + d], k01.x, acc[h]))));
+        for (int j = 0; j < CH; ++j) {
+            uint4 raw = make_uint4(0u, 0u, 0u, 0u);
+            if (valid) raw = *reinterpret_cast<const uint4*>(ks + (size_t)pp * D + (slot + j * tpp) * 8);
+            const __half2* k2 = reinterpret_cast<const __half2*>(&raw);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const float2 kf = __half22float2(k2[e]);
+#pragma unroll
+                for (int h = 0; h < HPG; ++h)
+                    acc[h] = fmaf(qr[h][j * 8 + 2 * e + 1], kf.y, fmaf(qr[h][j * 8 + 2 * e], kf.x, acc[h]));
+            }
         }
 #pragma unroll
-        for (int h = 0; h < kBatMaxGroup; ++h) {
-            if (h >= hpg) break;
-            float v = acc[h];
+        for (int h = 0; h < HPG; ++h)
+            for (int o = tpp >> 1; o >= 1; o >>= 1) acc[h] += __shfl_xor_sync(0xffffffffu, acc[h], o);
+        if (valid && slot == 0) {
 #pragma unroll
-            for (int o = 16; o >= 1; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-            if (lane == 0) sc[h][p] = v * scale;
+            for (int h = 0; h < HPG; ++h) sc[pp][h] = acc[h] * scale;
         }
     }
     __syncthreads();
-    for (int h = warp; h < hpg; h += kBatThreads / 32) {
+    for (int h = warp; h < HPG; h += kBatThreads / 32) {
+        const int lane = tid & 31;
         float m = -INFINITY;
-        for (int i = lane; i < np; i += 32) m = fmaxf(m, sc[h][i]);
+        for (int i = lane; i < np; i += 32) m = fmaxf(m, sc[i][h]);
 #pragma unroll
         for (int o = 16; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
         float l = 0.0f;
         for (int i = lane; i < np; i += 32) {
-            const float e = expf(sc[h][i] - m);
-            sc[h][i] = e;
+            const float e = expf(sc[i][h] - m);
+            sc[i][h] = e;
             l += e;
         }
 #pragma unroll
@@ -227,37 +252,46 @@ __global__ void __launch_bounds__(kBatThreads) bat_attn_kernel(const float* q, c
         }
     }
     __syncthreads();
-    // o[h][d] = sum_p e[h][p] v[p][d]: thread groups of D threads split the
-    // positions, then add up through shared memory (the K chunk is free now).
-    const int groups = kBatThreads / D;  // D <= 256
-    const int grp = tid / D, d = tid % D;
-    float o[kBatMaxGroup];
+    // Values.
+    const int dpairs = D >> 1;
+    const int VG = kBatThreads / dpairs;
+    const int dt = tid % dpairs, vg = tid / dpairs;
+    float o0[HPG], o1[HPG];
 #pragma unroll
-    for (int h = 0; h < kBatMaxGroup; ++h) o[h] = 0.0f;
-    if (grp < groups) {
-        for (int p = grp; p < np; p += groups) {
-            const float vv = __half2float(vs[(size_t)p * D + d]);
+    for (int h = 0; h < HPG; ++h) o0[h] = o1[h] = 0.0f;
+    for (int p = vg; p < np; p += VG) {
+        const float2 v = __half22float2(*reinterpret_cast<const __half2*>(vs + (size_t)p * D + 2 * dt));
+        float pr[HPG];
+        if constexpr (HPG % 4 == 0) {
 #pragma unroll
-            for (int h = 0; h < kBatMaxGroup; ++h)
-                if (h < hpg) o[h] = fmaf(sc[h][p], vv, o[h]);
+            for (int h = 0; h < HPG; h += 4) {
+                const float4 t = *reinterpret_cast<const float4*>(&sc[p][h]);
+                pr[h] = t.x; pr[h + 1] = t.y; pr[h + 2] = t.z; pr[h + 3] = t.w;
+            }
+        } else {
+#pragma unroll
+            for (int h = 0; h < HPG; ++h) pr[h] = sc[p][h];
+        }
+#pragma unroll
+        for (int h = 0; h < HPG; ++h) {
+            o0[h] = fmaf(pr[h], v.x, o0[h]);
+            o1[h] = fmaf(pr[h], v.y, o1[h]);
         }
     }
-    float* red = reinterpret_cast<float*>(smem);  // [groups][hpg][D]
-    if (grp < groups) {
+    float* red = reinterpret_cast<float*>(smem);  // [VG][HPG][D] over the K chunk, free now
 #pragma unroll
-        for (int h = 0; h < kBatMaxGroup; ++h)
-            if (h < hpg) red[((size_t)grp * hpg + h) * D + d] = o[h];
-    }
+    for (int h = 0; h < HPG; ++h)
+        *reinterpret_cast<float2*>(red + ((size_t)vg * HPG + h) * D + 2 * dt) = make_float2(o0[h], o1[h]);
     __syncthreads();
     const int stride = D + 2;
-    float* mine = part + ((size_t)(b * n_heads + g * hpg) * kBatMaxSplits + split) * stride;
-    for (int i = tid; i < hpg * D; i += kBatThreads) {
+    float* mine = part + ((size_t)(b * n_heads + g * HPG) * kBatMaxSplits + split) * stride;
+    for (int i = tid; i < HPG * D; i += kBatThreads) {
         const int h = i / D, dd = i % D;
         float acc = 0.0f;
-        for (int gg = 0; gg < groups; ++gg) acc += red[((size_t)gg * hpg + h) * D + dd];
+        for (int gg = 0; gg < VG; ++gg) acc += red[((size_t)gg * HPG + h) * D + dd];
         mine[(size_t)h * kBatMaxSplits * stride + dd] = acc;
     }
-    if (tid < hpg) {
+    if (tid < HPG) {
         float* st = mine + (size_t)tid * kBatMaxSplits * stride + D;
         st[0] = stat[tid][0];
         st[1] = stat[tid][1];
@@ -270,36 +304,47 @@ __global__ void __launch_bounds__(kBatThreads) bat_attn_kernel(const float* q, c
     __syncthreads();
     if (!last) return;
     __threadfence();
-    for (int i = tid; i < hpg * active; i += kBatThreads) {
+    float* ls = reinterpret_cast<float*>(smem);  // [HPG][kBatMaxSplits]
+    for (int i = tid; i < HPG * active; i += kBatThreads) {
         const int h = i / active, s = i % active;
-        const float* st = part + ((size_t)(b * n_heads + g * hpg + h) * kBatMaxSplits + s) * stride + D;
+        const float* st = part + ((size_t)(b * n_heads + g * HPG + h) * kBatMaxSplits + s) * stride + D;
         wsm[h][s] = st[0];
-        reinterpret_cast<float*>(smem)[h * kBatMaxSplits + s] = st[1];
+        ls[h * kBatMaxSplits + s] = st[1];
     }
     __syncthreads();
-    if (tid < hpg) {
-        const float* ls = reinterpret_cast<const float*>(smem) + tid * kBatMaxSplits;
+    if (tid < HPG) {
         float M = -INFINITY;
         for (int s = 0; s < active; ++s) M = fmaxf(M, wsm[tid][s]);
         float L = 0.0f;
         for (int s = 0; s < active; ++s) {
             const float e = expf(wsm[tid][s] - M);
             wsm[tid][s] = e;
-            L += ls[s] * e;
+            L += ls[tid * kBatMaxSplits + s] * e;
         }
         const float inv = 1.0f / fmaxf(L, 1e-20f);
         for (int s = 0; s < active; ++s) wsm[tid][s] *= inv;
     }
     __syncthreads();
-    for (int i = tid; i < hpg * D; i += kBatThreads) {
+    for (int i = tid; i < HPG * D; i += kBatThreads) {
         const int h = i / D, dd = i % D;
-        const float* src = part + (size_t)(b * n_heads + g * hpg + h) * kBatMaxSplits * stride + dd;
+        const float* src = part + (size_t)(b * n_heads + g * HPG + h) * kBatMaxSplits * stride + dd;
         float acc = 0.0f;
 #pragma unroll 8
         for (int s = 0; s < active; ++s) acc = fmaf(wsm[h][s], src[(size_t)s * stride], acc);
-        out[((long long)b * n_heads + g * hpg + h) * D + dd] = acc;
+        out[((long long)b * n_heads + g * HPG + h) * D + dd] = acc;
     }
     if (tid == 0) *cnt = 0u;
+}
+
+// The attention instantiation for a GQA group size (1, 2, 4 or 8).
+const void* attn_kernel_for(int hpg) {
+    switch (hpg) {
+        case 1: return (const void*)bat_attn_kernel<1>;
+        case 2: return (const void*)bat_attn_kernel<2>;
+        case 4: return (const void*)bat_attn_kernel<4>;
+        case 8: return (const void*)bat_attn_kernel<8>;
+        default: return nullptr;
+    }
 }
 
 // token[b] = argmax key's index; out[step][b] = token; pos[b] += 1.
@@ -448,7 +493,7 @@ cudaError_t enqueue_batch_step(aexis_batch* bt, cudaStream_t s, int B) {
             void* args[] = {(void*)&qp, (void*)&kcp, (void*)&vcp, &cap, &hd, &nh, &nkv, &sc, (void*)&pp, &part, &cnt,
                             &o, &status};
             const int splits = (bt->cap + kBatChunk - 1) / kBatChunk;
-            if ((e = launch_pdl((const void*)bat_attn_kernel, dim3(splits, KVH, B), dim3(kBatThreads), attn_smem(D),
+            if ((e = launch_pdl(attn_kernel_for(NH / KVH), dim3(splits, KVH, B), dim3(kBatThreads), attn_smem(D),
                                 s, args)) != cudaSuccess)
                 return e;
         }
@@ -534,8 +579,14 @@ AEXIS_API int aexis_cuda_batch_create(aexis_decoder* d, int max_batch, int kv_ca
     const int D = c.head_dim, qd = c.n_heads * D;
     if (c.hidden % 64 || qd % 64 || c.ffn % 64)
         return aexis_fail(ctx, AEXIS_E_UNSUPPORTED, "hidden, ffn and heads*head_dim must be multiples of 64");
-    if (D % 8 || (c.n_heads / c.n_kv_heads) * D > kBatMaxQ)
-        return aexis_fail(ctx, AEXIS_E_UNSUPPORTED, "head_dim %d (multiple of 8, group x head_dim <= %d)", D, kBatMaxQ);
+    {
+        // Attention layout: group 1, 2, 4 or 8; 64 / group query dims per
+        // thread, head_dim / that a power of two <= 32; head_dim 64..256.
+        const int hpg = c.n_heads / c.n_kv_heads, dpt = 64 / (hpg > 0 ? hpg : 1);
+        const int tpp = D / dpt;
+        if (!attn_kernel_for(hpg) || D < 64 || D > kBatMaxHeadDim || D % dpt || tpp < 1 || tpp > 32 || (tpp & (tpp - 1)))
+            return aexis_fail(ctx, AEXIS_E_UNSUPPORTED, "head_dim %d with %d query heads per KV head", D, hpg);
+    }
     if (max_batch < 1 || max_batch > 128) return aexis_fail(ctx, AEXIS_E_RANGE, "max_batch %d (1..128)", max_batch);
     if (kv_capacity < 1 || kv_capacity > kBatMaxCap)
         return aexis_fail(ctx, AEXIS_E_RANGE, "kv_capacity %d (1..%d)", kv_capacity, kBatMaxCap);
@@ -606,8 +657,9 @@ AEXIS_API int aexis_cuda_batch_create(aexis_decoder* d, int max_batch, int kv_ca
         static size_t configured[64] = {};
         const size_t smem = attn_smem(D);
         if (ctx->device >= 0 && ctx->device < 64 && smem > configured[ctx->device]) {
-            rc = aexis_cuda_check(ctx, cudaFuncSetAttribute(bat_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                            (int)smem), "attention smem");
+            rc = aexis_cuda_check(ctx, cudaFuncSetAttribute(attn_kernel_for(c.n_heads / c.n_kv_heads),
+                                                            cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+                                  "attention smem");
             if (!rc) configured[ctx->device] = smem;
         }
     }

@@ -319,6 +319,13 @@ def run_gpu(args):
         except Exception as e:  # reported, never silently replaced
             decoder = {"error": f"{type(e).__name__}: {e}"}
 
+    config4 = None
+    if not args.skip_config4:
+        try:
+            config4 = bench_config4(ops, peak, world, rank)
+        except Exception as e:
+            config4 = {"error": f"{type(e).__name__}: {e}"}
+
     config5 = None
     if not args.skip_config5:
         try:
@@ -356,6 +363,7 @@ def run_gpu(args):
             "per_shape": per_shape,
             "config1_q8": q8,
             "decoder": decoder,
+            "config4": config4,
             "config5": config5,
             "cpu_baseline": cpu,
             "e2e": {"value": round(e2e_steps * STEP_BYTES * world / e2e_s / 1e9, 2), "unit": "GB/s",
@@ -444,6 +452,63 @@ def bench_decoder(ops, peak, prompt_len: int = 512, new_tokens: int = 64):
             "kernels_per_token": 2 + 5 * cfg.n_layers + 1}
 
 
+def bench_config4(ops, peak, world: int, rank: int, steps: int = 128, total_seqs: int = 256, per_batch: int = 32):
+    """the Q8 decoder of config 3's shape, 256 sequences
+    with contexts U[256, 4096] (seeded), split over the ranks (strong
+    scaling: rank r decodes sequences r*256/G ..), 32 per batch, 128 greedy
+    steps per batch. The contexts are synthetic KV fills (stand-ins for the
+    prefill, outside the timed region); only the decode steps are timed, on
+    the device (CUDA events around each batch's generate call)."""
+    import torch
+    from aiimage_b200.decoder import BatchSession, DecoderSession
+    d = synth.QWEN35_08B_Q8.as_dict()
+    d.update(kv_capacity=256)
+    cfg = synth.DecoderCfg(**d)
+    model = synth.SyntheticDecoder(cfg, seed=4)
+    dec = DecoderSession(ops, cfg).load(model)
+    rng = np.random.default_rng([4, 256, 4096])
+    ctx_all = rng.integers(256, 4097, size=total_seqs).astype(np.int32)
+    first_all = rng.integers(0, cfg.vocab, size=total_seqs).astype(np.int32)
+    lo, hi = rank * total_seqs // world, (rank + 1) * total_seqs // world
+    cap = 4096 + steps
+    batch = BatchSession(dec, max_batch=per_batch, kv_capacity=cap, max_steps=steps)
+    # Warm-up: graph capture and first launches on the first batch.
+    batch.fill_context(ctx_all[lo:lo + per_batch], seed=4, first_seq_id=lo)
+    batch.generate(first_all[lo:lo + per_batch], 3)
+    torch.cuda.synchronize()
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    dev_s, tokens, kv_bytes, first_ids = 0.0, 0, 0, None
+    kv_row = cfg.n_layers * 2 * cfg.n_kv_heads * cfg.head_dim * 2  # K+V bytes per position, all layers
+    for b0 in range(lo, hi, per_batch):
+        b1 = min(hi, b0 + per_batch)
+        batch.fill_context(ctx_all[b0:b1], seed=4, first_seq_id=b0)
+        torch.cuda.synchronize()
+        e0.record()
+        out = batch.generate(first_all[b0:b1], steps)
+        e1.record()
+        e1.synchronize()
+        dev_s += e0.elapsed_time(e1) / 1e3
+        tokens += (b1 - b0) * steps
+        kv_bytes += int(sum(int(c) * steps + steps * (steps + 1) // 2 for c in ctx_all[b0:b1])) * kv_row
+        if first_ids is None:
+            first_ids = out[:4, 0].tolist()
+    total_s = max_over_ranks(dev_s, world)
+    w_bytes = model.weight_bytes_per_token() - cfg.hidden * 2  # linears + norms (embedding rows counted per token)
+    n_steps = (hi - lo + per_batch - 1) // per_batch * steps
+    byts = w_bytes * n_steps + kv_bytes
+    batch.close()
+    dec.close()
+    return {"workload": "config4_q8_decoder_batch32_ctxU256-4096_greedy128", "gpus": world,
+            "scaling": "strong", "sequences": total_seqs, "sequences_this_rank": hi - lo,
+            "tokens_per_s": round(total_seqs * steps / total_s, 1),
+            "tokens_per_s_per_gpu": round(tokens / dev_s, 1),
+            "ms_per_step": round(dev_s / n_steps * 1e3, 4),
+            "bytes_per_step_mean": int(byts / n_steps), "GB/s": round(byts / dev_s / 1e9, 1),
+            "frac": round(byts / dev_s / 1e9 / peak, 3), "first_ids": first_ids,
+            "timing": "device (CUDA events around each batch's generate), max over ranks"}
+
+
 def bench_config5(ops, world: int, rank: int, reps: int = 10):
     """lm_head 151936 x 1024 Q8 per row, batch 256 fp16
     hidden states, greedy argmax + top-50 per row. G > 1: vocab shards with
@@ -520,7 +585,8 @@ def run_only(args):
     --only dominant   W + K launches of the (1024, 151936) Q4 GEMV, rotating
                       over copies larger than L2, no graphs
     --only decoder    the config-3 decoder with --prompt-len / --new-tokens
-    --only tcgemm     the config-5 lm_head GEMM alone (M=256, tensor cores)"""
+    --only tcgemm     the config-5 lm_head GEMM alone (M=256, tensor cores)
+    --only config4    one config-4 batch (32 sequences, --new-tokens steps)"""
     import torch
     torch.cuda.set_device(0)
     from aiimage_b200.ops import AexisOps
@@ -528,6 +594,8 @@ def run_only(args):
     peak, _ = measured_peak()
     if args.only == "decoder":
         out = bench_decoder(ops, peak, args.prompt_len, args.new_tokens)
+    elif args.only == "config4":
+        out = bench_config4(ops, peak, 1, 0, steps=args.new_tokens, total_seqs=32)
     elif args.only == "tcgemm":
         vocab, hidden, m = 151936, 1024, 256
         p, s = synth.q8_weights(vocab, hidden, seed=5, tag=(vocab, hidden))
@@ -613,8 +681,9 @@ def main():
     ap.add_argument("--skip-decoder", action="store_true", help="omit the config-3 decoder measurement")
     ap.add_argument("--skip-cpu", action="store_true", help="omit the CPU oracle baseline")
     ap.add_argument("--skip-config5", action="store_true", help="omit the config-5 lm_head measurement")
+    ap.add_argument("--skip-config4", action="store_true", help="omit the config-4 batched decoder measurement")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
-    ap.add_argument("--only", choices=["dominant", "decoder", "tcgemm"], help="profiling mode (see run_only)")
+    ap.add_argument("--only", choices=["dominant", "decoder", "tcgemm", "config4"], help="profiling mode (see run_only)")
     ap.add_argument("--prompt-len", type=int, default=512)
     ap.add_argument("--new-tokens", type=int, default=64)
     args = ap.parse_args()
