@@ -233,8 +233,21 @@ static int weights_q(aexis_ctx* ctx, int kind, const uint32_t* packed, const voi
     w->scale_bytes = (size_t)nscales * dsize(scale_dtype);
     rc = upload(ctx, packed, w->data_bytes, &w->data, "weight upload");
     if (rc == AEXIS_OK) rc = upload(ctx, scales, w->scale_bytes, &w->scales, "scale upload");
+    // Q4: a second copy in the tensor-core GEMV's fragment layout.
+    if (rc == AEXIS_OK && gemv_mma_eligible(w)) {
+        size_t sb = 0;
+        const size_t wb = gemv_mma_frag_bytes(w, &sb);
+        cudaError_t e = cudaMalloc(&w->frag, wb);
+        if (e == cudaSuccess) e = cudaMalloc(&w->frag_scales, sb);
+        if (e == cudaSuccess) e = launch_repack_q4_frag(w, ctx->stream);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+        rc = aexis_cuda_check(ctx, e, "fragment repack");
+    }
     if (rc) {
         if (w->data) cudaFree(w->data);
+        if (w->scales) cudaFree(w->scales);
+        if (w->frag) cudaFree(w->frag);
+        if (w->frag_scales) cudaFree(w->frag_scales);
         delete w;
         return rc;
     }
@@ -283,6 +296,8 @@ AEXIS_API int aexis_cuda_weights_free(aexis_ctx* ctx, aexis_weights* w) {
     if (w->data) cudaFree(w->data);
     if (w->scales) cudaFree(w->scales);
     if (w->tc_tiled) cudaFree(w->tc_tiled);
+    if (w->frag) cudaFree(w->frag);
+    if (w->frag_scales) cudaFree(w->frag_scales);
     delete w;
     return AEXIS_OK;
 }
@@ -339,6 +354,11 @@ static int gemm_common(aexis_ctx* ctx, const void* a, int a_dtype, int lda, int 
     g.beta = beta;
     g.y_dtype = y_dtype;
     g.epilogue = epi;
+    // Programmatic dependent launch: the GEMV kernels read only the (immutable,
+    // library-owned) weights before waiting on the previous kernel of the
+    // stream, so their weight streaming overlaps that kernel's tail; every read
+    // of x and every write of y comes after the wait.
+    g.pdl = true;
     for (int r = 0; r < m; ++r) {
         g.x = (const char*)a + (size_t)r * lda * dsize(a_dtype);
         g.y = (char*)y + (size_t)r * ldy * dsize(y_dtype);

@@ -24,6 +24,10 @@ struct aexis_weights {
     // Q8 weights repacked into 128-row x 64-k blocks for the tensor-core
     // batched GEMM, built on the first batched call.
     void* tc_tiled = nullptr;
+    // Q4 weights and scales in the MMA-fragment layout of the tensor-core
+    // GEMV (k_gemv_mma.cu), built at upload when the shape allows it.
+    void* frag = nullptr;
+    void* frag_scales = nullptr;
 };
 
 struct aexis_ctx {
@@ -96,6 +100,13 @@ const char* gemv_kernel_name(const aexis_weights* w);
 // The bulk-copy streaming GEMV (k_gemv_stream.cu): whether it takes `w`, and
 // its launch.
 bool gemv_stream_supported(const aexis_weights* w);
+// Tensor-core Q4 GEMV (k_gemv_mma.cu): shapes with a fragment copy (K a
+// multiple of 64, group a multiple of 16); the copy's sizes and builder.
+bool gemv_mma_eligible(const aexis_weights* w);
+size_t gemv_mma_frag_bytes(const aexis_weights* w, size_t* scale_bytes);
+cudaError_t launch_repack_q4_frag(const aexis_weights* w, cudaStream_t s);
+bool gemv_mma_supported(const aexis_weights* w, int a_dtype);
+cudaError_t launch_gemv_mma(const GemvArgs& a, int sm_count, cudaStream_t stream);
 cudaError_t launch_gemv_stream(const GemvArgs& a, int sm_count, int* status, cudaStream_t stream);
 // Bytes of padding after every weight and scale allocation: bulk copies of a
 // partial last tile round their size up to 16 bytes.

@@ -395,6 +395,7 @@ int fast_scale_mode(const aexis_weights* w, int* gshift) {
 }  // namespace
 
 const char* gemv_kernel_name(const aexis_weights* w) {
+    if (gemv_mma_supported(w, AEXIS_F16)) return "q4_mma";
     if (gemv_stream_supported(w)) return w->kind == WK_Q4 ? "q4_stream" : "q8_stream";
     int gs;
     if (fast_scale_mode(w, &gs) < 0) return "generic";
@@ -403,6 +404,7 @@ const char* gemv_kernel_name(const aexis_weights* w) {
 
 cudaError_t launch_gemv(const GemvArgs& a, int sm_count, cudaStream_t stream) {
     const aexis_weights* w = a.w;
+    if (gemv_mma_supported(w, a.a_dtype)) return launch_gemv_mma(a, sm_count, stream);
     if (gemv_stream_supported(w)) return launch_gemv_stream(a, sm_count, a.status, stream);
     int gshift = 0;
     const int smode = fast_scale_mode(w, &gshift);

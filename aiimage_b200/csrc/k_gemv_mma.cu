@@ -1,0 +1,459 @@
+// k_gemv_mma.cu -- batch-1 Q4 dequant GEMV with the multiply-accumulate on
+// the tensor cores (mma.m16n8k16, fp16 x fp16 -> fp32).
+//
+// Same contract as the CUDA-core kernels (AexisGemm2DPack4LinearTexture-
+// AFromLinear / ...Tiled..., HLSL Pack4Matmul:1038-1104, 2245-2300, weight
+// read AexisGemm2DReadB :707-734). The CUDA-core decode spends about four
+// instructions per weight (isolate, exact magic-number subtract, FMA, plus
+// overhead) and cannot keep up with HBM. Here the weights are the A operand of
+// m16n8k16 MMAs: a 4-bit value and an fp16 activation are both exact in fp16,
+// the products are exact and the sums are fp32, so the arithmetic keeps the
+// reference's fp32 semantics up to summation order. Per 8 weights a thread
+// spends one shift, four LOP3 (nibble pairs under the fp16 exponent of 1024)
+// and four HADD2/HFMA2 (exact removal of the offset), plus one MMA.
+//
+// Layout (built from the reference packing at upload, launch_repack_q4_frag):
+//   * weights: 16-row tiles; per tile and per four k16 blocks, 32 lanes x 16
+//     bytes, the word of k16 block kb for lane L holding the 8 nibbles of its
+//     A fragment (rows L/4 and L/4+8, columns 2(L%4), +1, +8, +9) as offset-
+//     binary values u = q + 8, in slots (bit 4i) a0.lo a1.lo a2.lo a3.lo a0.hi
+//     a1.hi a2.hi a3.hi;
+//   * scales: per tile [group][16 rows].
+// Both are padded to a multiple of 8 tiles (rows past n decode to zero).
+//
+// Kernel: a producer warp bulk-copies one 16-row tile (weights and scales)
+// per ring stage; the 8 consumer warps form 8 / KW groups that take the
+// stages in turn, the KW warps of a group splitting K (KW = 1 for large N:
+// one warp per tile, no cross-warp reduction). Each
+// scale group accumulates in a fresh fp32 fragment and is added to the row sum
+// with its scale (fp32 FMA). fp32 activations ride as fp16 hi + lo (two MMAs).
+// The activation vector is staged once in fragment order (optionally through
+// the fused RMSNorm); only lanes 0-3 carry it (column 0 of B), the others
+// multiply zeros. Every barrier wait is bounded.
+#include "gemv_stream.cuh"
+
+namespace {
+
+using namespace aexis_dev;
+
+constexpr int kMW = 8;                     // consumer warps
+constexpr int kMmaThreads = (kMW + 1) * 32;
+
+struct MmaParams {
+    StreamParams sp;       // W / S: fragment-layout copies; n, k, x, epilogue fields as for the stream kernel
+    int nkb;               // K / 16
+    int gk;                // k16 blocks per scale group
+    int tile_wbytes, tile_sbytes;
+    int units;             // 16-row tiles (one per ring stage)
+    int ring_stages, stage_bytes;
+};
+
+// Repack: one thread per (tile, k16 block, lane) word.
+template <typename ST>
+__global__ void repack_q4_frag_kernel(const uint32_t* src, const ST* scales, int n, int k, int group, int ntiles_pad,
+                                      uint32_t* dst, ST* dst_s) {
+    const int nkb = k / 16;
+    const int kw = k / 8;  // source words per row
+    const long long total = (long long)ntiles_pad * nkb * 32;
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += (long long)gridDim.x * blockDim.x) {
+        const int lane = (int)(i & 31);
+        const int kb = (int)((i >> 5) % nkb);
+        const long long t = (i >> 5) / nkb;
+        const int g = lane >> 2, tig = lane & 3;
+        const long long r0 = t * 16 + g, r1 = r0 + 8;
+        const int k0 = kb * 16 + 2 * tig;
+        auto u = [&](long long r, int kk) -> uint32_t {
+            if (r >= n) return 8u;
+            const uint32_t wd = src[r * kw + (kk >> 3)];
+            return ((wd >> (4 * (kk & 7))) & 15u) ^ 8u;
+        };
+        const uint32_t word = u(r0, k0) | (u(r1, k0) << 4) | (u(r0, k0 + 8) << 8) | (u(r1, k0 + 8) << 12) |
+                              (u(r0, k0 + 1) << 16) | (u(r1, k0 + 1) << 20) | (u(r0, k0 + 9) << 24) |
+                              (u(r1, k0 + 9) << 28);
+        dst[(t * nkb + (kb >> 2) * 4) * 32 + (long long)lane * 4 + (kb & 3)] = word;
+    }
+    // Scales: [tile][group][16].
+    const int ng = group > 0 ? k / group : 1;
+    const long long stotal = (long long)ntiles_pad * ng * 16;
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < stotal;
+         i += (long long)gridDim.x * blockDim.x) {
+        const int row16 = (int)(i & 15);
+        const int grp = (int)((i >> 4) % ng);
+        const long long t = (i >> 4) / ng;
+        const long long r = t * 16 + row16;
+        dst_s[i] = r < n ? scales[r * ng + grp] : ST(0.0f);
+    }
+}
+
+__device__ __forceinline__ uint32_t lop3_f16pair(uint32_t q, uint32_t mask) {
+    uint32_t r;
+    asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(r) : "r"(q), "r"(mask), "r"(0x64006400u));  // (q & mask) | c
+    return r;
+}
+
+// The A fragment of one k16 block from its packed word: fp16 pairs of q.
+__device__ __forceinline__ void decode_frag(uint32_t q, uint32_t (&a)[4]) {
+    const __half2 off = __halves2half2(__ushort_as_half(0x6408), __ushort_as_half(0x6408));     // 1032
+    const __half2 inv16 = __halves2half2(__ushort_as_half(0x2C00), __ushort_as_half(0x2C00));   // 1/16
+    const __half2 off16 = __halves2half2(__ushort_as_half(0xD480), __ushort_as_half(0xD480));   // -72
+    const uint32_t q8 = q >> 8;
+    uint32_t t0 = lop3_f16pair(q, 0x000F000Fu), t1 = lop3_f16pair(q, 0x00F000F0u);
+    uint32_t t2 = lop3_f16pair(q8, 0x000F000Fu), t3 = lop3_f16pair(q8, 0x00F000F0u);
+    __half2 h0 = __hsub2(*reinterpret_cast<__half2*>(&t0), off);           // (1024 + u) - 1032 = q
+    __half2 h1 = __hfma2(*reinterpret_cast<__half2*>(&t1), inv16, off16);  // (1024 + 16u) / 16 - 72 = q
+    __half2 h2 = __hsub2(*reinterpret_cast<__half2*>(&t2), off);
+    __half2 h3 = __hfma2(*reinterpret_cast<__half2*>(&t3), inv16, off16);
+    a[0] = *reinterpret_cast<uint32_t*>(&h0);
+    a[1] = *reinterpret_cast<uint32_t*>(&h1);
+    a[2] = *reinterpret_cast<uint32_t*>(&h2);
+    a[3] = *reinterpret_cast<uint32_t*>(&h3);
+}
+
+__device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], uint2 b) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b.x), "r"(b.y));
+}
+
+// ST scale type; XF 1: fp16 activations, 2: fp32 as fp16 hi + lo; KW warps
+// per tile (K split).
+template <typename ST, int XF, int KW>
+__global__ void __launch_bounds__(kMmaThreads, 1) gemv_mma_kernel(MmaParams mp) {
+    constexpr int NG = kMW / KW;  // warp groups; group it % NG takes unit it
+    const StreamParams& p = mp.sp;
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int S = mp.ring_stages;
+    uint8_t* ring = smem;
+    uint2* xs = reinterpret_cast<uint2*>(smem + (size_t)S * mp.stage_bytes);  // [XF][nkb * 4] B fragments
+    float* red = reinterpret_cast<float*>(xs + (size_t)XF * mp.nkb * 4);       // [2][kMW][16]
+    uint64_t* full = reinterpret_cast<uint64_t*>(red + 2 * kMW * 16);
+    uint64_t* empty = full + S;
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + S);
+    float* redn = reinterpret_cast<float*>(const_cast<int*>(abort_flag) + 4);  // [kMW] RMSNorm partials
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int my_units = (int)blockIdx.x < mp.units ? (mp.units - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(full + s, 1);
+            mbar_init(empty + s, KW);
+        }
+        *abort_flag = 0;
+        fence_barrier_init();
+    }
+    __syncthreads();
+
+    if (warp == kMW) {
+        // ------------------------------------------------------------ producer
+        if (lane == 0) {
+            const uint64_t pol = policy_evict_first();
+            const uint32_t wb = (uint32_t)mp.tile_wbytes, sb = (uint32_t)mp.tile_sbytes;
+            int issued = 0;
+            for (int it = 0; it < my_units; ++it) {
+                const int s = it % S;
+                if (it >= S && !mbar_wait(empty + s, ((it / S) & 1) ^ 1)) {
+                    report_timeout(p.status);
+                    break;
+                }
+                if (*abort_flag) break;
+                const size_t u = (size_t)blockIdx.x + (size_t)it * gridDim.x;
+                uint8_t* dst = ring + (size_t)s * mp.stage_bytes;
+                mbar_arrive_expect_tx(full + s, wb + sb);
+                bulk_g2s(dst, p.W + u * wb, wb, full + s, pol);
+                bulk_g2s(dst + wb, p.S + u * sb, sb, full + s, pol);
+                ++issued;
+            }
+            for (int it = max(0, issued - S); it < issued; ++it)
+                if (!mbar_wait(full + it % S, (it / S) & 1)) { report_timeout(p.status); break; }
+        }
+        return;
+    }
+
+    // -------------------------------------------------------------- consumers
+    griddep_wait();
+    {
+        // x -> B fragments: element e of k16 block kb sits in lane t = (e % 8) / 2,
+        // register e / 8, half e % 2 (fp16 hi, and lo for XF 2), optionally
+        // RMS-normalised first (the fused RMSNorm layer).
+        const int tid = threadIdx.x;
+        const bool norm = p.norm_gamma != nullptr;
+        float inv = 1.0f;
+        if (norm) {
+            float ss = 0.0f;
+            for (int i = tid; i < p.k; i += kMW * 32) {
+                const float v = aexis_load_act(p.x, p.a_dtype, i);
+                ss = fmaf(v, v, ss);
+            }
+#pragma unroll
+            for (int o = 16; o >= 1; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+            if (lane == 0) redn[warp] = ss;
+            named_sync(1, kMW * 32);
+            float tot = 0.0f;
+#pragma unroll
+            for (int w = 0; w < kMW; ++w) tot += redn[w];
+            inv = 1.0f / sqrtf(fmaxf(tot / (float)p.k + p.norm_eps, 1e-20f));
+        }
+        __half* xh = reinterpret_cast<__half*>(xs);
+        for (int e = tid; e < p.k; e += kMW * 32) {
+            float v = aexis_load_act(p.x, p.a_dtype, e);
+            if (norm) v = v * inv * p.norm_gamma[e];
+            const int kb = e >> 4, w16 = e & 15;
+            const int slot = ((kb * 4 + ((w16 & 7) >> 1)) * 2 + (w16 >> 3)) * 2 + (w16 & 1);
+            const __half hi = __float2half_rn(v);
+            xh[slot] = hi;
+            if constexpr (XF == 2) xh[(size_t)mp.nkb * 16 + slot] = __float2half_rn(v - __half2float(hi));
+        }
+        named_sync(1, kMW * 32);
+    }
+    griddep_launch();
+
+    const int grp = warp / KW, ks = warp % KW;
+    const int kb_per = mp.nkb / KW;
+    const int kb0 = ks * kb_per;
+    const int g = lane >> 2, tig = lane & 3;
+    const bool bl = lane < 4;  // lanes holding column 0 of B
+    unsigned long long best_key = 0ull;
+
+    int local = 0;
+    for (int it = grp; it < my_units; it += NG, ++local) {
+        const int s = it % S;
+        const bool ready = mbar_wait(full + s, (it / S) & 1);
+        if (!ready) {
+            report_timeout(p.status);
+            *abort_flag = 1;
+        }
+        const size_t u = (size_t)blockIdx.x + (size_t)it * gridDim.x;  // 16-row tile
+        const uint8_t* wt = ring + (size_t)s * mp.stage_bytes;
+        const ST* st = reinterpret_cast<const ST*>(wt + mp.tile_wbytes);
+        float y0 = 0.0f, y1 = 0.0f;  // rows g and g + 8 (column 0: lanes with tig == 0)
+        if (ready) {
+            float c[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+            // Scale group of the current block, tracked without divisions:
+            // gi = kk / gk, gpos = kk % gk (the range starts on a group boundary
+            // or, with one scale per row, holds part of the single group).
+            int gi = kb0 / mp.gk, gpos = kb0 - gi * mp.gk;
+            for (int kb = kb0; kb < kb0 + kb_per; kb += 4) {
+                const uint4 wq = *reinterpret_cast<const uint4*>(wt + ((size_t)(kb >> 2) * 32 + lane) * 16);
+                const uint32_t words[4] = {wq.x, wq.y, wq.z, wq.w};
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    uint32_t a[4];
+                    decode_frag(words[j], a);
+                    const int kk = kb + j;
+                    uint2 b = make_uint2(0u, 0u);
+                    if (bl) b = xs[kk * 4 + lane];
+                    mma16816(c, a, b);
+                    if constexpr (XF == 2) {
+                        uint2 b2 = make_uint2(0u, 0u);
+                        if (bl) b2 = xs[(size_t)mp.nkb * 4 + kk * 4 + lane];
+                        mma16816(c, a, b2);
+                    }
+                    if (++gpos == mp.gk) {
+                        y0 = fmaf(c[0], to_float(st[gi * 16 + g]), y0);
+                        y1 = fmaf(c[2], to_float(st[gi * 16 + g + 8]), y1);
+                        c[0] = c[1] = c[2] = c[3] = 0.0f;
+                        gpos = 0;
+                        ++gi;
+                    }
+                }
+            }
+            if (gpos != 0) {  // one scale per row: this warp's share of the single group
+                y0 = fmaf(c[0], to_float(st[g]), y0);
+                y1 = fmaf(c[2], to_float(st[g + 8]), y1);
+            }
+        }
+        __syncwarp();
+        if (ready && lane == 0) mbar_arrive(empty + s);
+
+        // Add the KW partials of each row (KW > 1), then the epilogue (lanes
+        // 0-15 of the group's first warp; the pair partner of row r is r ^ 1).
+        float* rb = red + ((local & 1) * NG + grp) * KW * 16;
+        if (tig == 0) {
+            rb[ks * 16 + g] = y0;
+            rb[ks * 16 + g + 8] = y1;
+        }
+        if constexpr (KW > 1) named_sync(2 + grp, KW * 32);
+        else __syncwarp();
+        if (*abort_flag) break;
+        if (ks == 0) {
+            float v = 0.0f;
+            if (lane < 16)
+#pragma unroll
+                for (int w = 0; w < KW; ++w) v += rb[w * 16 + lane];
+            const float partner = __shfl_xor_sync(0xffffffffu, v, 1);
+            const long long row = (long long)u * 16 + lane;
+            if (lane < 16 && row < p.n) epilogue(p, (int)row, v, partner, best_key);
+        }
+    }
+    if (p.epi == EPI_LOGITS_ARGMAX) {
+#pragma unroll
+        for (int o = 16; o >= 1; o >>= 1) {
+            const unsigned long long other = __shfl_xor_sync(0xffffffffu, best_key, o);
+            best_key = other > best_key ? other : best_key;
+        }
+        if (lane == 0 && best_key != 0ull) atomicMax(p.argmax_key, best_key);
+    }
+}
+
+struct MmaPlan {
+    int kw = 0, units = 0, stages = 0, stage_bytes = 0, smem = 0, per_sm = 1;
+};
+
+int frag_tiles_padded(int n) { return ((n + 15) / 16 + 7) / 8 * 8; }
+
+int scale_groups(const aexis_weights* w) { return w->group > 0 ? w->k / w->group : 1; }
+
+// K split: enough (tile, K-share) units for every consumer warp of two CTAs
+// per SM (KW = 1 when the tiles alone suffice; up to 8 warps on one tile for
+// small N), within the alignment the fragment layout and the scale groups
+// allow. Ring: one tile per stage, as deep as the shared-memory budget of two
+// CTAs per SM allows (at least 3), else one CTA per SM.
+bool plan_mma(const aexis_weights* w, int xf, int sm_count, MmaPlan& pl) {
+    const int nkb = w->k / 16;
+    const int gk = w->group > 0 ? w->group / 16 : nkb;
+    const int ntiles = (w->n + 15) / 16;
+    const int st = w->scale_dtype == AEXIS_F16 ? 2 : 4;
+    const int stage = 8 * w->k + scale_groups(w) * 16 * st;
+    const int fixed = xf * nkb * 32 + 2 * kMW * 16 * 4 + 16 * 16 + 64 + kMW * 4 + 128;
+    const int want = 2 * sm_count * kMW;  // warp units that fill two CTAs per SM
+    int kw = 1;
+    while (kw < 8 && (long long)ntiles * kw < want) kw <<= 1;
+    for (; kw >= 1; kw >>= 1) {
+        if (nkb % (kw * 4) != 0) continue;
+        if ((nkb / kw) % gk != 0 && gk != nkb) continue;
+        break;
+    }
+    if (kw < 1) return false;
+    for (int per_sm = 2; per_sm >= 1; --per_sm) {
+        const int budget = per_sm == 2 ? 113 * 1024 : 227 * 1024;
+        int S = (budget - fixed) / stage;
+        S = S > 16 ? 16 : S;
+        if (S < (per_sm == 2 ? 3 : 2)) continue;
+        pl.kw = kw;
+        pl.units = ntiles;
+        pl.stages = S;
+        pl.stage_bytes = stage;
+        pl.smem = S * stage + fixed;
+        pl.per_sm = per_sm;
+        return true;
+    }
+    return false;
+}
+
+template <typename ST, int XF, int KW>
+cudaError_t launch_mma_t(const MmaParams& mp, int grid, int smem, bool pdl, cudaStream_t stream) {
+    static int configured[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    if (smem > configured[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(gemv_mma_kernel<ST, XF, KW>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e != cudaSuccess) return e;
+        configured[dev] = smem;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kMmaThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, gemv_mma_kernel<ST, XF, KW>, mp);
+}
+
+template <typename ST, int XF>
+cudaError_t launch_mma_kw(const MmaParams& mp, int kw, int grid, int smem, bool pdl, cudaStream_t s) {
+    switch (kw) {
+        case 1: return launch_mma_t<ST, XF, 1>(mp, grid, smem, pdl, s);
+        case 2: return launch_mma_t<ST, XF, 2>(mp, grid, smem, pdl, s);
+        case 4: return launch_mma_t<ST, XF, 4>(mp, grid, smem, pdl, s);
+        default: return launch_mma_t<ST, XF, 8>(mp, grid, smem, pdl, s);
+    }
+}
+
+}  // namespace
+
+bool gemv_mma_eligible(const aexis_weights* w) {
+    if (w->kind != WK_Q4 || w->k % 64 != 0 || w->n <= 0) return false;
+    if (w->group > 0 && (w->group % 16 != 0 || w->k % w->group != 0)) return false;
+    MmaPlan pl;
+    return plan_mma(w, 2, 148, pl);
+}
+
+size_t gemv_mma_frag_bytes(const aexis_weights* w, size_t* scale_bytes) {
+    const size_t tiles = (size_t)frag_tiles_padded(w->n);
+    if (scale_bytes)
+        *scale_bytes = tiles * scale_groups(w) * 16 * (w->scale_dtype == AEXIS_F16 ? 2 : 4);
+    return tiles * 8 * (size_t)w->k;
+}
+
+cudaError_t launch_repack_q4_frag(const aexis_weights* w, cudaStream_t s) {
+    const int tiles = frag_tiles_padded(w->n);
+    if (w->scale_dtype == AEXIS_F16)
+        repack_q4_frag_kernel<__half><<<148 * 8, 256, 0, s>>>(
+            reinterpret_cast<const uint32_t*>(w->data), reinterpret_cast<const __half*>(w->scales), w->n, w->k,
+            w->group, tiles, reinterpret_cast<uint32_t*>(w->frag), reinterpret_cast<__half*>(w->frag_scales));
+    else
+        repack_q4_frag_kernel<float><<<148 * 8, 256, 0, s>>>(
+            reinterpret_cast<const uint32_t*>(w->data), reinterpret_cast<const float*>(w->scales), w->n, w->k,
+            w->group, tiles, reinterpret_cast<uint32_t*>(w->frag), reinterpret_cast<float*>(w->frag_scales));
+    return cudaGetLastError();
+}
+
+bool gemv_mma_supported(const aexis_weights* w, int a_dtype) {
+    return w->frag && w->frag_scales && (a_dtype == AEXIS_F16 || a_dtype == AEXIS_F32);
+}
+
+cudaError_t launch_gemv_mma(const GemvArgs& a, int sm_count, cudaStream_t stream) {
+    const aexis_weights* w = a.w;
+    const int xf = a.a_dtype == AEXIS_F16 ? 1 : 2;
+    MmaPlan pl;
+    if (!plan_mma(w, xf, sm_count, pl)) return cudaErrorNotSupported;
+    MmaParams mp = {};
+    StreamParams& sp = mp.sp;
+    sp.W = reinterpret_cast<const uint8_t*>(w->frag);
+    sp.S = reinterpret_cast<const uint8_t*>(w->frag_scales);
+    sp.n = w->n;
+    sp.k = w->k;
+    sp.x = a.x;
+    sp.a_dtype = a.a_dtype;
+    sp.norm_gamma = a.norm_gamma;
+    sp.norm_eps = a.norm_eps;
+    sp.bias = a.bias;
+    sp.alpha = a.alpha;
+    sp.beta = a.beta;
+    sp.y = a.y;
+    sp.y_dtype = a.y_dtype;
+    sp.epi = a.epilogue;
+    sp.rope_cos = a.rope_cos;
+    sp.rope_sin = a.rope_sin;
+    sp.rope_map = a.rope_map;
+    sp.k_cache = a.k_cache;
+    sp.v_cache = a.v_cache;
+    sp.head_dim = a.head_dim;
+    sp.kv_cap = a.kv_cap;
+    sp.rot_dim = a.rot_dim;
+    sp.pos_ptr = a.pos_ptr;
+    sp.argmax_key = a.argmax_key;
+    sp.status = a.status;
+    mp.nkb = w->k / 16;
+    mp.gk = w->group > 0 ? w->group / 16 : mp.nkb;
+    mp.tile_wbytes = 8 * w->k;
+    mp.tile_sbytes = scale_groups(w) * 16 * (w->scale_dtype == AEXIS_F16 ? 2 : 4);
+    mp.units = pl.units;
+    mp.ring_stages = pl.stages;
+    mp.stage_bytes = pl.stage_bytes;
+    const int grid = pl.units < pl.per_sm * sm_count ? pl.units : pl.per_sm * sm_count;
+    if (w->scale_dtype == AEXIS_F16) {
+        if (xf == 1) return launch_mma_kw<__half, 1>(mp, pl.kw, grid, pl.smem, a.pdl, stream);
+        return launch_mma_kw<__half, 2>(mp, pl.kw, grid, pl.smem, a.pdl, stream);
+    }
+    if (xf == 1) return launch_mma_kw<float, 1>(mp, pl.kw, grid, pl.smem, a.pdl, stream);
+    return launch_mma_kw<float, 2>(mp, pl.kw, grid, pl.smem, a.pdl, stream);
+}
