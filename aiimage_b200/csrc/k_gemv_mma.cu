@@ -18,7 +18,7 @@
 //     A fragment (rows L/4 and L/4+8, columns 2(L%4), +1, +8, +9) as offset-
 //     binary values u = q + 8, in slots (bit 4i) a0.lo a1.lo a2.lo a3.lo a0.hi
 //     a1.hi a2.hi a3.hi;
-//   * scales: per tile [group][16 rows].
+//   * scales: per tile [group][8][2], the scales of rows r and r + 8 adjacent.
 // Both are padded to a multiple of 8 tiles (rows past n decode to zero).
 //
 // Kernel: a producer warp bulk-copies one 16-row tile (weights and scales)
@@ -73,12 +73,12 @@ __global__ void repack_q4_frag_kernel(const uint32_t* src, const ST* scales, int
                               (u(r1, k0 + 9) << 28);
         dst[(t * nkb + (kb >> 2) * 4) * 32 + (long long)lane * 4 + (kb & 3)] = word;
     }
-    // Scales: [tile][group][16].
+    // Scales: [tile][group][8][2], rows g and g + 8 adjacent.
     const int ng = group > 0 ? k / group : 1;
     const long long stotal = (long long)ntiles_pad * ng * 16;
     for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < stotal;
          i += (long long)gridDim.x * blockDim.x) {
-        const int row16 = (int)(i & 15);
+        const int row16 = (int)((i >> 1) & 7) + 8 * (int)(i & 1);
         const int grp = (int)((i >> 4) % ng);
         const long long t = (i >> 4) / ng;
         const long long r = t * 16 + row16;
@@ -118,17 +118,39 @@ __device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], 
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b.x), "r"(b.y));
 }
 
+// d = a b (accumulator input zero).
+__device__ __forceinline__ void mma16816_zc(float (&c)[4], const uint32_t (&a)[4], uint2 b) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%10, %10, %10, %10};"
+        : "=f"(c[0]), "=f"(c[1]), "=f"(c[2]), "=f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b.x), "r"(b.y), "f"(0.0f));
+}
+
+// Scales of rows g and g + 8 (adjacent in the fragment layout).
+__device__ __forceinline__ void load_scale_pair(const __half* p, float& s0, float& s1) {
+    const __half2 h = *reinterpret_cast<const __half2*>(p);
+    s0 = __low2float(h);
+    s1 = __high2float(h);
+}
+__device__ __forceinline__ void load_scale_pair(const float* p, float& s0, float& s1) {
+    const float2 f = *reinterpret_cast<const float2*>(p);
+    s0 = f.x;
+    s1 = f.y;
+}
+
 // ST scale type; XF 1: fp16 activations, 2: fp32 as fp16 hi + lo; KW warps
-// per tile (K split).
-template <typename ST, int XF, int KW>
-__global__ void __launch_bounds__(kMmaThreads, 1) gemv_mma_kernel(MmaParams mp) {
+// per tile (K split); GK 2: scale groups of two k16 blocks (group 32) with
+// static group ends, 0: any group length (tracked at run time).
+template <typename ST, int XF, int KW, int GK>
+__global__ void __launch_bounds__(kMmaThreads, 2) gemv_mma_kernel(MmaParams mp) {
     constexpr int NG = kMW / KW;  // warp groups; group it % NG takes unit it
     const StreamParams& p = mp.sp;
     extern __shared__ __align__(128) uint8_t smem[];
     const int S = mp.ring_stages;
     uint8_t* ring = smem;
     uint2* xs = reinterpret_cast<uint2*>(smem + (size_t)S * mp.stage_bytes);  // [XF][nkb * 4] B fragments
-    float* red = reinterpret_cast<float*>(xs + (size_t)XF * mp.nkb * 4);       // [2][kMW][16]
+    float* red = reinterpret_cast<float*>(xs + (size_t)XF * mp.nkb * 4 + 4);   // after a 32-byte zero block: [2][kMW][16]
     uint64_t* full = reinterpret_cast<uint64_t*>(red + 2 * kMW * 16);
     uint64_t* empty = full + S;
     volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + S);
@@ -196,16 +218,19 @@ __global__ void __launch_bounds__(kMmaThreads, 1) gemv_mma_kernel(MmaParams mp) 
             for (int w = 0; w < kMW; ++w) tot += redn[w];
             inv = 1.0f / sqrtf(fmaxf(tot / (float)p.k + p.norm_eps, 1e-20f));
         }
+        // Fragment order: for every four k16 blocks, lane t (0..3) owns 32
+        // contiguous bytes (blocks kb..kb+3, registers b0 b1 each).
         __half* xh = reinterpret_cast<__half*>(xs);
         for (int e = tid; e < p.k; e += kMW * 32) {
             float v = aexis_load_act(p.x, p.a_dtype, e);
             if (norm) v = v * inv * p.norm_gamma[e];
             const int kb = e >> 4, w16 = e & 15;
-            const int slot = ((kb * 4 + ((w16 & 7) >> 1)) * 2 + (w16 >> 3)) * 2 + (w16 & 1);
+            const int slot = (((((kb >> 2) * 4 + ((w16 & 7) >> 1)) * 4 + (kb & 3)) * 2) + (w16 >> 3)) * 2 + (w16 & 1);
             const __half hi = __float2half_rn(v);
             xh[slot] = hi;
             if constexpr (XF == 2) xh[(size_t)mp.nkb * 16 + slot] = __float2half_rn(v - __half2float(hi));
         }
+        if (tid < 8) reinterpret_cast<uint32_t*>(xs + (size_t)XF * mp.nkb * 4)[tid] = 0u;  // zero block
         named_sync(1, kMW * 32);
     }
     griddep_launch();
@@ -214,7 +239,12 @@ __global__ void __launch_bounds__(kMmaThreads, 1) gemv_mma_kernel(MmaParams mp) 
     const int kb_per = mp.nkb / KW;
     const int kb0 = ks * kb_per;
     const int g = lane >> 2, tig = lane & 3;
-    const bool bl = lane < 4;  // lanes holding column 0 of B
+    // B fragment sources: lanes 0-3 read their column-0 slice, the others a
+    // zero block (column 1..7 of B), so every lane loads unconditionally.
+    const uint4* xzero = reinterpret_cast<const uint4*>(xs + (size_t)XF * mp.nkb * 4);
+    const uint4* xhi = lane < 4 ? reinterpret_cast<const uint4*>(xs) + lane * 2 : xzero;
+    const uint4* xlo = lane < 4 ? reinterpret_cast<const uint4*>(xs + (size_t)mp.nkb * 4) + lane * 2 : xzero;
+    const int xstep = lane < 4 ? 8 : 0;  // uint4 per four blocks
     unsigned long long best_key = 0ull;
 
     int local = 0;
@@ -227,42 +257,61 @@ __global__ void __launch_bounds__(kMmaThreads, 1) gemv_mma_kernel(MmaParams mp) 
         }
         const size_t u = (size_t)blockIdx.x + (size_t)it * gridDim.x;  // 16-row tile
         const uint8_t* wt = ring + (size_t)s * mp.stage_bytes;
-        const ST* st = reinterpret_cast<const ST*>(wt + mp.tile_wbytes);
+        // Scales: [group][8][2], the pair (row g, row g + 8) adjacent.
+        const ST* st = reinterpret_cast<const ST*>(wt + mp.tile_wbytes) + g * 2;
         float y0 = 0.0f, y1 = 0.0f;  // rows g and g + 8 (column 0: lanes with tig == 0)
         if (ready) {
             float c[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-            // Scale group of the current block, tracked without divisions:
-            // gi = kk / gk, gpos = kk % gk (the range starts on a group boundary
-            // or, with one scale per row, holds part of the single group).
-            int gi = kb0 / mp.gk, gpos = kb0 - gi * mp.gk;
+            int gi = kb0 / mp.gk, gpos = kb0 - gi * mp.gk;  // runtime group tracking (GK == 0)
+#pragma unroll 2
             for (int kb = kb0; kb < kb0 + kb_per; kb += 4) {
                 const uint4 wq = *reinterpret_cast<const uint4*>(wt + ((size_t)(kb >> 2) * 32 + lane) * 16);
+                const uint4 bh01 = xhi[(kb >> 2) * xstep], bh23 = xhi[(kb >> 2) * xstep + 1];
+                uint4 bl01 = make_uint4(0u, 0u, 0u, 0u), bl23 = bl01;
+                if constexpr (XF == 2) {
+                    bl01 = xlo[(kb >> 2) * xstep];
+                    bl23 = xlo[(kb >> 2) * xstep + 1];
+                }
                 const uint32_t words[4] = {wq.x, wq.y, wq.z, wq.w};
+                const uint2 bh[4] = {make_uint2(bh01.x, bh01.y), make_uint2(bh01.z, bh01.w),
+                                     make_uint2(bh23.x, bh23.y), make_uint2(bh23.z, bh23.w)};
+                const uint2 blo[4] = {make_uint2(bl01.x, bl01.y), make_uint2(bl01.z, bl01.w),
+                                      make_uint2(bl23.x, bl23.y), make_uint2(bl23.z, bl23.w)};
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
                     uint32_t a[4];
                     decode_frag(words[j], a);
-                    const int kk = kb + j;
-                    uint2 b = make_uint2(0u, 0u);
-                    if (bl) b = xs[kk * 4 + lane];
-                    mma16816(c, a, b);
-                    if constexpr (XF == 2) {
-                        uint2 b2 = make_uint2(0u, 0u);
-                        if (bl) b2 = xs[(size_t)mp.nkb * 4 + kk * 4 + lane];
-                        mma16816(c, a, b2);
-                    }
-                    if (++gpos == mp.gk) {
-                        y0 = fmaf(c[0], to_float(st[gi * 16 + g]), y0);
-                        y1 = fmaf(c[2], to_float(st[gi * 16 + g + 8]), y1);
-                        c[0] = c[1] = c[2] = c[3] = 0.0f;
-                        gpos = 0;
-                        ++gi;
+                    if constexpr (GK == 2) {
+                        // Static groups of two blocks: fresh accumulator on even j.
+                        if ((j & 1) == 0) mma16816_zc(c, a, bh[j]);
+                        else mma16816(c, a, bh[j]);
+                        if constexpr (XF == 2) mma16816(c, a, blo[j]);
+                        if (j & 1) {
+                            float s0, s1;
+                            load_scale_pair(st + ((kb + j) >> 1) * 16, s0, s1);
+                            y0 = fmaf(c[0], s0, y0);
+                            y1 = fmaf(c[2], s1, y1);
+                        }
+                    } else {
+                        mma16816(c, a, bh[j]);
+                        if constexpr (XF == 2) mma16816(c, a, blo[j]);
+                        if (++gpos == mp.gk) {
+                            float s0, s1;
+                            load_scale_pair(st + gi * 16, s0, s1);
+                            y0 = fmaf(c[0], s0, y0);
+                            y1 = fmaf(c[2], s1, y1);
+                            c[0] = c[1] = c[2] = c[3] = 0.0f;
+                            gpos = 0;
+                            ++gi;
+                        }
                     }
                 }
             }
-            if (gpos != 0) {  // one scale per row: this warp's share of the single group
-                y0 = fmaf(c[0], to_float(st[g]), y0);
-                y1 = fmaf(c[2], to_float(st[g + 8]), y1);
+            if (GK == 0 && gpos != 0) {  // one scale per row: this warp's share of the single group
+                float s0, s1;
+                load_scale_pair(st, s0, s1);
+                y0 = fmaf(c[0], s0, y0);
+                y1 = fmaf(c[2], s1, y1);
             }
         }
         __syncwarp();
@@ -317,7 +366,7 @@ bool plan_mma(const aexis_weights* w, int xf, int sm_count, MmaPlan& pl) {
     const int ntiles = (w->n + 15) / 16;
     const int st = w->scale_dtype == AEXIS_F16 ? 2 : 4;
     const int stage = 8 * w->k + scale_groups(w) * 16 * st;
-    const int fixed = xf * nkb * 32 + 2 * kMW * 16 * 4 + 16 * 16 + 64 + kMW * 4 + 128;
+    const int fixed = xf * nkb * 32 + 32 + 2 * kMW * 16 * 4 + 16 * 16 + 64 + kMW * 4 + 128;
     const int want = 2 * sm_count * kMW;  // warp units that fill two CTAs per SM
     int kw = 1;
     while (kw < 8 && (long long)ntiles * kw < want) kw <<= 1;
@@ -343,14 +392,14 @@ bool plan_mma(const aexis_weights* w, int xf, int sm_count, MmaPlan& pl) {
     return false;
 }
 
-template <typename ST, int XF, int KW>
+template <typename ST, int XF, int KW, int GK>
 cudaError_t launch_mma_t(const MmaParams& mp, int grid, int smem, bool pdl, cudaStream_t stream) {
     static int configured[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
     if (smem > configured[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(gemv_mma_kernel<ST, XF, KW>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        cudaError_t e = cudaFuncSetAttribute(gemv_mma_kernel<ST, XF, KW, GK>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e != cudaSuccess) return e;
         configured[dev] = smem;
     }
@@ -364,17 +413,23 @@ cudaError_t launch_mma_t(const MmaParams& mp, int grid, int smem, bool pdl, cuda
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, gemv_mma_kernel<ST, XF, KW>, mp);
+    return cudaLaunchKernelEx(&cfg, gemv_mma_kernel<ST, XF, KW, GK>, mp);
+}
+
+template <typename ST, int XF, int GK>
+cudaError_t launch_mma_kw(const MmaParams& mp, int kw, int grid, int smem, bool pdl, cudaStream_t s) {
+    switch (kw) {
+        case 1: return launch_mma_t<ST, XF, 1, GK>(mp, grid, smem, pdl, s);
+        case 2: return launch_mma_t<ST, XF, 2, GK>(mp, grid, smem, pdl, s);
+        case 4: return launch_mma_t<ST, XF, 4, GK>(mp, grid, smem, pdl, s);
+        default: return launch_mma_t<ST, XF, 8, GK>(mp, grid, smem, pdl, s);
+    }
 }
 
 template <typename ST, int XF>
-cudaError_t launch_mma_kw(const MmaParams& mp, int kw, int grid, int smem, bool pdl, cudaStream_t s) {
-    switch (kw) {
-        case 1: return launch_mma_t<ST, XF, 1>(mp, grid, smem, pdl, s);
-        case 2: return launch_mma_t<ST, XF, 2>(mp, grid, smem, pdl, s);
-        case 4: return launch_mma_t<ST, XF, 4>(mp, grid, smem, pdl, s);
-        default: return launch_mma_t<ST, XF, 8>(mp, grid, smem, pdl, s);
-    }
+cudaError_t launch_mma_gk(const MmaParams& mp, int kw, int grid, int smem, bool pdl, cudaStream_t s) {
+    if (mp.gk == 2) return launch_mma_kw<ST, XF, 2>(mp, kw, grid, smem, pdl, s);
+    return launch_mma_kw<ST, XF, 0>(mp, kw, grid, smem, pdl, s);
 }
 
 }  // namespace
@@ -451,9 +506,9 @@ cudaError_t launch_gemv_mma(const GemvArgs& a, int sm_count, cudaStream_t stream
     mp.stage_bytes = pl.stage_bytes;
     const int grid = pl.units < pl.per_sm * sm_count ? pl.units : pl.per_sm * sm_count;
     if (w->scale_dtype == AEXIS_F16) {
-        if (xf == 1) return launch_mma_kw<__half, 1>(mp, pl.kw, grid, pl.smem, a.pdl, stream);
-        return launch_mma_kw<__half, 2>(mp, pl.kw, grid, pl.smem, a.pdl, stream);
+        if (xf == 1) return launch_mma_gk<__half, 1>(mp, pl.kw, grid, pl.smem, a.pdl, stream);
+        return launch_mma_gk<__half, 2>(mp, pl.kw, grid, pl.smem, a.pdl, stream);
     }
-    if (xf == 1) return launch_mma_kw<float, 1>(mp, pl.kw, grid, pl.smem, a.pdl, stream);
-    return launch_mma_kw<float, 2>(mp, pl.kw, grid, pl.smem, a.pdl, stream);
+    if (xf == 1) return launch_mma_gk<float, 1>(mp, pl.kw, grid, pl.smem, a.pdl, stream);
+    return launch_mma_gk<float, 2>(mp, pl.kw, grid, pl.smem, a.pdl, stream);
 }
