@@ -234,7 +234,25 @@ int alloc_weights(aexis_decoder* d, aexis_weights& w, int bits, int group, int s
 void free_weights(aexis_weights& w) {
     if (w.data) cudaFree(w.data);
     if (w.scales) cudaFree(w.scales);
-    w.data = w.scales = nullptr;
+    if (w.frag) cudaFree(w.frag);
+    if (w.frag_scales) cudaFree(w.frag_scales);
+    w.data = w.scales = w.frag = w.frag_scales = nullptr;
+}
+
+// The tensor-core GEMV's fragment copy of a Q4 matrix (built once; rebuilt
+// in place when the matrix is reloaded, so captured graphs stay valid).
+int build_frag(aexis_decoder* d, aexis_weights& w) {
+    if (!gemv_mma_eligible(&w)) return AEXIS_OK;
+    cudaError_t e = cudaSuccess;
+    if (!w.frag) {
+        size_t sb = 0;
+        const size_t wb = gemv_mma_frag_bytes(&w, &sb);
+        e = cudaMalloc(&w.frag, wb);
+        if (e == cudaSuccess) e = cudaMalloc(&w.frag_scales, sb);
+    }
+    if (e == cudaSuccess) e = launch_repack_q4_frag(&w, d->ctx->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(d->ctx->stream);
+    return aexis_cuda_check(d->ctx, e, "decoder fragment repack");
 }
 
 // Copies logical rows [0, rows) of a packed matrix into internal rows
@@ -415,6 +433,15 @@ int ready(aexis_decoder* d) {
     if (!d->lm_set || !d->final_set || !d->embed_set)
         return aexis_fail(d->ctx, AEXIS_E_STATE, "lm_head/final norm/embedding not set");
     if (!d->step_exec) {
+        for (auto& L : d->layers) {
+            aexis_weights* ws[4] = {&L.qkv, &L.o, &L.gateup, &L.down};
+            for (aexis_weights* w : ws) {
+                int rc = build_frag(d, *w);
+                if (rc) return rc;
+            }
+        }
+        int frc = build_frag(d, d->lm);
+        if (frc) return frc;
         int rc = capture(d, 1, &d->step_exec);
         if (rc) return rc;
         rc = capture(d, 0, &d->prefill_exec);
@@ -597,6 +624,7 @@ AEXIS_API int aexis_cuda_decoder_set_linear(aexis_decoder* d, int layer, int whi
     if (layer == -1) {
         if (which != 7) return aexis_fail(d->ctx, AEXIS_E_RANGE, "layer -1 takes which=7 (lm_head)");
         rc = scatter_rows(d, d->lm, packed, scales, scale_dtype, c.vocab, 0, 1, none);
+        if (!rc && d->lm.frag) rc = build_frag(d, d->lm);
         if (!rc) d->lm_set = 1;
         return rc;
     }
@@ -624,6 +652,10 @@ AEXIS_API int aexis_cuda_decoder_set_linear(aexis_decoder* d, int layer, int whi
         case 4: rc = scatter_rows(d, L.gateup, packed, scales, scale_dtype, c.ffn, 0, 2, none); break;
         case 5: rc = scatter_rows(d, L.gateup, packed, scales, scale_dtype, c.ffn, 1, 2, none); break;
         case 6: rc = scatter_rows(d, L.down, packed, scales, scale_dtype, c.hidden, 0, 1, none); break;
+    }
+    if (!rc) {
+        aexis_weights* w = which <= 2 ? &L.qkv : which == 3 ? &L.o : which <= 5 ? &L.gateup : &L.down;
+        if (w->frag) rc = build_frag(d, *w);
     }
     if (!rc) L.set_mask |= 1 << which;
     return rc;
