@@ -32,9 +32,24 @@ struct aexis_decoder {
     int host_pos = 0;
     cudaGraphExec_t step_exec = nullptr, prefill_exec = nullptr;
     std::vector<int> qkv_perm;      // internal row -> logical (kind, head, dim)
+    bool split_attn = false;        // decode attention by launch_split_attention
 };
 
 // cos/sin tables [cap][rot/2] of Qwen35DecoderSession.CreateRopeTextures
 // (Qwen35DecoderSession.cs:1660-1687): inv = 1 / theta^(j * 2/rot) in fp32,
 // angle = pos * inv in fp32, cos/sin evaluated in double and rounded.
 void decoder_rope_tables(int cap, int rot_dim, float theta, std::vector<float>& cs, std::vector<float>& sn);
+
+// Split decode attention over fp16 KV caches [B][kv][cap][D] (k_batch.cu):
+// sequence b's query heads q[b][n_heads][D] attend positions [0, pos[b]],
+// chunk (32 or 128) positions per CTA, K and V of a chunk staged by bulk
+// copies, the last CTA of (b, kv head) merging the splits into out[b][..][D].
+// part: split_attention_part_floats() floats; counters: [B][kv], zero, left
+// zero. Launched as a programmatic dependent of the previous kernel.
+bool split_attention_supported(int n_heads, int kvh, int D);
+int split_attention_max_cap();
+size_t split_attention_part_floats(int B, int n_heads, int D, int chunk);
+cudaError_t split_attention_configure(int n_heads, int kvh, int D, int chunk);
+cudaError_t launch_split_attention(const float* q, const __half* kc, const __half* vc, int cap, int D, int n_heads,
+                                   int kvh, float scale, const int* pos, int B, float* part, unsigned int* counters,
+                                   float* out, int* status, int chunk, cudaStream_t s);

@@ -39,7 +39,6 @@ constexpr int kBatChunk = 128;        // context positions per attention CTA
 constexpr int kBatMaxGroup = 8;       // query heads per KV head
 constexpr int kBatMaxHeadDim = 256;
 constexpr int kBatMaxCap = 8192;      // positions per sequence
-constexpr int kBatMaxSplits = kBatMaxCap / kBatChunk;
 
 // splitmix64 finaliser (Steele, Lea and Flood, "Fast splittable pseudorandom
 // number generators", OOPSLA 2014).
@@ -146,29 +145,30 @@ __global__ void bat_rope_kernel(const float* qkv, int rows, const int* rope_map,
 //   values: each thread owns two dims of every head over every VG-th
 //           position; the VG partial sums are added through shared memory.
 // Dynamic shared memory: K and V chunks (2 x kBatChunk x D fp16).
-template <int HPG>
+template <int HPG, int PC>
 __global__ void __launch_bounds__(kBatThreads, 3) bat_attn_kernel(const float* q, const __half* kc, const __half* vc,
                                                                int cap, int D, int n_heads, int kvh, float scale,
                                                                const int* pos, float* part, unsigned int* counters,
                                                                float* out, int* status) {
+    constexpr int MS = kBatMaxCap / PC;  // most splits of a sequence
     constexpr int DPT = 64 / HPG;
-    constexpr int CH = DPT / 8;  // 16-byte K chunks per thread and position
+    constexpr int KC = DPT / 8;  // 16-byte K chunks per thread and position
     extern __shared__ __align__(128) uint8_t smem[];
-    __shared__ __align__(16) float sc[kBatChunk][HPG];  // scores, then e = exp(s - m), [p][h]
+    __shared__ __align__(16) float sc[PC][HPG];  // scores, then e = exp(s - m), [p][h]
     __shared__ float stat[HPG][2];
-    __shared__ float wsm[HPG][kBatMaxSplits];
+    __shared__ float wsm[HPG][MS];
     __shared__ __align__(8) uint64_t bar;
     __shared__ bool last, ok;
     griddep_wait();
     griddep_launch();
     const int split = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
     const int ctx = pos[b] + 1;
-    const int active = (ctx + kBatChunk - 1) / kBatChunk;
+    const int active = (ctx + PC - 1) / PC;
     if (split >= active) return;
-    const int p0 = split * kBatChunk, p1 = min(ctx, p0 + kBatChunk), np = p1 - p0;
+    const int p0 = split * PC, p1 = min(ctx, p0 + PC), np = p1 - p0;
     const int tid = threadIdx.x, warp = tid >> 5;
     __half* ks = reinterpret_cast<__half*>(smem);
-    __half* vs = ks + (size_t)kBatChunk * D;
+    __half* vs = ks + (size_t)PC * D;
     const size_t head_off = ((size_t)b * kvh + g) * cap;
     if (tid == 0) {
         aexis_dev::mbar_init(&bar, 1);
@@ -189,7 +189,7 @@ __global__ void __launch_bounds__(kBatThreads, 3) bat_attn_kernel(const float* q
 #pragma unroll
     for (int h = 0; h < HPG; ++h)
 #pragma unroll
-        for (int j = 0; j < CH; ++j) {
+        for (int j = 0; j < KC; ++j) {
             const float4 a0 = *reinterpret_cast<const float4*>(qb + h * D + (slot + j * tpp) * 8);
             const float4 a1 = *reinterpret_cast<const float4*>(qb + h * D + (slot + j * tpp) * 8 + 4);
             qr[h][j * 8 + 0] = a0.x; qr[h][j * 8 + 1] = a0.y; qr[h][j * 8 + 2] = a0.z; qr[h][j * 8 + 3] = a0.w;
@@ -211,7 +211,7 @@ __global__ void __launch_bounds__(kBatThreads, 3) bat_attn_kernel(const float* q
 #pragma unroll
         for (int h = 0; h < HPG; ++h) acc[h] = 0.0f;
 #pragma unroll
-        for (int j = 0; j < CH; ++j) {
+        for (int j = 0; j < KC; ++j) {
             uint4 raw = make_uint4(0u, 0u, 0u, 0u);
             if (valid) raw = *reinterpret_cast<const uint4*>(ks + (size_t)pp * D + (slot + j * tpp) * 8);
             const __half2* k2 = reinterpret_cast<const __half2*>(&raw);
@@ -284,15 +284,15 @@ __global__ void __launch_bounds__(kBatThreads, 3) bat_attn_kernel(const float* q
         *reinterpret_cast<float2*>(red + ((size_t)vg * HPG + h) * D + 2 * dt) = make_float2(o0[h], o1[h]);
     __syncthreads();
     const int stride = D + 2;
-    float* mine = part + ((size_t)(b * n_heads + g * HPG) * kBatMaxSplits + split) * stride;
+    float* mine = part + ((size_t)(b * n_heads + g * HPG) * MS + split) * stride;
     for (int i = tid; i < HPG * D; i += kBatThreads) {
         const int h = i / D, dd = i % D;
         float acc = 0.0f;
         for (int gg = 0; gg < VG; ++gg) acc += red[((size_t)gg * HPG + h) * D + dd];
-        mine[(size_t)h * kBatMaxSplits * stride + dd] = acc;
+        mine[(size_t)h * MS * stride + dd] = acc;
     }
     if (tid < HPG) {
-        float* st = mine + (size_t)tid * kBatMaxSplits * stride + D;
+        float* st = mine + (size_t)tid * MS * stride + D;
         st[0] = stat[tid][0];
         st[1] = stat[tid][1];
     }
@@ -304,12 +304,12 @@ __global__ void __launch_bounds__(kBatThreads, 3) bat_attn_kernel(const float* q
     __syncthreads();
     if (!last) return;
     __threadfence();
-    float* ls = reinterpret_cast<float*>(smem);  // [HPG][kBatMaxSplits]
+    float* ls = reinterpret_cast<float*>(smem);  // [HPG][MS]
     for (int i = tid; i < HPG * active; i += kBatThreads) {
         const int h = i / active, s = i % active;
-        const float* st = part + ((size_t)(b * n_heads + g * HPG + h) * kBatMaxSplits + s) * stride + D;
+        const float* st = part + ((size_t)(b * n_heads + g * HPG + h) * MS + s) * stride + D;
         wsm[h][s] = st[0];
-        ls[h * kBatMaxSplits + s] = st[1];
+        ls[h * MS + s] = st[1];
     }
     __syncthreads();
     if (tid < HPG) {
@@ -319,7 +319,7 @@ __global__ void __launch_bounds__(kBatThreads, 3) bat_attn_kernel(const float* q
         for (int s = 0; s < active; ++s) {
             const float e = expf(wsm[tid][s] - M);
             wsm[tid][s] = e;
-            L += ls[tid * kBatMaxSplits + s] * e;
+            L += ls[tid * MS + s] * e;
         }
         const float inv = 1.0f / fmaxf(L, 1e-20f);
         for (int s = 0; s < active; ++s) wsm[tid][s] *= inv;
@@ -327,7 +327,7 @@ __global__ void __launch_bounds__(kBatThreads, 3) bat_attn_kernel(const float* q
     __syncthreads();
     for (int i = tid; i < HPG * D; i += kBatThreads) {
         const int h = i / D, dd = i % D;
-        const float* src = part + (size_t)(b * n_heads + g * HPG + h) * kBatMaxSplits * stride + dd;
+        const float* src = part + (size_t)(b * n_heads + g * HPG + h) * MS * stride + dd;
         float acc = 0.0f;
 #pragma unroll 8
         for (int s = 0; s < active; ++s) acc = fmaf(wsm[h][s], src[(size_t)s * stride], acc);
@@ -336,15 +336,35 @@ __global__ void __launch_bounds__(kBatThreads, 3) bat_attn_kernel(const float* q
     if (tid == 0) *cnt = 0u;
 }
 
-// The attention instantiation for a GQA group size (1, 2, 4 or 8).
-const void* attn_kernel_for(int hpg) {
+// The attention instantiation for a GQA group size (1, 2, 4 or 8) and a
+// chunk of 32 or 128 context positions per CTA.
+const void* attn_kernel_for(int hpg, int chunk) {
+    if (chunk == 32) {
+        switch (hpg) {
+            case 1: return (const void*)bat_attn_kernel<1, 32>;
+            case 2: return (const void*)bat_attn_kernel<2, 32>;
+            case 4: return (const void*)bat_attn_kernel<4, 32>;
+            case 8: return (const void*)bat_attn_kernel<8, 32>;
+            default: return nullptr;
+        }
+    }
     switch (hpg) {
-        case 1: return (const void*)bat_attn_kernel<1>;
-        case 2: return (const void*)bat_attn_kernel<2>;
-        case 4: return (const void*)bat_attn_kernel<4>;
-        case 8: return (const void*)bat_attn_kernel<8>;
+        case 1: return (const void*)bat_attn_kernel<1, 128>;
+        case 2: return (const void*)bat_attn_kernel<2, 128>;
+        case 4: return (const void*)bat_attn_kernel<4, 128>;
+        case 8: return (const void*)bat_attn_kernel<8, 128>;
         default: return nullptr;
     }
+}
+
+// Dynamic shared memory of an attention CTA: the K and V chunks, reused for
+// the value partials [VG][HPG][D] and the merge's sums [HPG][splits].
+size_t attn_smem_for(int hpg, int D, int chunk) {
+    size_t b = (size_t)2 * chunk * D * sizeof(__half);
+    const size_t red = (size_t)(kBatThreads / (D / 2)) * hpg * D * sizeof(float);
+    const size_t ls = (size_t)hpg * (kBatMaxCap / chunk) * sizeof(float);
+    b = b > red ? b : red;
+    return b > ls ? b : ls;
 }
 
 // token[b] = argmax key's index; out[step][b] = token; pos[b] += 1.
@@ -364,6 +384,56 @@ __global__ void bat_finish_kernel(const unsigned long long* keys, int B, int* to
 }
 
 }  // namespace
+
+// ------------------------------------------------------- shared attention
+bool split_attention_supported(int n_heads, int kvh, int D) {
+    if (kvh <= 0 || n_heads % kvh) return false;
+    const int hpg = n_heads / kvh;
+    if (!attn_kernel_for(hpg, 128)) return false;
+    const int dpt = 64 / hpg, tpp = D / dpt;
+    return D >= 64 && D <= kBatMaxHeadDim && D % dpt == 0 && tpp >= 1 && tpp <= 32 && (tpp & (tpp - 1)) == 0;
+}
+
+int split_attention_max_cap() { return kBatMaxCap; }
+
+size_t split_attention_part_floats(int B, int n_heads, int D, int chunk) {
+    return (size_t)B * n_heads * (kBatMaxCap / chunk) * (D + 2);
+}
+
+cudaError_t split_attention_configure(int n_heads, int kvh, int D, int chunk) {
+    const int hpg = n_heads / kvh;
+    static size_t configured[64][2][4] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    const int ci = chunk == 32 ? 0 : 1, hi = hpg == 1 ? 0 : hpg == 2 ? 1 : hpg == 4 ? 2 : 3;
+    const size_t smem = attn_smem_for(hpg, D, chunk);
+    if (smem <= configured[dev][ci][hi]) return cudaSuccess;
+    cudaError_t e = cudaFuncSetAttribute(attn_kernel_for(hpg, chunk), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)smem);
+    if (e == cudaSuccess) configured[dev][ci][hi] = smem;
+    return e;
+}
+
+cudaError_t launch_split_attention(const float* q, const __half* kc, const __half* vc, int cap, int D, int n_heads,
+                                   int kvh, float scale, const int* pos, int B, float* part, unsigned int* counters,
+                                   float* out, int* status, int chunk, cudaStream_t s) {
+    const int hpg = n_heads / kvh;
+    void* args[] = {(void*)&q, (void*)&kc, (void*)&vc, &cap, &D, &n_heads, &kvh, &scale, (void*)&pos, &part, &counters,
+                    &out, &status};
+    const int splits = (cap + chunk - 1) / chunk;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(splits, kvh, B);
+    cfg.blockDim = dim3(kBatThreads);
+    cfg.dynamicSmemBytes = attn_smem_for(hpg, D, chunk);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelExC(&cfg, attn_kernel_for(hpg, chunk), args);
+}
 
 // ------------------------------------------------------------------ host side
 struct aexis_batch {
@@ -412,7 +482,6 @@ cudaError_t launch_pdl(const void* fn, dim3 grid, dim3 block, size_t smem, cudaS
     return cudaLaunchKernelExC(&cfg, fn, args);
 }
 
-size_t attn_smem(int D) { return (size_t)2 * kBatChunk * D * sizeof(__half); }
 
 // Host copy of the per-sequence key: mix64(seed ^ mix64(sequence id)).
 unsigned long long seq_key(unsigned long long seed, long long id) {
@@ -479,24 +548,10 @@ cudaError_t enqueue_batch_step(aexis_batch* bt, cudaStream_t s, int B) {
             if ((e = launch_pdl((const void*)bat_rope_kernel, dim3(B), dim3(256), 0, s, args)) != cudaSuccess)
                 return e;
         }
-        {
-            const float* qp = bt->q;
-            const __half* kcp = kc;
-            const __half* vcp = vc;
-            int cap = bt->cap, hd = D, nh = NH, nkv = KVH;
-            float sc = scale;
-            const int* pp = pos;
-            float* part = bt->part;
-            unsigned int* cnt = bt->counters + (size_t)l * bt->max_batch * KVH;
-            float* o = bt->attn;
-            int* status = d->ctx->status;
-            void* args[] = {(void*)&qp, (void*)&kcp, (void*)&vcp, &cap, &hd, &nh, &nkv, &sc, (void*)&pp, &part, &cnt,
-                            &o, &status};
-            const int splits = (bt->cap + kBatChunk - 1) / kBatChunk;
-            if ((e = launch_pdl(attn_kernel_for(NH / KVH), dim3(splits, KVH, B), dim3(kBatThreads), attn_smem(D),
-                                s, args)) != cudaSuccess)
-                return e;
-        }
+        if ((e = launch_split_attention(bt->q, kc, vc, bt->cap, D, NH, KVH, scale, pos, B, bt->part,
+                                        bt->counters + (size_t)l * bt->max_batch * KVH, bt->attn, d->ctx->status,
+                                        kBatChunk, s)) != cudaSuccess)
+            return e;
         if ((e = launch_tc_prep(0, bt->attn, 0, qd, B, qd, nullptr, 0.0f, 1, bt->xt, nullptr, 0, 0, true, s)) !=
             cudaSuccess)
             return e;
@@ -582,10 +637,9 @@ AEXIS_API int aexis_cuda_batch_create(aexis_decoder* d, int max_batch, int kv_ca
     {
         // Attention layout: group 1, 2, 4 or 8; 64 / group query dims per
         // thread, head_dim / that a power of two <= 32; head_dim 64..256.
-        const int hpg = c.n_heads / c.n_kv_heads, dpt = 64 / (hpg > 0 ? hpg : 1);
-        const int tpp = D / dpt;
-        if (!attn_kernel_for(hpg) || D < 64 || D > kBatMaxHeadDim || D % dpt || tpp < 1 || tpp > 32 || (tpp & (tpp - 1)))
-            return aexis_fail(ctx, AEXIS_E_UNSUPPORTED, "head_dim %d with %d query heads per KV head", D, hpg);
+        if (!split_attention_supported(c.n_heads, c.n_kv_heads, D))
+            return aexis_fail(ctx, AEXIS_E_UNSUPPORTED, "head_dim %d with %d query heads per KV head", D,
+                              c.n_heads / c.n_kv_heads);
     }
     if (max_batch < 1 || max_batch > 128) return aexis_fail(ctx, AEXIS_E_RANGE, "max_batch %d (1..128)", max_batch);
     if (kv_capacity < 1 || kv_capacity > kBatMaxCap)
@@ -616,7 +670,7 @@ AEXIS_API int aexis_cuda_batch_create(aexis_decoder* d, int max_batch, int kv_ca
     if (!rc) rc = balloc(bt, (void**)&bt->attn, sizeof(float) * max_batch * qd);
     if (!rc) rc = balloc(bt, (void**)&bt->gu, sizeof(float) * max_batch * 2 * F);
     if (!rc) rc = balloc(bt, (void**)&bt->logits, sizeof(float) * max_batch * c.vocab);
-    if (!rc) rc = balloc(bt, (void**)&bt->part, sizeof(float) * max_batch * c.n_heads * kBatMaxSplits * (D + 2));
+    if (!rc) rc = balloc(bt, (void**)&bt->part, sizeof(float) * split_attention_part_floats(max_batch, c.n_heads, D, kBatChunk));
     if (!rc) {
         const int kmax = H > qd ? (H > F ? H : F) : (qd > F ? qd : F);
         rc = balloc(bt, &bt->xt, gemm_tc_xt_bytes(max_batch, kmax, AEXIS_F32));
@@ -654,14 +708,8 @@ AEXIS_API int aexis_cuda_batch_create(aexis_decoder* d, int max_batch, int kv_ca
             }
     }
     if (!rc) {
-        static size_t configured[64] = {};
-        const size_t smem = attn_smem(D);
-        if (ctx->device >= 0 && ctx->device < 64 && smem > configured[ctx->device]) {
-            rc = aexis_cuda_check(ctx, cudaFuncSetAttribute(attn_kernel_for(c.n_heads / c.n_kv_heads),
-                                                            cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
-                                  "attention smem");
-            if (!rc) configured[ctx->device] = smem;
-        }
+        rc = aexis_cuda_check(ctx, split_attention_configure(c.n_heads, c.n_kv_heads, D, kBatChunk),
+                              "attention smem");
     }
     if (!rc) rc = aexis_cuda_check(ctx, cudaStreamSynchronize(ctx->stream), "batch setup");
     if (rc) {

@@ -341,7 +341,11 @@ cudaError_t enqueue_step(aexis_decoder* d, cudaStream_t s, int emit) {
         g.rot_dim = c.rot_dim;
         g.pos_ptr = pos;
         if ((e = launch_gemv(g, d->ctx->sm_count, s)) != cudaSuccess) return e;
-        {
+        if (d->split_attn) {
+            e = launch_split_attention(d->q, kc, vc, c.kv_capacity, D, c.n_heads, c.n_kv_heads, scale, pos, 1, d->part,
+                                       d->counters + l * c.n_kv_heads, d->attn, d->ctx->status, 32, s);
+            if (e != cudaSuccess) return e;
+        } else {
             const float* qp = d->q;
             const __half* kcp = kc;
             const __half* vcp = vc;
@@ -543,7 +547,19 @@ AEXIS_API int aexis_cuda_decoder_create(aexis_ctx* ctx, const aexis_decoder_conf
     if (!rc) rc = alloc(d, (void**)&d->attn, sizeof(float) * qd, "alloc");
     if (!rc) rc = alloc(d, (void**)&d->act, sizeof(float) * c.ffn, "alloc");
     if (!rc) rc = alloc(d, (void**)&d->logits, sizeof(float) * c.vocab, "alloc");
-    if (!rc) rc = alloc(d, (void**)&d->part, sizeof(float) * (size_t)c.n_heads * kAttnSplits * (c.head_dim + 2), "alloc");
+    // Decode attention: the bulk-copy split kernel (32-position chunks) where
+    // the head shape allows it, else the direct-load kernel below.
+    d->split_attn = split_attention_supported(c.n_heads, c.n_kv_heads, c.head_dim);
+    {
+        size_t pf = (size_t)c.n_heads * kAttnSplits * (c.head_dim + 2);
+        if (d->split_attn) {
+            const size_t sf = split_attention_part_floats(1, c.n_heads, c.head_dim, 32);
+            pf = pf > sf ? pf : sf;
+            if (!rc) rc = aexis_cuda_check(ctx, split_attention_configure(c.n_heads, c.n_kv_heads, c.head_dim, 32),
+                                           "attention smem");
+        }
+        if (!rc) rc = alloc(d, (void**)&d->part, sizeof(float) * pf, "alloc");
+    }
     if (!rc) rc = alloc(d, (void**)&d->counters, sizeof(unsigned int) * c.n_layers * c.n_kv_heads, "alloc");
     if (!rc) rc = alloc(d, (void**)&d->key, sizeof(unsigned long long), "alloc");
     d->max_out = 1 << 16;
