@@ -270,7 +270,7 @@ def run_gpu(args):
     dom_s = ev0.elapsed_time(ev1) / 1e3 / dom_launches
     peak, peak_kind = measured_peak()
     achieved = SWEEP_BYTES[DOMINANT] / dom_s / 1e9
-    traffic = profile_traffic("q4_gemv_1024x151936.md")
+    traffic = profile_traffic("gemv_mma_q4_1024x151936.md")
 
     # Per-shape throughput (each GEMV alone, same method), config 1 Q8 GEMV.
     per_shape = {}
@@ -355,7 +355,7 @@ def run_gpu(args):
                        "bytes_per_step": STEP_BYTES, "weight_copies": copies,
                        "l2": f"weights rotated over {copies} copies ({copies * STEP_BYTES / 2**20:.0f} MiB > 4x L2)",
                        "parallelism": f"replicas x{world}"},
-            "roofline": {"bound": "hbm", "kernel": "gemv_fast q4 (1024x151936)",
+            "roofline": {"bound": "hbm", "kernel": "gemv_mma_kernel q4 g32 (1024x151936)",
                          "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": traffic,
                          "algorithmic_bytes_per_launch": SWEEP_BYTES[DOMINANT],
