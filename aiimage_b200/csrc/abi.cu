@@ -188,6 +188,19 @@ AEXIS_API int aexis_cuda_sync(aexis_ctx* ctx) {
     return aexis_check_status(ctx);
 }
 
+AEXIS_API int aexis_cuda_selftest_wait(aexis_ctx* ctx, long long limit_cycles) {
+    if (!ctx) return AEXIS_E_NULL;
+    if (limit_cycles < 1000 || limit_cycles > 4000000000LL)
+        return aexis_fail(ctx, AEXIS_E_RANGE, "limit_cycles %lld outside [1e3, 4e9]", limit_cycles);
+    int rc = bind(ctx);
+    if (rc) return rc;
+    void* flag = nullptr;
+    rc = aexis_scratch(ctx, sizeof(int), &flag);
+    if (rc) return rc;
+    return aexis_cuda_check(ctx, launch_selftest_wait(reinterpret_cast<int*>(flag), limit_cycles, ctx->status,
+                                                      ctx->stream), "self-test launch");
+}
+
 // ---------------------------------------------------------------- weights
 AEXIS_API int aexis_quantize_q8_rows(const float* data, int out_ch, int per_ch, int contiguous, uint32_t* packed,
                                      float* scales) {

@@ -147,6 +147,9 @@ struct TcLaunch {
 cudaError_t launch_gemm_tc_prepared(const TcLaunch& a, cudaStream_t s);
 
 cudaError_t launch_dequant(const aexis_weights* w, float* out, cudaStream_t s);
+// One bounded wait on a flag nothing sets (zeroed first): records
+// AEXIS_E_TIMEOUT in `status` after limit_cycles of SM clock.
+cudaError_t launch_selftest_wait(int* flag, long long limit_cycles, int* status, cudaStream_t s);
 cudaError_t launch_rmsnorm(const void* x, int x_dtype, int rows, int width, int ld,
                            const float* gamma, int affine_size, float eps, void* y, int y_dtype,
                            cudaStream_t s);

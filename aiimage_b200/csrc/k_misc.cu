@@ -260,6 +260,20 @@ __global__ void swiglu_kernel(const float* g, const float* u, int n, float* y) {
         y[i] = __fmul_rn(g[i] / (1.0f + expf(-g[i])), u[i]);
 }
 
+// Bounded wait on a flag nothing sets: one thread polls it until
+// limit_cycles of SM clock pass, then records AEXIS_E_TIMEOUT in the status
+// word and returns (the path every bounded barrier wait takes when it gives up).
+__global__ void selftest_wait_kernel(const volatile int* flag, long long limit_cycles, int* status) {
+    if (threadIdx.x != 0) return;
+    const long long t0 = clock64();
+    while (*flag == 0) {
+        if (clock64() - t0 > limit_cycles) {
+            atomicCAS(status, 0, (int)AEXIS_E_TIMEOUT);
+            return;
+        }
+    }
+}
+
 inline int grid_for(long long total, int threads = kT) {
     long long b = (total + threads - 1) / threads;
     if (b > 148LL * 32) b = 148LL * 32;
@@ -368,5 +382,12 @@ cudaError_t launch_swish(const float* x, int n, float* y, cudaStream_t s) {
 
 cudaError_t launch_swiglu(const float* g, const float* u, int n, float* y, cudaStream_t s) {
     swiglu_kernel<<<grid_for(n), kT, 0, s>>>(g, u, n, y);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_selftest_wait(int* flag, long long limit_cycles, int* status, cudaStream_t s) {
+    cudaError_t e = cudaMemsetAsync(flag, 0, sizeof(int), s);
+    if (e != cudaSuccess) return e;
+    selftest_wait_kernel<<<1, 32, 0, s>>>(flag, limit_cycles, status);
     return cudaGetLastError();
 }

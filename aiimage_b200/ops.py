@@ -114,6 +114,12 @@ class AexisOps:
     def sync(self):
         check(lib().aexis_cuda_sync(self.ctx), self.ctx)
 
+    def selftest_wait(self, limit_cycles: int):
+        """Enqueue one bounded wait on a flag nothing sets (aexis_cuda_selftest_wait):
+        the next sync raises DeviceTimeoutError and the context stays usable."""
+        self._bind_stream()
+        check(lib().aexis_cuda_selftest_wait(self.ctx, int(limit_cycles)), self.ctx)
+
     # -- weights ----------------------------------------------------------
     def new_int8_weight_only_upload(self, packed: np.ndarray, scales: np.ndarray, n: int, k: int) -> Weights:
         """AexisGraphSession.NewInt8WeightOnlyUpload(AexisQuantizedTensor, n) (:12887-12910)."""

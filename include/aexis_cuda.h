@@ -80,8 +80,16 @@ const char* aexis_cuda_last_error(const aexis_ctx* ctx);
  * (Ops Gemm2DPack4LinearTextureA(CommandBuffer, ...) overloads, Ops:3685). */
 int aexis_cuda_set_stream(aexis_ctx* ctx, void* cuda_stream);
 
-/* Graphics.ExecuteCommandBuffer + readback fence: wait for enqueued work. */
+/* Graphics.ExecuteCommandBuffer + readback fence: wait for enqueued work.
+ * Returns AEXIS_E_TIMEOUT (and clears it) when a kernel gave up on a bounded
+ * wait since the last sync; the context stays usable. */
 int aexis_cuda_sync(aexis_ctx* ctx);
+
+/* No reference counterpart: a self-test of the failure path above. Enqueues
+ * one kernel that waits on a device flag nothing sets for limit_cycles
+ * (1e3..4e9) of SM clock, then records AEXIS_E_TIMEOUT like any kernel whose
+ * bounded barrier wait runs out; the next aexis_cuda_sync reports it. */
+int aexis_cuda_selftest_wait(aexis_ctx* ctx, long long limit_cycles);
 
 /* ------------------------------------------------------------------ weights */
 

@@ -230,3 +230,23 @@ def test_swish_and_swiglu(ops, oracle):
     assert np.allclose(host(y), oracle.swish(x), rtol=2e-6, atol=1e-7)
     ops.swiglu(cuda(x), cuda(u), 4096, y)
     assert np.allclose(host(y), oracle.swiglu(x, u), rtol=2e-6, atol=1e-7)
+
+
+def test_bounded_wait_timeout_leaves_context_usable(ops):
+    """The failure path of every bounded barrier wait: a kernel waits on a
+    flag nothing sets, gives up after ~1 ms of SM clock, records
+    AEXIS_E_TIMEOUT; sync reports it once and the context keeps working."""
+    import torch
+    from aiimage_b200 import errors
+    ops.sync()
+    ops.selftest_wait(2_000_000)
+    with pytest.raises(errors.DeviceTimeoutError):
+        ops.sync()
+    ops.sync()  # the status word was cleared by the report
+    x = torch.tensor([[0.5, 3.0, -1.0, 3.0]], dtype=torch.float32, device="cuda")
+    out = torch.empty(1, dtype=torch.int32, device="cuda")
+    ops.arg_max_pack4_linear_mat(x, 4, 1, out)
+    ops.sync()
+    assert int(out.item()) == 1
+    with pytest.raises(errors.ArgumentOutOfRangeError):
+        ops.selftest_wait(10)
