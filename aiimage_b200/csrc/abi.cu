@@ -246,13 +246,13 @@ static int weights_q(aexis_ctx* ctx, int kind, const uint32_t* packed, const voi
     w->scale_bytes = (size_t)nscales * dsize(scale_dtype);
     rc = upload(ctx, packed, w->data_bytes, &w->data, "weight upload");
     if (rc == AEXIS_OK) rc = upload(ctx, scales, w->scale_bytes, &w->scales, "scale upload");
-    // Q4: a second copy in the tensor-core GEMV's fragment layout.
+    // A second copy in the tensor-core GEMV's fragment layout.
     if (rc == AEXIS_OK && gemv_mma_eligible(w)) {
         size_t sb = 0;
         const size_t wb = gemv_mma_frag_bytes(w, &sb);
         cudaError_t e = cudaMalloc(&w->frag, wb);
         if (e == cudaSuccess) e = cudaMalloc(&w->frag_scales, sb);
-        if (e == cudaSuccess) e = launch_repack_q4_frag(w, ctx->stream);
+        if (e == cudaSuccess) e = launch_repack_frag(w, ctx->stream);
         if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
         rc = aexis_cuda_check(ctx, e, "fragment repack");
     }

@@ -100,11 +100,11 @@ const char* gemv_kernel_name(const aexis_weights* w);
 // The bulk-copy streaming GEMV (k_gemv_stream.cu): whether it takes `w`, and
 // its launch.
 bool gemv_stream_supported(const aexis_weights* w);
-// Tensor-core Q4 GEMV (k_gemv_mma.cu): shapes with a fragment copy (K a
-// multiple of 64, group a multiple of 16); the copy's sizes and builder.
+// Tensor-core Q4/Q8 GEMV (k_gemv_mma.cu): shapes with a fragment copy (K a
+// multiple of 64; Q4 groups a multiple of 16); the copy's sizes and builder.
 bool gemv_mma_eligible(const aexis_weights* w);
 size_t gemv_mma_frag_bytes(const aexis_weights* w, size_t* scale_bytes);
-cudaError_t launch_repack_q4_frag(const aexis_weights* w, cudaStream_t s);
+cudaError_t launch_repack_frag(const aexis_weights* w, cudaStream_t s);
 bool gemv_mma_supported(const aexis_weights* w, int a_dtype);
 cudaError_t launch_gemv_mma(const GemvArgs& a, int sm_count, cudaStream_t stream);
 cudaError_t launch_gemv_stream(const GemvArgs& a, int sm_count, int* status, cudaStream_t stream);

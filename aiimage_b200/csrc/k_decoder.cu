@@ -250,7 +250,7 @@ int build_frag(aexis_decoder* d, aexis_weights& w) {
         e = cudaMalloc(&w.frag, wb);
         if (e == cudaSuccess) e = cudaMalloc(&w.frag_scales, sb);
     }
-    if (e == cudaSuccess) e = launch_repack_q4_frag(&w, d->ctx->stream);
+    if (e == cudaSuccess) e = launch_repack_frag(&w, d->ctx->stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize(d->ctx->stream);
     return aexis_cuda_check(d->ctx, e, "decoder fragment repack");
 }

@@ -395,7 +395,7 @@ int fast_scale_mode(const aexis_weights* w, int* gshift) {
 }  // namespace
 
 const char* gemv_kernel_name(const aexis_weights* w) {
-    if (gemv_mma_supported(w, AEXIS_F16)) return "q4_mma";
+    if (gemv_mma_supported(w, AEXIS_F16)) return w->kind == WK_Q4 ? "q4_mma" : "q8_mma";
     if (gemv_stream_supported(w)) return w->kind == WK_Q4 ? "q4_stream" : "q8_stream";
     int gs;
     if (fast_scale_mode(w, &gs) < 0) return "generic";

@@ -1,5 +1,5 @@
-// k_gemv_mma.cu -- batch-1 Q4 dequant GEMV with the multiply-accumulate on
-// the tensor cores (mma.m16n8k16, fp16 x fp16 -> fp32).
+// k_gemv_mma.cu -- batch-1 Q4 / Q8 dequant GEMV with the multiply-accumulate
+// on the tensor cores (mma.m16n8k16, fp16 x fp16 -> fp32).
 //
 // Same contract as the CUDA-core kernels (AexisGemm2DPack4LinearTexture-
 // AFromLinear / ...Tiled..., HLSL Pack4Matmul:1038-1104, 2245-2300, weight
@@ -12,7 +12,10 @@
 // spends one shift, four LOP3 (nibble pairs under the fp16 exponent of 1024)
 // and four HADD2/HFMA2 (exact removal of the offset), plus one MMA.
 //
-// Layout (built from the reference packing at upload, launch_repack_q4_frag):
+// Q8 works the same way with two words per lane and block (bytes placed under
+// the fp16 exponent by PRMT, one HSUB2 per pair) and one scale per row.
+//
+// Layout (built from the reference packing at upload, launch_repack_frag):
 //   * weights: 16-row tiles; per tile and per four k16 blocks, 32 lanes x 16
 //     bytes, the word of k16 block kb for lane L holding the 8 nibbles of its
 //     A fragment (rows L/4 and L/4+8, columns 2(L%4), +1, +8, +9) as offset-
@@ -86,6 +89,43 @@ __global__ void repack_q4_frag_kernel(const uint32_t* src, const ST* scales, int
     }
 }
 
+// Q8 repack: the two words of lane L for k16 block kb hold its A fragment as
+// offset-binary bytes u = q + 128: word 0 = (row g: k0, k0+1), (row g+8: k0,
+// k0+1); word 1 = the same at k0+8, k0+9. Per tile and four blocks a lane's 8
+// words are contiguous. Scales: one per row, [tile][8][2].
+template <typename ST>
+__global__ void repack_q8_frag_kernel(const uint32_t* src, const ST* scales, int n, int k, int ntiles_pad,
+                                      uint32_t* dst, ST* dst_s) {
+    const int nkb = k / 16;
+    const int kw = k / 4;  // source words per row
+    const long long total = (long long)ntiles_pad * nkb * 32;
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += (long long)gridDim.x * blockDim.x) {
+        const int lane = (int)(i & 31);
+        const int kb = (int)((i >> 5) % nkb);
+        const long long t = (i >> 5) / nkb;
+        const int g = lane >> 2, tig = lane & 3;
+        const long long r0 = t * 16 + g, r1 = r0 + 8;
+        const int k0 = kb * 16 + 2 * tig;
+        auto u = [&](long long r, int kk) -> uint32_t {
+            if (r >= n) return 128u;
+            return ((src[r * kw + (kk >> 2)] >> (8 * (kk & 3))) & 0xFFu) ^ 0x80u;
+        };
+        const uint32_t w0 = u(r0, k0) | (u(r0, k0 + 1) << 8) | (u(r1, k0) << 16) | (u(r1, k0 + 1) << 24);
+        const uint32_t w1 = u(r0, k0 + 8) | (u(r0, k0 + 9) << 8) | (u(r1, k0 + 8) << 16) | (u(r1, k0 + 9) << 24);
+        const long long o = (t * nkb + (kb >> 2) * 4) * 64 + (long long)lane * 8 + (kb & 3) * 2;
+        dst[o] = w0;
+        dst[o + 1] = w1;
+    }
+    const long long stotal = (long long)ntiles_pad * 16;
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < stotal;
+         i += (long long)gridDim.x * blockDim.x) {
+        const int row16 = (int)((i >> 1) & 7) + 8 * (int)(i & 1);
+        const long long r = (i >> 4) * 16 + row16;
+        dst_s[i] = r < n ? scales[r] : ST(0.0f);
+    }
+}
+
 __device__ __forceinline__ uint32_t lop3_f16pair(uint32_t q, uint32_t mask) {
     uint32_t r;
     asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(r) : "r"(q), "r"(mask), "r"(0x64006400u));  // (q & mask) | c
@@ -104,6 +144,22 @@ __device__ __forceinline__ void decode_frag(uint32_t q, uint32_t (&a)[4]) {
     __half2 h1 = __hfma2(*reinterpret_cast<__half2*>(&t1), inv16, off16);  // (1024 + 16u) / 16 - 72 = q
     __half2 h2 = __hsub2(*reinterpret_cast<__half2*>(&t2), off);
     __half2 h3 = __hfma2(*reinterpret_cast<__half2*>(&t3), inv16, off16);
+    a[0] = *reinterpret_cast<uint32_t*>(&h0);
+    a[1] = *reinterpret_cast<uint32_t*>(&h1);
+    a[2] = *reinterpret_cast<uint32_t*>(&h2);
+    a[3] = *reinterpret_cast<uint32_t*>(&h3);
+}
+
+// The A fragment of one k16 block from its two Q8 words: PRMT puts each
+// offset-binary byte under the fp16 exponent of 1024, HSUB2 removes 1152.
+__device__ __forceinline__ void decode_frag8(uint32_t w0, uint32_t w1, uint32_t (&a)[4]) {
+    const __half2 off = __halves2half2(__ushort_as_half(0x6480), __ushort_as_half(0x6480));  // 1152
+    const uint32_t t0 = __byte_perm(w0, 0x64646464u, 0x4140), t1 = __byte_perm(w0, 0x64646464u, 0x4342);
+    const uint32_t t2 = __byte_perm(w1, 0x64646464u, 0x4140), t3 = __byte_perm(w1, 0x64646464u, 0x4342);
+    __half2 h0 = __hsub2(*reinterpret_cast<const __half2*>(&t0), off);
+    __half2 h1 = __hsub2(*reinterpret_cast<const __half2*>(&t1), off);
+    __half2 h2 = __hsub2(*reinterpret_cast<const __half2*>(&t2), off);
+    __half2 h3 = __hsub2(*reinterpret_cast<const __half2*>(&t3), off);
     a[0] = *reinterpret_cast<uint32_t*>(&h0);
     a[1] = *reinterpret_cast<uint32_t*>(&h1);
     a[2] = *reinterpret_cast<uint32_t*>(&h2);
@@ -142,12 +198,13 @@ __device__ __forceinline__ void load_scale_pair(const float* p, float& s0, float
 // ST scale type; XF 1: fp16 activations, 2: fp32 as fp16 hi + lo; KW warps
 // per tile (K split); GK 2: scale groups of two k16 blocks (group 32) with
 // static group ends, 0: any group length (tracked at run time).
-template <typename ST, int XF, int KW, int GK>
+template <typename ST, int XF, int KW, int GK, int BITS>
 __global__ void __launch_bounds__(kMmaThreads, 2) gemv_mma_kernel(MmaParams mp) {
     constexpr int NG = kMW / KW;  // warp groups; group it % NG takes unit it
     const StreamParams& p = mp.sp;
     extern __shared__ __align__(128) uint8_t smem[];
-    const int S = mp.ring_stages;
+    const int S = mp.ring_stages;  // a multiple of NG
+    const int SPG = S / NG;        // stages per group
     uint8_t* ring = smem;
     uint2* xs = reinterpret_cast<uint2*>(smem + (size_t)S * mp.stage_bytes);  // [XF][nkb * 4] B fragments
     float* red = reinterpret_cast<float*>(xs + (size_t)XF * mp.nkb * 4 + 4);   // after a 32-byte zero block: [2][kMW][16]
@@ -175,8 +232,11 @@ __global__ void __launch_bounds__(kMmaThreads, 2) gemv_mma_kernel(MmaParams mp) 
             const uint32_t wb = (uint32_t)mp.tile_wbytes, sb = (uint32_t)mp.tile_sbytes;
             int issued = 0;
             for (int it = 0; it < my_units; ++it) {
-                const int s = it % S;
-                if (it >= S && !mbar_wait(empty + s, ((it / S) & 1) ^ 1)) {
+                // Unit it belongs to group it % NG (its j-th unit), which owns
+                // the private sub-ring of stages g, g + NG, ...
+                const int j = it / NG;
+                const int s = it % NG + NG * (j % SPG);
+                if (j >= SPG && !mbar_wait(empty + s, ((j / SPG) & 1) ^ 1)) {
                     report_timeout(p.status);
                     break;
                 }
@@ -188,8 +248,14 @@ __global__ void __launch_bounds__(kMmaThreads, 2) gemv_mma_kernel(MmaParams mp) 
                 bulk_g2s(dst + wb, p.S + u * sb, sb, full + s, pol);
                 ++issued;
             }
-            for (int it = max(0, issued - S); it < issued; ++it)
-                if (!mbar_wait(full + it % S, (it / S) & 1)) { report_timeout(p.status); break; }
+            // The last S units issued are the last fills of S distinct stages.
+            for (int it = max(0, issued - S); it < issued; ++it) {
+                const int j = it / NG;
+                if (!mbar_wait(full + it % NG + NG * (j % SPG), (j / SPG) & 1)) {
+                    report_timeout(p.status);
+                    break;
+                }
+            }
         }
         return;
     }
@@ -249,8 +315,10 @@ __global__ void __launch_bounds__(kMmaThreads, 2) gemv_mma_kernel(MmaParams mp) 
 
     int local = 0;
     for (int it = grp; it < my_units; it += NG, ++local) {
-        const int s = it % S;
-        const bool ready = mbar_wait(full + s, (it / S) & 1);
+        // This group's local-th unit sits in its private stage grp + NG * (local % SPG):
+        // the group waits for fill f of a stage only after it consumed fill f - 1.
+        const int s = grp + NG * (local % SPG);
+        const bool ready = mbar_wait(full + s, (local / SPG) & 1);
         if (!ready) {
             report_timeout(p.status);
             *abort_flag = 1;
@@ -265,14 +333,23 @@ __global__ void __launch_bounds__(kMmaThreads, 2) gemv_mma_kernel(MmaParams mp) 
             int gi = kb0 / mp.gk, gpos = kb0 - gi * mp.gk;  // runtime group tracking (GK == 0)
 #pragma unroll 2
             for (int kb = kb0; kb < kb0 + kb_per; kb += 4) {
-                const uint4 wq = *reinterpret_cast<const uint4*>(wt + ((size_t)(kb >> 2) * 32 + lane) * 16);
+                // This lane's words of blocks kb..kb+3: one (Q4) or two (Q8) per block.
+                uint32_t words[2 * 4];
+                if constexpr (BITS == 4) {
+                    const uint4 wq = *reinterpret_cast<const uint4*>(wt + ((size_t)(kb >> 2) * 32 + lane) * 16);
+                    words[0] = wq.x; words[1] = wq.y; words[2] = wq.z; words[3] = wq.w;
+                } else {
+                    const uint4* wp = reinterpret_cast<const uint4*>(wt + ((size_t)(kb >> 2) * 32 + lane) * 32);
+                    const uint4 w01 = wp[0], w23 = wp[1];
+                    words[0] = w01.x; words[1] = w01.y; words[2] = w01.z; words[3] = w01.w;
+                    words[4] = w23.x; words[5] = w23.y; words[6] = w23.z; words[7] = w23.w;
+                }
                 const uint4 bh01 = xhi[(kb >> 2) * xstep], bh23 = xhi[(kb >> 2) * xstep + 1];
                 uint4 bl01 = make_uint4(0u, 0u, 0u, 0u), bl23 = bl01;
                 if constexpr (XF == 2) {
                     bl01 = xlo[(kb >> 2) * xstep];
                     bl23 = xlo[(kb >> 2) * xstep + 1];
                 }
-                const uint32_t words[4] = {wq.x, wq.y, wq.z, wq.w};
                 const uint2 bh[4] = {make_uint2(bh01.x, bh01.y), make_uint2(bh01.z, bh01.w),
                                      make_uint2(bh23.x, bh23.y), make_uint2(bh23.z, bh23.w)};
                 const uint2 blo[4] = {make_uint2(bl01.x, bl01.y), make_uint2(bl01.z, bl01.w),
@@ -280,7 +357,8 @@ __global__ void __launch_bounds__(kMmaThreads, 2) gemv_mma_kernel(MmaParams mp) 
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
                     uint32_t a[4];
-                    decode_frag(words[j], a);
+                    if constexpr (BITS == 4) decode_frag(words[j], a);
+                    else decode_frag8(words[2 * j], words[2 * j + 1], a);
                     if constexpr (GK == 2) {
                         // Static groups of two blocks: fresh accumulator on even j.
                         if ((j & 1) == 0) mma16816_zc(c, a, bh[j]);
@@ -353,7 +431,10 @@ struct MmaPlan {
 
 int frag_tiles_padded(int n) { return ((n + 15) / 16 + 7) / 8 * 8; }
 
-int scale_groups(const aexis_weights* w) { return w->group > 0 ? w->k / w->group : 1; }
+int scale_groups(const aexis_weights* w) { return w->kind == WK_Q4 && w->group > 0 ? w->k / w->group : 1; }
+
+// Bytes of one 16-row tile of fragment words.
+int tile_wbytes(const aexis_weights* w) { return (w->kind == WK_Q8 ? 16 : 8) * w->k; }
 
 // K split: enough (tile, K-share) units for every consumer warp of two CTAs
 // per SM (KW = 1 when the tiles alone suffice; up to 8 warps on one tile for
@@ -362,25 +443,32 @@ int scale_groups(const aexis_weights* w) { return w->group > 0 ? w->k / w->group
 // CTAs per SM allows (at least 3), else one CTA per SM.
 bool plan_mma(const aexis_weights* w, int xf, int sm_count, MmaPlan& pl) {
     const int nkb = w->k / 16;
-    const int gk = w->group > 0 ? w->group / 16 : nkb;
+    const int gk = w->kind == WK_Q4 && w->group > 0 ? w->group / 16 : nkb;
     const int ntiles = (w->n + 15) / 16;
     const int st = w->scale_dtype == AEXIS_F16 ? 2 : 4;
-    const int stage = 8 * w->k + scale_groups(w) * 16 * st;
+    const int stage = tile_wbytes(w) + scale_groups(w) * 16 * st;
     const int fixed = xf * nkb * 32 + 32 + 2 * kMW * 16 * 4 + 16 * 16 + 64 + kMW * 4 + 128;
     const int want = 2 * sm_count * kMW;  // warp units that fill two CTAs per SM
-    int kw = 1;
-    while (kw < 8 && (long long)ntiles * kw < want) kw <<= 1;
-    for (; kw >= 1; kw >>= 1) {
-        if (nkb % (kw * 4) != 0) continue;
-        if ((nkb / kw) % gk != 0 && gk != nkb) continue;
-        break;
-    }
-    if (kw < 1) return false;
+    int kw0 = 1;
+    while (kw0 < 8 && (long long)ntiles * kw0 < want) kw0 <<= 1;
     for (int per_sm = 2; per_sm >= 1; --per_sm) {
         const int budget = per_sm == 2 ? 113 * 1024 : 227 * 1024;
         int S = (budget - fixed) / stage;
         S = S > 16 ? 16 : S;
         if (S < (per_sm == 2 ? 3 : 2)) continue;
+        // Every warp group owns S / NG stages: NG = 8 / kw must not exceed S.
+        // Preferred split first, then larger, then smaller ones that still fit.
+        int kw_min = 1;
+        while (kw_min < 8 && kMW / kw_min > S) kw_min <<= 1;
+        const int pref = kw0 > kw_min ? kw0 : kw_min;
+        auto fits = [&](int kw) { return nkb % (kw * 4) == 0 && ((nkb / kw) % gk == 0 || gk == nkb); };
+        int kw = 0;
+        for (int c = pref; c <= 8 && !kw; c <<= 1)
+            if (fits(c)) kw = c;
+        for (int c = pref >> 1; c >= kw_min && !kw; c >>= 1)
+            if (fits(c)) kw = c;
+        if (!kw) continue;
+        S -= S % (kMW / kw);
         pl.kw = kw;
         pl.units = ntiles;
         pl.stages = S;
@@ -392,14 +480,14 @@ bool plan_mma(const aexis_weights* w, int xf, int sm_count, MmaPlan& pl) {
     return false;
 }
 
-template <typename ST, int XF, int KW, int GK>
+template <typename ST, int XF, int KW, int GK, int BITS>
 cudaError_t launch_mma_t(const MmaParams& mp, int grid, int smem, bool pdl, cudaStream_t stream) {
     static int configured[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
     if (smem > configured[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(gemv_mma_kernel<ST, XF, KW, GK>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        cudaError_t e = cudaFuncSetAttribute(gemv_mma_kernel<ST, XF, KW, GK, BITS>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e != cudaSuccess) return e;
         configured[dev] = smem;
     }
@@ -413,30 +501,33 @@ cudaError_t launch_mma_t(const MmaParams& mp, int grid, int smem, bool pdl, cuda
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, gemv_mma_kernel<ST, XF, KW, GK>, mp);
+    return cudaLaunchKernelEx(&cfg, gemv_mma_kernel<ST, XF, KW, GK, BITS>, mp);
 }
 
-template <typename ST, int XF, int GK>
+template <typename ST, int XF, int GK, int BITS>
 cudaError_t launch_mma_kw(const MmaParams& mp, int kw, int grid, int smem, bool pdl, cudaStream_t s) {
     switch (kw) {
-        case 1: return launch_mma_t<ST, XF, 1, GK>(mp, grid, smem, pdl, s);
-        case 2: return launch_mma_t<ST, XF, 2, GK>(mp, grid, smem, pdl, s);
-        case 4: return launch_mma_t<ST, XF, 4, GK>(mp, grid, smem, pdl, s);
-        default: return launch_mma_t<ST, XF, 8, GK>(mp, grid, smem, pdl, s);
+        case 1: return launch_mma_t<ST, XF, 1, GK, BITS>(mp, grid, smem, pdl, s);
+        case 2: return launch_mma_t<ST, XF, 2, GK, BITS>(mp, grid, smem, pdl, s);
+        case 4: return launch_mma_t<ST, XF, 4, GK, BITS>(mp, grid, smem, pdl, s);
+        default: return launch_mma_t<ST, XF, 8, GK, BITS>(mp, grid, smem, pdl, s);
     }
 }
 
+// Q4 with groups of 32 takes the static group path; Q8 (one scale per row)
+// and other Q4 groups the run-time one.
 template <typename ST, int XF>
-cudaError_t launch_mma_gk(const MmaParams& mp, int kw, int grid, int smem, bool pdl, cudaStream_t s) {
-    if (mp.gk == 2) return launch_mma_kw<ST, XF, 2>(mp, kw, grid, smem, pdl, s);
-    return launch_mma_kw<ST, XF, 0>(mp, kw, grid, smem, pdl, s);
+cudaError_t launch_mma_gk(const MmaParams& mp, int bits, int kw, int grid, int smem, bool pdl, cudaStream_t s) {
+    if (bits == 8) return launch_mma_kw<ST, XF, 0, 8>(mp, kw, grid, smem, pdl, s);
+    if (mp.gk == 2) return launch_mma_kw<ST, XF, 2, 4>(mp, kw, grid, smem, pdl, s);
+    return launch_mma_kw<ST, XF, 0, 4>(mp, kw, grid, smem, pdl, s);
 }
 
 }  // namespace
 
 bool gemv_mma_eligible(const aexis_weights* w) {
-    if (w->kind != WK_Q4 || w->k % 64 != 0 || w->n <= 0) return false;
-    if (w->group > 0 && (w->group % 16 != 0 || w->k % w->group != 0)) return false;
+    if ((w->kind != WK_Q4 && w->kind != WK_Q8) || w->k % 64 != 0 || w->n <= 0) return false;
+    if (w->kind == WK_Q4 && w->group > 0 && (w->group % 16 != 0 || w->k % w->group != 0)) return false;
     MmaPlan pl;
     return plan_mma(w, 2, 148, pl);
 }
@@ -445,11 +536,22 @@ size_t gemv_mma_frag_bytes(const aexis_weights* w, size_t* scale_bytes) {
     const size_t tiles = (size_t)frag_tiles_padded(w->n);
     if (scale_bytes)
         *scale_bytes = tiles * scale_groups(w) * 16 * (w->scale_dtype == AEXIS_F16 ? 2 : 4);
-    return tiles * 8 * (size_t)w->k;
+    return tiles * (size_t)tile_wbytes(w);
 }
 
-cudaError_t launch_repack_q4_frag(const aexis_weights* w, cudaStream_t s) {
+cudaError_t launch_repack_frag(const aexis_weights* w, cudaStream_t s) {
     const int tiles = frag_tiles_padded(w->n);
+    if (w->kind == WK_Q8) {
+        if (w->scale_dtype == AEXIS_F16)
+            repack_q8_frag_kernel<__half><<<148 * 8, 256, 0, s>>>(
+                reinterpret_cast<const uint32_t*>(w->data), reinterpret_cast<const __half*>(w->scales), w->n, w->k,
+                tiles, reinterpret_cast<uint32_t*>(w->frag), reinterpret_cast<__half*>(w->frag_scales));
+        else
+            repack_q8_frag_kernel<float><<<148 * 8, 256, 0, s>>>(
+                reinterpret_cast<const uint32_t*>(w->data), reinterpret_cast<const float*>(w->scales), w->n, w->k,
+                tiles, reinterpret_cast<uint32_t*>(w->frag), reinterpret_cast<float*>(w->frag_scales));
+        return cudaGetLastError();
+    }
     if (w->scale_dtype == AEXIS_F16)
         repack_q4_frag_kernel<__half><<<148 * 8, 256, 0, s>>>(
             reinterpret_cast<const uint32_t*>(w->data), reinterpret_cast<const __half*>(w->scales), w->n, w->k,
@@ -498,17 +600,18 @@ cudaError_t launch_gemv_mma(const GemvArgs& a, int sm_count, cudaStream_t stream
     sp.argmax_key = a.argmax_key;
     sp.status = a.status;
     mp.nkb = w->k / 16;
-    mp.gk = w->group > 0 ? w->group / 16 : mp.nkb;
-    mp.tile_wbytes = 8 * w->k;
+    mp.gk = w->kind == WK_Q4 && w->group > 0 ? w->group / 16 : mp.nkb;
+    mp.tile_wbytes = tile_wbytes(w);
     mp.tile_sbytes = scale_groups(w) * 16 * (w->scale_dtype == AEXIS_F16 ? 2 : 4);
     mp.units = pl.units;
     mp.ring_stages = pl.stages;
     mp.stage_bytes = pl.stage_bytes;
     const int grid = pl.units < pl.per_sm * sm_count ? pl.units : pl.per_sm * sm_count;
+    const int bits = w->kind == WK_Q8 ? 8 : 4;
     if (w->scale_dtype == AEXIS_F16) {
-        if (xf == 1) return launch_mma_gk<__half, 1>(mp, pl.kw, grid, pl.smem, a.pdl, stream);
-        return launch_mma_gk<__half, 2>(mp, pl.kw, grid, pl.smem, a.pdl, stream);
+        if (xf == 1) return launch_mma_gk<__half, 1>(mp, bits, pl.kw, grid, pl.smem, a.pdl, stream);
+        return launch_mma_gk<__half, 2>(mp, bits, pl.kw, grid, pl.smem, a.pdl, stream);
     }
-    if (xf == 1) return launch_mma_gk<float, 1>(mp, pl.kw, grid, pl.smem, a.pdl, stream);
-    return launch_mma_gk<float, 2>(mp, pl.kw, grid, pl.smem, a.pdl, stream);
+    if (xf == 1) return launch_mma_gk<float, 1>(mp, bits, pl.kw, grid, pl.smem, a.pdl, stream);
+    return launch_mma_gk<float, 2>(mp, bits, pl.kw, grid, pl.smem, a.pdl, stream);
 }
