@@ -67,7 +67,8 @@ def build_native(force: bool = False, jobs: int | None = None) -> str:
         with cf.ThreadPoolExecutor(max_workers=jobs or min(len(todo), os.cpu_count() or 4)) as ex:
             list(ex.map(lambda a: _compile(*a), todo))
     if force or todo or _stale(LIB, objs):
-        cmd = [nvcc(), *ARCH, "-shared", "-cudart", "static", "-o", LIB, *objs]
+        # --no-undefined: a declaration without a definition fails here, not at load time.
+        cmd = [nvcc(), *ARCH, "-shared", "-cudart", "static", "-Xlinker", "--no-undefined", "-o", LIB, *objs]
         res = subprocess.run(cmd, capture_output=True, text=True)
         if res.returncode != 0:
             raise RuntimeError("link failed:\n" + res.stderr[-4000:])

@@ -520,7 +520,11 @@ AEXIS_API int aexis_cuda_topk(aexis_ctx* ctx, const float* logits, int rows, int
     if (ld < width) return aexis_fail(ctx, AEXIS_E_SHAPE, "ld=%d < width", ld);
     int rc = bind(ctx);
     if (rc) return rc;
-    return aexis_cuda_check(ctx, launch_topk(logits, rows, width, ld, k, out_vals, out_idx, ctx->stream), "topk launch");
+    void* scratch = nullptr;
+    rc = aexis_scratch(ctx, topk_scratch_bytes(rows, width, k, ctx->sm_count), &scratch);
+    if (rc) return rc;
+    return aexis_cuda_check(ctx, launch_topk(logits, rows, width, ld, k, out_vals, out_idx, scratch, ctx->sm_count,
+                                             ctx->stream), "topk launch");
 }
 
 AEXIS_API int aexis_cuda_embed(aexis_ctx* ctx, const int32_t* words, int count, const aexis_weights* table,

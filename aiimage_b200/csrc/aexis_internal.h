@@ -169,8 +169,10 @@ cudaError_t launch_argmax(const float* logits, int rows, int width, int ld, int3
                           unsigned long long* keys, int sm_count, cudaStream_t s);
 cudaError_t launch_argmax_keys(const float* logits, int rows, int width, int ld, long long offset,
                                unsigned long long* keys, int sm_count, cudaStream_t s);
-cudaError_t launch_topk(const float* logits, int rows, int width, int ld, int k, float* vals,
-                        int32_t* idx, cudaStream_t s);
+// Per-row top-k (k <= 64): scratch of topk_scratch_bytes() device bytes.
+size_t topk_scratch_bytes(int rows, int width, int k, int sm_count);
+cudaError_t launch_topk(const float* logits, int rows, int width, int ld, int k, float* vals, int32_t* idx,
+                        void* scratch, int sm_count, cudaStream_t s);
 cudaError_t launch_embed(const int32_t* words, int count, const aexis_weights* table,
                          const float* bias, float* out, cudaStream_t s);
 cudaError_t launch_swish(const float* x, int count, float* y, cudaStream_t s);

@@ -198,10 +198,39 @@ __global__ void argmax_partial_kernel(const float* logits, int width, int ld, un
                                       long long offset = 0) {
     const int row = blockIdx.y;
     const float* x = logits + (long long)row * ld;
-    unsigned long long best = 0ull;
-    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < width; i += gridDim.x * blockDim.x) {
-        const unsigned long long kk = argmax_key(x[i], (int)(offset + i));
-        best = kk > best ? kk : best;
+    // Each thread scans its elements in ascending index order keeping the
+    // first strict maximum (NaN never compares greater), then builds one key;
+    // the key order settles ties across threads (lower index wins, -0 == +0).
+    // A NaN at global index 0 wins, as in the reference's scan that starts
+    // from element 0.
+    float bv = -INFINITY;
+    int bi = -1;
+    const int tid = blockIdx.x * blockDim.x + threadIdx.x, nth = gridDim.x * blockDim.x;
+    auto take = [&](float v, int i) {
+        if (v > bv || (bi < 0 && v == v)) {
+            bv = v;
+            bi = i;
+        }
+    };
+    int start = 0;
+    if ((reinterpret_cast<uintptr_t>(x) & 15) == 0) {
+        const int nvec = width / 4;
+        const float4* x4 = reinterpret_cast<const float4*>(x);
+#pragma unroll 4
+        for (int q = tid; q < nvec; q += nth) {
+            const float4 v = x4[q];
+            take(v.x, 4 * q);
+            take(v.y, 4 * q + 1);
+            take(v.z, 4 * q + 2);
+            take(v.w, 4 * q + 3);
+        }
+        start = 4 * nvec;
+    }
+    for (int i = start + tid; i < width; i += nth) take(x[i], i);
+    unsigned long long best = bi >= 0 ? argmax_key(bv, (int)(offset + bi)) : 0ull;
+    if (tid == 0 && offset == 0 && width > 0) {
+        const unsigned long long k0 = argmax_key(x[0], 0);
+        best = k0 > best ? k0 : best;
     }
 #pragma unroll
     for (int o = 16; o >= 1; o >>= 1) {

@@ -611,6 +611,22 @@ def run_only(args):
     peak, _ = measured_peak()
     if args.only == "decoder":
         out = bench_decoder(ops, peak, args.prompt_len, args.new_tokens)
+    elif args.only == "topk":
+        m, vocab, k = 256, 151936, 50
+        g = torch.Generator(device="cuda").manual_seed(5)
+        logits = torch.randn((m, vocab), generator=g, device="cuda", dtype=torch.float32)
+        vals = torch.empty((m, k), dtype=torch.float32, device="cuda")
+        idx = torch.empty((m, k), dtype=torch.int32, device="cuda")
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        for i in range(args.warmup + args.steps):
+            if i == args.warmup:
+                e0.record()
+            ops.top_k(logits, vocab, m, k, vals, idx)
+        e1.record()
+        e1.synchronize()
+        t = e0.elapsed_time(e1) / 1e3 / max(1, args.steps)
+        out = {"kernel": "topk 256x151936 k50", "us": round(t * 1e6, 2),
+               "GB/s": round(m * vocab * 4 / t / 1e9, 1)}
     elif args.only == "config4":
         out = bench_config4(ops, peak, 1, 0, steps=args.new_tokens, total_seqs=32)
     elif args.only == "tcgemm":
@@ -700,7 +716,7 @@ def main():
     ap.add_argument("--skip-config5", action="store_true", help="omit the config-5 lm_head measurement")
     ap.add_argument("--skip-config4", action="store_true", help="omit the config-4 batched decoder measurement")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
-    ap.add_argument("--only", choices=["dominant", "decoder", "tcgemm", "config4"], help="profiling mode (see run_only)")
+    ap.add_argument("--only", choices=["dominant", "decoder", "tcgemm", "config4", "topk"], help="profiling mode (see run_only)")
     ap.add_argument("--prompt-len", type=int, default=512)
     ap.add_argument("--new-tokens", type=int, default=64)
     args = ap.parse_args()
