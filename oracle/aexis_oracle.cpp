@@ -333,21 +333,25 @@ ORACLE_API void oracle_argmax(const float* logits, int rows, int width, int ld, 
 }
 
 // Top-k per row: the k largest logits in descending order; equal values are
-// ordered by ascending index (the argmax tie rule extended to k entries).
+// ordered by ascending index (the argmax tie rule extended to k entries). NaN
+// is never selected; a row with fewer than k other values is padded with
+// (-inf, -1).
 ORACLE_API void oracle_topk(const float* logits, int rows, int width, int ld, int k,
                             float* out_vals, int32_t* out_idx) {
     for (int r = 0; r < rows; ++r) {
         const float* x = logits + (int64_t)r * ld;
-        std::vector<int> ord(width);
-        for (int i = 0; i < width; ++i) ord[i] = i;
-        int kk = std::min(k, width);
+        std::vector<int> ord;
+        ord.reserve(width);
+        for (int i = 0; i < width; ++i)
+            if (x[i] == x[i]) ord.push_back(i);
+        const int kk = std::min<int>(k, (int)ord.size());
         std::partial_sort(ord.begin(), ord.begin() + kk, ord.end(), [&](int a, int b) {
             if (x[a] != x[b]) return x[a] > x[b];
             return a < b;
         });
-        for (int j = 0; j < kk; ++j) {
-            out_vals[(int64_t)r * k + j] = x[ord[j]];
-            out_idx[(int64_t)r * k + j] = ord[j];
+        for (int j = 0; j < k; ++j) {
+            out_vals[(int64_t)r * k + j] = j < kk ? x[ord[j]] : -INFINITY;
+            out_idx[(int64_t)r * k + j] = j < kk ? ord[j] : -1;
         }
     }
 }

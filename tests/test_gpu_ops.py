@@ -186,6 +186,61 @@ def test_topk(ops, oracle):
     assert np.all(np.isneginf(host(vals)[:2, 30:]))
 
 
+def _wide_topk_rows(width: int, seed: int) -> np.ndarray:
+    """Rows built to defeat a sampled threshold: every case must fall back to
+    the exact per-row path or survive the candidate filter unchanged."""
+    r = np.random.default_rng(seed)
+    x = r.standard_normal((12, width)).astype(np.float32)
+    samples = (np.arange(4096, dtype=np.int64) * width) // 4096
+    off = np.setdiff1d(np.arange(width), samples)
+    x[1, :] = 1.0                                   # one plateau: candidate overflow
+    x[2, :] = -1.0                                  # large values only between samples
+    x[2, r.choice(off, 1000, replace=False)] = 5.0
+    x[3] *= 0.01                                    # 20 large values on sample positions:
+    x[3, samples[r.choice(4096, 20, replace=False)]] = 10.0  # fewer than k above t
+    x[4, ::2] = np.nan                              # half NaN
+    x[5, :] = np.nan                                # 30 selectable values: padding
+    x[5, r.choice(width, 30, replace=False)] = r.standard_normal(30)
+    x[6, :] = -np.inf                               # -inf is selectable, by index
+    x[6, r.choice(width, 10, replace=False)] = 1.0
+    x[7] = np.sort(x[7])                            # ascending along the index
+    x[8] = np.round(x[8] * 2) / 2                   # few levels: ties at t
+    x[9, :] = 0.0                                   # signed zeros plus 100 positives
+    x[9, ::3] = -0.0
+    x[9, r.choice(width, 100, replace=False)] = 2.0
+    x[10, -1] = 100.0                               # the row's last element wins
+    x[11, 1:] = x[11, 0]                            # tie at every index
+    return x
+
+
+@pytest.mark.parametrize("width,ld", [(151936, 151936), (40001, 40004), (40001, 40001), (32768, 32768)])
+def test_topk_wide_rows(ops, oracle, width, ld):
+    """The sampled path (width >= 32768, 16-byte rows) and the exact path
+    behind it against the oracle; ld == width odd takes the exact path."""
+    import torch
+    x = _wide_topk_rows(width, 12 + width)
+    rows, k = x.shape[0], 50
+    buf = np.full((rows, ld), 7.0, dtype=np.float32)  # ld padding never read
+    buf[:, :width] = x
+    vals = torch.zeros((rows, k), dtype=torch.float32, device="cuda")
+    idx = torch.zeros((rows, k), dtype=torch.int32, device="cuda")
+    ops.top_k(cuda(buf), width, rows, k, vals, idx, ld=ld)
+    rv, ri = oracle.topk(x, k)
+    assert np.array_equal(host(idx), ri)
+    assert np.array_equal(host(vals), rv)
+
+
+@pytest.mark.parametrize("k", [1, 7, 64])
+def test_topk_k_range(ops, oracle, k):
+    import torch
+    x = np.random.default_rng(13 + k).standard_normal((3, 151936)).astype(np.float32)
+    vals = torch.zeros((3, k), dtype=torch.float32, device="cuda")
+    idx = torch.zeros((3, k), dtype=torch.int32, device="cuda")
+    ops.top_k(cuda(x), 151936, 3, k, vals, idx)
+    rv, ri = oracle.topk(x, k)
+    assert np.array_equal(host(idx), ri) and np.array_equal(host(vals), rv)
+
+
 def test_topk_config5_shape(ops, oracle):
     """256 rows x 151936 logits, k = 50 (the config-5 sampler input)."""
     import torch
