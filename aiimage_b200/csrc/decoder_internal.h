@@ -33,7 +33,22 @@ struct aexis_decoder {
     cudaGraphExec_t step_exec = nullptr, prefill_exec = nullptr;
     std::vector<int> qkv_perm;      // internal row -> logical (kind, head, dim)
     bool split_attn = false;        // decode attention by launch_split_attention
+    // Persistent greedy loop (k_decoder_persist.cu): 0 never (default), 1
+    // always (generate fails where unsupported), -1 where supported.
+    int persist_mode = 0;
+    void* persist_phases = nullptr;  // device phase table of one step
+    int persist_nphases = 0;
+    void* persist_sync = nullptr;    // arrival counter, abort flag, greedy keys
+    void* persist_stream = nullptr;  // every CTA's weight units of one step, CTA-major
+    void* persist_off = nullptr;     // [sm_count + 1] unit offsets into persist_stream
+    bool persist_packed = false;     // persist_stream matches the current weights
 };
+
+// The persistent greedy loop: whether it runs this decoder, and `nsteps`
+// greedy steps from the device state (ints[0] token, [1] position, [2]
+// output cursor) in one cooperative launch.
+bool decoder_persist_supported(const aexis_decoder* d, int sm_count);
+cudaError_t decoder_persist_run(aexis_decoder* d, int nsteps, cudaStream_t s);
 
 // cos/sin tables [cap][rot/2] of Qwen35DecoderSession.CreateRopeTextures
 // (Qwen35DecoderSession.cs:1660-1687): inv = 1 / theta^(j * 2/rot) in fp32,

@@ -467,6 +467,11 @@ int upload_f32(aexis_decoder* d, float* dst, const void* src, int dtype, size_t 
                             "norm upload");
 }
 
+// Whether generate runs the persistent greedy loop.
+bool use_persist(aexis_decoder* d) {
+    return d->persist_mode != 0 && decoder_persist_supported(d, d->ctx->sm_count);
+}
+
 // Replays `count` decode steps; emit = 1 uses the full step graph (lm_head,
 // greedy token fed back on the device), emit = 0 the prompt-token graph.
 int run_steps(aexis_decoder* d, int emit, int count) {
@@ -622,7 +627,8 @@ AEXIS_API int aexis_cuda_decoder_destroy(aexis_decoder* d) {
     }
     free_weights(d->lm);
     void* bufs[] = {d->final_norm, d->embed, d->rope_map, d->rope_cos, d->rope_sin, d->kcache, d->vcache, d->h, d->q,
-                    d->attn, d->act, d->logits, d->part, d->counters, d->key, d->ints};
+                    d->attn, d->act, d->logits, d->part, d->counters, d->key, d->ints, d->persist_phases,
+                    d->persist_sync, d->persist_stream, d->persist_off};
     for (void* b : bufs)
         if (b) cudaFree(b);
     delete d;
@@ -641,6 +647,7 @@ AEXIS_API int aexis_cuda_decoder_set_linear(aexis_decoder* d, int layer, int whi
         if (which != 7) return aexis_fail(d->ctx, AEXIS_E_RANGE, "layer -1 takes which=7 (lm_head)");
         rc = scatter_rows(d, d->lm, packed, scales, scale_dtype, c.vocab, 0, 1, none);
         if (!rc && d->lm.frag) rc = build_frag(d, d->lm);
+        d->persist_packed = false;
         if (!rc) d->lm_set = 1;
         return rc;
     }
@@ -672,6 +679,7 @@ AEXIS_API int aexis_cuda_decoder_set_linear(aexis_decoder* d, int layer, int whi
     if (!rc) {
         aexis_weights* w = which <= 2 ? &L.qkv : which == 3 ? &L.o : which <= 5 ? &L.gateup : &L.down;
         if (w->frag) rc = build_frag(d, *w);
+        d->persist_packed = false;
     }
     if (!rc) L.set_mask |= 1 << which;
     return rc;
@@ -769,6 +777,27 @@ AEXIS_API int aexis_cuda_decoder_generate(aexis_decoder* d, const int32_t* promp
     if (!rc) rc = ready(d);
     if (rc) return rc;
     cudaStream_t s = d->ctx->stream;
+    if (use_persist(d)) {
+        // Prompt tokens but the last: the prefill graph (no lm_head). Then
+        // every emitting step in one persistent launch.
+        for (int i = 0; i + 1 < n_prompt; ++i) {
+            cudaError_t e = cudaMemcpyAsync(d->ints, prompt + i, sizeof(int), cudaMemcpyHostToDevice, s);
+            if (e != cudaSuccess) return aexis_cuda_check(d->ctx, e, "token upload");
+            rc = run_steps(d, 0, 1);
+            if (rc) return rc;
+        }
+        cudaError_t e = cudaMemcpyAsync(d->ints, prompt + n_prompt - 1, sizeof(int), cudaMemcpyHostToDevice, s);
+        if (e == cudaSuccess) e = cudaMemsetAsync(d->ints + 2, 0, sizeof(int), s);  // output cursor
+        if (e != cudaSuccess) return aexis_cuda_check(d->ctx, e, "token upload");
+        rc = aexis_cuda_check(d->ctx, decoder_persist_run(d, max_new, s), "persistent decode launch");
+        if (rc) return rc;
+        d->host_pos += n_prompt + max_new - 1;
+        rc = aexis_cuda_check(d->ctx, cudaMemcpyAsync(out_tokens, d->ints + 3, sizeof(int) * max_new,
+                                                      cudaMemcpyDeviceToHost, s), "readback");
+        if (!rc) rc = aexis_cuda_check(d->ctx, cudaStreamSynchronize(s), "sync");
+        if (!rc) rc = aexis_check_status(d->ctx);
+        return rc;
+    }
     // Prompt: one token upload + prefill graph per token, the last one emits.
     for (int i = 0; i < n_prompt; ++i) {
         cudaError_t e = cudaMemcpyAsync(d->ints, prompt + i, sizeof(int), cudaMemcpyHostToDevice, s);
@@ -790,6 +819,25 @@ AEXIS_API int aexis_cuda_decoder_generate(aexis_decoder* d, const int32_t* promp
     if (!rc) rc = aexis_cuda_check(d->ctx, cudaStreamSynchronize(s), "sync");
     if (!rc) rc = aexis_check_status(d->ctx);
     return rc;
+}
+
+AEXIS_API int aexis_cuda_decoder_set_schedule(aexis_decoder* d, int mode) {
+    if (!d) return AEXIS_E_NULL;
+    if (mode < -1 || mode > 1) return aexis_fail(d->ctx, AEXIS_E_RANGE, "mode=%d (-1, 0 or 1)", mode);
+    int rc = dbind(d);
+    if (rc) return rc;
+    if (mode == 1 && !decoder_persist_supported(d, d->ctx->sm_count))
+        return aexis_fail(d->ctx, AEXIS_E_UNSUPPORTED, "the persistent decode loop does not support this decoder");
+    d->persist_mode = mode;
+    return AEXIS_OK;
+}
+
+AEXIS_API int aexis_cuda_decoder_schedule(aexis_decoder* d, int32_t* out) {
+    if (!d || !out) return AEXIS_E_NULL;
+    int rc = dbind(d);
+    if (rc) return rc;
+    *out = use_persist(d) ? 1 : 0;
+    return AEXIS_OK;
 }
 
 AEXIS_API int aexis_cuda_decoder_logits(aexis_decoder* d, float* out) {

@@ -117,6 +117,16 @@ class DecoderSession:
         self._check(lib().aexis_cuda_decoder_logits(self.h, _np(out)))
         return out
 
+    def set_schedule(self, mode: int):
+        """How generate runs its greedy steps: 0 (default) one CUDA graph per
+        step, 1 one persistent kernel for the whole call, -1 1 where supported."""
+        self._check(lib().aexis_cuda_decoder_set_schedule(self.h, int(mode)))
+
+    def schedule(self) -> int:
+        out = np.zeros(1, dtype=np.int32)
+        self._check(lib().aexis_cuda_decoder_schedule(self.h, _np(out)))
+        return int(out[0])
+
 
 class BatchSession:
     """Batched greedy decoding of B independent sequences over one

@@ -69,6 +69,8 @@ SIGNATURES = {
     "aexis_cuda_decoder_step": (i32, [vp, C.c_int32, vp]),
     "aexis_cuda_decoder_generate": (i32, [vp, vp, i32, i32, vp]),
     "aexis_cuda_decoder_logits": (i32, [vp, vp]),
+    "aexis_cuda_decoder_set_schedule": (i32, [vp, i32]),
+    "aexis_cuda_decoder_schedule": (i32, [vp, vp]),
     "aexis_cuda_selftest_wait": (i32, [vp, C.c_longlong]),
     "aexis_cuda_batch_create": (i32, [vp, i32, i32, i32, C.POINTER(vp)]),
     "aexis_cuda_batch_destroy": (i32, [vp]),

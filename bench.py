@@ -443,13 +443,27 @@ def bench_decoder(ops, peak, prompt_len: int = 512, new_tokens: int = 64):
     step_s = time.perf_counter() - t0
     kv_mean = cfg.n_layers * 2 * cfg.n_kv_heads * cfg.head_dim * 2 * (prompt_len - 1 + new_tokens // 2)
     bytes_tok = model.weight_bytes_per_token() + kv_mean
+    # The same generate call under the persistent schedule (one cooperative
+    # kernel for every emitting step), reported beside the default graphs.
+    persist = None
+    sess.set_schedule(-1)
+    if sess.schedule() == 1:
+        sess.reset()
+        sess.prefill(prompt[:-1])
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        ptoks = sess.generate(prompt[-1:], new_tokens)
+        ps = time.perf_counter() - t0
+        persist = {"tokens_per_s": round(new_tokens / ps, 1), "ms_per_token": round(ps / new_tokens * 1e3, 4),
+                   "same_tokens": ptoks == toks}
     sess.close()
     n = new_tokens
     return {"workload": f"config3_q4_decoder_prompt{prompt_len}_greedy{n}", "tokens_per_s": round(n / gen_s, 1),
             "ms_per_token": round(gen_s / n * 1e3, 4), "e2e_tokens_per_s_host_roundtrip": round(n / step_s, 1),
             "bytes_per_token": bytes_tok, "GB/s": round(bytes_tok * n / gen_s / 1e9, 1),
             "frac": round(bytes_tok * n / gen_s / 1e9 / peak, 3), "first_tokens": toks[:8],
-            "kernels_per_token": 2 + 5 * cfg.n_layers + 1}
+            "kernels_per_token": 2 + 5 * cfg.n_layers + 1, "schedule": "graph per step",
+            "persistent_schedule": persist}
 
 
 def bench_config4(ops, peak, world: int, rank: int, steps: int = 128, total_seqs: int = 256, per_batch: int = 32):

@@ -332,6 +332,22 @@ int aexis_cuda_decoder_generate(aexis_decoder* dec, const int32_t* prompt, int n
  * greedy path (Qwen35DecoderSession.ProjectLogits :715-733). */
 int aexis_cuda_decoder_logits(aexis_decoder* dec, float* out_logits);
 
+/* How aexis_cuda_decoder_generate schedules its greedy steps (no reference
+ * counterpart: the reference dispatches per layer). mode 0: one CUDA graph
+ * per step (every kernel a programmatic dependent of the previous one);
+ * mode 1: every emitting step of the call in one persistent cooperative
+ * kernel (one CTA per SM, grid barriers between phases, weights streamed
+ * ahead through a bulk-copy ring), AEXIS_E_UNSUPPORTED unless the decoder is
+ * Q4 group-32 with fp16 scales, head_dim 128, at most 4 query heads per KV
+ * head, K dims multiples of 512 and kv_capacity <= 2048; mode -1: 1 where
+ * supported, else 0. The default is 0: on B200 the config-3 model decodes at
+ * about 1550 tokens/s with graphs and 1400 with the persistent kernel, both
+ * bound by about five dependent L2 round trips per layer phase. Both produce
+ * the same greedy tokens (fp32 sums in a different order).
+ * aexis_cuda_decoder_schedule reports the schedule generate will use (0 or 1). */
+int aexis_cuda_decoder_set_schedule(aexis_decoder* dec, int mode);
+int aexis_cuda_decoder_schedule(aexis_decoder* dec, int32_t* out_schedule);
+
 /* ---- batched greedy decoding ------------------------------------------------
  * B independent sequences decoded together on one GPU: Qwen35DecoderSession's
  * DecodeCore + SelectNextToken (Qwen35DecoderSession.cs:469-585, 734-809) run

@@ -72,14 +72,17 @@ def test_decoder_capacity_and_errors(ops):
         DecoderSession(ops, bad)
 
 
-@pytest.mark.parametrize("case", ["qwen35_08b_q4_prompt512", "qwen35_08b_q8_prompt64"])
-def test_full_decoder_matches_golden_tokens(ops, case):
+@pytest.mark.parametrize("case,schedule", [("qwen35_08b_q4_prompt512", 0), ("qwen35_08b_q4_prompt512", 1),
+                                           ("qwen35_08b_q8_prompt64", 0)])
+def test_full_decoder_matches_golden_tokens(ops, case, schedule):
     """BASELINE config 3 (and its Q8 variant): 64 greedy tokens identical to the
-    oracle's, generated offline into tests/golden/decoder_greedy.json."""
+    oracle's, generated offline into tests/golden/decoder_greedy.json; the Q4
+    model under both schedules (per-step graphs, one persistent kernel)."""
     gold = json.load(open(GOLDEN))[case]
     model = synth.SyntheticDecoder(getattr(synth, gold["cfg"]), seed=gold["seed"])
     prompt = model.prompt(gold["prompt_len"], seed=gold["prompt_seed"])
     sess = make_session(ops, model)
+    sess.set_schedule(schedule)
     got = sess.generate(prompt, gold["max_new"])
     assert got == gold["tokens"], (got[:10], gold["tokens"][:10])
     # The last step's logits: the oracle's 20 largest, within 1e-3 of their scale.
@@ -87,3 +90,53 @@ def test_full_decoder_matches_golden_tokens(ops, case):
     ref = np.array(gold["last_top20_logits"], dtype=np.float32)
     got_top = logits[np.array(gold["last_top20_ids"])]
     assert np.max(np.abs(got_top - ref)) <= 1e-3 * np.abs(ref).max()
+
+
+# Decoders the persistent greedy loop takes: GQA groups of 4 and 2, partial
+# rotation, a ragged last vocab tile, K dims of 512-multiples, contexts that
+# end inside an attention split.
+PERSIST_CFGS = {
+    "hpg4_rot64": dict(n_layers=2, hidden=512, n_heads=4, n_kv_heads=1, head_dim=128, ffn=1024, vocab=4000,
+                       kv_capacity=256, rot_dim=64, group=32, lm_group=32),
+    "hpg2_ragged": dict(n_layers=3, hidden=1024, n_heads=8, n_kv_heads=4, head_dim=128, ffn=1536, vocab=5003,
+                        kv_capacity=300, rot_dim=128, group=32, lm_group=32),
+}
+
+
+@pytest.mark.parametrize("name", list(PERSIST_CFGS))
+def test_persistent_schedule_matches_graph_and_oracle(ops, oracle, name):
+    cfg = synth.DecoderCfg(**{**synth.TINY.as_dict(), **PERSIST_CFGS[name]})
+    model = synth.SyntheticDecoder(cfg, seed=41)
+    prompt = model.prompt(200 if cfg.kv_capacity >= 300 else 40)
+    ref, _ = oracle.OracleDecoder(model).generate(prompt, 48)
+    sess = make_session(ops, model)
+    assert sess.schedule() == 0
+    sess.set_schedule(-1)
+    assert sess.schedule() == 1
+    got = sess.generate(prompt, 48)
+    assert got == ref, f"first mismatch at {next(i for i, (a, b) in enumerate(zip(got, ref)) if a != b)}"
+    assert sess.position == len(prompt) + 47
+    persistent_logits = sess.logits()
+    sess.reset()
+    sess.set_schedule(0)
+    assert sess.schedule() == 0
+    assert sess.generate(prompt, 48) == ref
+    graph_logits = sess.logits()
+    assert np.max(np.abs(persistent_logits - graph_logits)) <= 1e-4 * np.abs(graph_logits).max()
+    # A second call continues from the position the first one left.
+    sess.set_schedule(1)
+    more = sess.generate([ref[-1]], 5)
+    sess.reset()
+    sess.set_schedule(0)
+    assert more == sess.generate(np.concatenate([prompt, np.array(ref, dtype=prompt.dtype)]), 5)
+
+
+def test_persistent_schedule_errors(ops):
+    from aiimage_b200 import errors
+    model = synth.SyntheticDecoder(synth.TINY, seed=5)  # head_dim 64: graph schedule only
+    sess = make_session(ops, model)
+    assert sess.schedule() == 0
+    with pytest.raises(errors.NotSupportedError):
+        sess.set_schedule(1)
+    with pytest.raises(errors.ArgumentOutOfRangeError):
+        sess.set_schedule(2)
