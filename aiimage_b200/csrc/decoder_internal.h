@@ -68,3 +68,20 @@ cudaError_t split_attention_configure(int n_heads, int kvh, int D, int chunk);
 cudaError_t launch_split_attention(const float* q, const __half* kc, const __half* vc, int cap, int D, int n_heads,
                                    int kvh, float scale, const int* pos, int B, float* part, unsigned int* counters,
                                    float* out, int* status, int chunk, cudaStream_t s);
+
+// Batched decode attention on the tensor cores (k_batch_attn.cu): head_dim
+// 128, <= 4 query heads per KV head, caches [B][kvh][cap][D] stored with
+// swizzled rows. A fixed grid (from configure) streams the step's (sequence,
+// KV head, 64-position chunk) items, one partial per CTA segment into `part`
+// (batch_tc_attention_part_floats floats); the merge prep combines a head's
+// partials into the O projection's prepared fp16 hi / lo input (the
+// launch_tc_prep layout for B rows, fp32 split). Both are programmatic
+// dependents of the previous kernel.
+bool batch_tc_attention_supported(int n_heads, int kvh, int D, int max_batch, int cap);
+size_t batch_tc_attention_part_floats(int B, int n_heads);
+cudaError_t batch_tc_attention_configure(int sm_count, int* grid);
+cudaError_t launch_batch_tc_attention(const float* q, const __half* kc, const __half* vc, int cap, int n_heads, int kvh,
+                                      float scale, const int* pos, int B, float* part, int grid, int* status,
+                                      cudaStream_t s);
+cudaError_t launch_batch_attn_merge_prep(const float* part, const int* pos, int B, int n_heads, int kvh, int grid,
+                                         void* xt, cudaStream_t s);

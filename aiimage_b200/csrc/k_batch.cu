@@ -61,10 +61,20 @@ __device__ __forceinline__ __half ctx_value(unsigned long long seq_key, int laye
     return __float2half_rn(u);
 }
 
+// Element offset of dim d inside a cache row of position p. swz = 0: plain;
+// swz = 1 (D = 128, the tensor-core attention): the 16-byte chunks of each
+// 128-byte half row XOR-swizzled by p & 7, so a bulk copy of consecutive rows
+// lands in shared memory ready for conflict-free ldmatrix.
+__device__ __forceinline__ int cache_dim(int p, int d, int swz) {
+    if (!swz) return d;
+    const int ch = d >> 3;
+    return (((ch & 8) | ((ch & 7) ^ (p & 7))) << 3) | (d & 7);
+}
+
 // Fills positions [0, ctx[b]) of every layer's K and V cache of sequence b
 // with ctx_value and sets pos[b] = ctx[b]. Caches [layers][B][kvh][cap][D].
 __global__ void bat_fill_kernel(__half* kc, __half* vc, int layers, int B, int kvh, int cap, int D, const int* ctx,
-                                const unsigned long long* seq_keys, int* pos) {
+                                const unsigned long long* seq_keys, int* pos, int swz) {
     const int b = blockIdx.y;
     const int n = ctx[b];
     const long long per_layer = (long long)kvh * n * D;
@@ -77,7 +87,7 @@ __global__ void bat_fill_kernel(__half* kc, __half* vc, int layers, int B, int k
         const int g = (int)(r / ((long long)n * D));
         const int p = (int)((r / D) % n);
         const int d = (int)(r % D);
-        const size_t off = ((((size_t)l * B + b) * kvh + g) * cap + p) * D + d;
+        const size_t off = ((((size_t)l * B + b) * kvh + g) * cap + p) * D + cache_dim(p, d, swz);
         kc[off] = ctx_value(key, l, 0, g, p, d);
         vc[off] = ctx_value(key, l, 1, g, p, d);
     }
@@ -101,7 +111,7 @@ __global__ void bat_embed_kernel(const __half* table, int vocab, int hidden, con
 // rope_map), q -> q[b][n_heads * D] fp32, k and v -> fp16 caches at pos[b].
 __global__ void bat_rope_kernel(const float* qkv, int rows, const int* rope_map, const float* cosv,
                                 const float* sinv, const int* pos, int D, int rot, int n_heads, int kvh, int cap, int B,
-                                float* q, __half* kc, __half* vc) {
+                                float* q, __half* kc, __half* vc, int swz) {
     griddep_wait();
     griddep_launch();
     const int b = blockIdx.x;
@@ -126,7 +136,7 @@ __global__ void bat_rope_kernel(const float* qkv, int rows, const int* rope_map,
             q[((long long)b * n_heads + head) * D + dim] = out;
         } else {
             __half* cache = kind == 1 ? kc : vc;
-            cache[(((size_t)b * kvh + head) * cap + p) * D + dim] = __float2half_rn(out);
+            cache[(((size_t)b * kvh + head) * cap + p) * D + cache_dim(p, dim, swz)] = __float2half_rn(out);
         }
     }
 }
@@ -454,6 +464,10 @@ struct aexis_batch {
     std::vector<void*> tiled;            // tensor-core copies: 4 per layer, then the lm_head
     cudaGraphExec_t exec = nullptr;
     int exec_batch = 0;
+    // Tensor-core attention (k_batch_attn.cu, head_dim 128): caches stored
+    // with swizzled rows, the split merge folded into the O projection's prep.
+    bool tc_attn = false;
+    int tc_attn_grid = 0;
 };
 
 namespace {
@@ -543,18 +557,28 @@ cudaError_t enqueue_batch_step(aexis_batch* bt, cudaStream_t s, int B) {
             const float* sn = bt->sinv;
             const int* pp = pos;
             float* qo = bt->q;
+            int swz = bt->tc_attn ? 1 : 0;
             void* args[] = {(void*)&qkv, &r, (void*)&map, (void*)&cs, (void*)&sn, (void*)&pp, &hd, &rot, &nh, &nkv,
-                            &cap, &bb, &qo, &kc, &vc};
+                            &cap, &bb, &qo, &kc, &vc, &swz};
             if ((e = launch_pdl((const void*)bat_rope_kernel, dim3(B), dim3(256), 0, s, args)) != cudaSuccess)
                 return e;
         }
-        if ((e = launch_split_attention(bt->q, kc, vc, bt->cap, D, NH, KVH, scale, pos, B, bt->part,
-                                        bt->counters + (size_t)l * bt->max_batch * KVH, bt->attn, d->ctx->status,
-                                        kBatChunk, s)) != cudaSuccess)
-            return e;
-        if ((e = launch_tc_prep(0, bt->attn, 0, qd, B, qd, nullptr, 0.0f, 1, bt->xt, nullptr, 0, 0, true, s)) !=
-            cudaSuccess)
-            return e;
+        if (bt->tc_attn) {
+            if ((e = launch_batch_tc_attention(bt->q, kc, vc, bt->cap, NH, KVH, scale, pos, B, bt->part,
+                                               bt->tc_attn_grid, d->ctx->status, s)) != cudaSuccess)
+                return e;
+            if ((e = launch_batch_attn_merge_prep(bt->part, pos, B, NH, KVH, bt->tc_attn_grid, bt->xt, s)) !=
+                cudaSuccess)
+                return e;
+        } else {
+            if ((e = launch_split_attention(bt->q, kc, vc, bt->cap, D, NH, KVH, scale, pos, B, bt->part,
+                                            bt->counters + (size_t)l * bt->max_batch * KVH, bt->attn, d->ctx->status,
+                                            kBatChunk, s)) != cudaSuccess)
+                return e;
+            if ((e = launch_tc_prep(0, bt->attn, 0, qd, B, qd, nullptr, 0.0f, 1, bt->xt, nullptr, 0, 0, true, s)) !=
+                cudaSuccess)
+                return e;
+        }
         if ((e = gemm(bt, L.o, bt->tiled[l * 4 + 1], B, bt->h, H, 1, s)) != cudaSuccess) return e;
         if ((e = launch_tc_prep(1, bt->h, 0, H, B, H, L.norm[1], c.eps, 1, bt->xt, bt->gu, 2 * F, 2 * F, true, s)) !=
             cudaSuccess)
@@ -670,7 +694,13 @@ AEXIS_API int aexis_cuda_batch_create(aexis_decoder* d, int max_batch, int kv_ca
     if (!rc) rc = balloc(bt, (void**)&bt->attn, sizeof(float) * max_batch * qd);
     if (!rc) rc = balloc(bt, (void**)&bt->gu, sizeof(float) * max_batch * 2 * F);
     if (!rc) rc = balloc(bt, (void**)&bt->logits, sizeof(float) * max_batch * c.vocab);
-    if (!rc) rc = balloc(bt, (void**)&bt->part, sizeof(float) * split_attention_part_floats(max_batch, c.n_heads, D, kBatChunk));
+    bt->tc_attn = batch_tc_attention_supported(c.n_heads, KVH, D, max_batch, kv_capacity);
+    if (!rc) {
+        size_t pf = split_attention_part_floats(max_batch, c.n_heads, D, kBatChunk);
+        if (bt->tc_attn) pf = pf > batch_tc_attention_part_floats(max_batch, c.n_heads)
+                                  ? pf : batch_tc_attention_part_floats(max_batch, c.n_heads);
+        rc = balloc(bt, (void**)&bt->part, sizeof(float) * pf);
+    }
     if (!rc) {
         const int kmax = H > qd ? (H > F ? H : F) : (qd > F ? qd : F);
         rc = balloc(bt, &bt->xt, gemm_tc_xt_bytes(max_batch, kmax, AEXIS_F32));
@@ -711,6 +741,8 @@ AEXIS_API int aexis_cuda_batch_create(aexis_decoder* d, int max_batch, int kv_ca
         rc = aexis_cuda_check(ctx, split_attention_configure(c.n_heads, c.n_kv_heads, D, kBatChunk),
                               "attention smem");
     }
+    if (!rc && bt->tc_attn)
+        rc = aexis_cuda_check(ctx, batch_tc_attention_configure(ctx->sm_count, &bt->tc_attn_grid), "attention smem");
     if (!rc) rc = aexis_cuda_check(ctx, cudaStreamSynchronize(ctx->stream), "batch setup");
     if (rc) {
         aexis_cuda_batch_destroy(bt);
@@ -743,7 +775,7 @@ AEXIS_API int aexis_cuda_batch_fill_context(aexis_batch* bt, int batch, const in
         const auto& c = bt->d->cfg;
         bat_fill_kernel<<<dim3(ctx->sm_count * 4, batch), 256, 0, s>>>(
             bt->kc, bt->vc, c.n_layers, bt->max_batch, c.n_kv_heads, bt->cap, c.head_dim, bt->ctx, bt->seq_keys,
-            bt->ints + 1 + bt->max_batch);
+            bt->ints + 1 + bt->max_batch, bt->tc_attn ? 1 : 0);
         e = cudaGetLastError();
     }
     if (e == cudaSuccess) e = cudaMemsetAsync(bt->ints, 0, sizeof(int), s);

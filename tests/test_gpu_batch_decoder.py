@@ -119,3 +119,26 @@ def test_config4_batch_against_oracle(ops, oracle):
     omodel.cfg = q8(synth.QWEN35_08B_Q8, kv_capacity=4096 + 8)
     pick = [int(np.argmin(ctx_lens)), int(np.argmax(ctx_lens))]
     check_against_oracle(oracle, omodel, ctx_lens, seed, first, got, batch.logits(), seqs=pick)
+
+
+@pytest.mark.parametrize("hpg", [4, 2])
+def test_batch_tensor_core_attention_against_oracle(ops, oracle, hpg):
+    """head_dim 128 takes the tensor-core attention (swizzled caches, online
+    softmax over each CTA's chunks, the split merge in the O projection's
+    prep): contexts that end inside, at and just past 64-position chunks,
+    nine sequences (not a multiple of 16), every sequence checked."""
+    from aiimage_b200.decoder import BatchSession, DecoderSession
+    heads = 4 if hpg == 4 else 8
+    cfg = q8(synth.TINY, n_layers=2, hidden=512, n_heads=heads, n_kv_heads=heads // hpg, head_dim=128, ffn=1024,
+             vocab=4000, kv_capacity=1024, rot_dim=128)
+    model = synth.SyntheticDecoder(cfg, seed=51 + hpg)
+    dec = DecoderSession(ops, cfg).load(model)
+    ctx_lens = np.array([0, 1, 62, 63, 64, 127, 129, 300, 700], dtype=np.int32)
+    seed = 0xA77
+    first = np.random.default_rng(8).integers(0, cfg.vocab, size=ctx_lens.size).astype(np.int32)
+    batch = BatchSession(dec, max_batch=12, kv_capacity=1000, max_steps=8)
+    batch.fill_context(ctx_lens, seed)
+    got = batch.generate(first, 6)
+    assert np.array_equal(batch.positions, ctx_lens + 6)
+    exact = check_against_oracle(oracle, model, ctx_lens, seed, first, got, batch.logits())
+    assert exact >= got.size - 1
