@@ -527,6 +527,20 @@ AEXIS_API int aexis_cuda_topk(aexis_ctx* ctx, const float* logits, int rows, int
                                              ctx->stream), "topk launch");
 }
 
+AEXIS_API int aexis_cuda_topk_merge(aexis_ctx* ctx, const int32_t* gathered, int lists, int rows, int k,
+                                    int shard_rows, int64_t* out_ids, float* out_vals, int32_t* out_idx) {
+    if (!ctx) return AEXIS_E_NULL;
+    if (!gathered || !out_ids || !out_vals || !out_idx) return aexis_fail(ctx, AEXIS_E_NULL, "null pointer");
+    if (lists < 1 || lists > 8 || rows <= 0 || shard_rows <= 0)
+        return aexis_fail(ctx, AEXIS_E_RANGE, "lists=%d (1..8) rows=%d shard_rows=%d", lists, rows, shard_rows);
+    if (k < 1 || k > 64) return aexis_fail(ctx, AEXIS_E_RANGE, "k=%d (1..64)", k);
+    int rc = bind(ctx);
+    if (rc) return rc;
+    return aexis_cuda_check(ctx, launch_topk_shard_merge(gathered, lists, rows, k, shard_rows,
+                                                         reinterpret_cast<long long*>(out_ids), out_vals, out_idx,
+                                                         ctx->stream), "topk merge launch");
+}
+
 AEXIS_API int aexis_cuda_embed(aexis_ctx* ctx, const int32_t* words, int count, const aexis_weights* table,
                                const float* bias, float* out) {
     if (!ctx) return AEXIS_E_NULL;

@@ -171,6 +171,9 @@ cudaError_t launch_argmax_keys(const float* logits, int rows, int width, int ld,
                                unsigned long long* keys, int sm_count, cudaStream_t s);
 // Per-row top-k (k <= 64): scratch of topk_scratch_bytes() device bytes.
 size_t topk_scratch_bytes(int rows, int width, int k, int sm_count);
+// Merge of the shards' packed argmax keys and top-k lists (k_topk.cu).
+cudaError_t launch_topk_shard_merge(const int32_t* gathered, int lists, int rows, int k, int shard_rows, long long* ids,
+                                    float* vals, int32_t* idx, cudaStream_t s);
 cudaError_t launch_topk(const float* logits, int rows, int width, int ld, int k, float* vals, int32_t* idx,
                         void* scratch, int sm_count, cudaStream_t s);
 cudaError_t launch_embed(const int32_t* words, int count, const aexis_weights* table,

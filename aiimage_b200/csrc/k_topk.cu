@@ -440,6 +440,59 @@ __global__ void __launch_bounds__(kTkThreads) topk_exact_kernel(const float* log
     griddep_launch();
 }
 
+// Merge of per-shard results (vocab-sharded lm_head): `gathered` holds, for
+// each of `lists` shards, rows x 8-byte greedy keys (global indices), then
+// rows x k fp32 values and rows x k int32 LOCAL indices of the shard's top-k
+// (launch_topk's output, descending, (-inf, -1) padded). Shard r's local
+// index i is global r * shard_rows + i. Per row: the largest key (the
+// greedy id, the scan's tie rule) and the k largest (value, global index)
+// keys of the shards' lists (warp r loads list r, then the tree merge).
+__global__ void __launch_bounds__(kTkThreads) topk_shard_merge_kernel(const int32_t* gathered, int lists, int rows,
+                                                                       int k, int shard_rows, long long* ids,
+                                                                       float* vals, int32_t* idx) {
+    __shared__ unsigned long long xch[kTkThreads];
+    __shared__ unsigned long long best[kTkWarps];
+    const int row = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    griddep_wait();
+    const size_t per = (size_t)rows * 2 + (size_t)rows * k * 2;  // 32-bit words per shard
+    unsigned long long t[2] = {0ull, 0ull};
+    unsigned long long kmax = 0ull;
+    if (warp < lists) {
+        const int32_t* base = gathered + per * warp;
+        const unsigned long long* keys = reinterpret_cast<const unsigned long long*>(base);
+        const float* sv = reinterpret_cast<const float*>(base + (size_t)rows * 2) + (size_t)row * k;
+        const int32_t* si = base + (size_t)rows * 2 + (size_t)rows * k + (size_t)row * k;
+        kmax = __ldcg(keys + row);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int j = h * 32 + lane;
+            if (j < k) {
+                const int li = __ldcg(si + j);
+                t[h] = li < 0 ? 0ull : tk_key(__ldcg(sv + j), warp * shard_rows + li);
+            }
+        }
+    }
+    if (lane == 0) best[warp] = kmax;
+    block_tree_merge(t, lane, warp, xch);
+    if (warp == 0) {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int j = h * 32 + lane;
+            if (j < k) {
+                const unsigned long long key = t[h];
+                vals[(size_t)row * k + j] = key != 0ull ? tk_value32((unsigned int)(key >> 32)) : -INFINITY;
+                idx[(size_t)row * k + j] = key != 0ull ? (int32_t)(0xFFFFFFFFu - (unsigned int)(key & 0xFFFFFFFFull)) : -1;
+            }
+        }
+        if (lane == 0) {
+            unsigned long long m = 0ull;
+            for (int w = 0; w < kTkWarps; ++w) m = best[w] > m ? best[w] : m;
+            ids[row] = (long long)aexis_argmax_index(m);
+        }
+    }
+    griddep_launch();
+}
+
 bool topk_sampled(int width) { return width >= kTkMinSampledWidth; }
 
 // Rank r whose sample value leaves about 4.5k of the row's elements above it
@@ -506,4 +559,10 @@ cudaError_t launch_topk(const float* logits, int rows, int width, int ld, int k,
     blocks = blocks < by_work ? blocks : by_work;
     return launch_pdl(topk_filter_kernel, dim3((unsigned int)(blocks < 1 ? 1 : blocks)), s, logits, rows, width, ld,
                       k, (const float*)thr, cnt, done, cand, vals, idx);
+}
+
+cudaError_t launch_topk_shard_merge(const int32_t* gathered, int lists, int rows, int k, int shard_rows, long long* ids,
+                                    float* vals, int32_t* idx, cudaStream_t s) {
+    if (lists < 1 || lists > kTkWarps || k < 1 || k > kTkMaxK) return cudaErrorInvalidValue;
+    return launch_pdl(topk_shard_merge_kernel, dim3(rows), s, gathered, lists, rows, k, shard_rows, ids, vals, idx);
 }

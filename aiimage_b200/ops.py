@@ -253,6 +253,12 @@ class AexisOps:
         ld = ld if ld is not None else (logits.stride(0) if logits.dim() == 2 else width)
         self._call(lib().aexis_cuda_topk, _ptr(logits), rows, width, ld, k, _ptr(out_vals), _ptr(out_idx))
 
+    def topk_merge(self, gathered, lists, rows, k, shard_rows, out_ids, out_vals, out_idx):
+        """Merge of vocab shards' packed greedy keys and top-k lists (see
+        aexis_cuda_topk_merge)."""
+        self._call(lib().aexis_cuda_topk_merge, _ptr(gathered), lists, rows, k, shard_rows, _ptr(out_ids),
+                   _ptr(out_vals), _ptr(out_idx))
+
     def embed_texture(self, words, count, table: Weights, bias, output):
         """AexisOps.EmbedTexture (:10764-10810)."""
         self._call(lib().aexis_cuda_embed, _ptr(words), count, table.handle, _ptr(bias), _ptr(output))

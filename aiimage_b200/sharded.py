@@ -6,8 +6,10 @@ handle. One call:
   2. per row the shard's argmax as a 64-bit key carrying the GLOBAL index
      (aexis_cuda_argmax_keys) and the shard's top-k (aexis_cuda_topk, indices
      shifted by the shard offset);
-  3. one all-reduce MAX over the keys and one all-gather of the top-k lists
-     (NCCL over NVLink; gloo in the CPU tests), then a deterministic merge.
+  3. the keys and the top-k lists packed into one buffer, one all-gather of
+     those buffers (NCCL over NVLink; gloo in the CPU tests), then one merge
+     kernel (aexis_cuda_topk_merge): the largest key, and the k largest
+     (value, global index) keys of the shards' sorted lists.
 Every logit is computed by exactly one rank with the same kernel and the same
 K order whatever G is, and the key's tie rule (lowest global index) matches
 the single-device scan (AexisArgMaxPack4LinearMat, HLSL Pack4Matmul:645-686),
@@ -16,9 +18,6 @@ so the token ids are bit-identical for every G.
 from __future__ import annotations
 
 import torch
-
-_SIGN = -(1 << 63)  # int64 bit 63
-
 
 def shard_range(vocab: int, world: int, rank: int):
     per = (vocab + world - 1) // world
@@ -31,35 +30,33 @@ def keys_to_ids(keys: torch.Tensor) -> torch.Tensor:
     return (0xFFFFFFFF - (keys & 0xFFFFFFFF)).to(torch.int64)
 
 
-def reduce_keys(keys: torch.Tensor, group=None) -> torch.Tensor:
-    """All-reduce MAX of uint64 keys held in an int64 tensor: flipping bit 63
-    maps unsigned order onto signed order and back."""
-    import torch.distributed as dist
-    k = keys ^ _SIGN
-    dist.all_reduce(k, op=dist.ReduceOp.MAX, group=group)
-    return k ^ _SIGN
+def packed_words(rows: int, k: int) -> int:
+    """32-bit words of one shard's packed result: rows uint64 greedy keys,
+    rows x k fp32 top-k values, rows x k int32 shard-local indices."""
+    return 2 * rows + 2 * rows * k
 
 
-def merge_topk(vals: torch.Tensor, idx: torch.Tensor, k: int, group=None):
-    """All-gather the per-shard top-k (values, global indices) and keep the k
-    largest per row, equal values ordered by ascending index."""
+def pack_views(buf: torch.Tensor, rows: int, k: int):
+    """(keys int64 [rows], vals fp32 [rows, k], idx int32 [rows, k]) views of
+    one shard's packed buffer (int32 [packed_words])."""
+    keys = buf[: 2 * rows].view(torch.int64)
+    vals = buf[2 * rows: 2 * rows + rows * k].view(torch.float32).view(rows, k)
+    idx = buf[2 * rows + rows * k:].view(rows, k)
+    return keys, vals, idx
+
+
+def exchange(buf: torch.Tensor, group=None) -> torch.Tensor:
+    """All-gather of every rank's packed buffer into one tensor [world * W],
+    rank order: one NCCL all-gather over NVLink (gloo in the CPU tests)."""
     import torch.distributed as dist
     world = dist.get_world_size(group)
-    vs = [torch.empty_like(vals) for _ in range(world)]
-    ix = [torch.empty_like(idx) for _ in range(world)]
-    dist.all_gather(vs, vals.contiguous(), group=group)
-    dist.all_gather(ix, idx.contiguous(), group=group)
-    v = torch.cat(vs, dim=1)
-    i = torch.cat(ix, dim=1)
-    return topk_merge_local(v, i, k)
-
-
-def topk_merge_local(v: torch.Tensor, i: torch.Tensor, k: int):
-    # Stable sorts: by index ascending, then by value descending.
-    o1 = torch.argsort(i, dim=1, stable=True)
-    v1, i1 = torch.gather(v, 1, o1), torch.gather(i, 1, o1)
-    o2 = torch.argsort(v1, dim=1, descending=True, stable=True)
-    return torch.gather(v1, 1, o2)[:, :k], torch.gather(i1, 1, o2)[:, :k]
+    if dist.get_backend(group) == "nccl":
+        out = torch.empty(world * buf.numel(), dtype=buf.dtype, device=buf.device)
+        dist.all_gather_into_tensor(out, buf, group=group)
+        return out
+    parts = [torch.empty_like(buf) for _ in range(world)]
+    dist.all_gather(parts, buf, group=group)
+    return torch.cat(parts)
 
 
 class ShardedLmHead:
@@ -88,13 +85,23 @@ class ShardedLmHead:
         """Greedy ids [M] (int64) and the global top-k (values [M,k], ids [M,k])."""
         m = x.shape[0]
         logits = self.shard_logits(x, logits)
-        keys = torch.empty(m, dtype=torch.int64, device=x.device)
+        if self.world == 1:
+            keys = torch.empty(m, dtype=torch.int64, device=x.device)
+            self.ops.argmax_keys(logits, self.n, m, self.lo, keys)
+            vals = torch.empty((m, k), dtype=torch.float32, device=x.device)
+            idx = torch.empty((m, k), dtype=torch.int32, device=x.device)
+            self.ops.top_k(logits, self.n, m, k, vals, idx)
+            return keys_to_ids(keys), vals, idx.to(torch.int64)
+        # The shard's keys and top-k straight into one packed buffer, one
+        # all-gather, one merge kernel.
+        buf = torch.empty(packed_words(m, k), dtype=torch.int32, device=x.device)
+        keys, vals, idx = pack_views(buf, m, k)
         self.ops.argmax_keys(logits, self.n, m, self.lo, keys)
-        vals = torch.empty((m, k), dtype=torch.float32, device=x.device)
-        idx = torch.empty((m, k), dtype=torch.int32, device=x.device)
         self.ops.top_k(logits, self.n, m, k, vals, idx)
-        gidx = idx.to(torch.int64) + self.lo
-        if self.world > 1:
-            keys = reduce_keys(keys, self.group)
-            vals, gidx = merge_topk(vals, gidx, k, self.group)
-        return keys_to_ids(keys), vals, gidx
+        gathered = exchange(buf, self.group)
+        ids = torch.empty(m, dtype=torch.int64, device=x.device)
+        out_v = torch.empty((m, k), dtype=torch.float32, device=x.device)
+        out_i = torch.empty((m, k), dtype=torch.int32, device=x.device)
+        per = (self.vocab + self.world - 1) // self.world
+        self.ops.topk_merge(gathered, self.world, m, k, per, ids, out_v, out_i)
+        return ids, out_v, out_i.to(torch.int64)

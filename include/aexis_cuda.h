@@ -247,6 +247,18 @@ int aexis_cuda_argmax_static(const float* logits, int rows, int width, int ld, i
 int aexis_cuda_topk(aexis_ctx* ctx, const float* logits, int rows, int width, int ld, int k,
                     float* out_vals, int32_t* out_idx);
 
+/* No reference counterpart (the reference decodes on one device): the merge
+ * step of a vocab-sharded lm_head. `gathered` (device) holds, for each of
+ * `lists` (1..8) shards in shard order, rows uint64 greedy keys of
+ * aexis_cuda_argmax_keys (global indices), then rows x k fp32 values and rows
+ * x k int32 shard-local indices of aexis_cuda_topk on the shard, shard s
+ * starting at logical row s * shard_rows. Writes per row the greedy id
+ * (int64, device), and the k largest (value, global index) pairs under the
+ * aexis_cuda_topk order, (-inf, -1) padded: the same results as the
+ * single-device calls on the whole vocabulary. */
+int aexis_cuda_topk_merge(aexis_ctx* ctx, const int32_t* gathered, int lists, int rows, int k,
+                          int shard_rows, int64_t* out_ids, float* out_vals, int32_t* out_idx);
+
 /* Ops.EmbedTexture (Ops:10764-10810; HLSL BufferTensor AexisEmbedValue:37-62):
  * out[q, p] = W(clamp(words[q], 0, vocab-1), p) (+ bias[p]) for a Q4 (group
  * scales), Q8 (per-token scales) or dense table. words: device int32 [count];

@@ -305,3 +305,44 @@ def test_bounded_wait_timeout_leaves_context_usable(ops):
     assert int(out.item()) == 1
     with pytest.raises(errors.ArgumentOutOfRangeError):
         ops.selftest_wait(10)
+
+
+@pytest.mark.parametrize("world", [2, 3, 8])
+def test_topk_shard_merge_matches_full_vocab(ops, oracle, world):
+    """aexis_cuda_topk_merge over `world` simulated vocab shards (each through
+    argmax_keys and top_k, packed as the sharded lm_head packs them) gives
+    the greedy ids and top-k of the full-vocabulary calls and the oracle:
+    ties across shards, a tie at the k-th place, a row of -inf, a shard of
+    fewer than k values (the last one when the vocab does not divide)."""
+    import torch
+    from aiimage_b200 import sharded
+    rows, vocab, k = 7, 20003, 50
+    x = np.random.default_rng(30 + world).standard_normal((rows, vocab)).astype(np.float32)
+    per = (vocab + world - 1) // world
+    x[0, 5] = x[0, vocab - 3] = x[0].max() + 1         # greedy tie across shards: lowest index
+    x[1, 100:160] = 9.0                                 # 60 equal values straddling a boundary for small shards
+    x[2, :] = -np.inf                                   # -inf values are selectable, by index
+    x[3, per - 1] = x[3, per] = x[3].max() + 2          # tie at a shard boundary
+    x[4, ::7] = np.nan                                  # NaN never selected
+    xc = cuda(x)
+    w = sharded.packed_words(rows, k)
+    gathered = torch.zeros(world * w, dtype=torch.int32, device="cuda")
+    for r in range(world):
+        lo, hi = sharded.shard_range(vocab, world, r)
+        keys, vals, idx = sharded.pack_views(gathered[r * w:(r + 1) * w], rows, k)
+        part = xc[:, lo:hi]
+        ops.argmax_keys(part, hi - lo, rows, lo, keys, ld=vocab)
+        ops.top_k(part, hi - lo, rows, k, vals, idx, ld=vocab)
+    ids = torch.zeros(rows, dtype=torch.int64, device="cuda")
+    mv = torch.zeros((rows, k), dtype=torch.float32, device="cuda")
+    mi = torch.zeros((rows, k), dtype=torch.int32, device="cuda")
+    ops.topk_merge(gathered, world, rows, k, per, ids, mv, mi)
+    fv = torch.zeros((rows, k), dtype=torch.float32, device="cuda")
+    fi = torch.zeros((rows, k), dtype=torch.int32, device="cuda")
+    ops.top_k(xc, vocab, rows, k, fv, fi)
+    assert np.array_equal(host(mi), host(fi)) and np.array_equal(host(mv), host(fv))
+    rv, ri = oracle.topk(x, k)
+    assert np.array_equal(host(mi), ri)
+    full_keys = torch.zeros(rows, dtype=torch.int64, device="cuda")
+    ops.argmax_keys(xc, vocab, rows, 0, full_keys)
+    assert np.array_equal(host(ids), host(sharded.keys_to_ids(full_keys)))

@@ -1,6 +1,8 @@
 """The vocab-sharded lm_head exchange (config 5) on CPU: world size 2 over
-gloo. Each rank holds half of the logits, packs its argmax keys with global
-indices and its top-k, and the all-reduce / all-gather merge must give the
+gloo. Each rank holds half of the logits and packs its argmax keys (global
+indices) and its top-k (shard-local indices) into one buffer; one all-gather
+of the buffers, then the merge (restated here on the host; the device kernel
+is tested against full-vocabulary kernels in test_gpu_ops.py) must give the
 full-vocabulary oracle's greedy ids and top-k (ties included)."""
 import os
 import socket
@@ -42,6 +44,29 @@ def _logits():
     return x
 
 
+def _reference_merge(gathered, world, rows, k, per):
+    """The merge aexis_cuda_topk_merge performs on the device, restated on
+    the host: the largest unsigned key per row, and the k largest (value,
+    global index) pairs (value descending, index ascending)."""
+    import torch
+    from aiimage_b200 import sharded
+    w = sharded.packed_words(rows, k)
+    ids, vals, idx = [], [], []
+    for row in range(rows):
+        best, cand = None, []
+        for r in range(world):
+            keys, v, i = sharded.pack_views(gathered[r * w:(r + 1) * w], rows, k)
+            u = int(keys[row]) & ((1 << 64) - 1)
+            best = u if best is None else max(best, u)
+            cand += [(float(v[row, j]), r * per + int(i[row, j])) for j in range(k) if int(i[row, j]) >= 0]
+        cand.sort(key=lambda t: (-t[0], t[1]))
+        cand = cand[:k] + [(float("-inf"), -1)] * (k - len(cand[:k]))
+        ids.append(int(sharded.keys_to_ids(torch.tensor([_signed(best)]))[0]))
+        vals.append([c[0] for c in cand])
+        idx.append([c[1] for c in cand])
+    return ids, vals, idx
+
+
 def _worker(rank, world, port, out):
     import torch
     import torch.distributed as dist
@@ -53,18 +78,25 @@ def _worker(rank, world, port, out):
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
     x = _logits()
+    rows, k = x.shape[0], 10
     lo, hi = sharded.shard_range(x.shape[1], world, rank)
     part = x[:, lo:hi]
-    # Each shard's maximum is taken in unsigned key order, as the kernel does.
-    keys = torch.tensor([_signed(max(_ukey(float(v), lo + i) for i, v in enumerate(row))) for row in part],
-                        dtype=torch.int64)
-    vals, idx = O.topk(part, 10)
-    ids = sharded.keys_to_ids(sharded.reduce_keys(keys))
-    mv, mi = sharded.merge_topk(torch.from_numpy(vals), torch.from_numpy(idx.astype(np.int64)) + lo, 10)
+    # This rank's packed buffer: keys in unsigned key order (as the kernel
+    # computes them), then its top-k with shard-local indices.
+    buf = torch.zeros(sharded.packed_words(rows, k), dtype=torch.int32)
+    keys, vals, idx = sharded.pack_views(buf, rows, k)
+    keys[:] = torch.tensor([_signed(max(_ukey(float(v), lo + i) for i, v in enumerate(row))) for row in part],
+                           dtype=torch.int64)
+    v, i = O.topk(part, k)
+    vals[:] = torch.from_numpy(v)
+    idx[:] = torch.from_numpy(i)
+    gathered = sharded.exchange(buf)
     if rank == 0:
-        out["ids"] = ids.tolist()
-        out["vals"] = mv.numpy().tolist()
-        out["idx"] = mi.numpy().tolist()
+        per = (x.shape[1] + world - 1) // world
+        ids, mv, mi = _reference_merge(gathered, world, rows, k, per)
+        out["ids"] = ids
+        out["vals"] = mv
+        out["idx"] = mi
     dist.destroy_process_group()
 
 
@@ -97,6 +129,6 @@ def test_key_order_matches_scan():
     keys = [_signed(_ukey(v, i)) for i, v in enumerate(vals)]
     from aiimage_b200 import sharded
     import torch
-    best = max(k ^ (-(1 << 63)) for k in keys) ^ (-(1 << 63))
+    best = _signed(max(_ukey(v, i) for i, v in enumerate(vals)))
     assert int(sharded.keys_to_ids(torch.tensor([best]))[0]) == 4
     assert max(_ukey(v, i) for i, v in enumerate(vals)) == _ukey(2.5, 4)
