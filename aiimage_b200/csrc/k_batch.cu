@@ -109,16 +109,17 @@ __global__ void bat_embed_kernel(const __half* table, int vocab, int hidden, con
 // RoPE (rotate-half, HLSL Pack4PointwiseNorm:414-473) of the q and k rows of
 // qkv[b] (the decoder's internal row order: rotate-half pairs adjacent, see
 // rope_map), q -> q[b][n_heads * D] fp32, k and v -> fp16 caches at pos[b].
+// Grid (row blocks, B): one row per thread.
 __global__ void bat_rope_kernel(const float* qkv, int rows, const int* rope_map, const float* cosv,
                                 const float* sinv, const int* pos, int D, int rot, int n_heads, int kvh, int cap, int B,
                                 float* q, __half* kc, __half* vc, int swz) {
     griddep_wait();
     griddep_launch();
-    const int b = blockIdx.x;
+    const int b = blockIdx.y;
     const int p = pos[b];
     const int half = rot >> 1;
     const float* src = qkv + (long long)b * rows;
-    for (int r = threadIdx.x; r < rows; r += blockDim.x) {
+    for (int r = blockIdx.x * blockDim.x + threadIdx.x; r < rows; r += gridDim.x * blockDim.x) {
         const int desc = rope_map[r];
         const int kind = desc >> 24, head = (desc >> 12) & 0xFFF, dim = desc & 0xFFF;
         const float val = src[r];
@@ -560,7 +561,7 @@ cudaError_t enqueue_batch_step(aexis_batch* bt, cudaStream_t s, int B) {
             int swz = bt->tc_attn ? 1 : 0;
             void* args[] = {(void*)&qkv, &r, (void*)&map, (void*)&cs, (void*)&sn, (void*)&pp, &hd, &rot, &nh, &nkv,
                             &cap, &bb, &qo, &kc, &vc, &swz};
-            if ((e = launch_pdl((const void*)bat_rope_kernel, dim3(B), dim3(256), 0, s, args)) != cudaSuccess)
+            if ((e = launch_pdl((const void*)bat_rope_kernel, dim3((rows + 255) / 256, B), dim3(256), 0, s, args)) != cudaSuccess)
                 return e;
         }
         if (bt->tc_attn) {

@@ -52,6 +52,7 @@ struct TaShared {
     __align__(16) __half pt[8][kTaPtStride];  // rows 0-3: hi of head h, 4-7: lo
     float alpha[kTaMaxHpg], mrun[kTaMaxHpg], lrun[kTaMaxHpg];
     long long start[kTaMaxB + 1];               // item prefix over sequences
+    int pos[kTaMaxB];                           // the step's positions
     uint64_t full[2];
 };
 
@@ -82,8 +83,8 @@ __device__ __forceinline__ uint32_t pack_half2(float a, float b) {
     return *reinterpret_cast<const uint32_t*>(&h);
 }
 
-// Chunks of sequence b (ctx = pos[b] + 1 positions).
-__device__ __forceinline__ int seq_chunks(const int* pos, int b) { return (pos[b] + kTaC) / kTaC; }
+// Chunks of a sequence at position p (ctx = p + 1 positions); 0 for p = -1.
+__device__ __forceinline__ int seq_chunks(int p) { return (p + kTaC) / kTaC; }
 
 // First item of CTA i of G over T items.
 __device__ __forceinline__ long long cta_first(long long T, int i, int G) { return T * i / G; }
@@ -94,15 +95,37 @@ __device__ __forceinline__ bool starts_share(long long T, int G, long long it) {
     return i < G && cta_first(T, (int)i, G) == it;
 }
 
-// s[b] = items before sequence b (kvh chunks lists each), s[B] = T. One
-// thread; B <= kTaMaxB.
-__device__ void item_prefix(const int* pos, int B, int kvh, long long* s) {
-    long long acc = 0;
-    for (int b = 0; b < B; ++b) {
-        s[b] = acc;
-        acc += (long long)kvh * seq_chunks(pos, b);
+// s[b] = items before sequence b (kvh chunk lists each), s[B] = T, and
+// ps[b] = pos[b]. One warp (lane = its lane): the B <= kTaMaxB position loads
+// are issued together, then a shuffle scan per 32 sequences.
+__device__ void item_prefix(const int* pos, int B, int kvh, long long* s, int* ps, int lane) {
+    constexpr int J = kTaMaxB / 32;
+    int p[J];
+#pragma unroll
+    for (int j = 0; j < J; ++j) {
+        const int b = j * 32 + lane;
+        p[j] = b < B ? pos[b] : -1;
     }
-    s[B] = acc;
+    long long carry = 0;
+#pragma unroll
+    for (int j = 0; j < J; ++j) {
+        if (j * 32 < B) {  // uniform over the warp
+            const int b = j * 32 + lane;
+            const int n = kvh * seq_chunks(p[j]);
+            int x = n;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int y = __shfl_up_sync(0xffffffffu, x, o);
+                if (lane >= o) x += y;
+            }
+            if (b < B) {
+                s[b] = carry + x - n;
+                ps[b] = p[j];
+            }
+            carry += __shfl_sync(0xffffffffu, x, 31);
+        }
+    }
+    if (lane == 0) s[B] = carry;
 }
 
 // q: [B][n_heads][D] fp32 (RoPE applied); caches [B][kvh][cap][D] fp16,
@@ -117,7 +140,7 @@ __global__ void __launch_bounds__(kTaThreads, 3) bat_attn_tc_kernel(const float*
     const int hpg = n_heads / kvh;
     const int G = gridDim.x, blk = blockIdx.x;
     griddep_wait();
-    if (tid == 0) item_prefix(pos, B, kvh, sh.start);
+    if (warp == 0) item_prefix(pos, B, kvh, sh.start, sh.pos, lane);
     // Zero both chunk buffers (rows past a chunk's end are read by the MMAs,
     // weighted 0) and P^T (columns of unused heads stay 0).
     for (int i = tid; i < 4 * kTaBuf / 16; i += kTaThreads) reinterpret_cast<uint4*>(&sh.k[0][0])[i] = make_uint4(0, 0, 0, 0);
@@ -142,7 +165,7 @@ __global__ void __launch_bounds__(kTaThreads, 3) bat_attn_tc_kernel(const float*
         while (sh.start[cur + 1] <= it) ++cur;
         b = cur;
         const long long r = it - sh.start[cur];
-        const int n = seq_chunks(pos, cur);
+        const int n = seq_chunks(sh.pos[cur]);
         g = (int)(r / n);
         c = (int)(r - (long long)g * n);
     };
@@ -150,7 +173,7 @@ __global__ void __launch_bounds__(kTaThreads, 3) bat_attn_tc_kernel(const float*
     auto issue = [&](long long it, int buf) {  // thread 0
         int b, g, c;
         locate(cur_issue, it, b, g, c);
-        const int ctx = pos[b] + 1;
+        const int ctx = sh.pos[b] + 1;
         const int np = min(kTaC, ctx - c * kTaC);
         const size_t row0 = ((size_t)b * kvh + g) * cap + (size_t)c * kTaC;
         const uint32_t bytes = (uint32_t)np * kTaRow;
@@ -169,10 +192,10 @@ __global__ void __launch_bounds__(kTaThreads, 3) bat_attn_tc_kernel(const float*
         const int k = (int)(it - i0), buf = k & 1;
         int b, g, c;
         locate(cur, it, b, g, c);
-        const int ctx = pos[b] + 1;
+        const int ctx = sh.pos[b] + 1;
         const int np = min(kTaC, ctx - c * kTaC);
         const bool seg_start = it == i0 || c == 0;
-        const bool seg_end = it + 1 == i1 || c + 1 == seq_chunks(pos, b);
+        const bool seg_end = it + 1 == i1 || c + 1 == seq_chunks(sh.pos[b]);
         if (tid == 0 && it + 1 < i1) issue(it + 1, buf ^ 1);  // that buffer was freed by the last barrier
         if (seg_start) {
             seg_c = c;
@@ -333,16 +356,17 @@ __global__ void __launch_bounds__(kTaThreads, 3) bat_attn_tc_kernel(const float*
 __global__ void __launch_bounds__(kTaD) bat_attn_merge_prep_kernel(const float* part, const int* pos, int B,
                                                                    int n_heads, int kvh, int G, int nb, uint8_t* xt) {
     __shared__ long long start[kTaMaxB + 1];
+    __shared__ int ps[kTaMaxB];
     __shared__ float wsm[kTaSlots];
     __shared__ float red[kTaD / 32];
     griddep_wait();
     const int b = blockIdx.x, h = blockIdx.y, d = threadIdx.x, lane = d & 31, warp = d >> 5;
     float v = 0.0f;
     if (b < B) {
-        if (d == 0) item_prefix(pos, B, kvh, start);
+        if (warp == 0) item_prefix(pos, B, kvh, start, ps, lane);
         __syncthreads();
         const long long T = start[B];
-        const int n = seq_chunks(pos, b), hpg = n_heads / kvh, g = h / hpg;
+        const int n = seq_chunks(ps[b]), hpg = n_heads / kvh, g = h / hpg;
         const long long F = start[b] + (long long)g * n;
         const float* ph = part + ((size_t)b * n_heads + h) * kTaSlots * kTaStride;
         const bool valid = d < n && (d == 0 || starts_share(T, G, F + d));

@@ -79,6 +79,7 @@ class AexisOps:
             msg = lib().aexis_cuda_last_error(None)
             raise errors.BY_STATUS.get(st, errors.AexisError)(msg.decode() if msg else "create failed")
         self._use_torch_stream = use_torch_stream
+        self._bound_stream = None
         self._int8 = None
         self._int4 = None
         self._children = weakref.WeakSet()
@@ -105,7 +106,9 @@ class AexisOps:
         if self._use_torch_stream:
             import torch
             s = torch.cuda.current_stream(self.device).cuda_stream
-            lib().aexis_cuda_set_stream(self.ctx, C.c_void_p(s))
+            if s != self._bound_stream:
+                lib().aexis_cuda_set_stream(self.ctx, C.c_void_p(s))
+                self._bound_stream = s
 
     def _call(self, fn, *args):
         self._bind_stream()

@@ -176,10 +176,17 @@ class Sweep:
         self.w = [[ops.new_int4_weight_only_upload(p, s, n, k, GROUP) for (p, s), (k, n) in zip(host, SWEEP)]
                   for _ in range(self.copies)]
         self.x_host = [synth.activations(k, seed, tag=(k, n)) for (k, n) in SWEEP]
-        self.x = [torch.from_numpy(x).cuda() for x in self.x_host]
-        self.y = [torch.zeros((1, n), dtype=torch.float16, device="cuda") for (k, n) in SWEEP]
-        self.x_pin = [torch.from_numpy(x).pin_memory() for x in self.x_host]
-        self.y_pin = [torch.zeros((1, n), dtype=torch.float16).pin_memory() for (k, n) in SWEEP]
+        # The step's activations and outputs each live in one buffer (host and
+        # device), so a step moves its inputs and results with one copy each way.
+        xo = np.cumsum([0] + [x.size for x in self.x_host])
+        yo = np.cumsum([0] + [n for (k, n) in SWEEP])
+        x_flat = np.concatenate([x.ravel() for x in self.x_host])
+        self.x_all = torch.from_numpy(x_flat).cuda()
+        self.x_all_pin = torch.from_numpy(x_flat).pin_memory()
+        self.y_all = torch.zeros(int(yo[-1]), dtype=torch.float16, device="cuda")
+        self.y_all_pin = torch.zeros(int(yo[-1]), dtype=torch.float16).pin_memory()
+        self.x = [self.x_all[xo[i]:xo[i + 1]].view(1, -1) for i in range(len(SWEEP))]
+        self.y = [self.y_all[yo[i]:yo[i + 1]].view(1, -1) for i in range(len(SWEEP))]
 
     def gemv(self, copy: int, i: int):
         k, n = SWEEP[i]
@@ -288,15 +295,14 @@ def run_gpu(args):
     q8 = bench_q8(ops, peak)
 
     # End to end through the C ABI with host buffers: per step, H2D of the five
-    # activations from pinned memory, the five gemm calls, D2H of the outputs.
+    # activations from pinned memory (one packed copy), the five gemm calls, D2H
+    # of the five outputs (one packed copy).
     stream = torch.cuda.current_stream()
 
     def e2e_step(c):
-        for i in range(len(SWEEP)):
-            sw.x[i].copy_(sw.x_pin[i], non_blocking=True)
+        sw.x_all.copy_(sw.x_all_pin, non_blocking=True)
         sw.step(c)
-        for i in range(len(SWEEP)):
-            sw.y_pin[i].copy_(sw.y[i], non_blocking=True)
+        sw.y_all_pin.copy_(sw.y_all, non_blocking=True)
         stream.synchronize()
 
     e2e_steps = max(1, min(args.steps, 200))
