@@ -31,7 +31,7 @@ def nvcc() -> str:
 
 def _deps() -> list[str]:
     inc = os.path.join(ROOT, "include", "aexis_cuda.h")
-    return [os.path.join(CSRC, f) for f in os.listdir(CSRC) if f.endswith((".cu", ".h"))] + [inc]
+    return [os.path.join(CSRC, f) for f in os.listdir(CSRC) if f.endswith((".cu", ".cuh", ".h"))] + [inc]
 
 
 def _stale(target: str, deps: list[str]) -> bool:
@@ -54,7 +54,7 @@ def build_native(force: bool = False, jobs: int | None = None) -> str:
     """Compile and link libaexis_cuda.so if any source is newer than it."""
     os.makedirs(BUILD, exist_ok=True)
     deps = _deps()
-    headers = [d for d in deps if d.endswith(".h")]
+    headers = [d for d in deps if d.endswith((".h", ".cuh"))]
     todo = []
     objs = []
     for s in SOURCES:

@@ -71,7 +71,9 @@ cudaError_t launch_split_attention(const float* q, const __half* kc, const __hal
 
 // Batched decode attention on the tensor cores (k_batch_attn.cu): head_dim
 // 128, <= 4 query heads per KV head, caches [B][kvh][cap][D] stored with
-// swizzled rows. A fixed grid (from configure) streams the step's (sequence,
+// swizzled rows. The attention takes the QKV projection before RoPE (internal
+// row order, rows per sequence) and does RoPE and the KV append itself. A
+// fixed grid (from configure) streams the step's (sequence,
 // KV head, 64-position chunk) items, one partial per CTA segment into `part`
 // (batch_tc_attention_part_floats floats); the merge prep combines a head's
 // partials into the O projection's prepared fp16 hi / lo input (the
@@ -80,8 +82,8 @@ cudaError_t launch_split_attention(const float* q, const __half* kc, const __hal
 bool batch_tc_attention_supported(int n_heads, int kvh, int D, int max_batch, int cap);
 size_t batch_tc_attention_part_floats(int B, int n_heads);
 cudaError_t batch_tc_attention_configure(int sm_count, int* grid);
-cudaError_t launch_batch_tc_attention(const float* q, const __half* kc, const __half* vc, int cap, int n_heads, int kvh,
-                                      float scale, const int* pos, int B, float* part, int grid, int* status,
-                                      cudaStream_t s);
+cudaError_t launch_batch_tc_attention(const float* qkv, int rows, const float* cosv, const float* sinv, int rot,
+                                      __half* kc, __half* vc, int cap, int n_heads, int kvh, float scale,
+                                      const int* pos, int B, float* part, int grid, int* status, cudaStream_t s);
 cudaError_t launch_batch_attn_merge_prep(const float* part, const int* pos, int B, int n_heads, int kvh, int grid,
                                          void* xt, cudaStream_t s);

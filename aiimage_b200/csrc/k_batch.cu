@@ -550,7 +550,16 @@ cudaError_t enqueue_batch_step(aexis_batch* bt, cudaStream_t s, int B) {
             cudaSuccess)
             return e;
         if ((e = gemm(bt, L.qkv, bt->tiled[l * 4 + 0], B, bt->qkv, rows, 1, s)) != cudaSuccess) return e;
-        {
+        if (bt->tc_attn) {
+            // RoPE and the KV append happen inside the attention kernel.
+            if ((e = launch_batch_tc_attention(bt->qkv, rows, bt->cosv, bt->sinv, c.rot_dim, kc, vc, bt->cap, NH, KVH,
+                                               scale, pos, B, bt->part, bt->tc_attn_grid, d->ctx->status, s)) !=
+                cudaSuccess)
+                return e;
+            if ((e = launch_batch_attn_merge_prep(bt->part, pos, B, NH, KVH, bt->tc_attn_grid, bt->xt, s)) !=
+                cudaSuccess)
+                return e;
+        } else {
             const float* qkv = bt->qkv;
             int r = rows, hd = D, rot = c.rot_dim, nh = NH, nkv = KVH, cap = bt->cap, bb = B;
             const int* map = d->rope_map;
@@ -558,20 +567,12 @@ cudaError_t enqueue_batch_step(aexis_batch* bt, cudaStream_t s, int B) {
             const float* sn = bt->sinv;
             const int* pp = pos;
             float* qo = bt->q;
-            int swz = bt->tc_attn ? 1 : 0;
+            int swz = 0;
             void* args[] = {(void*)&qkv, &r, (void*)&map, (void*)&cs, (void*)&sn, (void*)&pp, &hd, &rot, &nh, &nkv,
                             &cap, &bb, &qo, &kc, &vc, &swz};
-            if ((e = launch_pdl((const void*)bat_rope_kernel, dim3((rows + 255) / 256, B), dim3(256), 0, s, args)) != cudaSuccess)
-                return e;
-        }
-        if (bt->tc_attn) {
-            if ((e = launch_batch_tc_attention(bt->q, kc, vc, bt->cap, NH, KVH, scale, pos, B, bt->part,
-                                               bt->tc_attn_grid, d->ctx->status, s)) != cudaSuccess)
-                return e;
-            if ((e = launch_batch_attn_merge_prep(bt->part, pos, B, NH, KVH, bt->tc_attn_grid, bt->xt, s)) !=
+            if ((e = launch_pdl((const void*)bat_rope_kernel, dim3((rows + 255) / 256, B), dim3(256), 0, s, args)) !=
                 cudaSuccess)
                 return e;
-        } else {
             if ((e = launch_split_attention(bt->q, kc, vc, bt->cap, D, NH, KVH, scale, pos, B, bt->part,
                                             bt->counters + (size_t)l * bt->max_batch * KVH, bt->attn, d->ctx->status,
                                             kBatChunk, s)) != cudaSuccess)

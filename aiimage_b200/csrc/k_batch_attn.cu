@@ -51,6 +51,7 @@ struct TaShared {
     float sc[kTaC][kTaMaxHpg];
     __align__(16) __half pt[8][kTaPtStride];  // rows 0-3: hi of head h, 4-7: lo
     float alpha[kTaMaxHpg], mrun[kTaMaxHpg], lrun[kTaMaxHpg];
+    float qs[kTaMaxHpg][kTaD];                  // a segment's query heads after RoPE
     long long start[kTaMaxB + 1];               // item prefix over sequences
     int pos[kTaMaxB];                           // the step's positions
     uint64_t full[2];
@@ -128,9 +129,38 @@ __device__ void item_prefix(const int* pos, int B, int kvh, long long* s, int* p
     if (lane == 0) s[B] = carry;
 }
 
-// q: [B][n_heads][D] fp32 (RoPE applied); caches [B][kvh][cap][D] fp16,
-// swizzled rows; part: [B][n_heads][kTaSlots][kTaStride].
-__global__ void __launch_bounds__(kTaThreads, 3) bat_attn_tc_kernel(const float* q, const __half* kc, const __half* vc,
+// Dim d (original order) of one head after RoPE (rotate-half over the first
+// rot dims, HLSL Pack4PointwiseNorm:414-473) at the position whose cos / sin
+// rows are cs / sn, from the head's rows in the decoder's internal order:
+// pair (j, j + rot / 2) at rows 2 j, 2 j + 1, then dims rot.. in order.
+__device__ __forceinline__ float rope_dim(const float* hr, int d, int rot, const float* cs, const float* sn) {
+    // Branch-free, so that the loads of several calls issue together.
+    const int half = rot >> 1;
+    const bool rd = d < rot;
+    const int j = rd ? (d < half ? d : d - half) : 0;
+    const float x0 = __ldcg(hr + (rd ? 2 * j : d));
+    const float x1 = __ldcg(hr + (rd ? 2 * j + 1 : d));
+    const float c = rd ? __ldg(cs + j) : 1.0f;
+    const float s = rd ? __ldg(sn + j) : 0.0f;
+    return rd ? (d < half ? x0 * c - x1 * s : x0 * s + x1 * c) : x0;
+}
+
+// Position of dim d in a swizzled cache row at position p (16-byte chunks
+// XOR p & 7 within each 128-byte half row).
+__device__ __forceinline__ int swz_dim(int p, int d) {
+    const int ch = d >> 3;
+    return (((ch & 8) | ((ch & 7) ^ (p & 7))) << 3) | (d & 7);
+}
+
+// qkv: [B][rows] fp32, the QKV projection in the decoder's internal row
+// order, before RoPE; cos / sin tables [position][rot / 2]; caches
+// [B][kvh][cap][D] fp16, swizzled rows; part: [B][n_heads][kTaSlots][kTaStride].
+// RoPE and the KV append are fused in: a segment's first chunk rotates its
+// query heads while loading them, and the CTA whose item is the last chunk
+// of (b, g) rotates the step's new K row (position pos[b]), writes it and the
+// V row to the caches and patches both into its copy of the chunk.
+__global__ void __launch_bounds__(kTaThreads, 3) bat_attn_tc_kernel(const float* qkv, int rows, const float* cosv,
+                                                                   const float* sinv, int rot, __half* kc, __half* vc,
                                                                    int cap, int n_heads, int kvh, float scale,
                                                                    const int* pos, int B, float* part, int* status) {
     extern __shared__ __align__(128) uint8_t smem_raw[];
@@ -194,21 +224,47 @@ __global__ void __launch_bounds__(kTaThreads, 3) bat_attn_tc_kernel(const float*
         locate(cur, it, b, g, c);
         const int ctx = sh.pos[b] + 1;
         const int np = min(kTaC, ctx - c * kTaC);
+        const int nch = seq_chunks(ctx - 1);
         const bool seg_start = it == i0 || c == 0;
-        const bool seg_end = it + 1 == i1 || c + 1 == seq_chunks(sh.pos[b]);
+        const bool seg_end = it + 1 == i1 || c + 1 == nch;
+        const bool appends = c + 1 == nch;  // the chunk holds the step's new row, position ctx - 1
+        const float* cs = cosv + (size_t)(ctx - 1) * (rot >> 1);
+        const float* sn = sinv + (size_t)(ctx - 1) * (rot >> 1);
         if (tid == 0 && it + 1 < i1) issue(it + 1, buf ^ 1);  // that buffer was freed by the last barrier
+        __half k_new = __float2half_rn(0.0f), v_new = k_new;
+        int new_off = 0;
+        if (appends) {  // thread tid = dim tid of the new K and V rows
+            const int p = ctx - 1;
+            const float* row = qkv + (size_t)b * rows;
+            k_new = __float2half_rn(rope_dim(row + (size_t)(n_heads + g) * kTaD, tid, rot, cs, sn));
+            v_new = __float2half_rn(__ldcg(row + (size_t)(n_heads + kvh + g) * kTaD + tid));
+            const int sd = swz_dim(p, tid);
+            const size_t at = (((size_t)b * kvh + g) * cap + p) * kTaD + sd;
+            kc[at] = k_new;
+            vc[at] = v_new;
+            new_off = (p - c * kTaC) * kTaRow + sd * 2;
+        }
         if (seg_start) {
             seg_c = c;
+            {  // dim tid of the segment's query heads, after RoPE
+                const float* qb = qkv + (size_t)b * rows + (size_t)g * hpg * kTaD;
+                float qv[kTaMaxHpg];
+#pragma unroll
+                for (int h = 0; h < kTaMaxHpg; ++h) qv[h] = h < hpg ? rope_dim(qb + h * kTaD, tid, rot, cs, sn) : 0.0f;
+#pragma unroll
+                for (int h = 0; h < kTaMaxHpg; ++h) sh.qs[h][tid] = qv[h];
+            }
+            __syncthreads();
             // q columns: lane group g8 < 4 -> hi of head g8, 4..7 -> lo of head g8 - 4.
             const int hh = g8 & 3;
             const bool use = hh < hpg;
-            const float* qh = q + ((size_t)b * n_heads + (size_t)g * hpg + (use ? hh : 0)) * kTaD;
 #pragma unroll
             for (int kb = 0; kb < 8; ++kb) {
 #pragma unroll
                 for (int r = 0; r < 2; ++r) {
                     const int d = kb * 16 + r * 8 + 2 * tig;
-                    float x0 = use ? __ldcg(qh + d) : 0.0f, x1 = use ? __ldcg(qh + d + 1) : 0.0f;
+                    float x0 = use ? sh.qs[hh][d] : 0.0f;
+                    float x1 = use ? sh.qs[hh][d + 1] : 0.0f;
                     if (g8 >= 4) {
                         x0 -= __half2float(__float2half_rn(x0));
                         x1 -= __half2float(__float2half_rn(x1));
@@ -232,6 +288,14 @@ __global__ void __launch_bounds__(kTaThreads, 3) bat_attn_tc_kernel(const float*
         if (!__syncthreads_and(ok)) {
             fail_it = it;
             break;
+        }
+        if (appends) {
+            // The copy read the row before this step's value; replace it. The
+            // fence orders these writes before the buffer's next bulk copy.
+            *reinterpret_cast<__half*>(&sh.k[buf][0] + new_off) = k_new;
+            *reinterpret_cast<__half*>(&sh.v[buf][0] + new_off) = v_new;
+            fence_proxy_async_smem();
+            __syncthreads();
         }
         const uint8_t* kbuf = &sh.k[buf][0];
         const uint8_t* vbuf = &sh.v[buf][0];
@@ -439,10 +503,12 @@ cudaError_t batch_tc_attention_configure(int sm_count, int* grid) {
     return cudaSuccess;
 }
 
-cudaError_t launch_batch_tc_attention(const float* q, const __half* kc, const __half* vc, int cap, int n_heads, int kvh,
-                                      float scale, const int* pos, int B, float* part, int grid, int* status,
-                                      cudaStream_t s) {
-    void* args[] = {(void*)&q, (void*)&kc, (void*)&vc, &cap, &n_heads, &kvh, &scale, (void*)&pos, &B, &part, &status};
+cudaError_t launch_batch_tc_attention(const float* qkv, int rows, const float* cosv, const float* sinv, int rot,
+                                      __half* kc, __half* vc, int cap, int n_heads, int kvh, float scale,
+                                      const int* pos, int B, float* part, int grid, int* status, cudaStream_t s) {
+    if (rot < 0 || rot > kTaD || (rot & 1)) return cudaErrorInvalidValue;
+    void* args[] = {(void*)&qkv, &rows, (void*)&cosv, (void*)&sinv, &rot, (void*)&kc, (void*)&vc, &cap, &n_heads,
+                    &kvh, &scale, (void*)&pos, &B, &part, &status};
     return launch_pdl_ex((const void*)bat_attn_tc_kernel, dim3(grid), dim3(kTaThreads), sizeof(TaShared), s, args);
 }
 
