@@ -290,8 +290,7 @@ __device__ void stage_x(const PArgs& a, const PPhase& p, int token, int pos, PSh
     for (int j = 0; j < kPer; ++j) {
         const int e = t + j * kPConsumers;
         if (e < k) {
-            const int kb = e >> 4, w16 = e & 15;
-            const int slot = (((((kb >> 2) * 4 + ((w16 & 7) >> 1)) * 4 + (kb & 3)) * 2) + (w16 >> 3)) * 2 + (w16 & 1);
+            const int slot = q4_x_slot(e);
             const __half hi = __float2half_rn(v[j]);
             sh.xs[slot] = hi;
             sh.xs[nkb * 16 + slot] = __float2half_rn(v[j] - __half2float(hi));

@@ -16,11 +16,14 @@
 // the fp16 exponent by PRMT, one HSUB2 per pair) and one scale per row.
 //
 // Layout (built from the reference packing at upload, launch_repack_frag):
-//   * weights: 16-row tiles; per tile and per four k16 blocks, 32 lanes x 16
-//     bytes, the word of k16 block kb for lane L holding the 8 nibbles of its
-//     A fragment (rows L/4 and L/4+8, columns 2(L%4), +1, +8, +9) as offset-
-//     binary values u = q + 8, in slots (bit 4i) a0.lo a1.lo a2.lo a3.lo a0.hi
-//     a1.hi a2.hi a3.hi;
+//   * Q4 weights: 16-row tiles; per tile and per four k16 blocks, 32 lanes x
+//     16 bytes, the word of k16 block kb for lane L = (g, t) holding, in byte
+//     i, the two's complement nibbles of rows g (low) and g + 8 (high) at
+//     k = 16 kb + 4t + i: the int8 MMA's A fragment of a k32 chunk is two
+//     such words masked, the fp16 decode (decode_frag) reads k in the order
+//     (4t, 4t + 2), (4t + 1, 4t + 3) and the B fragments follow it;
+//   * Q8 weights: per lane and k16 block two words of offset-binary bytes
+//     (repack_q8_frag_kernel);
 //   * scales: per tile [group][8][2], the scales of rows r and r + 8 adjacent.
 // Both are padded to a multiple of 8 tiles (rows past n decode to zero).
 //
@@ -52,7 +55,7 @@ struct MmaParams {
     int ring_stages, stage_bytes;
 };
 
-// Repack: one thread per (tile, k16 block, lane) word.
+// Q4 repack: one thread per (tile, k16 block, lane) word (layout above).
 template <typename ST>
 __global__ void repack_q4_frag_kernel(const uint32_t* src, const ST* scales, int n, int k, int group, int ntiles_pad,
                                       uint32_t* dst, ST* dst_s) {
@@ -66,15 +69,15 @@ __global__ void repack_q4_frag_kernel(const uint32_t* src, const ST* scales, int
         const long long t = (i >> 5) / nkb;
         const int g = lane >> 2, tig = lane & 3;
         const long long r0 = t * 16 + g, r1 = r0 + 8;
-        const int k0 = kb * 16 + 2 * tig;
-        auto u = [&](long long r, int kk) -> uint32_t {
-            if (r >= n) return 8u;
-            const uint32_t wd = src[r * kw + (kk >> 3)];
-            return ((wd >> (4 * (kk & 7))) & 15u) ^ 8u;
+        const int k0 = kb * 16 + 4 * tig;
+        auto nib = [&](long long r, int kk) -> uint32_t {
+            if (r >= n) return 0u;
+            return (src[r * kw + (kk >> 3)] >> (4 * (kk & 7))) & 15u;
         };
-        const uint32_t word = u(r0, k0) | (u(r1, k0) << 4) | (u(r0, k0 + 8) << 8) | (u(r1, k0 + 8) << 12) |
-                              (u(r0, k0 + 1) << 16) | (u(r1, k0 + 1) << 20) | (u(r0, k0 + 9) << 24) |
-                              (u(r1, k0 + 9) << 28);
+        // Byte i: rows g (low nibble) and g + 8 (high nibble) at k0 + i.
+        uint32_t word = 0u;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) word |= (nib(r0, k0 + i) | (nib(r1, k0 + i) << 4)) << (8 * i);
         dst[(t * nkb + (kb >> 2) * 4) * 32 + (long long)lane * 4 + (kb & 3)] = word;
     }
     // Scales: [tile][group][8][2], rows g and g + 8 adjacent.
@@ -139,6 +142,26 @@ __device__ __forceinline__ void load_scale_pair(const float* p, float& s0, float
     s1 = f.y;
 }
 
+// The int8 path: Q4 group-32 weights with fp16 activations. Each scale group
+// (k32 chunk) of the activations becomes a 15-bit fixed-point vector
+// x_int = x 2^-E (E from the group's largest magnitude, so values within
+// three octaves of it are exact and the rest round at 2^(E-1)), split into
+// two int8 digits x_int = 256 hi + lo; one m16n8k32 MMA per group takes the
+// weights straight from their nibbles (s8_frag) and gives exact int32
+// sums. Four groups share one accumulator: group j of a window puts its hi /
+// lo digits in B columns 2j / 2j + 1, so lane (g, t) ends the window holding
+// group t's hi and lo sums for rows g and g + 8.
+template <int XF, int GK, int BITS>
+constexpr bool kS8Path = XF == 1 && GK == 2 && BITS == 4;
+
+// Bytes of the staged activations: fp16 B fragments [XF][nkb * 4] uint2 plus
+// a 32-byte zero block, or for the int8 path the B tiles (per window of four
+// groups, two halves x 32 lanes x 16 bytes) and per group {X = sum x_int,
+// 2^E, 2^E / 16, 0}.
+__host__ __device__ inline int mma_x_bytes(bool s8, int xf, int nkb) {
+    return s8 ? nkb * 128 + nkb * 8 : xf * nkb * 32 + 32;
+}
+
 // ST scale type; XF 1: fp16 activations, 2: fp32 as fp16 hi + lo; KW warps
 // per tile (K split); GK 2: scale groups of two k16 blocks (group 32) with
 // static group ends, 0: any group length (tracked at run time).
@@ -149,9 +172,11 @@ __global__ void __launch_bounds__(kMmaThreads, 2) gemv_mma_kernel(MmaParams mp) 
     extern __shared__ __align__(128) uint8_t smem[];
     const int S = mp.ring_stages;  // a multiple of NG
     const int SPG = S / NG;        // stages per group
+    constexpr bool S8 = kS8Path<XF, GK, BITS>;
     uint8_t* ring = smem;
-    uint2* xs = reinterpret_cast<uint2*>(smem + (size_t)S * mp.stage_bytes);  // [XF][nkb * 4] B fragments
-    float* red = reinterpret_cast<float*>(xs + (size_t)XF * mp.nkb * 4 + 4);   // after a 32-byte zero block: [2][kMW][16]
+    uint8_t* xreg = smem + (size_t)S * mp.stage_bytes;  // staged activations (mma_x_bytes)
+    uint2* xs = reinterpret_cast<uint2*>(xreg);
+    float* red = reinterpret_cast<float*>(xreg + mma_x_bytes(S8, XF, mp.nkb));  // [2][kMW][16]
     uint64_t* full = reinterpret_cast<uint64_t*>(red + 2 * kMW * 16);
     uint64_t* empty = full + S;
     volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + S);
@@ -228,19 +253,61 @@ __global__ void __launch_bounds__(kMmaThreads, 2) gemv_mma_kernel(MmaParams mp) 
             for (int w = 0; w < kMW; ++w) tot += redn[w];
             inv = 1.0f / sqrtf(fmaxf(tot / (float)p.k + p.norm_eps, 1e-20f));
         }
-        // Fragment order: for every four k16 blocks, lane t (0..3) owns 32
-        // contiguous bytes (blocks kb..kb+3, registers b0 b1 each).
-        __half* xh = reinterpret_cast<__half*>(xs);
-        for (int e = tid; e < p.k; e += kMW * 32) {
-            float v = aexis_load_act(p.x, p.a_dtype, e);
-            if (norm) v = v * inv * p.norm_gamma[e];
-            const int kb = e >> 4, w16 = e & 15;
-            const int slot = (((((kb >> 2) * 4 + ((w16 & 7) >> 1)) * 4 + (kb & 3)) * 2) + (w16 >> 3)) * 2 + (w16 & 1);
-            const __half hi = __float2half_rn(v);
-            xh[slot] = hi;
-            if constexpr (XF == 2) xh[(size_t)mp.nkb * 16 + slot] = __float2half_rn(v - __half2float(hi));
+        if constexpr (S8) {
+            uint4* bt = reinterpret_cast<uint4*>(xreg);
+            for (int i = tid; i < mp.nkb * 8; i += kMW * 32) bt[i] = make_uint4(0u, 0u, 0u, 0u);
+            named_sync(1, kMW * 32);
+            int4* gq = reinterpret_cast<int4*>(xreg + (size_t)mp.nkb * 128);
+            for (int q = warp; q < (p.k >> 5); q += kMW) {  // one warp per group, lane = element
+                const int e = q * 32 + lane;
+                float v = aexis_load_act(p.x, p.a_dtype, e);
+                if (norm) v = v * inv * p.norm_gamma[e];
+                float amax = fabsf(v);
+#pragma unroll
+                for (int o = 16; o >= 1; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+                int xi = 0;
+                float ge = 0.0f;
+                if (!(amax <= 3.402823466e38f)) {
+                    ge = __int_as_float(0x7fc00000);  // Inf or NaN in the group: the rows become NaN
+                } else if (amax > 0.0f) {
+                    int ex;
+                    frexpf(amax, &ex);  // amax = m 2^ex, m in [0.5, 1)
+                    xi = __float2int_rn(ldexpf(v, 14 - ex));  // |xi| <= 2^14
+                    ge = ldexpf(1.0f, ex - 14);
+                }
+                const int lo = ((xi + 128) & 255) - 128, hi = (xi - lo) >> 8;
+                int X = xi;
+#pragma unroll
+                for (int o = 16; o >= 1; o >>= 1) X += __shfl_xor_sync(0xffffffffu, X, o);
+                // Element k = lane: window q / 4, MMA j = q % 4 (half j / 2, slot j % 2),
+                // B row k -> lane t = (k % 16) / 4, byte k % 4 of register b0 (k < 16) or b1.
+                const int j = q & 3, t = (lane & 15) >> 2;
+                uint8_t* half = xreg + (size_t)((q >> 2) * 2 + (j >> 1)) * 32 * 16;
+                const int off = ((j & 1) * 2 + (lane >> 4)) * 4 + (lane & 3);
+                half[(2 * j * 4 + t) * 16 + off] = (uint8_t)hi;
+                half[((2 * j + 1) * 4 + t) * 16 + off] = (uint8_t)lo;
+                if (lane == 0) gq[q] = make_int4(X, __float_as_int(ge), __float_as_int(ge * 0.0625f), 0);
+            }
+        } else {
+            // Fragment order: for every four k16 blocks, lane t (0..3) owns 32
+            // contiguous bytes (blocks kb..kb+3, registers b0 b1 each).
+            __half* xh = reinterpret_cast<__half*>(xs);
+            for (int e = tid; e < p.k; e += kMW * 32) {
+                float v = aexis_load_act(p.x, p.a_dtype, e);
+                if (norm) v = v * inv * p.norm_gamma[e];
+                int slot;
+                if constexpr (BITS == 4) {
+                    slot = q4_x_slot(e);
+                } else {
+                    const int kb = e >> 4, w16 = e & 15;
+                    slot = (((((kb >> 2) * 4 + ((w16 & 7) >> 1)) * 4 + (kb & 3)) * 2) + (w16 >> 3)) * 2 + (w16 & 1);
+                }
+                const __half hi = __float2half_rn(v);
+                xh[slot] = hi;
+                if constexpr (XF == 2) xh[(size_t)mp.nkb * 16 + slot] = __float2half_rn(v - __half2float(hi));
+            }
+            if (tid < 8) reinterpret_cast<uint32_t*>(xs + (size_t)XF * mp.nkb * 4)[tid] = 0u;  // zero block
         }
-        if (tid < 8) reinterpret_cast<uint32_t*>(xs + (size_t)XF * mp.nkb * 4)[tid] = 0u;  // zero block
         named_sync(1, kMW * 32);
     }
     griddep_launch();
@@ -262,7 +329,8 @@ __global__ void __launch_bounds__(kMmaThreads, 2) gemv_mma_kernel(MmaParams mp) 
         // This group's local-th unit sits in its private stage grp + NG * (local % SPG):
         // the group waits for fill f of a stage only after it consumed fill f - 1.
         const int s = grp + NG * (local % SPG);
-        const bool ready = mbar_wait(full + s, (local / SPG) & 1);
+        // Warp-uniform, so that the MMAs and shuffles below see the whole warp.
+        const bool ready = __all_sync(0xffffffffu, mbar_wait(full + s, (local / SPG) & 1));
         if (!ready) {
             report_timeout(p.status);
             *abort_flag = 1;
@@ -272,7 +340,45 @@ __global__ void __launch_bounds__(kMmaThreads, 2) gemv_mma_kernel(MmaParams mp) 
         // Scales: [group][8][2], the pair (row g, row g + 8) adjacent.
         const ST* st = reinterpret_cast<const ST*>(wt + mp.tile_wbytes) + g * 2;
         float y0 = 0.0f, y1 = 0.0f;  // rows g and g + 8 (column 0: lanes with tig == 0)
-        if (ready) {
+        if constexpr (S8) {
+            if (ready) {
+                // Windows of four groups (k128): two 16-byte weight loads (words
+                // W0 W1 of each group), two B loads, four MMAs into one
+                // accumulator; lane (g, t) then scales group 4w + t.
+                const int wpw = (mp.nkb >> 3) / KW, w0 = ks * wpw;
+                const uint4* wv = reinterpret_cast<const uint4*>(wt) + lane;
+                const uint4* bv = reinterpret_cast<const uint4*>(xreg) + lane;
+                const int4* gq = reinterpret_cast<const int4*>(xreg + (size_t)mp.nkb * 128);
+#pragma unroll 2
+                for (int w = w0; w < w0 + wpw; ++w) {
+                    const uint4 wa = wv[(2 * w) * 32], wb = wv[(2 * w + 1) * 32];
+                    const uint4 ba = bv[(2 * w) * 32], bb = bv[(2 * w + 1) * 32];
+                    int c[4];
+                    uint32_t a[4];
+                    s8_frag(wa.x, wa.y, a);
+                    mma_s8_zc(c, a, make_uint2(ba.x, ba.y));
+                    s8_frag(wa.z, wa.w, a);
+                    mma_s8(c, a, make_uint2(ba.z, ba.w));
+                    s8_frag(wb.x, wb.y, a);
+                    mma_s8(c, a, make_uint2(bb.x, bb.y));
+                    s8_frag(wb.z, wb.w, a);
+                    mma_s8(c, a, make_uint2(bb.z, bb.w));
+                    const int q = 4 * w + tig;
+                    const int4 gi = gq[q];
+                    float s0, s1;
+                    load_scale_pair(st + q * 16, s0, s1);
+                    // Row g: sum u x_int - 8 X (u = q + 8); row g + 8: 16 sum q x_int.
+                    const int v0 = c[0] * 256 + c[1] - 8 * gi.x;
+                    const int v1 = c[2] * 256 + c[3];
+                    y0 = fmaf((float)v0, s0 * __int_as_float(gi.y), y0);
+                    y1 = fmaf((float)v1, s1 * __int_as_float(gi.z), y1);
+                }
+                y0 += __shfl_xor_sync(0xffffffffu, y0, 1);
+                y0 += __shfl_xor_sync(0xffffffffu, y0, 2);
+                y1 += __shfl_xor_sync(0xffffffffu, y1, 1);
+                y1 += __shfl_xor_sync(0xffffffffu, y1, 2);
+            }
+        } else if (ready) {
             float c[4] = {0.0f, 0.0f, 0.0f, 0.0f};
             int gi = kb0 / mp.gk, gpos = kb0 - gi * mp.gk;  // runtime group tracking (GK == 0)
 #pragma unroll 2
@@ -391,7 +497,9 @@ bool plan_mma(const aexis_weights* w, int xf, int sm_count, MmaPlan& pl) {
     const int ntiles = (w->n + 15) / 16;
     const int st = w->scale_dtype == AEXIS_F16 ? 2 : 4;
     const int stage = tile_wbytes(w) + scale_groups(w) * 16 * st;
-    const int fixed = xf * nkb * 32 + 32 + 2 * kMW * 16 * 4 + 16 * 16 + 64 + kMW * 4 + 128;
+    // The int8 path (fp16 activations, Q4 group 32, K a multiple of 128).
+    const bool s8 = xf == 1 && w->kind == WK_Q4 && gk == 2 && nkb % 8 == 0;
+    const int fixed = mma_x_bytes(s8, xf, nkb) + 2 * kMW * 16 * 4 + 16 * 16 + 64 + kMW * 4 + 128;
     const int want = 2 * sm_count * kMW;  // warp units that fill two CTAs per SM
     int kw0 = 1;
     while (kw0 < 8 && (long long)ntiles * kw0 < want) kw0 <<= 1;
@@ -405,7 +513,9 @@ bool plan_mma(const aexis_weights* w, int xf, int sm_count, MmaPlan& pl) {
         int kw_min = 1;
         while (kw_min < 8 && kMW / kw_min > S) kw_min <<= 1;
         const int pref = kw0 > kw_min ? kw0 : kw_min;
-        auto fits = [&](int kw) { return nkb % (kw * 4) == 0 && ((nkb / kw) % gk == 0 || gk == nkb); };
+        auto fits = [&](int kw) {
+            return nkb % (kw * 4) == 0 && ((nkb / kw) % gk == 0 || gk == nkb) && (!s8 || (nkb / 8) % kw == 0);
+        };
         int kw = 0;
         for (int c = pref; c <= 8 && !kw; c <<= 1)
             if (fits(c)) kw = c;
@@ -463,7 +573,8 @@ cudaError_t launch_mma_kw(const MmaParams& mp, int kw, int grid, int smem, bool 
 template <typename ST, int XF>
 cudaError_t launch_mma_gk(const MmaParams& mp, int bits, int kw, int grid, int smem, bool pdl, cudaStream_t s) {
     if (bits == 8) return launch_mma_kw<ST, XF, 0, 8>(mp, kw, grid, smem, pdl, s);
-    if (mp.gk == 2) return launch_mma_kw<ST, XF, 2, 4>(mp, kw, grid, smem, pdl, s);
+    // Group 32 with fp16 activations takes the int8 path (kS8Path), which needs K % 128 == 0.
+    if (mp.gk == 2 && (XF != 1 || mp.nkb % 8 == 0)) return launch_mma_kw<ST, XF, 2, 4>(mp, kw, grid, smem, pdl, s);
     return launch_mma_kw<ST, XF, 0, 4>(mp, kw, grid, smem, pdl, s);
 }
 
