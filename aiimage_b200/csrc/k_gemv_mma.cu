@@ -143,23 +143,26 @@ __device__ __forceinline__ void load_scale_pair(const float* p, float& s0, float
 }
 
 // The int8 path: Q4 group-32 weights with fp16 activations. Each scale group
-// (k32 chunk) of the activations becomes a 15-bit fixed-point vector
-// x_int = x 2^-E (E from the group's largest magnitude, so values within
-// three octaves of it are exact and the rest round at 2^(E-1)), split into
-// two int8 digits x_int = 256 hi + lo; one m16n8k32 MMA per group takes the
-// weights straight from their nibbles (s8_frag) and gives exact int32
-// sums. Four groups share one accumulator: group j of a window puts its hi /
-// lo digits in B columns 2j / 2j + 1, so lane (g, t) ends the window holding
-// group t's hi and lo sums for rows g and g + 8.
+// (k32 chunk) of the activations becomes a 23-bit fixed-point vector
+// x_int = x 2^-E, E from the group's largest magnitude: values within eleven
+// octaves of it (every fp16 value, up to outliers 2048 times the rest) are
+// exact, smaller ones round at 2^(E-1), i.e. 2^-23 of the group maximum,
+// the size of an fp32 rounding of a sum that maximum dominates. x_int is
+// split into balanced int8 digits x_int = 65536 d2 + 256 d1 + d0, and the
+// m16n8k32 MMAs take the weights straight from their nibbles (s8_frag) and
+// give exact int32 digit sums. Four groups share an accumulator: group j of
+// a window puts d2 / d1 in B columns 2j / 2j + 1 of tile A and d0 in column
+// 2j of tile B, so lane (g, t) ends the window holding group t's three
+// digit sums for rows g and g + 8.
 template <int XF, int GK, int BITS>
 constexpr bool kS8Path = XF == 1 && GK == 2 && BITS == 4;
 
 // Bytes of the staged activations: fp16 B fragments [XF][nkb * 4] uint2 plus
-// a 32-byte zero block, or for the int8 path the B tiles (per window of four
-// groups, two halves x 32 lanes x 16 bytes) and per group {X = sum x_int,
-// 2^E, 2^E / 16, 0}.
+// a 32-byte zero block, or for the int8 path the B tiles A and B (each per
+// window of four groups, two halves x 32 lanes x 16 bytes) and per group
+// {8 sum d2, 8 sum d1, 8 sum d0, 2^E}.
 __host__ __device__ inline int mma_x_bytes(bool s8, int xf, int nkb) {
-    return s8 ? nkb * 128 + nkb * 8 : xf * nkb * 32 + 32;
+    return s8 ? nkb * 256 + nkb * 8 : xf * nkb * 32 + 32;
 }
 
 // ST scale type; XF 1: fp16 activations, 2: fp32 as fp16 hi + lo; KW warps
@@ -255,9 +258,9 @@ __global__ void __launch_bounds__(kMmaThreads, 2) gemv_mma_kernel(MmaParams mp) 
         }
         if constexpr (S8) {
             uint4* bt = reinterpret_cast<uint4*>(xreg);
-            for (int i = tid; i < mp.nkb * 8; i += kMW * 32) bt[i] = make_uint4(0u, 0u, 0u, 0u);
+            for (int i = tid; i < mp.nkb * 16; i += kMW * 32) bt[i] = make_uint4(0u, 0u, 0u, 0u);
             named_sync(1, kMW * 32);
-            int4* gq = reinterpret_cast<int4*>(xreg + (size_t)mp.nkb * 128);
+            int4* gq = reinterpret_cast<int4*>(xreg + (size_t)mp.nkb * 256);
             for (int q = warp; q < (p.k >> 5); q += kMW) {  // one warp per group, lane = element
                 const int e = q * 32 + lane;
                 float v = aexis_load_act(p.x, p.a_dtype, e);
@@ -272,21 +275,28 @@ __global__ void __launch_bounds__(kMmaThreads, 2) gemv_mma_kernel(MmaParams mp) 
                 } else if (amax > 0.0f) {
                     int ex;
                     frexpf(amax, &ex);  // amax = m 2^ex, m in [0.5, 1)
-                    xi = __float2int_rn(ldexpf(v, 14 - ex));  // |xi| <= 2^14
-                    ge = ldexpf(1.0f, ex - 14);
+                    xi = __float2int_rn(ldexpf(v, 22 - ex));  // |xi| <= 2^22
+                    ge = ldexpf(1.0f, ex - 22);
                 }
-                const int lo = ((xi + 128) & 255) - 128, hi = (xi - lo) >> 8;
-                int X = xi;
+                const int d0 = ((xi + 128) & 255) - 128, x1 = (xi - d0) >> 8;
+                const int d1 = ((x1 + 128) & 255) - 128, d2 = (x1 - d1) >> 8;  // |d2| <= 64
+                int X0 = d0, X1 = d1, X2 = d2;
 #pragma unroll
-                for (int o = 16; o >= 1; o >>= 1) X += __shfl_xor_sync(0xffffffffu, X, o);
+                for (int o = 16; o >= 1; o >>= 1) {
+                    X0 += __shfl_xor_sync(0xffffffffu, X0, o);
+                    X1 += __shfl_xor_sync(0xffffffffu, X1, o);
+                    X2 += __shfl_xor_sync(0xffffffffu, X2, o);
+                }
                 // Element k = lane: window q / 4, MMA j = q % 4 (half j / 2, slot j % 2),
                 // B row k -> lane t = (k % 16) / 4, byte k % 4 of register b0 (k < 16) or b1.
                 const int j = q & 3, t = (lane & 15) >> 2;
                 uint8_t* half = xreg + (size_t)((q >> 2) * 2 + (j >> 1)) * 32 * 16;
+                uint8_t* half_b = half + (size_t)mp.nkb * 128;
                 const int off = ((j & 1) * 2 + (lane >> 4)) * 4 + (lane & 3);
-                half[(2 * j * 4 + t) * 16 + off] = (uint8_t)hi;
-                half[((2 * j + 1) * 4 + t) * 16 + off] = (uint8_t)lo;
-                if (lane == 0) gq[q] = make_int4(X, __float_as_int(ge), __float_as_int(ge * 0.0625f), 0);
+                half[(2 * j * 4 + t) * 16 + off] = (uint8_t)d2;
+                half[((2 * j + 1) * 4 + t) * 16 + off] = (uint8_t)d1;
+                half_b[(2 * j * 4 + t) * 16 + off] = (uint8_t)d0;
+                if (lane == 0) gq[q] = make_int4(8 * X2, 8 * X1, 8 * X0, __float_as_int(ge));
             }
         } else {
             // Fragment order: for every four k16 blocks, lane t (0..3) owns 32
@@ -348,30 +358,39 @@ __global__ void __launch_bounds__(kMmaThreads, 2) gemv_mma_kernel(MmaParams mp) 
                 const int wpw = (mp.nkb >> 3) / KW, w0 = ks * wpw;
                 const uint4* wv = reinterpret_cast<const uint4*>(wt) + lane;
                 const uint4* bv = reinterpret_cast<const uint4*>(xreg) + lane;
-                const int4* gq = reinterpret_cast<const int4*>(xreg + (size_t)mp.nkb * 128);
+                const uint4* bv0 = reinterpret_cast<const uint4*>(xreg + (size_t)mp.nkb * 128) + lane;
+                const int4* gq = reinterpret_cast<const int4*>(xreg + (size_t)mp.nkb * 256);
 #pragma unroll 2
                 for (int w = w0; w < w0 + wpw; ++w) {
                     const uint4 wa = wv[(2 * w) * 32], wb = wv[(2 * w + 1) * 32];
                     const uint4 ba = bv[(2 * w) * 32], bb = bv[(2 * w + 1) * 32];
-                    int c[4];
+                    const uint4 ea = bv0[(2 * w) * 32], eb = bv0[(2 * w + 1) * 32];
+                    int c[4], d[4];
                     uint32_t a[4];
                     s8_frag(wa.x, wa.y, a);
                     mma_s8_zc(c, a, make_uint2(ba.x, ba.y));
+                    mma_s8_zc(d, a, make_uint2(ea.x, ea.y));
                     s8_frag(wa.z, wa.w, a);
                     mma_s8(c, a, make_uint2(ba.z, ba.w));
+                    mma_s8(d, a, make_uint2(ea.z, ea.w));
                     s8_frag(wb.x, wb.y, a);
                     mma_s8(c, a, make_uint2(bb.x, bb.y));
+                    mma_s8(d, a, make_uint2(eb.x, eb.y));
                     s8_frag(wb.z, wb.w, a);
                     mma_s8(c, a, make_uint2(bb.z, bb.w));
+                    mma_s8(d, a, make_uint2(eb.z, eb.w));
                     const int q = 4 * w + tig;
                     const int4 gi = gq[q];
                     float s0, s1;
                     load_scale_pair(st + q * 16, s0, s1);
-                    // Row g: sum u x_int - 8 X (u = q + 8); row g + 8: 16 sum q x_int.
-                    const int v0 = c[0] * 256 + c[1] - 8 * gi.x;
-                    const int v1 = c[2] * 256 + c[3];
-                    y0 = fmaf((float)v0, s0 * __int_as_float(gi.y), y0);
-                    y1 = fmaf((float)v1, s1 * __int_as_float(gi.z), y1);
+                    // Row g (weights u = q + 8): digit sums minus 8 sum(d); row
+                    // g + 8 (weights 16 q): the digit sums, 1/16 in the factor.
+                    const float f0 = fmaf((float)(c[0] - gi.x), 65536.0f,
+                                          fmaf((float)(c[1] - gi.y), 256.0f, (float)(d[0] - gi.z)));
+                    const float f1 = fmaf((float)c[2], 65536.0f, fmaf((float)c[3], 256.0f, (float)d[2]));
+                    const float ge = __int_as_float(gi.w);
+                    y0 = fmaf(f0, s0 * ge, y0);
+                    y1 = fmaf(f1, s1 * (ge * 0.0625f), y1);
                 }
                 y0 += __shfl_xor_sync(0xffffffffu, y0, 1);
                 y0 += __shfl_xor_sync(0xffffffffu, y0, 2);

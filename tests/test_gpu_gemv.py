@@ -87,6 +87,50 @@ def test_fast_kernel_formats(ops, oracle, bits, k, n, group, sdt):
     assert_gemv_close(got, ref)
 
 
+@pytest.mark.parametrize("k,n", [(1024, 4100), (3584, 1000), (1024, 48)])
+def test_q4_fp16_int8_path_wide_range_groups(ops, oracle, k, n):
+    """fp16 activations on Q4 group-32 weights run on int8 MMAs with each group
+    as 23-bit fixed point (exact within 2^11 of the group maximum). Groups with
+    outliers up to 2000 times the rest, an all-zero group, subnormals, tiny
+    groups and a group of large values up to the fp16 maximum: every row
+    within 3e-5 of sum|w s x| of the exact result (the size of fp32
+    accumulation error), and the north-star tolerance. N off the 16-row tile,
+    K = 3584 splits a tile over several warps, N = 48 over all eight."""
+    import torch
+    p, s = synth.q4_weights(n, k, 32, seed=7, tag=(k, n))
+    x = synth.activations(k, seed=7, tag=(k, n)).astype(np.float32)[0]
+    x[5] = 1900.0
+    x[32 * 3 + 7] = -1024.5
+    x[64:96] = 0.0
+    x[300] = 3e-6          # fp16 subnormal
+    x[301] = -6e-8
+    x[32 * 20:32 * 21] = np.clip(x[32 * 20:32 * 21] * 20000.0, -65504.0, 65504.0)
+    x[32 * 20 + 1] = 65504.0  # fp16 max in a group of large values
+    x[32 * 21:32 * 22] *= 1e-3
+    x16 = x.astype(np.float16)
+    w = ops.new_int4_weight_only_upload(p, s, n, k, 32)
+    got = run_gemv(ops, w, x16.reshape(1, -1), n, torch.float32)[0].astype(np.float64)
+    ref = oracle.gemm(x16.reshape(1, -1).astype(np.float32), 4, p, s.astype(np.float32), 32, n)[0].astype(np.float64)
+    wq = synth.unpack_q4(p, n, k).astype(np.float64) * np.repeat(s.astype(np.float64).reshape(n, k // 32), 32, 1)
+    absum = np.abs(wq * x16.astype(np.float64)[None, :]).sum(1)
+    err = np.abs(got - ref)
+    assert (err <= 3e-5 * absum).all(), f"worst row {int((err / absum).argmax())}: {(err / absum).max():.3g}"
+    assert_gemv_close(got[None, :], ref[None, :])
+
+
+def test_q4_fp16_nonfinite_activation_gives_nonfinite_rows(ops):
+    """An Inf in a group of fp16 activations makes the rows non-finite (the
+    reference's fp32 sum would too), not a silently finite number."""
+    import torch
+    k, n = 1024, 64
+    p, s = synth.q4_weights(n, k, 32, seed=8, tag=(k, n))
+    x = synth.activations(k, seed=8, tag=(k, n))
+    x[0, 40] = np.float16(np.inf)
+    w = ops.new_int4_weight_only_upload(p, s, n, k, 32)
+    got = run_gemv(ops, w, x, n, torch.float32)[0]
+    assert not np.isfinite(got).any()
+
+
 @pytest.mark.parametrize("bits,k,n,group", [(4, 100, 37, 10), (4, 48, 33, 16), (8, 40, 19, 0), (8, 7, 5, 0),
                                             (4, 5, 3, 5)])
 def test_generic_kernel_odd_shapes(ops, oracle, bits, k, n, group):
