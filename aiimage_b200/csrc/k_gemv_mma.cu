@@ -154,8 +154,10 @@ __device__ __forceinline__ void load_scale_pair(const float* p, float& s0, float
 // a window puts d2 / d1 in B columns 2j / 2j + 1 of tile A and d0 in column
 // 2j of tile B, so lane (g, t) ends the window holding group t's three
 // digit sums for rows g and g + 8.
+// It pays where a CTA streams many tiles (the activations are quantised once
+// per CTA): plan_mma picks it for N >= 8 x 16 x SM-count rows.
 template <int XF, int GK, int BITS>
-constexpr bool kS8Path = XF == 1 && GK == 2 && BITS == 4;
+constexpr bool kS8Able = XF == 1 && GK == 2 && BITS == 4;
 
 // Bytes of the staged activations: fp16 B fragments [XF][nkb * 4] uint2 plus
 // a 32-byte zero block, or for the int8 path the B tiles A and B (each per
@@ -168,14 +170,14 @@ __host__ __device__ inline int mma_x_bytes(bool s8, int xf, int nkb) {
 // ST scale type; XF 1: fp16 activations, 2: fp32 as fp16 hi + lo; KW warps
 // per tile (K split); GK 2: scale groups of two k16 blocks (group 32) with
 // static group ends, 0: any group length (tracked at run time).
-template <typename ST, int XF, int KW, int GK, int BITS>
+template <typename ST, int XF, int KW, int GK, int BITS, bool S8P>
 __global__ void __launch_bounds__(kMmaThreads, 2) gemv_mma_kernel(MmaParams mp) {
     constexpr int NG = kMW / KW;  // warp groups; group it % NG takes unit it
     const StreamParams& p = mp.sp;
     extern __shared__ __align__(128) uint8_t smem[];
     const int S = mp.ring_stages;  // a multiple of NG
     const int SPG = S / NG;        // stages per group
-    constexpr bool S8 = kS8Path<XF, GK, BITS>;
+    constexpr bool S8 = S8P && kS8Able<XF, GK, BITS>;
     uint8_t* ring = smem;
     uint8_t* xreg = smem + (size_t)S * mp.stage_bytes;  // staged activations (mma_x_bytes)
     uint2* xs = reinterpret_cast<uint2*>(xreg);
@@ -496,6 +498,7 @@ __global__ void __launch_bounds__(kMmaThreads, 2) gemv_mma_kernel(MmaParams mp) 
 
 struct MmaPlan {
     int kw = 0, units = 0, stages = 0, stage_bytes = 0, smem = 0, per_sm = 1;
+    bool s8 = false;  // the int8 path (kS8Able, many tiles per CTA)
 };
 
 int frag_tiles_padded(int n) { return ((n + 15) / 16 + 7) / 8 * 8; }
@@ -517,7 +520,7 @@ bool plan_mma(const aexis_weights* w, int xf, int sm_count, MmaPlan& pl) {
     const int st = w->scale_dtype == AEXIS_F16 ? 2 : 4;
     const int stage = tile_wbytes(w) + scale_groups(w) * 16 * st;
     // The int8 path (fp16 activations, Q4 group 32, K a multiple of 128).
-    const bool s8 = xf == 1 && w->kind == WK_Q4 && gk == 2 && nkb % 8 == 0;
+    const bool s8 = xf == 1 && w->kind == WK_Q4 && gk == 2 && nkb % 8 == 0 && ntiles >= 8 * sm_count;
     const int fixed = mma_x_bytes(s8, xf, nkb) + 2 * kMW * 16 * 4 + 16 * 16 + 64 + kMW * 4 + 128;
     const int want = 2 * sm_count * kMW;  // warp units that fill two CTAs per SM
     int kw0 = 1;
@@ -548,19 +551,20 @@ bool plan_mma(const aexis_weights* w, int xf, int sm_count, MmaPlan& pl) {
         pl.stage_bytes = stage;
         pl.smem = S * stage + fixed;
         pl.per_sm = per_sm;
+        pl.s8 = s8;
         return true;
     }
     return false;
 }
 
-template <typename ST, int XF, int KW, int GK, int BITS>
+template <typename ST, int XF, int KW, int GK, int BITS, bool S8P>
 cudaError_t launch_mma_t(const MmaParams& mp, int grid, int smem, bool pdl, cudaStream_t stream) {
     static int configured[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
     if (smem > configured[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(gemv_mma_kernel<ST, XF, KW, GK, BITS>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        cudaError_t e = cudaFuncSetAttribute(gemv_mma_kernel<ST, XF, KW, GK, BITS, S8P>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e != cudaSuccess) return e;
         configured[dev] = smem;
     }
@@ -574,26 +578,30 @@ cudaError_t launch_mma_t(const MmaParams& mp, int grid, int smem, bool pdl, cuda
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, gemv_mma_kernel<ST, XF, KW, GK, BITS>, mp);
+    return cudaLaunchKernelEx(&cfg, gemv_mma_kernel<ST, XF, KW, GK, BITS, S8P>, mp);
 }
 
-template <typename ST, int XF, int GK, int BITS>
+template <typename ST, int XF, int GK, int BITS, bool S8P = false>
 cudaError_t launch_mma_kw(const MmaParams& mp, int kw, int grid, int smem, bool pdl, cudaStream_t s) {
     switch (kw) {
-        case 1: return launch_mma_t<ST, XF, 1, GK, BITS>(mp, grid, smem, pdl, s);
-        case 2: return launch_mma_t<ST, XF, 2, GK, BITS>(mp, grid, smem, pdl, s);
-        case 4: return launch_mma_t<ST, XF, 4, GK, BITS>(mp, grid, smem, pdl, s);
-        default: return launch_mma_t<ST, XF, 8, GK, BITS>(mp, grid, smem, pdl, s);
+        case 1: return launch_mma_t<ST, XF, 1, GK, BITS, S8P>(mp, grid, smem, pdl, s);
+        case 2: return launch_mma_t<ST, XF, 2, GK, BITS, S8P>(mp, grid, smem, pdl, s);
+        case 4: return launch_mma_t<ST, XF, 4, GK, BITS, S8P>(mp, grid, smem, pdl, s);
+        default: return launch_mma_t<ST, XF, 8, GK, BITS, S8P>(mp, grid, smem, pdl, s);
     }
 }
 
 // Q4 with groups of 32 takes the static group path; Q8 (one scale per row)
 // and other Q4 groups the run-time one.
 template <typename ST, int XF>
-cudaError_t launch_mma_gk(const MmaParams& mp, int bits, int kw, int grid, int smem, bool pdl, cudaStream_t s) {
+cudaError_t launch_mma_gk(const MmaParams& mp, int bits, int kw, bool s8, int grid, int smem, bool pdl,
+                          cudaStream_t s) {
     if (bits == 8) return launch_mma_kw<ST, XF, 0, 8>(mp, kw, grid, smem, pdl, s);
-    // Group 32 with fp16 activations takes the int8 path (kS8Path), which needs K % 128 == 0.
-    if (mp.gk == 2 && (XF != 1 || mp.nkb % 8 == 0)) return launch_mma_kw<ST, XF, 2, 4>(mp, kw, grid, smem, pdl, s);
+    if (mp.gk == 2) {
+        if constexpr (XF == 1)
+            if (s8) return launch_mma_kw<ST, XF, 2, 4, true>(mp, kw, grid, smem, pdl, s);
+        return launch_mma_kw<ST, XF, 2, 4>(mp, kw, grid, smem, pdl, s);
+    }
     return launch_mma_kw<ST, XF, 0, 4>(mp, kw, grid, smem, pdl, s);
 }
 
@@ -683,9 +691,9 @@ cudaError_t launch_gemv_mma(const GemvArgs& a, int sm_count, cudaStream_t stream
     const int grid = pl.units < pl.per_sm * sm_count ? pl.units : pl.per_sm * sm_count;
     const int bits = w->kind == WK_Q8 ? 8 : 4;
     if (w->scale_dtype == AEXIS_F16) {
-        if (xf == 1) return launch_mma_gk<__half, 1>(mp, bits, pl.kw, grid, pl.smem, a.pdl, stream);
-        return launch_mma_gk<__half, 2>(mp, bits, pl.kw, grid, pl.smem, a.pdl, stream);
+        if (xf == 1) return launch_mma_gk<__half, 1>(mp, bits, pl.kw, pl.s8, grid, pl.smem, a.pdl, stream);
+        return launch_mma_gk<__half, 2>(mp, bits, pl.kw, pl.s8, grid, pl.smem, a.pdl, stream);
     }
-    if (xf == 1) return launch_mma_gk<float, 1>(mp, bits, pl.kw, grid, pl.smem, a.pdl, stream);
-    return launch_mma_gk<float, 2>(mp, bits, pl.kw, grid, pl.smem, a.pdl, stream);
+    if (xf == 1) return launch_mma_gk<float, 1>(mp, bits, pl.kw, pl.s8, grid, pl.smem, a.pdl, stream);
+    return launch_mma_gk<float, 2>(mp, bits, pl.kw, pl.s8, grid, pl.smem, a.pdl, stream);
 }

@@ -361,7 +361,7 @@ def run_gpu(args):
                        "bytes_per_step": STEP_BYTES, "weight_copies": copies,
                        "l2": f"weights rotated over {copies} copies ({copies * STEP_BYTES / 2**20:.0f} MiB > 4x L2)",
                        "parallelism": f"replicas x{world}"},
-            "roofline": {"bound": "hbm", "kernel": "gemv_mma_kernel q4 g32 (1024x151936)",
+            "roofline": {"bound": "hbm", "kernel": "gemv_mma_kernel q4 g32 fp16-x int8-MMA path (1024x151936)",
                          "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": traffic,
                          "algorithmic_bytes_per_launch": SWEEP_BYTES[DOMINANT],

@@ -87,15 +87,16 @@ def test_fast_kernel_formats(ops, oracle, bits, k, n, group, sdt):
     assert_gemv_close(got, ref)
 
 
-@pytest.mark.parametrize("k,n", [(1024, 4100), (3584, 1000), (1024, 48)])
+@pytest.mark.parametrize("k,n", [(1024, 20000), (3584, 19000), (1024, 4100), (1024, 48)])
 def test_q4_fp16_int8_path_wide_range_groups(ops, oracle, k, n):
-    """fp16 activations on Q4 group-32 weights run on int8 MMAs with each group
-    as 23-bit fixed point (exact within 2^11 of the group maximum). Groups with
-    outliers up to 2000 times the rest, an all-zero group, subnormals, tiny
-    groups and a group of large values up to the fp16 maximum: every row
-    within 3e-5 of sum|w s x| of the exact result (the size of fp32
-    accumulation error), and the north-star tolerance. N off the 16-row tile,
-    K = 3584 splits a tile over several warps, N = 48 over all eight."""
+    """fp16 activations on Q4 group-32 weights with N >= 8 x 16 x 148 rows run
+    on int8 MMAs with each group as 23-bit fixed point (exact within 2^11 of
+    the group maximum); smaller N on the fp16 MMAs. Groups with outliers up to
+    2000 times the rest, an all-zero group, subnormals, tiny groups and a
+    group of large values up to the fp16 maximum: every row within 3e-5 of
+    sum|w s x| of the exact result (the size of fp32 accumulation error), and
+    the north-star tolerance. N off the 16-row tile; K = 3584 splits tiles
+    over warps."""
     import torch
     p, s = synth.q4_weights(n, k, 32, seed=7, tag=(k, n))
     x = synth.activations(k, seed=7, tag=(k, n)).astype(np.float32)[0]
