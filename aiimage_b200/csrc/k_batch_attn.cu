@@ -169,7 +169,10 @@ __global__ void __launch_bounds__(kTaThreads, 3) bat_attn_tc_kernel(const float*
     const int g8 = lane >> 2, tig = lane & 3;
     const int hpg = n_heads / kvh;
     const int G = gridDim.x, blk = blockIdx.x;
-    griddep_wait();
+    // Before the wait on the previous kernel (programmatic dependent launch):
+    // the positions (written by the previous step) and the cache rows below
+    // them are final, so the item prefix and the first chunk's copies start
+    // here; the QKV projection (the previous kernel's output) is read after.
     if (warp == 0) item_prefix(pos, B, kvh, sh.start, sh.pos, lane);
     // Zero both chunk buffers (rows past a chunk's end are read by the MMAs,
     // weighted 0) and P^T (columns of unused heads stay 0).
@@ -186,6 +189,7 @@ __global__ void __launch_bounds__(kTaThreads, 3) bat_attn_tc_kernel(const float*
     const long long T = sh.start[B];
     const long long i0 = cta_first(T, blk, G), i1 = cta_first(T, blk + 1, G);
     if (i0 >= i1) {
+        griddep_wait();
         griddep_launch();
         return;
     }
@@ -212,6 +216,8 @@ __global__ void __launch_bounds__(kTaThreads, 3) bat_attn_tc_kernel(const float*
         bulk_g2s_plain(&sh.v[buf][0], vc + row0 * kTaD, bytes, &sh.full[buf]);
     };
     if (tid == 0) issue(i0, 0);
+    griddep_wait();
+    griddep_launch();
 
     uint32_t qf[8][2];     // B fragments of q (hi / lo columns), per 16-dim block
     float acc[2][4];       // O partials: rows d (2 m-tiles), columns 2 tig, 2 tig + 1
@@ -408,7 +414,6 @@ __global__ void __launch_bounds__(kTaThreads, 3) bat_attn_tc_kernel(const float*
         mbar_wait(&sh.full[k & 1], (uint32_t)((k >> 1) & 1));
         if (fail_it + 1 < i1) mbar_wait(&sh.full[(k + 1) & 1], (uint32_t)(((k + 1) >> 1) & 1));
     }
-    griddep_launch();
 }
 
 // Row b, query head h of the O projection's input: the merge of the head's
@@ -424,6 +429,7 @@ __global__ void __launch_bounds__(kTaD) bat_attn_merge_prep_kernel(const float* 
     __shared__ float wsm[kTaSlots];
     __shared__ float red[kTaD / 32];
     griddep_wait();
+    griddep_launch();
     const int b = blockIdx.x, h = blockIdx.y, d = threadIdx.x, lane = d & 31, warp = d >> 5;
     float v = 0.0f;
     if (b < B) {
@@ -464,7 +470,6 @@ __global__ void __launch_bounds__(kTaD) bat_attn_merge_prep_kernel(const float* 
     const int rlo = nb / 2 + b;
     *reinterpret_cast<__half*>(xt + ((size_t)kb * nb + b) * 128 + ((((cc >> 3) ^ (b & 7)) << 4)) + (cc & 7) * 2) = hi;
     *reinterpret_cast<__half*>(xt + ((size_t)kb * nb + rlo) * 128 + ((((cc >> 3) ^ (rlo & 7)) << 4)) + (cc & 7) * 2) = lo;
-    griddep_launch();
 }
 
 cudaError_t launch_pdl_ex(const void* fn, dim3 grid, dim3 block, size_t smem, cudaStream_t s, void** args) {

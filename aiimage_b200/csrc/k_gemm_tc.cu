@@ -241,8 +241,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_q8_tc_kernel(TcParams p) {
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    griddep_wait();
-    griddep_launch();  // every CTA is resident (grid <= SMs): dependents may start their prologue
+    // Programmatic dependent launch: the weights are immutable, so their bulk
+    // copies (warp 0) and dequantisation (warps 2-5) start before the wait on
+    // the previous kernel; the activation producer (6), the MMA issuer (1)
+    // and every epilogue wait first. The CTA lets its dependents launch only
+    // after that wait (warps 1 and 6), so a dependent's own pre-wait reads
+    // never see a kernel older than this one still running.
 
     if (warp == 0) {
         // ------------------------------------------------- int8 weight producer
@@ -275,6 +279,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_q8_tc_kernel(TcParams p) {
         }
     } else if (warp == 6) {
         // ---------------------------------------------- activation producer
+        griddep_wait();
+        griddep_launch();
         if (lane == 0) {
             int it = 0, issued = 0;
             for (int t = 0; t < my_tiles && !*abort_flag; ++t) {
@@ -298,6 +304,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_q8_tc_kernel(TcParams p) {
         }
     } else if (warp == 1) {
         // ---------------------------------------------------------- MMA issuer
+        griddep_wait();
+        griddep_launch();
         if (lane == 0) {
             const uint32_t idesc = idesc_f16_f32(kTM, p.nb);
             int it = 0;
@@ -386,7 +394,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_q8_tc_kernel(TcParams p) {
             }
             if (*abort_flag) break;
             // Epilogue: wait for the tile's accumulators, then each thread owns
-            // one weight row (TMEM lane) of each 128-row slab.
+            // one weight row (TMEM lane) of each 128-row slab. The outputs and
+            // the bias belong to the stream order: after the previous kernel.
+            griddep_wait();
             if (!mbar_wait(acc_full, t & 1)) {
                 report_timeout(p.status);
                 *abort_flag = 1;
@@ -524,12 +534,15 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_q8_tc_kernel(TcParams p) {
 //   op 2: SwiGLU of interleaved pairs, silu(x[b][2k]) * x[b][2k+1]
 //         (HLSL Pack4Matmul:91-94, 118-128; x fp32).
 // With `zero`, the CTA of row b also clears zero[b][0, zero_n) (the output
-// of a following accumulating GEMM). Waits for the previous grid (PDL).
+// of a following accumulating GEMM). Waits for the previous grid (PDL) and
+// then lets its dependents launch, so a following GEMM streams its weights
+// during this kernel.
 __global__ void __launch_bounds__(256) tc_prep_kernel(const void* x, int x_f16, int lda, int m, int k, int op,
                                                       const float* gamma, float eps, int nb, int split, uint8_t* xt,
                                                       float* zero, int zero_ld, int zero_n) {
     __shared__ float red[8];
     griddep_wait();
+    griddep_launch();  // after the wait: a dependent's pre-wait reads see every older kernel complete
     const int b = blockIdx.x;
     const int half = split ? nb >> 1 : nb;
     const float* xf = reinterpret_cast<const float*>(x);
@@ -577,7 +590,6 @@ __global__ void __launch_bounds__(256) tc_prep_kernel(const void* x, int x_f16, 
     }
     if (zero && b < m)
         for (int i = threadIdx.x; i < zero_n; i += 256) zero[(long long)b * zero_ld + i] = 0.0f;
-    griddep_launch();
 }
 
 // Row-major Q8 [n][k] -> [ceil(n/256)*2][k/64][128][64] (rows past n zero;
