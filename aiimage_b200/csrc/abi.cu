@@ -568,3 +568,52 @@ AEXIS_API int aexis_cuda_swiglu(aexis_ctx* ctx, const float* gate, const float* 
     if (rc) return rc;
     return aexis_cuda_check(ctx, launch_swiglu(gate, up, count, y, ctx->stream), "swiglu launch");
 }
+
+// ------------------------------------------------------ linear-attention decode
+
+AEXIS_API int aexis_cuda_short_conv(aexis_ctx* ctx, const float* weight, const float* mixed, const float* cache_in,
+                                    float* out, float* cache_out, int groups, int kernel_size, int seq_len,
+                                    int cache_len) {
+    if (!ctx) return AEXIS_E_NULL;
+    if (!weight || !mixed || !cache_in || !out || !cache_out)
+        return aexis_fail(ctx, AEXIS_E_NULL, "ShortConv texture input/output is null.");
+    if (groups <= 0 || kernel_size <= 0 || seq_len <= 0 || cache_len < kernel_size - 1)
+        return aexis_fail(ctx, AEXIS_E_RANGE, "groups=%d kernel=%d seq=%d cache=%d", groups, kernel_size, seq_len,
+                          cache_len);
+    if (kernel_size > 16)
+        return aexis_fail(ctx, AEXIS_E_UNSUPPORTED, "ShortConv kernel size %d > 16", kernel_size);
+    if (out == mixed || out == cache_in || cache_out == mixed || out == cache_out)
+        return aexis_fail(ctx, AEXIS_E_SHAPE, "ShortConv output aliases an input (only cache_out == cache_in is allowed)");
+    int rc = bind(ctx);
+    if (rc) return rc;
+    return aexis_cuda_check(ctx, launch_short_conv(weight, mixed, cache_in, out, cache_out, groups, kernel_size,
+                                                   seq_len, cache_len, ctx->stream),
+                            "short conv launch");
+}
+
+AEXIS_API int aexis_cuda_gated_delta_rule(aexis_ctx* ctx, const float* a_log, const float* dt_bias, const float* b,
+                                          const float* a, const float* q, const float* k, const float* v,
+                                          const float* state_in, float* out, float* state_out, int heads, int key_dim,
+                                          int value_dim, int seq_len, int first_token, int token_count, float eps) {
+    if (!ctx) return AEXIS_E_NULL;
+    if (!a_log || !dt_bias || !b || !a || !q || !k || !v || !state_in || !out || !state_out)
+        return aexis_fail(ctx, AEXIS_E_NULL, "GatedDeltaRule texture input/output is null.");
+    if (heads <= 0 || key_dim <= 0 || value_dim <= 0 || seq_len <= 0)
+        return aexis_fail(ctx, AEXIS_E_RANGE, "heads=%d keyDim=%d valueDim=%d seq=%d", heads, key_dim, value_dim,
+                          seq_len);
+    if (first_token < 0 || token_count <= 0 || first_token > seq_len - token_count)
+        return aexis_fail(ctx, AEXIS_E_RANGE, "tokens [%d, %d) outside the sequence of %d", first_token,
+                          first_token + token_count, seq_len);
+    if (key_dim > gdr_max_kdim())
+        return aexis_fail(ctx, AEXIS_E_UNSUPPORTED, "GatedDeltaRule key dim %d > %d", key_dim, gdr_max_kdim());
+    if ((reinterpret_cast<uintptr_t>(state_in) | reinterpret_cast<uintptr_t>(state_out)) & 15)
+        return aexis_fail(ctx, AEXIS_E_SHAPE, "GatedDeltaRule state buffers must be 16-byte aligned");
+    if (out == q || out == k || out == v || out == state_out)
+        return aexis_fail(ctx, AEXIS_E_SHAPE, "GatedDeltaRule output aliases an input");
+    int rc = bind(ctx);
+    if (rc) return rc;
+    return aexis_cuda_check(ctx, launch_gated_delta_rule(a_log, dt_bias, b, a, q, k, v, state_in, out, state_out,
+                                                         heads, key_dim, value_dim, first_token, token_count, eps,
+                                                         ctx->stream),
+                            "gated delta rule launch");
+}

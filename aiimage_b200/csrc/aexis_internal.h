@@ -180,6 +180,14 @@ cudaError_t launch_embed(const int32_t* words, int count, const aexis_weights* t
                          const float* bias, float* out, cudaStream_t s);
 cudaError_t launch_swish(const float* x, int count, float* y, cudaStream_t s);
 cudaError_t launch_swiglu(const float* g, const float* u, int count, float* y, cudaStream_t s);
+// Linear-attention decode kernels (k_recurrent.cu).
+cudaError_t launch_short_conv(const float* weight, const float* mixed, const float* cache_in, float* out,
+                              float* cache_out, int groups, int kernel, int seq, int cache_len, cudaStream_t s);
+int gdr_max_kdim();
+cudaError_t launch_gated_delta_rule(const float* a_log, const float* dt_bias, const float* b, const float* a,
+                                    const float* q, const float* k, const float* v, const float* state_in,
+                                    float* out, float* state_out, int heads, int kdim, int vdim, int first,
+                                    int count, float eps, cudaStream_t s);
 
 // Device helpers shared by kernels.
 #ifdef __CUDACC__

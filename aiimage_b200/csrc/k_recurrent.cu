@@ -1,0 +1,237 @@
+// k_recurrent.cu -- decode kernels of the linear-attention blocks of Qwen3.5
+// (18 of its 24 decoder blocks): the causal depthwise ShortConv with its
+// streaming cache, and the recurrent Gated Delta Rule.
+//
+// Reference (paths relative to Packages/com.aexis/Runtime/):
+//   AexisShortConvPack4       Resources/Aexis/AexisCommon.compute:623-678
+//   AexisGatedDeltaRulePack4  Resources/Aexis/AexisCommon.compute:680-753
+//   Ops.ShortConvPack4 / GatedDeltaRulePack4  Execution/Graph/AexisOps.cs:12593-12657
+//   AexisGatedDeltaRuleLayer  Execution/Layers/AexisGatedDeltaRuleLayer.cs:32-98
+//     (one dispatch per token, ping-pong state textures)
+//
+// The reference dispatches the Gated Delta Rule once per token, re-reading
+// and re-writing the whole [heads, kdim, vdim] state each time. Here one
+// launch runs any number of tokens: each CTA owns a 16-column slice of one
+// head's state and keeps it in registers from the first token to the last,
+// so the state crosses HBM once in and once out per call. For batch-1 decode
+// (one token) the kernel is bound by that 2 x heads x kdim x vdim x 4 bytes
+// and by launch latency.
+#include "aexis_internal.h"
+
+namespace {
+
+constexpr int kConvMaxKernel = 16;
+
+// AexisShortConvPack4 (COMMON:623-678). One thread per channel (group).
+// Layouts: weight Pack4 CDHW [w=kernel, h=1, c=groups] (element (k, g) at
+// ((g/4)*kernel + k)*4 + (g&3)); mixed/out [seq][ld], cache_in/cache_out
+// [cache_len][ld], ld = ceil(groups/4)*4 (Pack4 linear rows).
+//   out[t][g] = silu(sum_k hist(cache_len - kernel + t + 1 + k) * w[g][k])
+//   hist(i)   = i < 0 ? 0 : i < cache_len ? cache_in[i] : mixed[i - cache_len]
+//   cache_out[i] = hist(seq + i), the tail of [cache_in; mixed].
+// All outputs are computed before the cache is rewritten, and cache_out[i]
+// reads hist(seq + i) with seq + i > i, so cache_out may be cache_in itself.
+__global__ void short_conv_kernel(const float* __restrict__ weight, const float* __restrict__ mixed,
+                                  const float* cache_in, float* __restrict__ out, float* cache_out,
+                                  int groups, int kernel, int seq, int cache_len) {
+    const int g = blockIdx.x * blockDim.x + threadIdx.x;
+    if (g >= groups) return;
+    const long long ld = (long long)((groups + 3) / 4) * 4;
+    float w[kConvMaxKernel];
+#pragma unroll
+    for (int k = 0; k < kConvMaxKernel; ++k)
+        w[k] = k < kernel ? weight[((long long)(g >> 2) * kernel + k) * 4 + (g & 3)] : 0.0f;
+    for (int t = 0; t < seq; ++t) {
+        float sum = 0.0f;
+#pragma unroll
+        for (int k = 0; k < kConvMaxKernel; ++k) {
+            if (k < kernel) {
+                const int hi = cache_len - kernel + t + 1 + k;
+                const float x = hi < 0 ? 0.0f
+                              : (hi < cache_len ? cache_in[hi * ld + g] : mixed[(hi - cache_len) * ld + g]);
+                sum = fmaf(x, w[k], sum);
+            }
+        }
+        out[t * ld + g] = sum / (1.0f + expf(-sum));
+    }
+    for (int i = 0; i < cache_len; ++i) {
+        const int src = seq + i;
+        cache_out[i * ld + g] = src < cache_len ? cache_in[src * ld + g] : mixed[(src - cache_len) * ld + g];
+    }
+}
+
+struct GdrArgs {
+    const float* a_log;     // [heads]
+    const float* dt_bias;   // [heads]
+    const float* b;         // [seq][heads]
+    const float* a;         // [seq][heads]
+    const float* q;         // Pack4 CDHW [w=kdim, h=heads, c=seq]
+    const float* k;         // Pack4 CDHW [w=kdim, h=heads, c=seq]
+    const float* v;         // Pack4 CDHW [w=vdim, h=heads, c=seq]
+    const float* state_in;  // [heads][kdim][vdim4]
+    float* out;             // Pack4 CDHW [w=vdim, h=heads, c=seq]
+    float* state_out;       // [heads][kdim][vdim4]
+    int heads, kdim, vdim, first, count;
+    float eps;
+};
+
+constexpr int kGdrThreads = 128;   // 32 row groups x 4 column quads
+constexpr int kGdrCols = 16;       // value columns per CTA
+
+// AexisGatedDeltaRulePack4 (COMMON:680-753), for tokens first..first+count-1.
+// Per token and head, with q, k the raw vectors:
+//   decay = exp(-exp(a_log) * softplus(a + dt_bias)),  beta = sigmoid(b)
+//   S    <- S * decay
+//   mem   = (k / |k|) . S                  |x| = sqrt(sum x^2 + eps)
+//   delta = (v - mem) * beta
+//   S    <- S + (k / |k|) outer delta
+//   out   = (q / |q|) . S / sqrt(kdim)
+// Thread (r, qd) holds rows r, r+32, ... (RPT rows) of the CTA's columns
+// 4qd..4qd+3: every dot product over rows is a partial sum per thread,
+// three xor shuffles over the warp's 8 row groups and one pass over four
+// warps' partials in shared memory. The two norms ride in the same reduction
+// as `mem`. Columns past vdim (up to the Pack4 width vdim4) carry v = 0, as in
+// the reference, which writes whole texels.
+template <int RPT>
+__global__ void __launch_bounds__(kGdrThreads) gdr_kernel(GdrArgs p) {
+    const int tid = threadIdx.x;
+    const int qd = tid & 3;
+    const int r = tid >> 2;
+    const int warp = tid >> 5, lane = tid & 31;
+    const int h = blockIdx.y;
+    const int heads = p.heads, kdim = p.kdim, vdim = p.vdim;
+    const int vdim4 = (vdim + 3) & ~3;
+    const int c0 = blockIdx.x * kGdrCols + qd * 4;
+    const bool col_ok = c0 < vdim4;
+
+    __shared__ float red_a[4][4][6];
+    __shared__ float red_b[4][4][4];
+
+    float S[RPT][4];
+#pragma unroll
+    for (int i = 0; i < RPT; ++i) {
+        const int j = r + 32 * i;
+        float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (j < kdim && col_ok)
+            s = *reinterpret_cast<const float4*>(p.state_in + ((long long)h * kdim + j) * vdim4 + c0);
+        S[i][0] = s.x; S[i][1] = s.y; S[i][2] = s.z; S[i][3] = s.w;
+    }
+    const float ealog = expf(p.a_log[h]);
+    const float dt = p.dt_bias[h];
+    const float inv_sqrt_k = rsqrtf((float)kdim);
+
+    for (int t = p.first; t < p.first + p.count; ++t) {
+        const int lane_t = t & 3;
+        const long long qk_texel = ((long long)(t >> 2) * heads + h) * kdim;
+        float qv[RPT], kv[RPT];
+#pragma unroll
+        for (int i = 0; i < RPT; ++i) {
+            const int j = r + 32 * i;
+            qv[i] = j < kdim ? p.q[(qk_texel + j) * 4 + lane_t] : 0.f;
+            kv[i] = j < kdim ? p.k[(qk_texel + j) * 4 + lane_t] : 0.f;
+        }
+        const float bb = p.b[(long long)t * heads + h];
+        const float x = p.a[(long long)t * heads + h] + dt;
+        const float beta = 1.0f / (1.0f + expf(-bb));
+        const float decay = expf(-ealog * (fmaxf(x, 0.0f) + logf(1.0f + expf(-fabsf(x)))));
+
+        float part[6] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int i = 0; i < RPT; ++i) {
+            part[0] = fmaf(qv[i], qv[i], part[0]);
+            part[1] = fmaf(kv[i], kv[i], part[1]);
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                S[i][c] *= decay;
+                part[2 + c] = fmaf(kv[i], S[i][c], part[2 + c]);
+            }
+        }
+#pragma unroll
+        for (int m = 4; m < 32; m <<= 1)
+#pragma unroll
+            for (int e = 0; e < 6; ++e) part[e] += __shfl_xor_sync(0xffffffffu, part[e], m);
+        if (lane < 4) {
+#pragma unroll
+            for (int e = 0; e < 6; ++e) red_a[warp][qd][e] = part[e];
+        }
+        __syncthreads();
+        float tot[6];
+#pragma unroll
+        for (int e = 0; e < 6; ++e) tot[e] = (red_a[0][qd][e] + red_a[1][qd][e]) + (red_a[2][qd][e] + red_a[3][qd][e]);
+        const float qs = rsqrtf(tot[0] + p.eps);
+        const float ks = rsqrtf(tot[1] + p.eps);
+
+        const long long v_texel = ((long long)(t >> 2) * heads + h) * vdim;
+        float delta[4];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            const int col = c0 + c;
+            const float val = col < vdim ? p.v[(v_texel + col) * 4 + lane_t] : 0.f;
+            delta[c] = (val - tot[2 + c] * ks) * beta;
+        }
+        float o[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int i = 0; i < RPT; ++i) {
+            const float kn = kv[i] * ks;
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                S[i][c] = fmaf(kn, delta[c], S[i][c]);
+                o[c] = fmaf(qv[i], S[i][c], o[c]);
+            }
+        }
+#pragma unroll
+        for (int m = 4; m < 32; m <<= 1)
+#pragma unroll
+            for (int c = 0; c < 4; ++c) o[c] += __shfl_xor_sync(0xffffffffu, o[c], m);
+        if (lane < 4) {
+#pragma unroll
+            for (int c = 0; c < 4; ++c) red_b[warp][qd][c] = o[c];
+        }
+        __syncthreads();
+        if (r == 0) {
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                const int col = c0 + c;
+                if (col < vdim) {
+                    const float sum = (red_b[0][qd][c] + red_b[1][qd][c]) + (red_b[2][qd][c] + red_b[3][qd][c]);
+                    p.out[(v_texel + col) * 4 + lane_t] = sum * qs * inv_sqrt_k;
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < RPT; ++i) {
+        const int j = r + 32 * i;
+        if (j < kdim && col_ok)
+            *reinterpret_cast<float4*>(p.state_out + ((long long)h * kdim + j) * vdim4 + c0) =
+                make_float4(S[i][0], S[i][1], S[i][2], S[i][3]);
+    }
+}
+
+}  // namespace
+
+cudaError_t launch_short_conv(const float* weight, const float* mixed, const float* cache_in, float* out,
+                              float* cache_out, int groups, int kernel, int seq, int cache_len, cudaStream_t s) {
+    if (kernel > kConvMaxKernel) return cudaErrorInvalidValue;
+    const int threads = 128;
+    short_conv_kernel<<<(groups + threads - 1) / threads, threads, 0, s>>>(weight, mixed, cache_in, out, cache_out,
+                                                                          groups, kernel, seq, cache_len);
+    return cudaGetLastError();
+}
+
+int gdr_max_kdim() { return 256; }
+
+cudaError_t launch_gated_delta_rule(const float* a_log, const float* dt_bias, const float* b, const float* a,
+                                    const float* q, const float* k, const float* v, const float* state_in,
+                                    float* out, float* state_out, int heads, int kdim, int vdim, int first,
+                                    int count, float eps, cudaStream_t s) {
+    GdrArgs p{a_log, dt_bias, b, a, q, k, v, state_in, out, state_out, heads, kdim, vdim, first, count, eps};
+    const int vdim4 = (vdim + 3) & ~3;
+    dim3 grid((vdim4 + kGdrCols - 1) / kGdrCols, heads);
+    if (kdim <= 32) gdr_kernel<1><<<grid, kGdrThreads, 0, s>>>(p);
+    else if (kdim <= 64) gdr_kernel<2><<<grid, kGdrThreads, 0, s>>>(p);
+    else if (kdim <= 128) gdr_kernel<4><<<grid, kGdrThreads, 0, s>>>(p);
+    else if (kdim <= 256) gdr_kernel<8><<<grid, kGdrThreads, 0, s>>>(p);
+    else return cudaErrorInvalidValue;
+    return cudaGetLastError();
+}

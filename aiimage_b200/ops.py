@@ -271,3 +271,50 @@ class AexisOps:
 
     def swiglu(self, gate, up, count, y):
         self._call(lib().aexis_cuda_swiglu, _ptr(gate), _ptr(up), count, _ptr(y))
+
+    # -- linear-attention blocks (Qwen3.5 ShortConv + GatedDeltaRule) ---------
+    def short_conv_pack4(self, weight, mixed, cache_in, output, cache_out, groups, kernel_size, sequence_length,
+                         cache_length):
+        """AexisOps.ShortConvPack4 (:12593-12618). weight: Pack4 CDHW [kernel, 1, groups]; mixed/output
+        [seq, ceil(groups/4)*4]; caches [cache_length, ceil(groups/4)*4]; cache_out may be cache_in."""
+        self._call(lib().aexis_cuda_short_conv, _ptr(weight), _ptr(mixed), _ptr(cache_in), _ptr(output),
+                   _ptr(cache_out), groups, kernel_size, sequence_length, cache_length)
+
+    def gated_delta_rule_pack4(self, a_log, dt_bias, b, a, query, key, value, state_in, output, state_out, heads,
+                               key_dim, value_dim, sequence_length, token_index=0, token_count=None,
+                               epsilon=1e-6):
+        """AexisOps.GatedDeltaRulePack4 (:12620-12657) for tokens token_index .. token_index+token_count-1
+        (default: the rest of the sequence, the whole per-token loop of AexisGatedDeltaRuleLayer in one
+        call). q/k/v/output: Pack4 CDHW [dim, heads, seq]; state: [heads, key_dim, ceil(value_dim/4)*4]."""
+        if token_count is None:
+            token_count = sequence_length - token_index
+        self._call(lib().aexis_cuda_gated_delta_rule, _ptr(a_log), _ptr(dt_bias), _ptr(b), _ptr(a), _ptr(query),
+                   _ptr(key), _ptr(value), _ptr(state_in), _ptr(output), _ptr(state_out), heads, key_dim,
+                   value_dim, sequence_length, token_index, token_count, float(epsilon))
+
+
+def pack4_cdhw(x: np.ndarray) -> np.ndarray:
+    """Logical [c, h, w] (ncnn d3: c=channels or sequence, h, w) -> flat Pack4 CDHW storage, element (x, y, c)
+    at ((c/4*H + y)*W + x)*4 + (c & 3); lanes past c are zero."""
+    x = np.asarray(x, dtype=np.float32)
+    c, h, w = x.shape
+    c4 = (c + 3) // 4 * 4
+    pad = np.zeros((c4, h, w), dtype=np.float32)
+    pad[:c] = x
+    return np.ascontiguousarray(pad.reshape(c4 // 4, 4, h, w).transpose(0, 2, 3, 1)).reshape(-1)
+
+
+def unpack4_cdhw(flat: np.ndarray, c: int, h: int, w: int) -> np.ndarray:
+    """Inverse of pack4_cdhw: flat Pack4 CDHW storage -> logical [c, h, w]."""
+    c4 = (c + 3) // 4 * 4
+    x = np.asarray(flat, dtype=np.float32).reshape(c4 // 4, h, w, 4).transpose(0, 3, 1, 2).reshape(c4, h, w)
+    return np.ascontiguousarray(x[:c])
+
+
+def pack4_rows(x: np.ndarray) -> np.ndarray:
+    """Logical [rows, width] -> Pack4 linear [rows, ceil(width/4)*4] (zero padded)."""
+    x = np.asarray(x, dtype=np.float32)
+    rows, width = x.shape
+    out = np.zeros((rows, (width + 3) // 4 * 4), dtype=np.float32)
+    out[:, :width] = x
+    return out

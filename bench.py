@@ -339,6 +339,13 @@ def run_gpu(args):
         except Exception as e:
             config5 = {"error": f"{type(e).__name__}: {e}"}
 
+    linear_attn = None
+    if not args.skip_linear_attention:
+        try:
+            linear_attn = bench_linear_attention(ops, peak)
+        except Exception as e:
+            linear_attn = {"error": f"{type(e).__name__}: {e}"}
+
     cpu = None
     if rank == 0 and world == 1 and not args.skip_cpu:
         cpu = cpu_baseline(args.cpu_seconds)
@@ -371,6 +378,7 @@ def run_gpu(args):
             "decoder": decoder,
             "config4": config4,
             "config5": config5,
+            "linear_attention": linear_attn,
             "cpu_baseline": cpu,
             "e2e": {"value": round(e2e_steps * STEP_BYTES * world / e2e_s / 1e9, 2), "unit": "GB/s",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
@@ -531,6 +539,88 @@ def bench_config4(ops, peak, world: int, rank: int, steps: int = 128, total_seqs
             "timing": "device (CUDA events around each batch's generate), max over ranks"}
 
 
+def bench_linear_attention(ops, peak, prefill: int = 512):
+    """Linear-attention layers of Qwen3.5-0.8B (18 of its 24 blocks), batch-1
+    decode: the Gated Delta Rule over 16 heads with key/value dims 128 and the
+    causal ShortConv over 6144 channels (kernel 4). One decode launch of the
+    GDR reads and writes the fp32 state once (2 x 1 MiB); the states rotate
+    over copies larger than L2 (updated in place), each launch timed inside a
+    graph by CUDA events. Also one 512-token prefill call (state kept on chip)."""
+    import torch
+    heads, kd, vd = 16, 128, 128
+    rng = np.random.default_rng(17)
+    state_bytes = heads * kd * vd * 4
+    copies = max(2, -(-2 * L2_BYTES // state_bytes))
+    states = [torch.from_numpy(rng.normal(0, 0.05, heads * kd * vd).astype(np.float32)).cuda() for _ in range(copies)]
+
+    def vec(n, mu=0.0, sd=0.5):
+        return torch.from_numpy(rng.normal(mu, sd, n).astype(np.float32)).cuda()
+
+    a_log, dt = vec(heads, -1.0, 0.2), vec(heads, 0.0, 0.2)
+    b, a = vec(prefill * heads, 0, 0.4), vec(prefill * heads, 0, 0.4)
+    q, k, v = vec(prefill * heads * kd), vec(prefill * heads * kd), vec(prefill * heads * vd)
+    out = torch.zeros(prefill * heads * vd, dtype=torch.float32, device="cuda")
+
+    def gdr(c, first=0, count=1):
+        ops.gated_delta_rule_pack4(a_log, dt, b, a, q, k, v, states[c], out, states[c], heads, kd, vd, prefill,
+                                   token_index=first, token_count=count)
+
+    groups, kernel = 6144, 4
+    ld = groups
+    conv_w = vec(groups * kernel, 0, 0.3)
+    conv_x = vec(ld)
+    conv_cache = vec(kernel * ld)
+    conv_out = torch.zeros(ld, dtype=torch.float32, device="cuda")
+
+    def conv(c):
+        ops.short_conv_pack4(conv_w, conv_x, conv_cache, conv_out, conv_cache, groups, kernel, 1, kernel)
+
+    def timed(fn, launches):
+        for c in range(min(launches, 3)):
+            fn(c)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        st = torch.cuda.Stream()
+        st.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(st):
+            with torch.cuda.graph(g, stream=st):
+                for c in range(launches):
+                    fn(c)
+        torch.cuda.current_stream().wait_stream(st)
+        g.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(3):
+            g.replay()
+        e1.record()
+        e1.synchronize()
+        return e0.elapsed_time(e1) / 1e3 / (3 * launches)
+
+    gdr_s = timed(lambda c: gdr(c % copies), copies)
+    gdr_bytes = 2 * state_bytes + 4 * heads * (2 * kd + 2 * vd) + 4 * 2 * heads
+    conv_s = timed(conv, 64)
+    conv_bytes = 4 * (groups * kernel + 2 * kernel * groups + 2 * groups)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    gdr(0, 0, prefill)
+    e0.record()
+    for c in range(1, 4):
+        gdr(c, 0, prefill)
+    e1.record()
+    e1.synchronize()
+    pre_s = e0.elapsed_time(e1) / 1e3 / 3
+    return {"workload": "qwen35_08b_linear_attention_decode_b1 (GDR 16 heads x 128 x 128; ShortConv 6144 ch, k4)",
+            "gdr_decode_us": round(gdr_s * 1e6, 3), "gdr_decode_bytes": gdr_bytes,
+            "gdr_decode_GB/s": round(gdr_bytes / gdr_s / 1e9, 1),
+            "gdr_decode_frac": round(gdr_bytes / gdr_s / 1e9 / peak, 3),
+            "gdr_state_copies": copies,
+            "short_conv_decode_us": round(conv_s * 1e6, 3), "short_conv_bytes": conv_bytes,
+            "gdr_prefill_tokens": prefill, "gdr_prefill_us": round(pre_s * 1e6, 1),
+            "gdr_prefill_tokens_per_s": round(prefill / pre_s, 1),
+            "timing": "CUDA events around graph replays (decode), back-to-back calls (prefill)"}
+
+
 def bench_config5(ops, world: int, rank: int, reps: int = 10):
     """lm_head 151936 x 1024 Q8 per row, batch 256 fp16
     hidden states, greedy argmax + top-50 per row. G > 1: vocab shards with
@@ -625,7 +715,8 @@ def run_only(args):
                       over copies larger than L2, no graphs
     --only decoder    the config-3 decoder with --prompt-len / --new-tokens
     --only tcgemm     the config-5 lm_head GEMM alone (M=256, tensor cores)
-    --only config4    one config-4 batch (32 sequences, --new-tokens steps)"""
+    --only config4    one config-4 batch (32 sequences, --new-tokens steps)
+    --only linear_attention  the Qwen3.5 GatedDeltaRule / ShortConv decode kernels"""
     import torch
     torch.cuda.set_device(0)
     from aiimage_b200.ops import AexisOps
@@ -633,6 +724,8 @@ def run_only(args):
     peak, _ = measured_peak()
     if args.only == "decoder":
         out = bench_decoder(ops, peak, args.prompt_len, args.new_tokens)
+    elif args.only == "linear_attention":
+        out = bench_linear_attention(ops, peak)
     elif args.only == "topk":
         m, vocab, k = 256, 151936, 50
         g = torch.Generator(device="cuda").manual_seed(5)
@@ -737,8 +830,10 @@ def main():
     ap.add_argument("--skip-cpu", action="store_true", help="omit the CPU oracle baseline")
     ap.add_argument("--skip-config5", action="store_true", help="omit the config-5 lm_head measurement")
     ap.add_argument("--skip-config4", action="store_true", help="omit the config-4 batched decoder measurement")
+    ap.add_argument("--skip-linear-attention", action="store_true",
+                    help="omit the GatedDeltaRule / ShortConv decode measurement")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
-    ap.add_argument("--only", choices=["dominant", "decoder", "tcgemm", "config4", "topk"], help="profiling mode (see run_only)")
+    ap.add_argument("--only", choices=["dominant", "decoder", "tcgemm", "config4", "topk", "linear_attention"], help="profiling mode (see run_only)")
     ap.add_argument("--prompt-len", type=int, default=512)
     ap.add_argument("--new-tokens", type=int, default=64)
     args = ap.parse_args()

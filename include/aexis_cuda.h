@@ -273,6 +273,49 @@ int aexis_cuda_swish(aexis_ctx* ctx, const float* x, int count, float* y);
  * (HLSL Pack4Matmul:91-94,118-128): y = silu(gate) * up. */
 int aexis_cuda_swiglu(aexis_ctx* ctx, const float* gate, const float* up, int count, float* y);
 
+/* --------------------------------------------- linear-attention decode layers */
+/* Ops.ShortConvPack4(weight, mixed, cacheIn, output, cacheOut, groups,
+ * kernelSize, sequenceLength, cacheLength) (Ops:12593-12618; COMMON
+ * AexisShortConvPack4:623-678; layer AexisShortConvLayer.cs:30-60): causal
+ * depthwise Conv1D + SiLU with a streaming cache,
+ *   out[t][g]    = silu(sum_j hist(cache_len - kernel + t + 1 + j) * w(g, j))
+ *   hist(i)      = i < 0 ? 0 : i < cache_len ? cache_in[i][g] : mixed[i - cache_len][g]
+ *   cache_out[i] = hist(seq_len + i)   (the tail of [cache_in; mixed]).
+ * weight: device Pack4 CDHW [w=kernel, h=1, c=groups] (element (j, g) at
+ * ((g/4)*kernel + j)*4 + (g&3)); mixed/out: device [seq_len][ld];
+ * cache_in/cache_out: device [cache_len][ld]; ld = ceil(groups/4)*4.
+ * cache_out may be cache_in (updated in place); out may alias no input.
+ * Errors: NULL -> E_NULL; groups, kernel_size, seq_len <= 0 or cache_len <
+ * kernel_size - 1 -> E_RANGE (as the reference); kernel_size > 16 ->
+ * E_UNSUPPORTED; aliasing other than the cache -> E_SHAPE. */
+int aexis_cuda_short_conv(aexis_ctx* ctx, const float* weight, const float* mixed, const float* cache_in,
+                          float* out, float* cache_out, int groups, int kernel_size, int seq_len,
+                          int cache_len);
+/* Ops.GatedDeltaRulePack4(aLog, dtBias, b, a, query, key, value, stateIn,
+ * output, stateOut, heads, keyDim, valueDim, sequenceLength, tokenIndex,
+ * epsilon) (Ops:12620-12657; COMMON AexisGatedDeltaRulePack4:680-753) for the
+ * tokens first_token .. first_token + token_count - 1 in one call: the
+ * reference's per-token loop of AexisGatedDeltaRuleLayer (AexisGatedDelta-
+ * RuleLayer.cs:71-78, ping-pong state) is token_count = seq_len. Per token t
+ * and head h:
+ *   decay = exp(-exp(a_log[h]) * softplus(a[t][h] + dt_bias[h]))
+ *   beta  = sigmoid(b[t][h]);  k^ = k / sqrt(|k|^2 + eps);  q^ likewise
+ *   S     = S * decay;  delta = (v - k^ . S) * beta;  S += k^ (x) delta
+ *   out   = (q^ . S) / sqrt(key_dim)
+ * a_log, dt_bias: device fp32 [heads]; a, b: device fp32 [seq_len][heads];
+ * q, k: device Pack4 CDHW [w=key_dim, h=heads, c=seq_len] (element (j, h, t)
+ * at ((t/4*heads + h)*key_dim + j)*4 + (t&3)); v, out: CDHW [w=value_dim,
+ * h=heads, c=seq_len] (only the lanes of the processed tokens are written);
+ * state_in/state_out: device fp32 [heads][key_dim][ceil(value_dim/4)*4],
+ * 16-byte aligned; state_out may be state_in (updated in place).
+ * Errors: NULL -> E_NULL; sizes <= 0 or tokens outside [0, seq_len) ->
+ * E_RANGE; key_dim > 256 -> E_UNSUPPORTED; misaligned state or out aliasing
+ * an input -> E_SHAPE. */
+int aexis_cuda_gated_delta_rule(aexis_ctx* ctx, const float* a_log, const float* dt_bias, const float* b,
+                                const float* a, const float* q, const float* k, const float* v,
+                                const float* state_in, float* out, float* state_out, int heads, int key_dim,
+                                int value_dim, int seq_len, int first_token, int token_count, float eps);
+
 /* ------------------------------------------------------------------ decoder */
 
 /* Shape of the full-attention decoder stack driven by Qwen35DecoderSession

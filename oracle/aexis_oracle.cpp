@@ -702,3 +702,100 @@ ORACLE_API int oracle_num_threads(void) {
     return 1;
 #endif
 }
+
+// ---------------------------------------------------------------------------
+// Linear-attention decode layers of Qwen3.5 (COMMON = Packages/com.aexis/
+// Runtime/Resources/Aexis/AexisCommon.compute). Pinned against the
+// reference's own fp32 NumPy gold operators (Tools/Qwen35NcnnBaseline/
+// reference_ops.py:36-152) through tests/golden/recurrent_ops.npz.
+// ---------------------------------------------------------------------------
+
+// AexisShortConvPack4 (COMMON:623-678). weight: Pack4 CDHW [w=kernel, h=1,
+// c=groups] (RecurrentLoadShortConvWeight, COMMON:586-592); mixed/out
+// [seq][ld], cache_in/cache_out [cache_len][ld], ld = ceil(groups/4)*4
+// (RecurrentLoad2, COMMON:574-578). The cache rows are the tail of
+// [cache_in; mixed] (COMMON:630-648); each output sums the kernel window in
+// order, then SiLU = sum / (1 + exp(-sum)) (COMMON:657-674).
+ORACLE_API void oracle_short_conv(const float* weight, const float* mixed, const float* cache_in, float* out,
+                                  float* cache_out, int groups, int kernel, int seq, int cache_len) {
+    const int64_t ld = (int64_t)((groups + 3) / 4) * 4;
+    auto hist = [&](int i, int g) -> float {
+        if (i < 0) return 0.0f;
+        return i < cache_len ? cache_in[i * ld + g] : mixed[(i - cache_len) * ld + g];
+    };
+    for (int t = 0; t < seq; ++t)
+        for (int g = 0; g < groups; ++g) {
+            float sum = 0.0f;
+            for (int k = 0; k < kernel; ++k) {
+                float w = weight[((int64_t)(g / 4) * kernel + k) * 4 + (g & 3)];
+                sum = sum + hist(cache_len - kernel + t + 1 + k, g) * w;
+            }
+            out[t * ld + g] = sum / (1.0f + std::exp(-sum));
+        }
+    std::vector<float> tail((size_t)std::max(cache_len, 0) * groups);
+    for (int i = 0; i < cache_len; ++i)
+        for (int g = 0; g < groups; ++g) tail[(size_t)i * groups + g] = hist(seq + i, g);
+    for (int i = 0; i < cache_len; ++i)
+        for (int g = 0; g < groups; ++g) cache_out[i * ld + g] = tail[(size_t)i * groups + g];
+}
+
+// AexisGatedDeltaRulePack4 (COMMON:680-753), one dispatch per token as
+// AexisGatedDeltaRuleLayer issues them (AexisGatedDeltaRuleLayer.cs:71-78),
+// for tokens first..first+count-1. q/k/v/out are Pack4 CDHW with the sequence
+// packed by 4 (RecurrentLoadGdrTensor, COMMON:600-604); a/b are [seq][heads]
+// and a_log/dt_bias [heads] (RecurrentLoadLinearScalar, COMMON:594-598); the
+// state is [heads][kdim][vdim4] (texel x = column / 4, y = key row, slice =
+// head). Per token: norms by rsqrt(sum + eps) (COMMON:689-700), beta and
+// decay (:701-706), memory over the decayed state (:708-714), delta (:716-
+// 722), state update and projection (:723-731), scaled by rsqrt(kdim)
+// (:732). Columns past vdim read v = 0 (the HLSL writes whole texels).
+ORACLE_API void oracle_gated_delta_rule(const float* a_log, const float* dt_bias, const float* b, const float* a,
+                                        const float* q, const float* k, const float* v, const float* state_in,
+                                        float* out, float* state_out, int heads, int kdim, int vdim, int first,
+                                        int count, float eps) {
+    const int vdim4 = (vdim + 3) / 4 * 4;
+    const size_t n_state = (size_t)heads * kdim * vdim4;
+    std::vector<float> cur(state_in, state_in + n_state), next(n_state);
+    auto gdr = [&](const float* t_, int64_t tok, int h, int j, int W) -> float {
+        return t_[(((tok / 4) * heads + h) * (int64_t)W + j) * 4 + (tok & 3)];
+    };
+    for (int tok = first; tok < first + count; ++tok) {
+        for (int h = 0; h < heads; ++h) {
+            float qn2 = 0.0f, kn2 = 0.0f;
+            for (int j = 0; j < kdim; ++j) {
+                float qj = gdr(q, tok, h, j, kdim), kj = gdr(k, tok, h, j, kdim);
+                qn2 = qn2 + qj * qj;
+                kn2 = kn2 + kj * kj;
+            }
+            const float q_scale = 1.0f / std::sqrt(qn2 + eps);
+            const float k_scale = 1.0f / std::sqrt(kn2 + eps);
+            const float bb = b[(int64_t)tok * heads + h], aa = a[(int64_t)tok * heads + h];
+            const float alog = a_log[h], dt = dt_bias[h];
+            const float beta = 1.0f / (1.0f + std::exp(-bb));
+            const float x = aa + dt;
+            const float decay = std::exp(-std::exp(alog) * (std::max(x, 0.0f) + std::log(1.0f + std::exp(-std::fabs(x)))));
+            for (int c = 0; c < vdim4; ++c) {
+                float memory = 0.0f;
+                for (int j = 0; j < kdim; ++j) {
+                    float kj = gdr(k, tok, h, j, kdim) * k_scale;
+                    memory = memory + kj * (cur[((size_t)h * kdim + j) * vdim4 + c] * decay);
+                }
+                const float val = c < vdim ? gdr(v, tok, h, c, vdim) : 0.0f;
+                const float delta = (val - memory) * beta;
+                float projected = 0.0f;
+                for (int j = 0; j < kdim; ++j) {
+                    float kj = gdr(k, tok, h, j, kdim) * k_scale;
+                    float qj = gdr(q, tok, h, j, kdim) * q_scale;
+                    size_t si = ((size_t)h * kdim + j) * vdim4 + c;
+                    float updated = cur[si] * decay + kj * delta;
+                    next[si] = updated;
+                    projected = projected + qj * updated;
+                }
+                projected = projected * (1.0f / std::sqrt((float)kdim));
+                if (c < vdim) out[(((int64_t)(tok / 4) * heads + h) * vdim + c) * 4 + (tok & 3)] = projected;
+            }
+        }
+        cur.swap(next);
+    }
+    std::memcpy(state_out, cur.data(), sizeof(float) * n_state);
+}

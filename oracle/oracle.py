@@ -55,6 +55,8 @@ def lib():
         L.oracle_embed.argtypes = [I32P, C.c_int, C.c_int, vp, vp, C.c_int, vp, C.c_int, C.c_int, vp, F32P]
         L.oracle_swish.argtypes = [F32P, C.c_int, F32P]
         L.oracle_swiglu.argtypes = [F32P, F32P, C.c_int, F32P]
+        L.oracle_short_conv.argtypes = [F32P, F32P, F32P, F32P, F32P, C.c_int, C.c_int, C.c_int, C.c_int]
+        L.oracle_gated_delta_rule.argtypes = [F32P] * 10 + [C.c_int] * 5 + [C.c_float]
         L.oracle_round_f16.argtypes = [C.c_float]
         L.oracle_round_f16.restype = C.c_float
         L.oracle_f32_to_f16.argtypes = [F32P, C.c_int64, U16P]
@@ -211,6 +213,32 @@ def swiglu(gate, up) -> np.ndarray:
     y = np.empty_like(g)
     lib().oracle_swiglu(g, _f32(up).reshape(-1), g.size, y)
     return y
+
+
+def short_conv(weight, mixed, cache_in, groups: int, kernel: int, seq: int, cache_len: int):
+    """AexisShortConvPack4 on flat storage (see oracle_short_conv): weight Pack4 CDHW [kernel, 1, groups],
+    mixed [seq, ld], cache_in [cache_len, ld], ld = ceil(groups/4)*4. Returns (out, cache_out)."""
+    ld = (groups + 3) // 4 * 4
+    out = np.zeros(seq * ld, dtype=np.float32)
+    cache_out = np.zeros(max(cache_len, 0) * ld, dtype=np.float32)
+    lib().oracle_short_conv(_f32(weight).ravel(), _f32(mixed).ravel(), _f32(cache_in).ravel(), out, cache_out,
+                            groups, kernel, seq, cache_len)
+    return out, cache_out
+
+
+def gated_delta_rule(a_log, dt_bias, b, a, q, k, v, state_in, heads: int, kdim: int, vdim: int, seq: int,
+                     first: int = 0, count: int | None = None, eps: float = 1e-6, out=None):
+    """AexisGatedDeltaRulePack4 per token on flat storage (see oracle_gated_delta_rule): q/k/v Pack4 CDHW
+    [dim, heads, seq], state [heads, kdim, ceil(vdim/4)*4]. Returns (out, state_out); `out` (flat CDHW
+    [vdim, heads, seq]) is updated in place when given, as the kernel writes only processed tokens' lanes."""
+    count = seq - first if count is None else count
+    s4 = (seq + 3) // 4 * 4
+    out = np.zeros(s4 * heads * vdim, dtype=np.float32) if out is None else _f32(out).ravel().copy()
+    state_out = np.zeros(heads * kdim * ((vdim + 3) // 4 * 4), dtype=np.float32)
+    lib().oracle_gated_delta_rule(_f32(a_log).ravel(), _f32(dt_bias).ravel(), _f32(b).ravel(), _f32(a).ravel(),
+                                  _f32(q).ravel(), _f32(k).ravel(), _f32(v).ravel(), _f32(state_in).ravel(), out,
+                                  state_out, heads, kdim, vdim, first, count, eps)
+    return out, state_out
 
 
 def round_f16(x) -> np.ndarray:
