@@ -161,6 +161,7 @@ AEXIS_API int aexis_cuda_destroy(aexis_ctx* ctx) {
     cudaSetDevice(ctx->device);
     if (ctx->own_stream) cudaStreamSynchronize(ctx->own_stream);
     if (ctx->scratch) cudaFree(ctx->scratch);
+    if (ctx->act_q) cudaFree(ctx->act_q);
     if (ctx->status) cudaFree(ctx->status);
     if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
     delete ctx;
@@ -342,6 +343,34 @@ static int gemm_common(aexis_ctx* ctx, const void* a, int a_dtype, int lda, int 
         return aexis_fail(ctx, AEXIS_E_UNSUPPORTED, "dtype a=%d y=%d", a_dtype, y_dtype);
     int rc = bind(ctx);
     if (rc) return rc;
+    if (ctx->act_quant) {
+        // W8A8: the GEMM reads the integer codes q - zp (fp16, exact) instead of
+        // the activations and the scale moves into the epilogue:
+        //   alpha*(beta*bias + sum (q-zp)*s*W) = (alpha*s)*((beta/s)*bias + sum (q-zp)*W)
+        //   beta*bias + alpha*sum (q-zp)*s*W   = beta*bias + (alpha*s)*sum (q-zp)*W
+        const size_t need = (size_t)m * k * sizeof(__half);
+        if (need > ctx->act_q_bytes) {
+            if (ctx->act_q) {
+                cudaStreamSynchronize(ctx->stream);
+                cudaFree(ctx->act_q);
+                ctx->act_q = nullptr;
+                ctx->act_q_bytes = 0;
+            }
+            const size_t sz = std::max<size_t>(need, 1 << 16);
+            rc = aexis_cuda_check(ctx, cudaMalloc(&ctx->act_q, sz), "activation code buffer");
+            if (rc) return rc;
+            ctx->act_q_bytes = sz;
+        }
+        rc = aexis_cuda_check(ctx, launch_act_quant_i8(a, a_dtype, lda, m, k, ctx->act_scale, ctx->act_zero_point,
+                                                       ctx->act_unsigned, (__half*)ctx->act_q, ctx->stream),
+                              "activation quantisation launch");
+        if (rc) return rc;
+        a = ctx->act_q;
+        a_dtype = AEXIS_F16;
+        lda = k;
+        if (epi == EPI_STORE) beta = beta / ctx->act_scale;
+        alpha = alpha * ctx->act_scale;
+    }
     // Batched Q8: one pass over the weights on the tensor cores.
     if (m >= kTcMinRows && gemm_tc_supported(w, m, a_dtype)) {
         aexis_weights* wm = const_cast<aexis_weights*>(w);
@@ -378,6 +407,27 @@ static int gemm_common(aexis_ctx* ctx, const void* a, int a_dtype, int lda, int 
         rc = aexis_cuda_check(ctx, launch_gemv(g, ctx->sm_count, ctx->stream), "gemv launch");
         if (rc) return rc;
     }
+    return AEXIS_OK;
+}
+
+AEXIS_API int aexis_cuda_set_int8_activations(aexis_ctx* ctx, int enable, float scale, int zero_point,
+                                             int is_unsigned) {
+    if (!ctx) return AEXIS_E_NULL;
+    if (!enable) {
+        ctx->act_quant = 0;
+        ctx->act_scale = 1.0f;
+        ctx->act_zero_point = 0;
+        ctx->act_unsigned = 0;
+        return AEXIS_OK;
+    }
+    if (!(scale > 0.0f) || !std::isfinite(scale))
+        return aexis_fail(ctx, AEXIS_E_RANGE, "activation scale %g must be positive and finite", (double)scale);
+    if (zero_point < -1024 || zero_point > 1024)
+        return aexis_fail(ctx, AEXIS_E_RANGE, "activation zero point %d outside [-1024, 1024]", zero_point);
+    ctx->act_quant = 1;
+    ctx->act_scale = scale;
+    ctx->act_zero_point = zero_point;
+    ctx->act_unsigned = is_unsigned ? 1 : 0;
     return AEXIS_OK;
 }
 

@@ -42,6 +42,16 @@ struct aexis_ctx {
     // Device status word: kernels whose bounded waits run out record
     // AEXIS_E_TIMEOUT here; aexis_cuda_sync reports and clears it.
     int* status = nullptr;
+    // W8A8 activation fake-quantisation (Ops.SetInt8ActivationQuantization):
+    // when enabled, aexis_cuda_gemm* first writes the activations' integer
+    // codes (q - zero_point) as fp16 into act_q and multiplies by act_scale in
+    // the epilogue.
+    int act_quant = 0;
+    float act_scale = 1.0f;
+    int act_zero_point = 0;
+    int act_unsigned = 0;
+    void* act_q = nullptr;
+    size_t act_q_bytes = 0;
 };
 
 // Records `msg` on the context and returns `code`.
@@ -180,6 +190,9 @@ cudaError_t launch_embed(const int32_t* words, int count, const aexis_weights* t
                          const float* bias, float* out, cudaStream_t s);
 cudaError_t launch_swish(const float* x, int count, float* y, cudaStream_t s);
 cudaError_t launch_swiglu(const float* g, const float* u, int count, float* y, cudaStream_t s);
+// AexisQuantizeGemmActivationForInt8 codes: out[r*k + i] = (half)(clamp(rint(a/scale) + zp) - zp).
+cudaError_t launch_act_quant_i8(const void* a, int a_dtype, int lda, int m, int k, float scale, int zero_point,
+                                int is_unsigned, __half* out, cudaStream_t s);
 // Linear-attention decode kernels (k_recurrent.cu).
 cudaError_t launch_short_conv(const float* weight, const float* mixed, const float* cache_in, float* out,
                               float* cache_out, int groups, int kernel, int seq, int cache_len, cudaStream_t s);

@@ -289,6 +289,27 @@ __global__ void swiglu_kernel(const float* g, const float* u, int n, float* y) {
         y[i] = __fmul_rn(g[i] / (1.0f + expf(-g[i])), u[i]);
 }
 
+// W8A8 activation codes (AexisQuantizeGemmActivationForInt8, HLSL
+// Pack4Matmul:792-800): q = clamp(round(v / scale) + zp) over [-128, 127]
+// (signed) or [0, 255] (unsigned), rounding half to even. The GEMM consumes
+// the integer q - zp, exact in fp16 for |zp| <= 1024, and applies `scale` in
+// its epilogue, so each product (q - zp) * w is exact.
+__global__ void act_quant_i8_kernel(const void* a, int a_dtype, int lda, int m, int k, float scale, int zp,
+                                    int is_unsigned, __half* out) {
+    const long long total = (long long)m * k;
+    const int lo = is_unsigned ? 0 : -128, hi = is_unsigned ? 255 : 127;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+         i += (long long)gridDim.x * blockDim.x) {
+        const long long r = i / k, c = i - r * k;
+        const float v = aexis_load_act(a, a_dtype, r * lda + c);
+        float qf = rintf(__fdiv_rn(v, scale));
+        qf = fminf(fmaxf(qf, -1.0e6f), 1.0e6f);   // clamp before the integer conversion
+        int q = (int)qf + zp;
+        q = q < lo ? lo : (q > hi ? hi : q);
+        out[i] = __int2half_rn(q - zp);
+    }
+}
+
 // Bounded wait on a flag nothing sets: one thread polls it until
 // limit_cycles of SM clock pass, then records AEXIS_E_TIMEOUT in the status
 // word and returns (the path every bounded barrier wait takes when it gives up).
@@ -411,6 +432,13 @@ cudaError_t launch_swish(const float* x, int n, float* y, cudaStream_t s) {
 
 cudaError_t launch_swiglu(const float* g, const float* u, int n, float* y, cudaStream_t s) {
     swiglu_kernel<<<grid_for(n), kT, 0, s>>>(g, u, n, y);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_act_quant_i8(const void* a, int a_dtype, int lda, int m, int k, float scale, int zero_point,
+                                int is_unsigned, __half* out, cudaStream_t s) {
+    act_quant_i8_kernel<<<grid_for((long long)m * k), kT, 0, s>>>(a, a_dtype, lda, m, k, scale, zero_point,
+                                                                   is_unsigned, out);
     return cudaGetLastError();
 }
 

@@ -44,6 +44,7 @@ SIGNATURES = {
     "aexis_cuda_weights_dequant": (i32, [vp, vp, vp]),
     "aexis_quantize_q8_rows": (i32, [vp, i32, i32, i32, vp, vp]),
     "aexis_quantize_q4_rows": (i32, [vp, i32, i32, i32, vp, vp]),
+    "aexis_cuda_set_int8_activations": (i32, [vp, i32, f32, i32, i32]),
     "aexis_cuda_gemm": (i32, [vp, vp, i32, i32, i32, i32, vp, vp, f32, f32, vp, i32, i32, i32]),
     "aexis_cuda_gemm_tiled": (i32, [vp, vp, i32, i32, i32, i32, vp, vp, f32, f32, vp, i32, i32, i32]),
     "aexis_cuda_rmsnorm": (i32, [vp, vp, i32, i32, i32, i32, vp, i32, f32, vp, i32]),

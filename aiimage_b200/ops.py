@@ -172,6 +172,24 @@ class AexisOps:
         """AexisOps.SetInt4GemmWeights (:730-739)."""
         self._int4 = w
 
+    def set_int8_activation_quantization(self, plan):
+        """AexisOps.SetInt8ActivationQuantization (:741-785). `plan` is None (plain activations), a
+        QuantizedNodePlan-like object (mode "Int8W8A8", activation_scale, activation_zero_point) or a
+        QuantizedActivationPlan-like object (packing "Pack4UnsignedInt8" or signed, calibration minimum /
+        maximum), resolved as the reference resolves it (resolve_int8_activation_plan)."""
+        if plan is None:
+            self._call(lib().aexis_cuda_set_int8_activations, 0, 1.0, 0, 0)
+            return
+        if hasattr(plan, "activation_scale"):
+            if getattr(plan, "mode", "Int8W8A8") != "Int8W8A8":
+                self._call(lib().aexis_cuda_set_int8_activations, 0, 1.0, 0, 0)
+                return
+            scale, zp, uns = float(plan.activation_scale), int(plan.activation_zero_point), False
+        else:
+            scale, zp, uns = resolve_int8_activation_plan(plan.minimum, plan.maximum,
+                                                          plan.packing == "Pack4UnsignedInt8")
+        self._call(lib().aexis_cuda_set_int8_activations, 1, scale, zp, int(uns))
+
     def dequant(self, w: Weights, out):
         self._call(lib().aexis_cuda_weights_dequant, w.handle, _ptr(out))
 
@@ -291,6 +309,24 @@ class AexisOps:
         self._call(lib().aexis_cuda_gated_delta_rule, _ptr(a_log), _ptr(dt_bias), _ptr(b), _ptr(a), _ptr(query),
                    _ptr(key), _ptr(value), _ptr(state_in), _ptr(output), _ptr(state_out), heads, key_dim,
                    value_dim, sequence_length, token_index, token_count, float(epsilon))
+
+
+def resolve_int8_activation_plan(minimum: float, maximum: float, unsigned: bool):
+    """(scale, zero_point, unsigned) of a calibrated activation plan, as AexisOps.SetInt8ActivationQuantization
+    (QuantizedActivationPlan) computes them (AexisOps.cs:763-785; ActivationCalibrationRange.SymmetricScale,
+    Core/AexisPrecisionContracts.cs:30-37): unsigned packing -> scale = (max - min)/255 (1 if empty) and
+    zero_point = clamp(RoundToInt(-min/scale), 0, 255); signed -> scale = max(|min|, |max|)/127 (1 if 0),
+    zero_point 0. Bounds must be finite and ordered (InferenceContractException otherwise)."""
+    lo, hi = np.float32(minimum), np.float32(maximum)
+    if not (np.isfinite(lo) and np.isfinite(hi)) or lo > hi:
+        raise errors.InvalidOperationError("Activation calibration range must contain finite ordered bounds.")
+    if unsigned:
+        rng = np.float32(hi - lo)
+        scale = np.float32(rng / np.float32(255.0)) if rng > 0 else np.float32(1.0)
+        zp = int(min(max(int(np.rint(np.float32(-lo) / scale)), 0), 255))
+        return float(scale), zp, True
+    mag = max(abs(lo), abs(hi))
+    return float(np.float32(mag / np.float32(127.0)) if mag != 0 else np.float32(1.0)), 0, False
 
 
 def pack4_cdhw(x: np.ndarray) -> np.ndarray:

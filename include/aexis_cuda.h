@@ -150,6 +150,18 @@ int aexis_cuda_gemm(aexis_ctx* ctx, const void* a, int a_dtype, int lda, int m, 
                     const aexis_weights* w, const float* bias, float alpha, float beta,
                     void* y, int y_dtype, int ldy, int n);
 
+/* Ops.SetInt8ActivationQuantization (Ops:741-785) with its plan resolved to
+ * (scale, zero_point, unsigned): while enabled, aexis_cuda_gemm and
+ * aexis_cuda_gemm_tiled fake-quantise every activation as the HLSL
+ * AexisQuantizeGemmActivationForInt8 does (Pack4Matmul:792-800),
+ *   q = clamp(round(a / scale) + zero_point, -128..127 or 0..255 unsigned),
+ *   a' = (q - zero_point) * scale      (round half to even),
+ * before the product (the W8A8 mode of Int8W8A8 node plans). The library
+ * computes sum (q - zp) * W exactly (integer codes, exact fp16 products, fp32
+ * sums) and applies `scale` in the epilogue. enable = 0 restores plain
+ * activations. Errors: scale not positive and finite, or |zero_point| > 1024
+ * -> E_RANGE. The decoder entry points are not affected. */
+int aexis_cuda_set_int8_activations(aexis_ctx* ctx, int enable, float scale, int zero_point, int is_unsigned);
 /* Ops.Gemm2DPack4TiledTextureAFromLinear (Ops:3722-3752), the lm_head
  * variant (HLSL Pack4Matmul:2245-2300): bias is added after the sum,
  *   y[r, c] = beta * bias[c] + alpha * sum_k a[r, k] * W(c, k).
