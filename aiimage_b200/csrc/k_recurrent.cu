@@ -120,20 +120,33 @@ __global__ void __launch_bounds__(kGdrThreads) gdr_kernel(GdrArgs p) {
     const float dt = p.dt_bias[h];
     const float inv_sqrt_k = rsqrtf((float)kdim);
 
-    for (int t = p.first; t < p.first + p.count; ++t) {
+    // Per-token inputs, loaded one token ahead: the loads of token t+1 are in
+    // flight while token t runs its two reductions (prefill is then bound by
+    // the reductions, not by L2 latency).
+    float qv[RPT], kv[RPT], vv[4], bb, xa;
+    auto load_token = [&](int t, float (&qo)[RPT], float (&ko)[RPT], float (&vo)[4], float& bo, float& xo) {
         const int lane_t = t & 3;
         const long long qk_texel = ((long long)(t >> 2) * heads + h) * kdim;
-        float qv[RPT], kv[RPT];
 #pragma unroll
         for (int i = 0; i < RPT; ++i) {
             const int j = r + 32 * i;
-            qv[i] = j < kdim ? p.q[(qk_texel + j) * 4 + lane_t] : 0.f;
-            kv[i] = j < kdim ? p.k[(qk_texel + j) * 4 + lane_t] : 0.f;
+            qo[i] = j < kdim ? p.q[(qk_texel + j) * 4 + lane_t] : 0.f;
+            ko[i] = j < kdim ? p.k[(qk_texel + j) * 4 + lane_t] : 0.f;
         }
-        const float bb = p.b[(long long)t * heads + h];
-        const float x = p.a[(long long)t * heads + h] + dt;
+        const long long v_texel = ((long long)(t >> 2) * heads + h) * vdim;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) vo[c] = c0 + c < vdim ? p.v[(v_texel + c0 + c) * 4 + lane_t] : 0.f;
+        bo = p.b[(long long)t * heads + h];
+        xo = p.a[(long long)t * heads + h] + dt;
+    };
+    const int t_end = p.first + p.count;
+    load_token(p.first, qv, kv, vv, bb, xa);
+    for (int t = p.first; t < t_end; ++t) {
+        const int lane_t = t & 3;
+        float qn[RPT], kn_[RPT], vn[4], bn = 0.f, xn = 0.f;
+        if (t + 1 < t_end) load_token(t + 1, qn, kn_, vn, bn, xn);
         const float beta = 1.0f / (1.0f + expf(-bb));
-        const float decay = expf(-ealog * (fmaxf(x, 0.0f) + logf(1.0f + expf(-fabsf(x)))));
+        const float decay = expf(-ealog * (fmaxf(xa, 0.0f) + logf(1.0f + expf(-fabsf(xa)))));
 
         float part[6] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
@@ -164,11 +177,7 @@ __global__ void __launch_bounds__(kGdrThreads) gdr_kernel(GdrArgs p) {
         const long long v_texel = ((long long)(t >> 2) * heads + h) * vdim;
         float delta[4];
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-            const int col = c0 + c;
-            const float val = col < vdim ? p.v[(v_texel + col) * 4 + lane_t] : 0.f;
-            delta[c] = (val - tot[2 + c] * ks) * beta;
-        }
+        for (int c = 0; c < 4; ++c) delta[c] = (vv[c] - tot[2 + c] * ks) * beta;
         float o[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
         for (int i = 0; i < RPT; ++i) {
@@ -197,6 +206,14 @@ __global__ void __launch_bounds__(kGdrThreads) gdr_kernel(GdrArgs p) {
                     p.out[(v_texel + col) * 4 + lane_t] = sum * qs * inv_sqrt_k;
                 }
             }
+        }
+        if (t + 1 < t_end) {
+#pragma unroll
+            for (int i = 0; i < RPT; ++i) { qv[i] = qn[i]; kv[i] = kn_[i]; }
+#pragma unroll
+            for (int c = 0; c < 4; ++c) vv[c] = vn[c];
+            bb = bn;
+            xa = xn;
         }
     }
 #pragma unroll
