@@ -162,6 +162,7 @@ AEXIS_API int aexis_cuda_destroy(aexis_ctx* ctx) {
     if (ctx->own_stream) cudaStreamSynchronize(ctx->own_stream);
     if (ctx->scratch) cudaFree(ctx->scratch);
     if (ctx->act_q) cudaFree(ctx->act_q);
+    if (ctx->samp) cudaFree(ctx->samp);
     if (ctx->status) cudaFree(ctx->status);
     if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
     delete ctx;
@@ -666,4 +667,59 @@ AEXIS_API int aexis_cuda_gated_delta_rule(aexis_ctx* ctx, const float* a_log, co
                                                          heads, key_dim, value_dim, first_token, token_count, eps,
                                                          ctx->stream),
                             "gated delta rule launch");
+}
+
+// ------------------------------------------------------------------ sampler
+
+AEXIS_API int aexis_cuda_sample(aexis_ctx* ctx, const float* logits, int rows, int width, int ld,
+                                const uint32_t* history, float repetition_penalty, float temperature, int top_k,
+                                float top_p, const double* uniforms, int32_t* out_idx) {
+    if (!ctx) return AEXIS_E_NULL;
+    if (!logits || !out_idx) return aexis_fail(ctx, AEXIS_E_NULL, "logits or output is null");
+    if (rows <= 0 || width <= 0) return aexis_fail(ctx, AEXIS_E_RANGE, "rows=%d width=%d", rows, width);
+    if (ld < width) return aexis_fail(ctx, AEXIS_E_SHAPE, "LM head logits do not cover the tokenizer vocabulary.");
+    if (!(repetition_penalty > 0.0f) || !std::isfinite(repetition_penalty))
+        return aexis_fail(ctx, AEXIS_E_RANGE, "repetition penalty %g", (double)repetition_penalty);
+    if (!std::isfinite(temperature) || !std::isfinite(top_p))
+        return aexis_fail(ctx, AEXIS_E_RANGE, "temperature %g top_p %g", (double)temperature, (double)top_p);
+    const bool sample = temperature > 0.0f;
+    if (sample && (top_k < 1 || top_k > 64))
+        return aexis_fail(ctx, AEXIS_E_UNSUPPORTED,
+                          "top_k=%d: sampling keeps 1..64 candidates (top_k 0, the whole vocabulary, is not built)",
+                          top_k);
+    if (sample && !uniforms) return aexis_fail(ctx, AEXIS_E_NULL, "uniform draws are null");
+    int rc = bind(ctx);
+    if (rc) return rc;
+    const bool penalised = history != nullptr && repetition_penalty != 1.0f;
+    const size_t need = sample_scratch_bytes(rows, width, ctx->sm_count, penalised);
+    if (need > ctx->samp_bytes) {
+        if (ctx->samp) {
+            cudaStreamSynchronize(ctx->stream);
+            cudaFree(ctx->samp);
+            ctx->samp = nullptr;
+            ctx->samp_bytes = 0;
+        }
+        rc = aexis_cuda_check(ctx, cudaMalloc(&ctx->samp, need), "sampler scratch");
+        if (rc) return rc;
+        ctx->samp_bytes = need;
+    }
+    void* tk = nullptr;
+    if (sample) {
+        rc = aexis_scratch(ctx, topk_scratch_bytes(rows, width, top_k < width ? top_k : width, ctx->sm_count), &tk);
+        if (rc) return rc;
+    }
+    return aexis_cuda_check(ctx, launch_sample(logits, rows, width, ld, history, repetition_penalty, temperature,
+                                               top_k, top_p, uniforms, out_idx, ctx->samp, tk, ctx->sm_count,
+                                               ctx->stream),
+                            "sample launch");
+}
+
+AEXIS_API int aexis_cuda_sample_history_add(aexis_ctx* ctx, uint32_t* history, int rows, int width,
+                                            const int32_t* tokens) {
+    if (!ctx) return AEXIS_E_NULL;
+    if (!history || !tokens) return aexis_fail(ctx, AEXIS_E_NULL, "history or tokens is null");
+    if (rows <= 0 || width <= 0) return aexis_fail(ctx, AEXIS_E_RANGE, "rows=%d width=%d", rows, width);
+    int rc = bind(ctx);
+    if (rc) return rc;
+    return aexis_cuda_check(ctx, launch_history_add(history, rows, width, tokens, ctx->stream), "history launch");
 }

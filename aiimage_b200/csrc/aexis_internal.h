@@ -52,6 +52,9 @@ struct aexis_ctx {
     int act_unsigned = 0;
     void* act_q = nullptr;
     size_t act_q_bytes = 0;
+    // Device sampler partials, candidates and penalised scores (grow-only).
+    void* samp = nullptr;
+    size_t samp_bytes = 0;
 };
 
 // Records `msg` on the context and returns `code`.
@@ -193,6 +196,12 @@ cudaError_t launch_swiglu(const float* g, const float* u, int count, float* y, c
 // AexisQuantizeGemmActivationForInt8 codes: out[r*k + i] = (half)(clamp(rint(a/scale) + zp) - zp).
 cudaError_t launch_act_quant_i8(const void* a, int a_dtype, int lda, int m, int k, float scale, int zero_point,
                                 int is_unsigned, __half* out, cudaStream_t s);
+// Device sampler (k_sample.cu). `topk_scratch` holds topk_scratch_bytes(rows, width, min(top_k, width)).
+size_t sample_scratch_bytes(int rows, int width, int sm_count, bool scores);
+cudaError_t launch_sample(const float* logits, int rows, int width, int ld, const uint32_t* history, float pen,
+                          float temperature, int top_k, float top_p, const double* uniforms, int32_t* out,
+                          void* scratch, void* topk_scratch, int sm_count, cudaStream_t s);
+cudaError_t launch_history_add(uint32_t* history, int rows, int width, const int32_t* tokens, cudaStream_t s);
 // Linear-attention decode kernels (k_recurrent.cu).
 cudaError_t launch_short_conv(const float* weight, const float* mixed, const float* cache_in, float* out,
                               float* cache_out, int groups, int kernel, int seq, int cache_len, cudaStream_t s);

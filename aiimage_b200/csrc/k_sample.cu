@@ -1,0 +1,313 @@
+// k_sample.cu -- token sampling on the device: Qwen35Sampler.Select
+// (Samples/AIImageApplicationExample/Runtime/Scripts/Qwen35DecoderSession.cs:
+// 1823-1900) for `rows` logit rows at once.
+//
+// The reference copies the logits to the host, applies the repetition
+// penalty over its history set, takes a temperature softmax over the whole
+// vocabulary (float exp, double sum), sorts every probability, keeps the top
+// k, then the top-p nucleus, and draws with System.Random.NextDouble. Here
+// the probabilities never leave the GPU and nothing is fully sorted:
+//   1. sample_prep_kernel: each CTA takes a segment of a row, applies the
+//      penalty (history bitmap), writes the penalised scores when a penalty
+//      applies, and leaves (max, sum exp((s - max)/T), greedy key) per
+//      segment (an online softmax per thread, merged per CTA);
+//   2. the top-k kernels (k_topk.cu) give the k largest penalised scores in
+//      descending order, equal values by ascending index -- the first k of
+//      the reference's descending probability order;
+//   3. sample_finish_kernel: one warp per row merges the segments, turns the
+//      k candidates into the reference's float probabilities
+//      (float)(exp((s - max)/T) / sum), cuts the nucleus, scales the caller's
+//      uniform draw by the kept mass and walks the cumulative sums.
+// Greedy rows (temperature <= 0) and rows whose sum is not finite and
+// positive take the first maximum of the penalised scores, as the reference's
+// ArgMax does.
+#include "aexis_internal.h"
+
+#include <cfloat>
+
+namespace {
+
+constexpr int kSpThreads = 256;
+
+struct SamplePartial {
+    unsigned long long key;  // greedy key of the segment's first maximum
+    double sum;              // sum of exp((s - m)/T) over the segment
+    float m;                 // segment maximum (-inf when none)
+    float pad;
+};
+
+__device__ __forceinline__ float penalise(float s, const uint32_t* hist_row, int i, float pen) {
+    if (hist_row && ((hist_row[i >> 5] >> (i & 31)) & 1u)) s = s < 0.0f ? s * pen : s / pen;
+    return s;
+}
+
+// Merge of two online-softmax states (m, s): the sum relative to the larger
+// maximum. A NaN sum (a NaN score was seen) is sticky; otherwise a state with
+// no finite maximum contributes nothing.
+__device__ __forceinline__ void softmax_merge(float& m, double& s, float m2, double s2, float inv_t) {
+    if (s != s) return;
+    if (s2 != s2) { s = s2; return; }
+    if (m2 == -INFINITY) return;
+    if (m == -INFINITY) { m = m2; s = s2; return; }
+    if (m2 > m) {
+        s = s * (double)expf((m - m2) * inv_t) + s2;
+        m = m2;
+    } else {
+        s = s + s2 * (double)expf((m2 - m) * inv_t);
+    }
+}
+
+// Running state of the prep pass over a thread's scores, in index order:
+// the first maximum (strict >, as the reference's ArgMax; NaN and -inf never
+// become it) and the online softmax sum relative to that maximum. A quad of
+// scores is summed in fp32 and folded into the fp64 sum once.
+struct PrepState {
+    float m = -INFINITY;  // running maximum
+    int im = -1;          // its first index
+    double s = 0.0;       // sum of exp((v - m)/T) over the scores seen (NaN once a NaN was seen)
+    bool nan = false;
+    template <int N>
+    __device__ __forceinline__ void add(const float (&e)[N], int i, bool sample, float inv_t) {
+        const float m_old = m;
+#pragma unroll
+        for (int c = 0; c < N; ++c) {
+            nan |= e[c] != e[c];
+            if (e[c] > m) { m = e[c]; im = i + c; }
+        }
+        if (!sample || m == -INFINITY) return;
+        if (m > m_old) s = m_old == -INFINITY ? 0.0 : s * (double)expf((m_old - m) * inv_t);
+        float q = 0.0f;
+#pragma unroll
+        for (int c = 0; c < N; ++c) q += expf((e[c] - m) * inv_t);
+        s += (double)q;
+    }
+    __device__ __forceinline__ unsigned long long key() const {
+        return im < 0 ? 0ull : aexis_argmax_key(m, im);
+    }
+};
+
+// Segment [lo, hi) of one row. Rows whose base and stride allow it are read
+// as float4 (`vec`), four loads in flight per thread before any arithmetic,
+// so the pass runs at HBM rate rather than at one load latency per element.
+__global__ void __launch_bounds__(kSpThreads) sample_prep_kernel(const float* __restrict__ logits, int width, int ld,
+                                                                 const uint32_t* __restrict__ history, int hist_words,
+                                                                 float pen, float temperature, int seg_len, bool vec,
+                                                                 float* __restrict__ scores, int ld_scores,
+                                                                 SamplePartial* __restrict__ parts) {
+    const int row = blockIdx.y, seg = blockIdx.x;
+    const int lo = seg * seg_len, hi = min(width, lo + seg_len);
+    const float* x = logits + (long long)row * ld;
+    const uint32_t* hrow = history ? history + (long long)row * hist_words : nullptr;
+    float* srow = scores ? scores + (long long)row * ld_scores : nullptr;
+    const bool sample = temperature > 0.0f;
+    const float inv_t = sample ? 1.0f / temperature : 0.0f;
+    PrepState st;
+    int i0 = lo;
+    if (vec) {
+        // lo is a multiple of 4 (seg_len is); whole quads up to hi.
+        const int q_lo = lo >> 2, q_hi = hi >> 2;
+        const float4* x4 = reinterpret_cast<const float4*>(x);
+        constexpr int U = 4;
+        for (int q = q_lo + threadIdx.x; q < q_hi; q += U * kSpThreads) {
+            float4 v[U];
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int qq = q + u * kSpThreads;
+                v[u] = qq < q_hi ? __ldcs(x4 + qq) : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+            }
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int qq = q + u * kSpThreads;
+                if (qq >= q_hi) break;
+                const int i = qq * 4;
+                float e[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+                if (hrow) {
+                    const uint32_t w = hrow[i >> 5] >> (i & 31);
+#pragma unroll
+                    for (int c = 0; c < 4; ++c)
+                        if ((w >> c) & 1u) e[c] = e[c] < 0.0f ? e[c] * pen : e[c] / pen;
+                }
+                if (srow) *reinterpret_cast<float4*>(srow + i) = make_float4(e[0], e[1], e[2], e[3]);
+                st.add(e, i, sample, inv_t);
+            }
+        }
+        i0 = max(lo, q_hi * 4);   // a segment past the row's end (hi <= lo) reads nothing
+    }
+    for (int i = i0 + threadIdx.x; i < hi; i += kSpThreads) {
+        const float v[1] = {penalise(x[i], hrow, i, pen)};
+        if (srow) srow[i] = v[0];
+        st.add(v, i, sample, inv_t);
+    }
+    unsigned long long key = st.key();
+    // ArgMax keeps index 0 when nothing is greater than its score, a NaN or
+    // -inf included: the key of element 0 itself covers that.
+    if (lo == 0 && threadIdx.x == 0 && hi > 0) {
+        const unsigned long long k0 = aexis_argmax_key(penalise(x[0], hrow, 0, pen), 0);
+        key = k0 > key ? k0 : key;
+    }
+    float m = st.m;
+    double s = st.s;
+    if (st.nan) s = __longlong_as_double(0x7ff8000000000000ll);  // exp(NaN) poisons the reference's sum
+    // Block merge: warps by shuffles, then warp 0 over the warps' states.
+    __shared__ SamplePartial red[kSpThreads / 32];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) {
+        const unsigned long long k2 = __shfl_xor_sync(0xffffffffu, key, o);
+        const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
+        const double s2 = __shfl_xor_sync(0xffffffffu, s, o);
+        key = k2 > key ? k2 : key;
+        softmax_merge(m, s, m2, s2, inv_t);
+    }
+    if (lane == 0) red[warp] = SamplePartial{key, s, m, 0.0f};
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < kSpThreads / 32; ++w) {
+            key = red[w].key > key ? red[w].key : key;
+            softmax_merge(m, s, red[w].m, red[w].sum, inv_t);
+        }
+        parts[(long long)row * gridDim.x + seg] = SamplePartial{key, s, m, 0.0f};
+    }
+}
+
+__global__ void sample_finish_kernel(const SamplePartial* __restrict__ parts, int segs, float temperature, int top_k,
+                                     float top_p, int width, const float* __restrict__ cand_vals,
+                                     const int32_t* __restrict__ cand_idx, int cand_ld,
+                                     const double* __restrict__ uniforms, int32_t* __restrict__ out) {
+    const int row = blockIdx.x, lane = threadIdx.x;
+    const bool sample = temperature > 0.0f;
+    const float inv_t = sample ? 1.0f / temperature : 0.0f;
+    const int n_cand = sample ? (top_k < width ? top_k : width) : 0;
+    // Candidates and the draw are loaded first, in parallel with the merge.
+    const float* cv = cand_vals + (long long)row * cand_ld;
+    const int32_t* ci = cand_idx + (long long)row * cand_ld;
+    const float c_v0 = lane < n_cand ? cv[lane] : 0.0f, c_v1 = lane + 32 < n_cand ? cv[lane + 32] : 0.0f;
+    const int c_i0 = lane < n_cand ? ci[lane] : 0, c_i1 = lane + 32 < n_cand ? ci[lane + 32] : 0;
+    const double u = sample && lane == 0 ? uniforms[row] : 0.0;
+    unsigned long long key = 0ull;
+    float m = -INFINITY;
+    double s = 0.0;
+    for (int i = lane; i < segs; i += 32) {
+        const SamplePartial p = parts[(long long)row * segs + i];
+        key = p.key > key ? p.key : key;
+        softmax_merge(m, s, p.m, p.sum, inv_t);
+    }
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) {
+        const unsigned long long k2 = __shfl_xor_sync(0xffffffffu, key, o);
+        const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
+        const double s2 = __shfl_xor_sync(0xffffffffu, s, o);
+        key = k2 > key ? k2 : key;
+        softmax_merge(m, s, m2, s2, inv_t);
+    }
+    // s is a NaN when any penalised score is a NaN (exp(NaN) poisons the sum
+    // as in the reference); no finite maximum leaves s = 0.
+    if (!sample || !(s > 0.0 && s <= DBL_MAX)) {
+        if (lane == 0) out[row] = aexis_argmax_index(key);
+        return;
+    }
+    int keep = n_cand;
+    // The candidates' probabilities in parallel (one double division each);
+    // the cumulative sums below stay sequential, in the reference's order.
+    __shared__ float prob[64];
+    __shared__ int32_t ix[64];
+    if (lane < keep) {
+        prob[lane] = (float)((double)expf((c_v0 - m) / temperature) / s);
+        ix[lane] = c_i0;
+    }
+    if (lane + 32 < keep) {
+        prob[lane + 32] = (float)((double)expf((c_v1 - m) / temperature) / s);
+        ix[lane + 32] = c_i1;
+    }
+    __syncwarp();
+    if (lane != 0) return;
+    if (top_p < 1.0f) {
+        double cumulative = 0.0;
+        int nucleus = 0;
+        while (nucleus < keep) {
+            cumulative += prob[nucleus++];
+            if (cumulative >= top_p) break;
+        }
+        keep = nucleus > 1 ? nucleus : 1;
+    }
+    double kept = 0.0;
+    for (int j = 0; j < keep; ++j) kept += prob[j];
+    if (!(kept > 0.0 && kept <= DBL_MAX)) {
+        out[row] = aexis_argmax_index(key);
+        return;
+    }
+    const double draw = u * kept;
+    double cursor = 0.0;
+    for (int j = 0; j < keep; ++j) {
+        cursor += prob[j];
+        if (draw <= cursor) {
+            out[row] = ix[j];
+            return;
+        }
+    }
+    out[row] = ix[keep - 1];
+}
+
+__global__ void history_add_kernel(uint32_t* history, int rows, int hist_words, int width, const int32_t* tokens) {
+    const int r = blockIdx.x * blockDim.x + threadIdx.x;
+    if (r >= rows) return;
+    const int t = tokens[r];
+    if (t >= 0 && t < width) atomicOr(history + (long long)r * hist_words + (t >> 5), 1u << (t & 31));
+}
+
+}  // namespace
+
+int sample_segments(int rows, int width, int sm_count) {
+    const int by_width = (width + 1023) / 1024;
+    const int by_sms = (2 * sm_count + rows - 1) / rows;
+    int segs = by_width < by_sms ? by_width : by_sms;
+    return segs < 1 ? 1 : segs;
+}
+
+size_t sample_scratch_bytes(int rows, int width, int sm_count, bool scores) {
+    const size_t ld_s = (size_t)((width + 3) & ~3);
+    size_t b = (size_t)rows * sample_segments(rows, width, sm_count) * sizeof(SamplePartial);
+    b = (b + 255) & ~(size_t)255;
+    b += (size_t)rows * 64 * (sizeof(float) + sizeof(int32_t));
+    b = (b + 255) & ~(size_t)255;
+    if (scores) b += (size_t)rows * ld_s * sizeof(float);
+    return b;
+}
+
+cudaError_t launch_sample(const float* logits, int rows, int width, int ld, const uint32_t* history, float pen,
+                          float temperature, int top_k, float top_p, const double* uniforms, int32_t* out,
+                          void* scratch, void* topk_scratch, int sm_count, cudaStream_t s) {
+    const bool sample = temperature > 0.0f;
+    const bool penalised = history != nullptr && pen != 1.0f;
+    const int segs = sample_segments(rows, width, sm_count);
+    const int seg_len = ((width + segs - 1) / segs + 3) & ~3;
+    const bool vec = (reinterpret_cast<uintptr_t>(logits) & 15) == 0 && (ld & 3) == 0;
+    char* p = reinterpret_cast<char*>(scratch);
+    SamplePartial* parts = reinterpret_cast<SamplePartial*>(p);
+    size_t off = ((size_t)rows * segs * sizeof(SamplePartial) + 255) & ~(size_t)255;
+    float* cand_vals = reinterpret_cast<float*>(p + off);
+    int32_t* cand_idx = reinterpret_cast<int32_t*>(cand_vals + (size_t)rows * 64);
+    off = (off + (size_t)rows * 64 * 8 + 255) & ~(size_t)255;
+    const int ld_s = (width + 3) & ~3;
+    float* scores = penalised ? reinterpret_cast<float*>(p + off) : nullptr;
+    const int hist_words = (width + 31) / 32;
+    sample_prep_kernel<<<dim3(segs, rows), kSpThreads, 0, s>>>(logits, width, ld, penalised ? history : nullptr,
+                                                               hist_words, pen, temperature, seg_len, vec, scores,
+                                                               ld_s, parts);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    const int k = sample ? (top_k < width ? top_k : width) : 1;
+    if (sample) {
+        e = launch_topk(penalised ? scores : logits, rows, width, penalised ? ld_s : ld, k, cand_vals, cand_idx,
+                        topk_scratch, sm_count, s);
+        if (e != cudaSuccess) return e;
+    }
+    sample_finish_kernel<<<rows, 32, 0, s>>>(parts, segs, temperature, top_k, top_p, width, cand_vals, cand_idx, k,
+                                              uniforms, out);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_history_add(uint32_t* history, int rows, int width, const int32_t* tokens, cudaStream_t s) {
+    history_add_kernel<<<(rows + 127) / 128, 128, 0, s>>>(history, rows, (width + 31) / 32, width, tokens);
+    return cudaGetLastError();
+}

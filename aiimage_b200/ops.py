@@ -290,6 +290,21 @@ class AexisOps:
     def swiglu(self, gate, up, count, y):
         self._call(lib().aexis_cuda_swiglu, _ptr(gate), _ptr(up), count, _ptr(y))
 
+    # -- sampling (Qwen35Sampler.Select on the device) -------------------------
+    def sample(self, logits, rows, width, history, repetition_penalty, temperature, top_k, top_p, uniforms,
+               output, ld=None):
+        """Qwen35Sampler.Select (Qwen35DecoderSession.cs:1847-1892) for `rows` logit rows: penalty on the history
+        bitmap, temperature softmax, top-k, top-p, one draw per row from `uniforms` (fp64 [rows], the NextDouble
+        values). temperature <= 0 is the greedy ArgMax. output: int32 [rows]."""
+        ld = ld if ld is not None else (logits.stride(0) if logits.dim() == 2 else width)
+        self._call(lib().aexis_cuda_sample, _ptr(logits), rows, width, ld, _ptr(history), float(repetition_penalty),
+                   float(temperature), int(top_k), float(top_p), _ptr(uniforms), _ptr(output))
+
+    def sample_history_add(self, history, rows, width, tokens):
+        """Qwen35Sampler.AddHistory (:1840-1844) on the device bitmap: sets bit tokens[r] of row r (ids outside
+        [0, width) are ignored)."""
+        self._call(lib().aexis_cuda_sample_history_add, _ptr(history), rows, width, _ptr(tokens))
+
     # -- linear-attention blocks (Qwen3.5 ShortConv + GatedDeltaRule) ---------
     def short_conv_pack4(self, weight, mixed, cache_in, output, cache_out, groups, kernel_size, sequence_length,
                          cache_length):

@@ -339,6 +339,13 @@ def run_gpu(args):
         except Exception as e:
             config5 = {"error": f"{type(e).__name__}: {e}"}
 
+    sampler = None
+    if not args.skip_sampler:
+        try:
+            sampler = bench_sampler(ops, peak)
+        except Exception as e:
+            sampler = {"error": f"{type(e).__name__}: {e}"}
+
     linear_attn = None
     if not args.skip_linear_attention:
         try:
@@ -379,6 +386,7 @@ def run_gpu(args):
             "config4": config4,
             "config5": config5,
             "linear_attention": linear_attn,
+            "sampler": sampler,
             "cpu_baseline": cpu,
             "e2e": {"value": round(e2e_steps * STEP_BYTES * world / e2e_s / 1e9, 2), "unit": "GB/s",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
@@ -537,6 +545,40 @@ def bench_config4(ops, peak, world: int, rank: int, steps: int = 128, total_seqs
             "bytes_per_step_mean": int(byts / n_steps), "GB/s": round(byts / dev_s / 1e9, 1),
             "frac": round(byts / dev_s / 1e9 / peak, 3), "first_ids": first_ids,
             "timing": "device (CUDA events around each batch's generate), max over ranks"}
+
+
+def bench_sampler(ops, peak):
+    """Device sampling (Qwen35Sampler.Select with Qwen35SamplingConfig's defaults: T 0.3, top-k 50, top-p 0.8,
+    repetition penalty 1.1 over a 64-token history) on the 151936-wide vocabulary, batch 1 (one decode step)
+    and batch 256 (config 5's rows). Logits already on the device; CUDA events over back-to-back calls."""
+    import torch
+    vocab = 151936
+    out = {}
+    for rows in (1, 256):
+        g = torch.Generator(device="cuda").manual_seed(11)
+        logits = torch.randn((rows, vocab), generator=g, device="cuda", dtype=torch.float32) * 4
+        hist = torch.zeros((rows, (vocab + 31) // 32), dtype=torch.int32, device="cuda")
+        toks = torch.randint(0, vocab, (64, rows), generator=g, device="cuda", dtype=torch.int32)
+        for t in range(64):
+            ops.sample_history_add(hist, rows, vocab, toks[t])
+        u = torch.rand(rows, generator=g, device="cuda", dtype=torch.float64)
+        ids = torch.empty(rows, dtype=torch.int32, device="cuda")
+        for _ in range(5):
+            ops.sample(logits, rows, vocab, hist, 1.1, 0.3, 50, 0.8, u, ids)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        n = 50
+        e0.record()
+        for _ in range(n):
+            ops.sample(logits, rows, vocab, hist, 1.1, 0.3, 50, 0.8, u, ids)
+        e1.record()
+        e1.synchronize()
+        t = e0.elapsed_time(e1) / 1e3 / n
+        read = rows * vocab * 4
+        out[f"rows{rows}"] = {"us_per_call": round(t * 1e6, 2), "logits_GB/s": round(read / t / 1e9, 1)}
+    out["workload"] = "Qwen35Sampler.Select defaults (T 0.3, top-k 50, top-p 0.8, penalty 1.1), vocab 151936"
+    out["timing"] = "CUDA events over 50 back-to-back calls, logits resident"
+    return out
 
 
 def bench_linear_attention(ops, peak, prefill: int = 512):
@@ -716,7 +758,8 @@ def run_only(args):
     --only decoder    the config-3 decoder with --prompt-len / --new-tokens
     --only tcgemm     the config-5 lm_head GEMM alone (M=256, tensor cores)
     --only config4    one config-4 batch (32 sequences, --new-tokens steps)
-    --only linear_attention  the Qwen3.5 GatedDeltaRule / ShortConv decode kernels"""
+    --only linear_attention  the Qwen3.5 GatedDeltaRule / ShortConv decode kernels
+    --only sampler    the device sampler (Qwen35Sampler defaults) at 1 and 256 rows"""
     import torch
     torch.cuda.set_device(0)
     from aiimage_b200.ops import AexisOps
@@ -726,6 +769,8 @@ def run_only(args):
         out = bench_decoder(ops, peak, args.prompt_len, args.new_tokens)
     elif args.only == "linear_attention":
         out = bench_linear_attention(ops, peak)
+    elif args.only == "sampler":
+        out = bench_sampler(ops, peak)
     elif args.only == "topk":
         m, vocab, k = 256, 151936, 50
         g = torch.Generator(device="cuda").manual_seed(5)
@@ -830,10 +875,11 @@ def main():
     ap.add_argument("--skip-cpu", action="store_true", help="omit the CPU oracle baseline")
     ap.add_argument("--skip-config5", action="store_true", help="omit the config-5 lm_head measurement")
     ap.add_argument("--skip-config4", action="store_true", help="omit the config-4 batched decoder measurement")
+    ap.add_argument("--skip-sampler", action="store_true", help="omit the device sampler measurement")
     ap.add_argument("--skip-linear-attention", action="store_true",
                     help="omit the GatedDeltaRule / ShortConv decode measurement")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
-    ap.add_argument("--only", choices=["dominant", "decoder", "tcgemm", "config4", "topk", "linear_attention"], help="profiling mode (see run_only)")
+    ap.add_argument("--only", choices=["dominant", "decoder", "tcgemm", "config4", "topk", "linear_attention", "sampler"], help="profiling mode (see run_only)")
     ap.add_argument("--prompt-len", type=int, default=512)
     ap.add_argument("--new-tokens", type=int, default=64)
     args = ap.parse_args()

@@ -259,6 +259,34 @@ int aexis_cuda_argmax_static(const float* logits, int rows, int width, int ld, i
 int aexis_cuda_topk(aexis_ctx* ctx, const float* logits, int rows, int width, int ld, int k,
                     float* out_vals, int32_t* out_idx);
 
+/* Qwen35Sampler.Select (Samples/.../Qwen35DecoderSession.cs:1847-1900) for
+ * `rows` logit rows on the device. Per row:
+ *   s = logits with the repetition penalty on history tokens
+ *       (s < 0 ? s * penalty : s / penalty);
+ *   temperature <= 0: the first maximum of s (ArgMax, :1894-1900);
+ *   else p = (float)(exp((s - max)/T) / sum) with the sum in double; the
+ *   top_k most probable, then the smallest prefix whose cumulative reaches
+ *   top_p (at least one); draw = uniforms[r] * kept mass; the first token
+ *   whose cumulative reaches the draw. A sum that is not finite and positive
+ *   (a NaN score, no finite score) falls back to ArgMax, as the reference.
+ * logits: device fp32 [rows, ld]; history: NULL or a device bitmap
+ * [rows][ceil(width/32)] uint32 (bit t % 32 of word t / 32 = token t was
+ * emitted, see aexis_cuda_sample_history_add); uniforms: device fp64 [rows],
+ * the System.Random.NextDouble draw of each row (may be NULL when greedy);
+ * out_idx: device int32 [rows]. Equal probabilities rank by ascending index
+ * (the reference's Array.Sort leaves exact ties unordered).
+ * Errors: NULL logits/out -> E_NULL; rows, width <= 0, penalty <= 0 or a
+ * non-finite temperature / top_p -> E_RANGE; ld < width -> E_SHAPE; when
+ * sampling: top_k outside 1..64 -> E_UNSUPPORTED (top_k 0, sampling over the
+ * whole vocabulary, is not built), uniforms NULL -> E_NULL. */
+int aexis_cuda_sample(aexis_ctx* ctx, const float* logits, int rows, int width, int ld,
+                      const uint32_t* history, float repetition_penalty, float temperature, int top_k,
+                      float top_p, const double* uniforms, int32_t* out_idx);
+/* Qwen35Sampler.AddHistory (:1840-1844) for every row: sets bit tokens[r] of
+ * row r of the history bitmap (tokens: device int32 [rows]; ids outside
+ * [0, width) are ignored). */
+int aexis_cuda_sample_history_add(aexis_ctx* ctx, uint32_t* history, int rows, int width,
+                                  const int32_t* tokens);
 /* No reference counterpart (the reference decodes on one device): the merge
  * step of a vocab-sharded lm_head. `gathered` (device) holds, for each of
  * `lists` (1..8) shards in shard order, rows uint64 greedy keys of

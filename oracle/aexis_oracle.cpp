@@ -799,3 +799,86 @@ ORACLE_API void oracle_gated_delta_rule(const float* a_log, const float* dt_bias
     }
     std::memcpy(state_out, cur.data(), sizeof(float) * n_state);
 }
+
+// ---------------------------------------------------------------------------
+// Qwen35Sampler.Select (DECODER:1847-1892) for `rows` logit rows, with the
+// NextDouble draw of each row given in `uniforms` (the System.Random stream
+// is the caller's). history: NULL or a bitmap [rows][ceil(width/32)] (bit i
+// of word i/32 = token i is in the history set, DECODER:1840-1844).
+//   scores = logits with the repetition penalty on history tokens (:1852-1853)
+//   greedy when temperature <= 0 (:1855-1856), ArgMax = first maximum (:1894-1900)
+//   value_i = (float)exp((s_i - max)/T), sum in double (:1858-1866); fallback
+//   to ArgMax when the sum is not finite and positive (:1867-1868)
+//   p_i = (float)(value_i / sum); order by p descending (:1869-1872); equal
+//   probabilities keep ascending index here (the reference's Array.Sort is
+//   unstable, so its order among exact ties is unspecified)
+//   keep = min(TopK, V) (TopK <= 0: V), nucleus while cumulative < TopP (:1873-1884)
+//   draw = u * kept mass, first cumulative >= draw (:1886-1894)
+// margin[r] (optional): distance of the draw, and of the nucleus cut, from
+// the nearest cumulative boundary, relative to the kept mass (a GPU/CPU
+// difference in the last bits can only change the token when it is tiny).
+// ---------------------------------------------------------------------------
+ORACLE_API void oracle_sample(const float* logits, int rows, int width, int ld, const uint32_t* history,
+                              float pen, float temperature, int top_k, float top_p, const double* uniforms,
+                              int32_t* out, double* margin) {
+    const int words = (width + 31) / 32;
+    for (int r = 0; r < rows; ++r) {
+        std::vector<float> scores(logits + (int64_t)r * ld, logits + (int64_t)r * ld + width);
+        if (history)
+            for (int i = 0; i < width; ++i)
+                if ((history[(int64_t)r * words + i / 32] >> (i % 32)) & 1u)
+                    scores[i] = scores[i] < 0.0f ? scores[i] * pen : scores[i] / pen;
+        auto argmax = [&]() {
+            int best = 0;
+            for (int i = 1; i < width; ++i)
+                if (scores[i] > scores[best]) best = i;
+            return best;
+        };
+        if (margin) margin[r] = 1.0;
+        if (temperature <= 0.0f) { out[r] = argmax(); continue; }
+        const float mx = scores[argmax()];
+        std::vector<float> prob(width);
+        double sum = 0.0;
+        for (int i = 0; i < width; ++i) {
+            float value = std::exp((scores[i] - mx) / temperature);
+            prob[i] = value;
+            sum += value;
+        }
+        if (!std::isfinite(sum) || sum <= 0.0) { out[r] = argmax(); continue; }
+        for (int i = 0; i < width; ++i) prob[i] = (float)(prob[i] / sum);
+        int keep = top_k > 0 ? std::min(top_k, width) : width;
+        std::vector<int> order(width);
+        for (int i = 0; i < width; ++i) order[i] = i;
+        auto by_prob = [&](int a, int b) { return prob[a] > prob[b] || (prob[a] == prob[b] && a < b); };
+        std::partial_sort(order.begin(), order.begin() + keep, order.end(), by_prob);
+        double cut_margin = 1.0;
+        if (top_p < 1.0f) {
+            double cumulative = 0.0;
+            int nucleus = 0;
+            while (nucleus < keep) {
+                cumulative += prob[order[nucleus++]];
+                cut_margin = std::min(cut_margin, std::fabs(cumulative - (double)top_p));
+                if (cumulative >= top_p) break;
+            }
+            keep = std::max(1, nucleus);
+        }
+        double kept = 0.0;
+        for (int i = 0; i < keep; ++i) kept += prob[order[i]];
+        if (!std::isfinite(kept) || kept <= 0.0) { out[r] = argmax(); continue; }
+        const double sample = uniforms[r] * kept;
+        double cursor = 0.0, prev = 0.0;
+        int pick = order[keep - 1];
+        double dm = 1.0;
+        for (int i = 0; i < keep; ++i) {
+            prev = cursor;
+            cursor += prob[order[i]];
+            if (sample <= cursor) {
+                pick = order[i];
+                dm = std::min(sample - prev, cursor - sample) / kept;
+                break;
+            }
+        }
+        out[r] = pick;
+        if (margin) margin[r] = std::min(dm, cut_margin);
+    }
+}

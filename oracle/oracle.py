@@ -55,6 +55,8 @@ def lib():
         L.oracle_embed.argtypes = [I32P, C.c_int, C.c_int, vp, vp, C.c_int, vp, C.c_int, C.c_int, vp, F32P]
         L.oracle_swish.argtypes = [F32P, C.c_int, F32P]
         L.oracle_swiglu.argtypes = [F32P, F32P, C.c_int, F32P]
+        L.oracle_sample.argtypes = [F32P, C.c_int, C.c_int, C.c_int, vp, C.c_float, C.c_float, C.c_int, C.c_float,
+                                    np.ctypeslib.ndpointer(dtype=np.float64, flags="C_CONTIGUOUS"), I32P, vp]
         L.oracle_short_conv.argtypes = [F32P, F32P, F32P, F32P, F32P, C.c_int, C.c_int, C.c_int, C.c_int]
         L.oracle_gated_delta_rule.argtypes = [F32P] * 10 + [C.c_int] * 5 + [C.c_float]
         L.oracle_round_f16.argtypes = [C.c_float]
@@ -239,6 +241,22 @@ def gated_delta_rule(a_log, dt_bias, b, a, q, k, v, state_in, heads: int, kdim: 
                                   _f32(q).ravel(), _f32(k).ravel(), _f32(v).ravel(), _f32(state_in).ravel(), out,
                                   state_out, heads, kdim, vdim, first, count, eps)
     return out, state_out
+
+
+def sample(logits, history=None, penalty: float = 1.0, temperature: float = 0.0, top_k: int = 0,
+           top_p: float = 1.0, uniforms=None):
+    """Qwen35Sampler.Select per row with the given NextDouble draws (see oracle_sample). logits [rows, width];
+    history: None or uint32 bitmap [rows, ceil(width/32)]. Returns (token ids, margins)."""
+    x = _f32(logits)
+    if x.ndim == 1:
+        x = x.reshape(1, -1)
+    rows, width = x.shape
+    u = np.ascontiguousarray(np.zeros(rows) if uniforms is None else uniforms, dtype=np.float64)
+    h = None if history is None else np.ascontiguousarray(history, dtype=np.uint32)
+    out = np.zeros(rows, dtype=np.int32)
+    margin = np.zeros(rows, dtype=np.float64)
+    lib().oracle_sample(x, rows, width, width, _ptr(h), penalty, temperature, top_k, top_p, u, out, _ptr(margin))
+    return out, margin
 
 
 def round_f16(x) -> np.ndarray:
