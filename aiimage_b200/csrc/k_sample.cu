@@ -122,10 +122,12 @@ __global__ void __launch_bounds__(kSpThreads) sample_prep_kernel(const float* __
                 const int i = qq * 4;
                 float e[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
                 if (hrow) {
-                    const uint32_t w = hrow[i >> 5] >> (i & 31);
+                    const uint32_t w = (hrow[i >> 5] >> (i & 31)) & 15u;
+                    if (w) {  // rare: the history is sparse
 #pragma unroll
-                    for (int c = 0; c < 4; ++c)
-                        if ((w >> c) & 1u) e[c] = e[c] < 0.0f ? e[c] * pen : e[c] / pen;
+                        for (int c = 0; c < 4; ++c)
+                            if ((w >> c) & 1u) e[c] = e[c] < 0.0f ? e[c] * pen : e[c] / pen;
+                    }
                 }
                 if (srow) *reinterpret_cast<float4*>(srow + i) = make_float4(e[0], e[1], e[2], e[3]);
                 st.add(e, i, sample, inv_t);
@@ -257,9 +259,12 @@ __global__ void history_add_kernel(uint32_t* history, int rows, int hist_words, 
 
 }  // namespace
 
+// Segments per row: at least 1024 scores each, and about as many CTAs in
+// total as fit on the GPU at once (8 of 256 threads per SM), so that enough
+// loads are in flight to keep HBM busy.
 int sample_segments(int rows, int width, int sm_count) {
     const int by_width = (width + 1023) / 1024;
-    const int by_sms = (2 * sm_count + rows - 1) / rows;
+    const int by_sms = (8 * sm_count) / rows;
     int segs = by_width < by_sms ? by_width : by_sms;
     return segs < 1 ? 1 : segs;
 }
