@@ -18,22 +18,26 @@
 //     1024 bytes). fp32 activations are split into fp16 hi and lo rows
 //     (x = hi + lo to about 22 bits) that ride in the same MMA as extra
 //     columns, so fp32 inputs keep fp32-class accuracy.
-// Per CTA (persistent, one per SM): a contiguous range of 128-row slabs, two
-// slabs per accumulator tile (two M=128 MMAs sharing the activation tile),
-// each over all K. Three shared-memory rings decouple the latencies: int8
-// weights (up to 8 k-blocks deep, freed as soon as they are dequantised),
-// fp16 A tiles (2 deep, freed by the MMA commit) and activations (3-4 deep,
-// freed by the MMA commit). Warp roles: 0 int8 bulk-copy producer, 1 MMA
-// issuer and TMEM owner, 2-5 dequantise int8 -> fp16 into the swizzled A
-// tiles and run the epilogue from TMEM, 6 activation bulk-copy producer.
-// Every barrier wait is bounded.
+// Per CTA (persistent, one per SM): a contiguous range of 128-row slabs,
+// taken two per accumulator tile (two M=128 MMAs sharing the activation tile)
+// when two such tiles fit in TMEM (MMA width nb <= 128), else one, each over
+// all K. TMEM holds two accumulator tiles: tile t accumulates into buffer
+// t & 1 while the epilogue drains tile t - 1 from the other, so the output
+// stores overlap the next tile's weight stream, dequantisation and MMAs.
+// Three shared-memory rings decouple the latencies: int8 weights (up to 8
+// k-blocks deep, freed as soon as they are dequantised), fp16 A tiles (2
+// deep, freed by the MMA commit) and activations (2-4 deep, freed by the MMA
+// commit). Warp roles: 0 int8 bulk-copy producer, 1 MMA issuer and TMEM
+// owner, 2-5 dequantise int8 -> fp16 into the swizzled A tiles, 6 activation
+// bulk-copy producer, 7-10 the epilogue (TMEM -> registers -> staging buffers
+// of their own -> 16-byte row stores). Every barrier wait is bounded.
 #include "gemv_dev.cuh"
 
 namespace {
 
 using namespace aexis_dev;
 
-constexpr int kTcThreads = 224;          // 7 warps
+constexpr int kTcThreads = 352;          // 11 warps
 constexpr int kTM = 128;                 // rows per MMA (M) = rows per slab
 constexpr int kTile = 256;               // at most two slabs per accumulator tile
 constexpr int kKB = 64;                  // K per stage (one 128-byte swizzle atom of fp16)
@@ -42,6 +46,12 @@ constexpr int kATileBytes = kTM * 128;   // fp16 bytes of one slab k-block (16 K
 constexpr int kADepth = 2;               // fp16 A ring
 constexpr int kMaxDepth = 8;             // int8 and activation rings
 constexpr int kSmemBudget = 227 * 1024;
+constexpr int kStgBytes = 32 * kTM * 4;  // one epilogue staging buffer: 32 output rows x 128 outputs, fp32
+constexpr int kStgBufs = 4;
+
+// Slabs per accumulator tile: two when two such tiles (2 x 2 x nb columns)
+// fit in the 512 TMEM columns, else one.
+__host__ __device__ inline int tc_tile_slabs(int nb) { return 4 * nb <= 512 ? 2 : 1; }
 
 struct TcParams {
     const uint8_t* wt;        // tiled int8 weights
@@ -71,8 +81,9 @@ struct TcTile {
 __device__ __forceinline__ TcTile tc_tile(const TcParams& p, int lo, int hi, int t, int nkb) {
     TcTile T;
     if (p.k_splits <= 1) {
-        T.slab0 = lo + 2 * t;
-        T.ns = hi - T.slab0 < 2 ? 1 : 2;
+        const int ts = tc_tile_slabs(p.nb);
+        T.slab0 = lo + ts * t;
+        T.ns = hi - T.slab0 < ts ? hi - T.slab0 : ts;
         T.kb0 = 0;
         T.kb1 = nkb;
     } else {
@@ -87,30 +98,37 @@ __device__ __forceinline__ TcTile tc_tile(const TcParams& p, int lo, int hi, int
 }
 
 // Shared-memory carve-up (offsets from a 1024-aligned base): the fp16 A ring
-// (kADepth x two slabs), the activation ring, the int8 ring, the barriers.
+// (kADepth x one tile's slabs), the activation ring, the epilogue staging
+// buffers, the int8 ring (one tile's slabs per stage), the barriers.
 struct TcLayout {
-    int b_bytes, b_stage, a_off, b_off, raw_off, bar_off, total;
+    int ts, b_bytes, b_stage, a_stage, raw_stage, a_off, b_off, stg_off, raw_off, bar_off, total;
 };
 
 __host__ __device__ inline TcLayout tc_layout(int nb, int raw_depth, int b_depth) {
     TcLayout L;
+    L.ts = tc_tile_slabs(nb);
     L.b_bytes = nb * 128;
     L.b_stage = (L.b_bytes + 1023) & ~1023;
+    L.a_stage = L.ts * kATileBytes;
+    L.raw_stage = L.ts * kSlabBytes;
     L.a_off = 0;
-    L.b_off = kADepth * 2 * kATileBytes;
-    L.raw_off = L.b_off + b_depth * L.b_stage;
-    L.bar_off = L.raw_off + raw_depth * 2 * kSlabBytes;
+    L.b_off = kADepth * L.a_stage;
+    L.stg_off = L.b_off + b_depth * L.b_stage;
+    L.raw_off = L.stg_off + kStgBufs * kStgBytes;
+    L.bar_off = L.raw_off + raw_depth * L.raw_stage;
     L.total = L.bar_off + 512;
     return L;
 }
 
-// Ring depths for MMA width nb: activations 3 deep at nb >= 192, else 4; the
-// int8 ring takes what is left, up to 8. False when fewer than 2 fit.
+// Ring depths for MMA width nb: activations 2 deep at nb >= 192 (they come
+// from L2), 3 at nb >= 128, else 4; the int8 ring takes what is left, up to
+// 8. False when fewer than 2 fit.
 bool tc_depths(int nb, int& raw_depth, int& b_depth) {
     const int b_stage = (nb * 128 + 1023) & ~1023;
-    b_depth = nb >= 192 ? 3 : 4;
-    const int avail = kSmemBudget - 1024 - 512 - kADepth * 2 * kATileBytes - b_depth * b_stage;
-    raw_depth = avail / (2 * kSlabBytes);
+    const int ts = tc_tile_slabs(nb);
+    b_depth = nb >= 192 ? 2 : (nb >= 128 ? 3 : 4);
+    const int avail = kSmemBudget - 1024 - 512 - kADepth * ts * kATileBytes - b_depth * b_stage - kStgBufs * kStgBytes;
+    raw_depth = avail / (ts * kSlabBytes);
     if (raw_depth > kMaxDepth) raw_depth = kMaxDepth;
     return raw_depth >= 2;
 }
@@ -190,9 +208,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_q8_tc_kernel(TcParams p) {
     uint64_t* b_empty = bars + 3 * kMaxDepth;     // MMA commit
     uint64_t* a_ready = bars + 4 * kMaxDepth;     // 4 dequant warps
     uint64_t* a_empty = a_ready + kADepth;        // MMA commit
-    uint64_t* acc_full = a_empty + kADepth;       // MMA commit after a tile
-    uint64_t* acc_empty = acc_full + 1;           // 4 epilogue warps
-    uint64_t* drain = acc_empty + 1;              // final MMA commit before TMEM is freed
+    uint64_t* acc_full = a_empty + kADepth;       // [2] MMA commit after a tile (per TMEM buffer)
+    uint64_t* acc_empty = acc_full + 2;           // [2] 4 epilogue warps
+    uint64_t* drain = acc_empty + 2;              // final MMA commit before TMEM is freed
     uint64_t* stg_full = drain + 1;               // 4 epilogue staging buffers: 128 writers
     uint64_t* stg_free = stg_full + 4;            // 128 readers done with the buffer
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(stg_free + 4);
@@ -206,9 +224,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_q8_tc_kernel(TcParams p) {
     const int units = p.k_splits > 1 ? p.n_slabs * p.k_splits : p.n_slabs;
     const int s_lo = (int)((long long)blockIdx.x * units / gridDim.x);
     const int s_hi = (int)((long long)(blockIdx.x + 1) * units / gridDim.x);
-    const int my_tiles = p.k_splits > 1 ? s_hi - s_lo : (s_hi - s_lo + 1) / 2;
-    const uint32_t tmem_cols = (uint32_t)(2 * p.nb <= 32 ? 32 : (2 * p.nb <= 64 ? 64 : (2 * p.nb <= 128 ? 128 :
-                                          (2 * p.nb <= 256 ? 256 : 512))));
+    const int ts = L.ts;
+    const int my_tiles = p.k_splits > 1 ? s_hi - s_lo : (s_hi - s_lo + ts - 1) / ts;
+    // Two accumulator tiles of ts x nb columns each.
+    const int acc_cols = ts * p.nb;
+    const uint32_t tmem_cols = (uint32_t)(2 * acc_cols <= 32 ? 32 : (2 * acc_cols <= 64 ? 64 :
+                                          (2 * acc_cols <= 128 ? 128 : (2 * acc_cols <= 256 ? 256 : 512))));
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kMaxDepth; ++s) {
@@ -221,8 +242,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_q8_tc_kernel(TcParams p) {
             mbar_init(a_ready + s, 4);
             mbar_init(a_empty + s, 1);
         }
-        mbar_init(acc_full, 1);
-        mbar_init(acc_empty, 4);
+        for (int s = 0; s < 2; ++s) {
+            mbar_init(acc_full + s, 1);
+            mbar_init(acc_empty + s, 4);
+        }
         mbar_init(drain, 1);
         for (int s = 0; s < 4; ++s) {
             mbar_init(stg_full + s, 128);
@@ -264,7 +287,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_q8_tc_kernel(TcParams p) {
                         break;
                     }
                     if (*abort_flag) break;
-                    uint8_t* st = base + L.raw_off + s * 2 * kSlabBytes;
+                    uint8_t* st = base + L.raw_off + s * L.raw_stage;
                     mbar_arrive_expect_tx(raw_full + s, (uint32_t)(ns * kSlabBytes));
                     for (int j = 0; j < ns; ++j)
                         bulk_g2s(st + j * kSlabBytes, p.wt + ((size_t)(slab0 + j) * nkb + kb) * kSlabBytes,
@@ -312,7 +335,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_q8_tc_kernel(TcParams p) {
             for (int t = 0; t < my_tiles && !*abort_flag; ++t) {
                 const TcTile T = tc_tile(p, s_lo, s_hi, t, nkb);
                 const int ns = T.ns;
-                if (t > 0 && !mbar_wait(acc_empty, (t - 1) & 1)) {
+                const uint32_t acc = tmem + (uint32_t)((t & 1) * acc_cols);
+                // Buffer t & 1 was last drained by the epilogue of tile t - 2.
+                if (t >= 2 && !mbar_wait(acc_empty + (t & 1), ((t >> 1) + 1) & 1)) {
                     report_timeout(p.status);
                     *abort_flag = 1;
                     break;
@@ -326,14 +351,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_q8_tc_kernel(TcParams p) {
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t a0 = smem_u32(base + L.a_off + sa * 2 * kATileBytes);
+                    const uint32_t a0 = smem_u32(base + L.a_off + sa * L.a_stage);
                     const uint32_t b0 = smem_u32(base + L.b_off + sb * L.b_stage);
 #pragma unroll
                     for (int j = 0; j < 2; ++j) {
                         if (j < ns) {
 #pragma unroll
                             for (int kk = 0; kk < kKB / 16; ++kk)
-                                mma_f16(tmem + (uint32_t)(j * p.nb), sw128_desc(a0 + j * kATileBytes + kk * 32),
+                                mma_f16(acc + (uint32_t)(j * p.nb), sw128_desc(a0 + j * kATileBytes + kk * 32),
                                         sw128_desc(b0 + kk * 32), idesc, (kb > T.kb0 || kk > 0) ? 1 : 0);
                         }
                     }
@@ -341,22 +366,20 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_q8_tc_kernel(TcParams p) {
                     mma_commit(b_empty + sb);
                 }
                 if (*abort_flag) break;
-                mma_commit(acc_full);
+                mma_commit(acc_full + (t & 1));
             }
             // Every MMA this thread issued has completed before TMEM is freed.
             mma_commit(drain);
             if (!mbar_wait(drain, 0)) report_timeout(p.status);
         }
-    } else {
-        // ----------------------------------------- dequantise + epilogue (2..5)
+    } else if (warp >= 2 && warp <= 5) {
+        // ------------------------------------------ dequantise int8 -> fp16 (2..5)
         const int dw = warp - 2;              // 0..3
         const int dt = dw * 32 + lane;        // 0..127
-        const int quad = warp & 3;            // TMEM lane quadrant this warp may access
         int it = 0;
-        int chunk = 0;                        // staged epilogue chunks so far (all tiles)
         for (int t = 0; t < my_tiles && !*abort_flag; ++t) {
             const TcTile T = tc_tile(p, s_lo, s_hi, t, nkb);
-            const int slab0 = T.slab0, ns = T.ns;
+            const int ns = T.ns;
             for (int kb = T.kb0; kb < T.kb1; ++kb, ++it) {
                 const int sr = it % RD, sa = it % kADepth;
                 if (!mbar_wait(raw_full + sr, (it / RD) & 1) ||
@@ -365,8 +388,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_q8_tc_kernel(TcParams p) {
                     *abort_flag = 1;
                     break;
                 }
-                const uint8_t* st = base + L.raw_off + sr * 2 * kSlabBytes;
-                uint8_t* a_t = base + L.a_off + sa * 2 * kATileBytes;
+                const uint8_t* st = base + L.raw_off + sr * L.raw_stage;
+                uint8_t* a_t = base + L.a_off + sa * L.a_stage;
                 // Thread dt converts 16 int8 (chunk dt & 3 of row dt >> 2) of
                 // each 32-row group: conflict-free reads and swizzled writes.
 #pragma unroll 2
@@ -392,12 +415,20 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_q8_tc_kernel(TcParams p) {
                     mbar_arrive(a_ready + sa);
                 }
             }
-            if (*abort_flag) break;
-            // Epilogue: wait for the tile's accumulators, then each thread owns
+        }
+    } else {
+        // ------------------------------------------------------ epilogue (7..10)
+        const int dw = warp - 7;              // 0..3: output rows dw, dw + 4, ... of a staged chunk
+        const int quad = warp & 3;            // TMEM lane quadrant this warp may access
+        int chunk = 0;                        // staged epilogue chunks so far (all tiles)
+        for (int t = 0; t < my_tiles && !*abort_flag; ++t) {
+            const TcTile T = tc_tile(p, s_lo, s_hi, t, nkb);
+            const int slab0 = T.slab0, ns = T.ns;
+            // Wait for the tile's accumulators (TMEM buffer t & 1), then each thread owns
             // one weight row (TMEM lane) of each 128-row slab. The outputs and
             // the bias belong to the stream order: after the previous kernel.
             griddep_wait();
-            if (!mbar_wait(acc_full, t & 1)) {
+            if (!mbar_wait(acc_full + (t & 1), (t >> 1) & 1)) {
                 report_timeout(p.status);
                 *abort_flag = 1;
                 break;
@@ -420,16 +451,16 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_q8_tc_kernel(TcParams p) {
                                      : reinterpret_cast<const float*>(p.scales)[n];
                     bb = p.bias && T.first ? p.beta * p.bias[n] : 0.0f;
                 }
-                const uint32_t lane_addr = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(j * p.nb);
+                const uint32_t lane_addr =
+                    tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)((t & 1) * acc_cols + j * p.nb);
                 const int cnt = p.n - slab * kTM < kTM ? p.n - slab * kTM : kTM;  // valid outputs of the slab
                 if (p.bulk_out && ((cnt * esz) & 15) == 0) {
                     // Staged path: 32 output rows at a time are transposed
-                    // through shared memory (the idle fp16 A ring: the tile's
-                    // MMAs have retired and the next tile's dequantisation
-                    // has not started), then each warp writes whole 128-output
-                    // row segments with 16-byte (8-byte for fp16) stores: a
-                    // quarter of the store instructions of the lane-per-output
-                    // layout TMEM delivers. Four 16 KB buffers rotate.
+                    // through shared memory (four 16 KB buffers of the
+                    // epilogue's own, rotating), then each warp writes whole
+                    // 128-output row segments with 16-byte (8-byte for fp16)
+                    // stores: a quarter of the store instructions of the
+                    // lane-per-output layout TMEM delivers.
                     for (int c0 = 0; c0 < mrows && !*abort_flag; c0 += 32, ++chunk) {
                         const int nrows = mrows - c0 < 32 ? mrows - c0 : 32;
                         const int buf = chunk & 3;
@@ -447,7 +478,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_q8_tc_kernel(TcParams p) {
                             if (nrows > 16) tmem_ld16(lane_addr + (uint32_t)(hi_cols + c0 + 16), q + 16);
                         }
                         tmem_wait();
-                        float* stg = reinterpret_cast<float*>(base + L.a_off + buf * (32 * kTM * 4));
+                        float* stg = reinterpret_cast<float*>(base + L.stg_off + buf * kStgBytes);
 #pragma unroll
                         for (int i = 0; i < 32; ++i) {
                             float acc = __uint_as_float(r[i]);
@@ -505,15 +536,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_q8_tc_kernel(TcParams p) {
                     }
                 }
             }
-            // The staging buffers alias the A ring: every copy must have read
-            // them before this tile's dequantisation of the next one starts.
-            if (chunk > 0 && !mbar_wait(stg_free + ((chunk - 1) & 3), (uint32_t)((chunk - 1) >> 2) & 1)) {
-                report_timeout(p.status);
-                *abort_flag = 1;
-            }
+            // Every TMEM load of this tile has completed (tmem_wait): the MMA
+            // warp may reuse the buffer for tile t + 2.
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(acc_empty);
+            if (lane == 0) mbar_arrive(acc_empty + (t & 1));
         }
     }
 
