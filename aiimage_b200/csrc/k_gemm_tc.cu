@@ -26,7 +26,7 @@
 // stores overlap the next tile's weight stream, dequantisation and MMAs.
 // Three shared-memory rings decouple the latencies: int8 weights (up to 8
 // k-blocks deep, freed as soon as they are dequantised), fp16 A tiles (2
-// deep, freed by the MMA commit) and activations (2-4 deep, freed by the MMA
+// deep, freed by the MMA commit) and activations (3-4 deep, freed by the MMA
 // commit). Warp roles: 0 int8 bulk-copy producer, 1 MMA issuer and TMEM
 // owner, 2-5 dequantise int8 -> fp16 into the swizzled A tiles, 6 activation
 // bulk-copy producer, 7-10 the epilogue (TMEM -> registers -> staging buffers
@@ -120,13 +120,12 @@ __host__ __device__ inline TcLayout tc_layout(int nb, int raw_depth, int b_depth
     return L;
 }
 
-// Ring depths for MMA width nb: activations 2 deep at nb >= 192 (they come
-// from L2), 3 at nb >= 128, else 4; the int8 ring takes what is left, up to
-// 8. False when fewer than 2 fit.
+// Ring depths for MMA width nb: activations 3 deep at nb >= 128, else 4; the
+// int8 ring takes what is left, up to 8. False when fewer than 2 fit.
 bool tc_depths(int nb, int& raw_depth, int& b_depth) {
     const int b_stage = (nb * 128 + 1023) & ~1023;
     const int ts = tc_tile_slabs(nb);
-    b_depth = nb >= 192 ? 2 : (nb >= 128 ? 3 : 4);
+    b_depth = nb >= 128 ? 3 : 4;
     const int avail = kSmemBudget - 1024 - 512 - kADepth * ts * kATileBytes - b_depth * b_stage - kStgBufs * kStgBytes;
     raw_depth = avail / (ts * kSlabBytes);
     if (raw_depth > kMaxDepth) raw_depth = kMaxDepth;
