@@ -344,7 +344,14 @@ static int gemm_common(aexis_ctx* ctx, const void* a, int a_dtype, int lda, int 
         return aexis_fail(ctx, AEXIS_E_UNSUPPORTED, "dtype a=%d y=%d", a_dtype, y_dtype);
     int rc = bind(ctx);
     if (rc) return rc;
-    if (ctx->act_quant) {
+    // W8A8 on the batch-1 tensor-core GEMV: the kernel stages the codes itself
+    // (no extra launch). Every other path reads codes written by one more kernel.
+    const bool tc_path = m >= kTcMinRows && gemm_tc_supported(w, m, AEXIS_F16);
+    const bool fused_codes = ctx->act_quant && !tc_path && gemv_mma_supported(w, a_dtype);
+    if (fused_codes) {
+        if (epi == EPI_STORE) beta = beta / ctx->act_scale;
+        alpha = alpha * ctx->act_scale;
+    } else if (ctx->act_quant) {
         // W8A8: the GEMM reads the integer codes q - zp (fp16, exact) instead of
         // the activations and the scale moves into the epilogue:
         //   alpha*(beta*bias + sum (q-zp)*s*W) = (alpha*s)*((beta/s)*bias + sum (q-zp)*W)
@@ -397,6 +404,12 @@ static int gemm_common(aexis_ctx* ctx, const void* a, int a_dtype, int lda, int 
     g.beta = beta;
     g.y_dtype = y_dtype;
     g.epilogue = epi;
+    if (fused_codes) {
+        g.act_quant = 1;
+        g.act_scale = ctx->act_scale;
+        g.act_zero_point = ctx->act_zero_point;
+        g.act_unsigned = ctx->act_unsigned;
+    }
     // Programmatic dependent launch: the GEMV kernels read only the (immutable,
     // library-owned) weights before waiting on the previous kernel of the
     // stream, so their weight streaming overlaps that kernel's tail; every read

@@ -103,6 +103,10 @@ struct GemvArgs {
     unsigned long long* argmax_key = nullptr;  // EPI_LOGITS_ARGMAX target
     int* status = nullptr;             // context status word (bounded-wait timeouts)
     bool pdl = false;                  // launch with programmatic dependent launch
+    // W8A8: stage the activation codes (aexis_act_code) instead of x (gemv_mma only).
+    int act_quant = 0;
+    float act_scale = 1.0f;
+    int act_zero_point = 0, act_unsigned = 0;
 };
 
 // y = W x for one activation row; picks the fast streaming kernel when the
@@ -216,6 +220,18 @@ cudaError_t launch_gated_delta_rule(const float* a_log, const float* dt_bias, co
 __device__ __forceinline__ float aexis_load_act(const void* p, int dtype, long long i) {
     return dtype == AEXIS_F16 ? __half2float(reinterpret_cast<const __half*>(p)[i])
                               : reinterpret_cast<const float*>(p)[i];
+}
+// W8A8 activation code (AexisQuantizeGemmActivationForInt8, HLSL Pack4Matmul:
+// 792-800): q = clamp(round(v / scale) + zp) over [-128, 127] or [0, 255]
+// (unsigned), rounding half to even; returns the integer q - zp, which the
+// GEMMs multiply exactly and scale by `scale` in their epilogue.
+__device__ __forceinline__ float aexis_act_code(float v, float scale, int zp, int is_unsigned) {
+    float qf = rintf(__fdiv_rn(v, scale));
+    qf = fminf(fmaxf(qf, -1.0e6f), 1.0e6f);   // clamp before the integer conversion
+    int q = (int)qf + zp;
+    const int lo = is_unsigned ? 0 : -128, hi = is_unsigned ? 255 : 127;
+    q = q < lo ? lo : (q > hi ? hi : q);
+    return (float)(q - zp);
 }
 __device__ __forceinline__ void aexis_store_out(void* p, int dtype, long long i, float v) {
     if (dtype == AEXIS_F16) reinterpret_cast<__half*>(p)[i] = __float2half_rn(v);

@@ -30,6 +30,9 @@ struct StreamParams {
     unsigned long long* argmax_key;
     int* status;
     uint32_t zero;   // 0, opaque to the compiler (keeps decode constants in registers)
+    int act_quant;   // W8A8 codes instead of x (gemv_mma_kernel)
+    float act_scale;
+    int act_zero_point, act_unsigned;
 };
 
 // Output of one row (lane-local), shared with the register-streaming kernel's

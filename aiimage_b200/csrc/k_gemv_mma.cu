@@ -267,6 +267,7 @@ __global__ void __launch_bounds__(kMmaThreads, 2) gemv_mma_kernel(MmaParams mp) 
                 const int e = q * 32 + lane;
                 float v = aexis_load_act(p.x, p.a_dtype, e);
                 if (norm) v = v * inv * p.norm_gamma[e];
+                if (p.act_quant) v = aexis_act_code(v, p.act_scale, p.act_zero_point, p.act_unsigned);
                 float amax = fabsf(v);
 #pragma unroll
                 for (int o = 16; o >= 1; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
@@ -307,6 +308,7 @@ __global__ void __launch_bounds__(kMmaThreads, 2) gemv_mma_kernel(MmaParams mp) 
             for (int e = tid; e < p.k; e += kMW * 32) {
                 float v = aexis_load_act(p.x, p.a_dtype, e);
                 if (norm) v = v * inv * p.norm_gamma[e];
+                if (p.act_quant) v = aexis_act_code(v, p.act_scale, p.act_zero_point, p.act_unsigned);
                 int slot;
                 if constexpr (BITS == 4) {
                     slot = q4_x_slot(e);
@@ -681,6 +683,10 @@ cudaError_t launch_gemv_mma(const GemvArgs& a, int sm_count, cudaStream_t stream
     sp.pos_ptr = a.pos_ptr;
     sp.argmax_key = a.argmax_key;
     sp.status = a.status;
+    sp.act_quant = a.act_quant;
+    sp.act_scale = a.act_scale;
+    sp.act_zero_point = a.act_zero_point;
+    sp.act_unsigned = a.act_unsigned;
     mp.nkb = w->k / 16;
     mp.gk = w->kind == WK_Q4 && w->group > 0 ? w->group / 16 : mp.nkb;
     mp.tile_wbytes = tile_wbytes(w);

@@ -297,16 +297,10 @@ __global__ void swiglu_kernel(const float* g, const float* u, int n, float* y) {
 __global__ void act_quant_i8_kernel(const void* a, int a_dtype, int lda, int m, int k, float scale, int zp,
                                     int is_unsigned, __half* out) {
     const long long total = (long long)m * k;
-    const int lo = is_unsigned ? 0 : -128, hi = is_unsigned ? 255 : 127;
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
          i += (long long)gridDim.x * blockDim.x) {
         const long long r = i / k, c = i - r * k;
-        const float v = aexis_load_act(a, a_dtype, r * lda + c);
-        float qf = rintf(__fdiv_rn(v, scale));
-        qf = fminf(fmaxf(qf, -1.0e6f), 1.0e6f);   // clamp before the integer conversion
-        int q = (int)qf + zp;
-        q = q < lo ? lo : (q > hi ? hi : q);
-        out[i] = __int2half_rn(q - zp);
+        out[i] = __float2half_rn(aexis_act_code(aexis_load_act(a, a_dtype, r * lda + c), scale, zp, is_unsigned));
     }
 }
 

@@ -339,6 +339,13 @@ def run_gpu(args):
         except Exception as e:
             config5 = {"error": f"{type(e).__name__}: {e}"}
 
+    w8a8 = None
+    if not args.skip_w8a8:
+        try:
+            w8a8 = bench_w8a8(ops, peak)
+        except Exception as e:
+            w8a8 = {"error": f"{type(e).__name__}: {e}"}
+
     sampler = None
     if not args.skip_sampler:
         try:
@@ -387,6 +394,7 @@ def run_gpu(args):
             "config5": config5,
             "linear_attention": linear_attn,
             "sampler": sampler,
+            "w8a8": w8a8,
             "cpu_baseline": cpu,
             "e2e": {"value": round(e2e_steps * STEP_BYTES * world / e2e_s / 1e9, 2), "unit": "GB/s",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
@@ -545,6 +553,57 @@ def bench_config4(ops, peak, world: int, rank: int, steps: int = 128, total_seqs
             "bytes_per_step_mean": int(byts / n_steps), "GB/s": round(byts / dev_s / 1e9, 1),
             "frac": round(byts / dev_s / 1e9 / peak, 3), "first_ids": first_ids,
             "timing": "device (CUDA events around each batch's generate), max over ranks"}
+
+
+def bench_w8a8(ops, peak):
+    """W8A8 activation fake-quantisation (SetInt8ActivationQuantization) on the Q8 paths: the config-1 GEMV
+    (K 1024, N 3584, batch 1) and the same weights at 32 rows (tensor cores), each timed with and without the
+    activation codes. Weights rotate over copies larger than L2 (GEMV) inside a CUDA graph; CUDA events."""
+    import torch
+    import types
+    k, n = 1024, 3584
+    p, s = synth.q8_weights(n, k, seed=0)
+    b = synth.gemv_bytes(8, n, k)
+    copies = max(2, -(-4 * L2_BYTES // b))
+    ws = [ops.new_int8_weight_only_upload(p, s, n, k) for _ in range(copies)]
+    out = {}
+    for rows in (1, 32):
+        x = torch.from_numpy(synth.activations(k, seed=0, m=rows)).cuda()
+        y = torch.zeros((rows, n), dtype=torch.float16, device="cuda")
+        for quant in (False, True):
+            ops.set_int8_activation_quantization(types.SimpleNamespace(mode="Int8W8A8", activation_scale=0.03,
+                                                                       activation_zero_point=0) if quant else None)
+
+            def call(c):
+                ops.set_int4_gemm_weights(None)
+                ops.set_int8_gemm_weights(ws[c])
+                ops.gemm2d_pack4_linear_texture_a(x, None, rows, n, k, True, 1.0, 1.0, False, 4, y)
+
+            for c in range(copies):
+                call(c)
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            st = torch.cuda.Stream()
+            st.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(st):
+                with torch.cuda.graph(g, stream=st):
+                    for c in range(copies):
+                        call(c)
+            torch.cuda.current_stream().wait_stream(st)
+            g.replay()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(3):
+                g.replay()
+            e1.record()
+            e1.synchronize()
+            t = e0.elapsed_time(e1) / 1e3 / (3 * copies)
+            out[f"rows{rows}_{'w8a8' if quant else 'w8a16'}_us"] = round(t * 1e6, 3)
+    ops.set_int8_activation_quantization(None)
+    out["workload"] = "Q8 K1024 N3584 (config 1 weights), activation scale 0.03, zero point 0"
+    out["timing"] = "CUDA events over graph replays, weights rotated over copies > L2"
+    return out
 
 
 def bench_sampler(ops, peak):
@@ -759,7 +818,8 @@ def run_only(args):
     --only tcgemm     the config-5 lm_head GEMM alone (M=256, tensor cores)
     --only config4    one config-4 batch (32 sequences, --new-tokens steps)
     --only linear_attention  the Qwen3.5 GatedDeltaRule / ShortConv decode kernels
-    --only sampler    the device sampler (Qwen35Sampler defaults) at 1 and 256 rows"""
+    --only sampler    the device sampler (Qwen35Sampler defaults) at 1 and 256 rows
+    --only w8a8       the Q8 GEMV / 32-row GEMM with and without W8A8 activation codes"""
     import torch
     torch.cuda.set_device(0)
     from aiimage_b200.ops import AexisOps
@@ -771,6 +831,8 @@ def run_only(args):
         out = bench_linear_attention(ops, peak)
     elif args.only == "sampler":
         out = bench_sampler(ops, peak)
+    elif args.only == "w8a8":
+        out = bench_w8a8(ops, peak)
     elif args.only == "topk":
         m, vocab, k = 256, 151936, 50
         g = torch.Generator(device="cuda").manual_seed(5)
@@ -876,10 +938,11 @@ def main():
     ap.add_argument("--skip-config5", action="store_true", help="omit the config-5 lm_head measurement")
     ap.add_argument("--skip-config4", action="store_true", help="omit the config-4 batched decoder measurement")
     ap.add_argument("--skip-sampler", action="store_true", help="omit the device sampler measurement")
+    ap.add_argument("--skip-w8a8", action="store_true", help="omit the W8A8 GEMV/GEMM measurement")
     ap.add_argument("--skip-linear-attention", action="store_true",
                     help="omit the GatedDeltaRule / ShortConv decode measurement")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
-    ap.add_argument("--only", choices=["dominant", "decoder", "tcgemm", "config4", "topk", "linear_attention", "sampler"], help="profiling mode (see run_only)")
+    ap.add_argument("--only", choices=["dominant", "decoder", "tcgemm", "config4", "topk", "linear_attention", "sampler", "w8a8"], help="profiling mode (see run_only)")
     ap.add_argument("--prompt-len", type=int, default=512)
     ap.add_argument("--new-tokens", type=int, default=64)
     args = ap.parse_args()
