@@ -139,6 +139,10 @@ def dist_setup(n_gpus: int):
         import datetime
         import torch.distributed as dist
         os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        # NCCL's version banner goes to stdout, where rank 0's one JSON line must stand
+        # alone; an explicit request for more (INFO, e.g. to see NVLS) is kept.
+        if os.environ.get("NCCL_DEBUG", "").upper() in ("", "VERSION"):
+            os.environ["NCCL_DEBUG"] = "WARN"
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
