@@ -39,6 +39,8 @@ def run_batched(ops, w, x, n, out_dtype, bias=None, alpha=1.0, beta=1.0, tiled=F
     (128, 384, 256, "f32"),     # hi/lo split at the full MMA width (nb = 256)
     (7, 1001, 128, "f16"),      # odd row stride: direct stores instead of staged bulk copies
     (40, 1003, 192, "f32"),
+    (150, 76000, 128, "f16"),   # nb = 160: one slab per tile, four tiles per CTA (both TMEM buffers twice)
+    (64, 151936, 128, "f16"),   # nb = 64: two slabs per tile, four tiles per CTA
 ])
 def test_tc_gemm_matches_oracle(ops, oracle, m, n, k, act):
     import torch
