@@ -56,6 +56,8 @@ def test_w8a8_known_answer(w8a8):
     (8, 3, 1024, 512, True, False),       # several rows through the GEMV
     (8, 32, 1024, 3584, False, False),    # tcgen05 batched GEMM
     (8, 256, 1024, 4096, True, True),     # tcgen05, lm_head epilogue, fp32 activations
+    (8, 1, 96, 50, True, False),          # odd shape: codes from the separate kernel, generic GEMV
+    (4, 2, 160, 72, False, True),
 ])
 @pytest.mark.parametrize("mode", ["signed", "unsigned", "zero_point"])
 def test_w8a8_gemm_against_oracle(w8a8, oracle, bits, m, k, n, x_f32, tiled, mode):
