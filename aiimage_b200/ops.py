@@ -22,13 +22,27 @@ def _ptr(t):
     return None if t is None else C.c_void_p(t.data_ptr())
 
 
-def _dtype_code(t) -> int:
+_DTYPES = None          # {torch dtype: ABI dtype code}, filled on first use
+_raw_stream = None      # device index -> raw cudaStream_t of torch's current stream
+
+
+def _torch_hooks():
+    """Looks up, once, what every call needs from torch: the dtype codes and a raw current-stream getter
+    (torch's internal one when present: a few hundred nanoseconds instead of a Stream object per call)."""
+    global _DTYPES, _raw_stream
     import torch
-    if t.dtype == torch.float32:
-        return F32
-    if t.dtype == torch.float16:
-        return F16
-    raise errors.NotSupportedError(f"dtype {t.dtype} (float32 or float16)")
+    _DTYPES = {torch.float32: F32, torch.float16: F16}
+    raw = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+    _raw_stream = raw if raw is not None else (lambda dev: torch.cuda.current_stream(dev).cuda_stream)
+
+
+def _dtype_code(t) -> int:
+    if _DTYPES is None:
+        _torch_hooks()
+    code = _DTYPES.get(t.dtype)
+    if code is None:
+        raise errors.NotSupportedError(f"dtype {t.dtype} (float32 or float16)")
+    return code
 
 
 def _np_ptr(a: np.ndarray):
@@ -104,8 +118,9 @@ class AexisOps:
 
     def _bind_stream(self):
         if self._use_torch_stream:
-            import torch
-            s = torch.cuda.current_stream(self.device).cuda_stream
+            if _raw_stream is None:
+                _torch_hooks()
+            s = _raw_stream(self.device)
             if s != self._bound_stream:
                 lib().aexis_cuda_set_stream(self.ctx, C.c_void_p(s))
                 self._bound_stream = s
