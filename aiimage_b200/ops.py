@@ -19,7 +19,8 @@ from .native import F16, F32, check, lib
 
 
 def _ptr(t):
-    return None if t is None else C.c_void_p(t.data_ptr())
+    # A plain int: every pointer parameter is declared c_void_p, and ctypes converts ints itself.
+    return None if t is None else t.data_ptr()
 
 
 _DTYPES = None          # {torch dtype: ABI dtype code}, filled on first use
