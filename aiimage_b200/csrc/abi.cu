@@ -591,6 +591,23 @@ AEXIS_API int aexis_cuda_topk(aexis_ctx* ctx, const float* logits, int rows, int
                                              ctx->stream), "topk launch");
 }
 
+AEXIS_API int aexis_cuda_topk_greedy_keys(aexis_ctx* ctx, const float* logits, int rows, int width, int ld, int k,
+                                          const float* top_vals, const int32_t* top_idx, int64_t index_offset,
+                                          uint64_t* keys) {
+    if (!ctx) return AEXIS_E_NULL;
+    if (!logits || !top_vals || !top_idx || !keys) return aexis_fail(ctx, AEXIS_E_NULL, "null pointer");
+    if (width <= 0 || rows <= 0) return aexis_fail(ctx, AEXIS_E_RANGE, "rows=%d width=%d", rows, width);
+    if (k < 1 || k > 64) return aexis_fail(ctx, AEXIS_E_RANGE, "k=%d (1..64)", k);
+    if (ld < width) return aexis_fail(ctx, AEXIS_E_SHAPE, "ld=%d < width", ld);
+    if (index_offset < 0 || index_offset + width > 0x7fffffffLL)
+        return aexis_fail(ctx, AEXIS_E_RANGE, "index_offset=%lld", (long long)index_offset);
+    int rc = bind(ctx);
+    if (rc) return rc;
+    return aexis_cuda_check(ctx, launch_topk_greedy_keys(logits, rows, ld, top_vals, top_idx, k, index_offset,
+                                                         reinterpret_cast<unsigned long long*>(keys), ctx->stream),
+                            "greedy keys launch");
+}
+
 AEXIS_API int aexis_cuda_topk_merge(aexis_ctx* ctx, const int32_t* gathered, int lists, int rows, int k,
                                     int shard_rows, int64_t* out_ids, float* out_vals, int32_t* out_idx) {
     if (!ctx) return AEXIS_E_NULL;

@@ -191,6 +191,9 @@ size_t topk_scratch_bytes(int rows, int width, int k, int sm_count);
 // Merge of the shards' packed argmax keys and top-k lists (k_topk.cu).
 cudaError_t launch_topk_shard_merge(const int32_t* gathered, int lists, int rows, int k, int shard_rows, long long* ids,
                                     float* vals, int32_t* idx, cudaStream_t s);
+// Greedy keys (aexis_argmax_key, global indices) from per-row top-k lists.
+cudaError_t launch_topk_greedy_keys(const float* logits, int rows, int ld, const float* vals, const int32_t* idx, int k,
+                                    long long offset, unsigned long long* keys, cudaStream_t s);
 cudaError_t launch_topk(const float* logits, int rows, int width, int ld, int k, float* vals, int32_t* idx,
                         void* scratch, int sm_count, cudaStream_t s);
 cudaError_t launch_embed(const int32_t* words, int count, const aexis_weights* table,

@@ -566,3 +566,35 @@ cudaError_t launch_topk_shard_merge(const int32_t* gathered, int lists, int rows
     if (lists < 1 || lists > kTkWarps || k < 1 || k > kTkMaxK) return cudaErrorInvalidValue;
     return launch_pdl(topk_shard_merge_kernel, dim3(rows), s, gathered, lists, rows, k, shard_rows, ids, vals, idx);
 }
+
+namespace {
+
+// Greedy key of each row from its top-k list (the list's first entry is the
+// row's largest value at its lowest index, -0 counted as +0, NaN never
+// listed), so no second pass over the logits is needed. The one case the
+// list cannot show is the ArgMax rule that a NaN at global index 0 wins
+// (AexisArgMaxPack4LinearMat, HLSL Pack4Matmul:645-686): the shard holding
+// index 0 reads that one element. An empty list (a row of NaN) gives key 0.
+__global__ void topk_greedy_keys_kernel(const float* __restrict__ logits, int rows, int ld,
+                                        const float* __restrict__ vals, const int32_t* __restrict__ idx, int k,
+                                        long long offset, unsigned long long* __restrict__ keys) {
+    griddep_wait();
+    griddep_launch();
+    const int r = blockIdx.x * blockDim.x + threadIdx.x;
+    if (r >= rows) return;
+    const int i0 = idx[(long long)r * k];
+    unsigned long long key = i0 >= 0 ? aexis_argmax_key(vals[(long long)r * k], (int)(offset + i0)) : 0ull;
+    if (offset == 0) {
+        const float x0 = logits[(long long)r * ld];
+        if (x0 != x0) key = aexis_argmax_key(x0, 0);
+    }
+    keys[r] = key;
+}
+
+}  // namespace
+
+cudaError_t launch_topk_greedy_keys(const float* logits, int rows, int ld, const float* vals, const int32_t* idx, int k,
+                                    long long offset, unsigned long long* keys, cudaStream_t s) {
+    return launch_pdl(topk_greedy_keys_kernel, dim3((rows + kTkThreads - 1) / kTkThreads), s, logits, rows, ld, vals,
+                      idx, k, offset, keys);
+}

@@ -60,6 +60,7 @@ SIGNATURES = {
     "aexis_cuda_embed": (i32, [vp, vp, i32, vp, vp, vp]),
     "aexis_cuda_swish": (i32, [vp, vp, i32, vp]),
     "aexis_cuda_swiglu": (i32, [vp, vp, vp, i32, vp]),
+    "aexis_cuda_topk_greedy_keys": (i32, [vp, vp, i32, i32, i32, i32, vp, vp, C.c_int64, vp]),
     "aexis_cuda_sample": (i32, [vp, vp, i32, i32, i32, vp, f32, f32, i32, f32, vp, vp]),
     "aexis_cuda_sample_history_add": (i32, [vp, vp, i32, i32, vp]),
     "aexis_cuda_short_conv": (i32, [vp, vp, vp, vp, vp, vp, i32, i32, i32, i32]),

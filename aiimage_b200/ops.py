@@ -290,6 +290,12 @@ class AexisOps:
         ld = ld if ld is not None else (logits.stride(0) if logits.dim() == 2 else width)
         self._call(lib().aexis_cuda_topk, _ptr(logits), rows, width, ld, k, _ptr(out_vals), _ptr(out_idx))
 
+    def topk_greedy_keys(self, logits, width, rows, k, top_vals, top_idx, index_offset, keys, ld=None):
+        """The shard's argmax keys (as argmax_keys) from its top-k lists, without re-reading the logits."""
+        ld = ld if ld is not None else (logits.stride(0) if logits.dim() == 2 else width)
+        self._call(lib().aexis_cuda_topk_greedy_keys, _ptr(logits), rows, width, ld, k, _ptr(top_vals), _ptr(top_idx),
+                   index_offset, _ptr(keys))
+
     def topk_merge(self, gathered, lists, rows, k, shard_rows, out_ids, out_vals, out_idx):
         """Merge of vocab shards' packed greedy keys and top-k lists (see
         aexis_cuda_topk_merge)."""

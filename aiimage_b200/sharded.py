@@ -3,9 +3,10 @@
 Rank r of G holds the contiguous lm_head rows [r*V/G, (r+1)*V/G) as a Q8 weight
 handle. One call:
   1. logits of the shard, [M, V/G] fp32, on the tensor cores (aexis_cuda_gemm);
-  2. per row the shard's argmax as a 64-bit key carrying the GLOBAL index
-     (aexis_cuda_argmax_keys) and the shard's top-k (aexis_cuda_topk, indices
-     shifted by the shard offset);
+  2. per row the shard's top-k (aexis_cuda_topk, indices shifted by the shard
+     offset), and from its first entry the shard's argmax as a 64-bit key
+     carrying the GLOBAL index (aexis_cuda_topk_greedy_keys: the same keys as
+     aexis_cuda_argmax_keys without a second pass over the logits);
   3. the keys and the top-k lists packed into one buffer, one all-gather of
      those buffers (NCCL over NVLink; gloo in the CPU tests), then one merge
      kernel (aexis_cuda_topk_merge): the largest key, and the k largest
@@ -87,17 +88,18 @@ class ShardedLmHead:
         logits = self.shard_logits(x, logits)
         if self.world == 1:
             keys = torch.empty(m, dtype=torch.int64, device=x.device)
-            self.ops.argmax_keys(logits, self.n, m, self.lo, keys)
             vals = torch.empty((m, k), dtype=torch.float32, device=x.device)
             idx = torch.empty((m, k), dtype=torch.int32, device=x.device)
             self.ops.top_k(logits, self.n, m, k, vals, idx)
+            self.ops.topk_greedy_keys(logits, self.n, m, k, vals, idx, self.lo, keys)
             return keys_to_ids(keys), vals, idx.to(torch.int64)
         # The shard's keys and top-k straight into one packed buffer, one
         # all-gather, one merge kernel.
         buf = torch.empty(packed_words(m, k), dtype=torch.int32, device=x.device)
         keys, vals, idx = pack_views(buf, m, k)
-        self.ops.argmax_keys(logits, self.n, m, self.lo, keys)
+        # One pass over the shard's logits: the greedy keys come from the top-k lists.
         self.ops.top_k(logits, self.n, m, k, vals, idx)
+        self.ops.topk_greedy_keys(logits, self.n, m, k, vals, idx, self.lo, keys)
         gathered = exchange(buf, self.group)
         ids = torch.empty(m, dtype=torch.int64, device=x.device)
         out_v = torch.empty((m, k), dtype=torch.float32, device=x.device)

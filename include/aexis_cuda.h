@@ -229,6 +229,16 @@ int aexis_cuda_argmax(aexis_ctx* ctx, const float* logits, int rows, int width, 
 int aexis_cuda_argmax_keys(aexis_ctx* ctx, const float* logits, int rows, int width, int ld,
                            int64_t index_offset, uint64_t* keys);
 
+/* The same keys as aexis_cuda_argmax_keys, from the shard's top-k lists of
+ * aexis_cuda_topk (top_vals/top_idx: device [rows, k], shard-local indices)
+ * instead of a second pass over the logits: the first list entry is the
+ * row's largest value at its lowest index (-0 counted as +0, NaN never
+ * listed). With index_offset 0 the call also reads logits[r][0], since a NaN
+ * there wins the reference's ArgMax. No single reference counterpart (the
+ * vocab-sharded lm_head; AexisArgMaxPack4LinearMat, HLSL Pack4Matmul:645-686). */
+int aexis_cuda_topk_greedy_keys(aexis_ctx* ctx, const float* logits, int rows, int width, int ld, int k,
+                                const float* top_vals, const int32_t* top_idx, int64_t index_offset,
+                                uint64_t* keys);
 /* Rows that aexis_cuda_argmax_static accepts in one call (the size of its
  * fixed key array: 4096 x 8 bytes, held on every GPU that loads the library). */
 #define AEXIS_ARGMAX_STATIC_MAX_ROWS 4096

@@ -346,3 +346,48 @@ def test_topk_shard_merge_matches_full_vocab(ops, oracle, world):
     full_keys = torch.zeros(rows, dtype=torch.int64, device="cuda")
     ops.argmax_keys(xc, vocab, rows, 0, full_keys)
     assert np.array_equal(host(ids), host(sharded.keys_to_ids(full_keys)))
+
+
+@pytest.mark.parametrize("world", [1, 3, 8])
+def test_topk_greedy_keys_match_argmax_keys(ops, world):
+    """aexis_cuda_topk_greedy_keys (the shard's argmax key from its top-k list) against aexis_cuda_argmax_keys
+    (a pass over the logits) on every shard: a NaN at global index 0 (wins) and at a shard's local 0 (does not),
+    a row of NaN, -0 before +0 at the maximum, ties, a row of -inf, shards narrower than k."""
+    import torch
+    from aiimage_b200 import sharded
+    rows, vocab, k = 9, 300 if world == 8 else 20003, 50
+    x = np.random.default_rng(40 + world).standard_normal((rows, vocab)).astype(np.float32)
+    per = (vocab + world - 1) // world
+    x[0, 0] = np.nan                                    # NaN at global index 0: ArgMax keeps index 0
+    x[1, per if world > 1 else 1] = np.nan              # NaN at the second shard's first element: never wins
+    x[2, :] = np.nan
+    x[3, :] = -1.0
+    x[3, 10], x[3, 20] = -0.0, 0.0                      # -0 first: equal to +0, the lower index wins
+    x[4, 7] = x[4, vocab - 2] = x[4].max() + 3          # tie across shards
+    x[5, :] = -np.inf
+    x[6, ::3] = np.nan
+    xc = cuda(x)
+    ids_a, ids_b = [], []
+    for r in range(world):
+        lo, hi = sharded.shard_range(vocab, world, r)
+        part = xc[:, lo:hi]
+        ka = torch.zeros(rows, dtype=torch.int64, device="cuda")
+        kb = torch.zeros(rows, dtype=torch.int64, device="cuda")
+        kk = min(k, hi - lo)
+        vals = torch.zeros((rows, kk), dtype=torch.float32, device="cuda")
+        idx = torch.zeros((rows, kk), dtype=torch.int32, device="cuda")
+        ops.argmax_keys(part, hi - lo, rows, lo, ka, ld=vocab)
+        ops.top_k(part, hi - lo, rows, kk, vals, idx, ld=vocab)
+        ops.topk_greedy_keys(part, hi - lo, rows, kk, vals, idx, lo, kb, ld=vocab)
+        a, b = host(ka).view(np.uint64), host(kb).view(np.uint64)
+        # Equal keys wherever the shard row holds a non-NaN value or global index 0; a shard row of NaN
+        # only (which can never win) gives key 0 here.
+        all_nan = np.isnan(x[:, lo:hi]).all(axis=1) & (lo > 0)
+        np.testing.assert_array_equal(a[~all_nan], b[~all_nan])
+        ids_a.append(a)
+        ids_b.append(b)
+    best_a = np.max(np.stack(ids_a), axis=0)
+    best_b = np.max(np.stack(ids_b), axis=0)
+    tok = lambda key: np.where(key == 0, 0, (0xFFFFFFFF - (key & np.uint64(0xFFFFFFFF))).astype(np.int64))
+    np.testing.assert_array_equal(tok(best_a), tok(best_b))
+    assert tok(best_b)[0] == 0 and tok(best_b)[2] == 0 and tok(best_b)[3] == 10 and tok(best_b)[5] == 0
