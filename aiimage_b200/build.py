@@ -16,7 +16,7 @@ ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 BUILD = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "libaexis_cuda.so")
-SOURCES = ["abi.cu", "k_gemv.cu", "k_gemv_stream.cu", "k_gemv_mma.cu", "k_misc.cu", "k_decoder.cu", "k_noalloc.cu", "k_gemm_tc.cu", "k_topk.cu", "k_batch.cu", "k_decoder_persist.cu", "k_batch_attn.cu", "k_recurrent.cu", "k_sample.cu"]
+SOURCES = ["abi.cu", "k_gemv.cu", "k_gemv_stream.cu", "k_gemv_mma.cu", "k_misc.cu", "k_decoder.cu", "k_noalloc.cu", "k_gemm_tc.cu", "k_topk.cu", "k_batch.cu", "k_decoder_persist.cu", "k_batch_attn.cu", "k_recurrent.cu", "k_sample.cu", "k_kvstate.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC,-fvisibility=hidden", "-Xptxas", "-v",
          "--expt-relaxed-constexpr"]

@@ -163,6 +163,7 @@ AEXIS_API int aexis_cuda_destroy(aexis_ctx* ctx) {
     if (ctx->scratch) cudaFree(ctx->scratch);
     if (ctx->act_q) cudaFree(ctx->act_q);
     if (ctx->samp) cudaFree(ctx->samp);
+    if (ctx->pack_a) cudaFree(ctx->pack_a);
     if (ctx->status) cudaFree(ctx->status);
     if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
     delete ctx;
@@ -455,6 +456,47 @@ AEXIS_API int aexis_cuda_gemm_tiled(aexis_ctx* ctx, const void* a, int a_dtype, 
                                     const aexis_weights* w, const float* bias, float alpha, float beta, void* y,
                                     int y_dtype, int ldy, int n) {
     return gemm_common(ctx, a, a_dtype, lda, m, k, w, bias, alpha, beta, y, y_dtype, ldy, n, EPI_STORE_TILED);
+}
+
+AEXIS_API int aexis_cuda_gemm_pack4a(aexis_ctx* ctx, const void* a, int a_dtype, int a_width, int a_height,
+                                     int a_slices, int m, int k, const aexis_weights* w, const float* bias,
+                                     float alpha, float beta, void* y, int y_dtype, int ldy, int n) {
+    if (!ctx) return AEXIS_E_NULL;
+    if (!a) return aexis_fail(ctx, AEXIS_E_NULL, "a is null");
+    if (m <= 0) return aexis_fail(ctx, AEXIS_E_RANGE, "m=%d", m);
+    if (k <= 0) return aexis_fail(ctx, AEXIS_E_RANGE, "k=%d", k);
+    if (a_width <= 0 || a_slices <= 0 || a_height < m)
+        return aexis_fail(ctx, AEXIS_E_SHAPE, "Pack4 input texture %dx%d with %d slices cannot hold %d rows",
+                          a_width, a_height, a_slices, m);
+    if (!valid_dtype(a_dtype)) return aexis_fail(ctx, AEXIS_E_UNSUPPORTED, "dtype a=%d", a_dtype);
+    // Every K value in slice 0: rows are row-major with a stride of 4*width.
+    if ((long long)a_width * 4 >= k)
+        return gemm_common(ctx, a, a_dtype, a_width * 4, m, k, w, bias, alpha, beta, y, y_dtype, ldy, n, EPI_STORE);
+    // Validate the GEMM itself before the gather runs.
+    if (!w) return aexis_fail(ctx, AEXIS_E_NULL, "b is null");
+    if (!y) return aexis_fail(ctx, AEXIS_E_NULL, "output is null");
+    if (n <= 0) return aexis_fail(ctx, AEXIS_E_RANGE, "n=%d", n);
+    if (w->n != n || w->k != k)
+        return aexis_fail(ctx, AEXIS_E_SHAPE, "weight is [%d, %d], call asks for n=%d k=%d", w->n, w->k, n, k);
+    int rc = bind(ctx);
+    if (rc) return rc;
+    const size_t need = (size_t)m * k * dsize(a_dtype);
+    if (need > ctx->pack_a_bytes) {
+        if (ctx->pack_a) {
+            cudaStreamSynchronize(ctx->stream);
+            cudaFree(ctx->pack_a);
+            ctx->pack_a = nullptr;
+            ctx->pack_a_bytes = 0;
+        }
+        const size_t sz = std::max<size_t>(need, 1 << 16);
+        rc = aexis_cuda_check(ctx, cudaMalloc(&ctx->pack_a, sz), "Pack4 input buffer");
+        if (rc) return rc;
+        ctx->pack_a_bytes = sz;
+    }
+    rc = aexis_cuda_check(ctx, launch_gather_pack4a(a, a_dtype, a_width, a_height, a_slices, m, k, ctx->pack_a,
+                                                    ctx->stream), "Pack4 input gather launch");
+    if (rc) return rc;
+    return gemm_common(ctx, ctx->pack_a, a_dtype, k, m, k, w, bias, alpha, beta, y, y_dtype, ldy, n, EPI_STORE);
 }
 
 // ------------------------------------------------------- pointwise layers

@@ -55,6 +55,10 @@ struct aexis_ctx {
     // Device sampler partials, candidates and penalised scores (grow-only).
     void* samp = nullptr;
     size_t samp_bytes = 0;
+    // Row-major copy of a Pack4 texture-array activation (aexis_cuda_gemm_pack4a
+    // with more than one slice; grow-only).
+    void* pack_a = nullptr;
+    size_t pack_a_bytes = 0;
 };
 
 // Records `msg` on the context and returns `code`.
@@ -203,6 +207,10 @@ cudaError_t launch_swiglu(const float* g, const float* u, int count, float* y, c
 // AexisQuantizeGemmActivationForInt8 codes: out[r*k + i] = (half)(clamp(rint(a/scale) + zp) - zp).
 cudaError_t launch_act_quant_i8(const void* a, int a_dtype, int lda, int m, int k, float scale, int zero_point,
                                 int is_unsigned, __half* out, cudaStream_t s);
+// Pack4 texture-array activation [slices][height][width][4] -> row-major [m][k]
+// (the inputPacked A of AexisGemm2DPack4LinearTextureAFromPack4).
+cudaError_t launch_gather_pack4a(const void* a, int a_dtype, int width, int height, int slices, int m, int k,
+                                 void* out, cudaStream_t s);
 // Device sampler (k_sample.cu). `topk_scratch` holds topk_scratch_bytes(rows, width, min(top_k, width)).
 size_t sample_scratch_bytes(int rows, int width, int sm_count, bool scores);
 cudaError_t launch_sample(const float* logits, int rows, int width, int ld, const uint32_t* history, float pen,

@@ -44,6 +44,15 @@ struct aexis_decoder {
     bool persist_packed = false;     // persist_stream matches the current weights
 };
 
+// One layer of one sequence's KV cache (fp16 [kvh][cap][D], rows swizzled
+// when swz) to and from Pack4 CDHW fp32 [w = D, h = rows, c = kvh]
+// (k_kvstate.cu). Export writes every texel, zero past len; import rounds
+// positions [0, len) to fp16.
+cudaError_t launch_kv_export(const __half* kc, const __half* vc, int kvh, int cap, int D, int swz, int len, int rows,
+                             float* k_out, float* v_out, cudaStream_t s);
+cudaError_t launch_kv_import(const float* k_in, const float* v_in, int kvh, int cap, int D, int swz, int len, int rows,
+                             __half* kc, __half* vc, cudaStream_t s);
+
 // The persistent greedy loop: whether it runs this decoder, and `nsteps`
 // greedy steps from the device state (ints[0] token, [1] position, [2]
 // output cursor) in one cooperative launch.

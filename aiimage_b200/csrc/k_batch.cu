@@ -789,6 +789,76 @@ AEXIS_API int aexis_cuda_batch_fill_context(aexis_batch* bt, int batch, const in
     return AEXIS_OK;
 }
 
+AEXIS_API int aexis_cuda_batch_set_positions(aexis_batch* bt, int batch, const int32_t* positions) {
+    if (!bt) return AEXIS_E_NULL;
+    aexis_ctx* ctx = bt->d->ctx;
+    if (!positions) return aexis_fail(ctx, AEXIS_E_NULL, "positions is null");
+    if (batch < 1 || batch > bt->max_batch)
+        return aexis_fail(ctx, AEXIS_E_RANGE, "batch %d (1..%d)", batch, bt->max_batch);
+    for (int i = 0; i < batch; ++i)
+        if (positions[i] < 0 || positions[i] >= bt->cap)
+            return aexis_fail(ctx, AEXIS_E_RANGE, "position %d of sequence %d outside [0, %d)", positions[i], i,
+                              bt->cap);
+    int rc = bbind(bt);
+    if (rc) return rc;
+    cudaStream_t s = ctx->stream;
+    cudaError_t e = cudaMemcpyAsync(bt->ints + 1 + bt->max_batch, positions, sizeof(int) * batch,
+                                    cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess) e = cudaMemsetAsync(bt->ints, 0, sizeof(int), s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    rc = aexis_cuda_check(ctx, e, "position upload");
+    if (rc) return rc;
+    bt->batch = batch;
+    for (int i = 0; i < batch; ++i) bt->host_pos[i] = positions[i];
+    return AEXIS_OK;
+}
+
+static int batch_kv_args(aexis_batch* bt, int seq, int layer, int rows, const void* k, const void* v) {
+    aexis_ctx* ctx = bt->d->ctx;
+    if (!k || !v) return aexis_fail(ctx, AEXIS_E_NULL, "K/V buffer is null");
+    if (seq < 0 || seq >= bt->max_batch)
+        return aexis_fail(ctx, AEXIS_E_RANGE, "sequence %d outside [0, %d)", seq, bt->max_batch);
+    if (layer < 0 || layer >= bt->d->cfg.n_layers)
+        return aexis_fail(ctx, AEXIS_E_RANGE, "layer %d outside [0, %d)", layer, bt->d->cfg.n_layers);
+    if (rows <= 0) return aexis_fail(ctx, AEXIS_E_RANGE, "rows=%d", rows);
+    return bbind(bt);
+}
+
+static size_t batch_kv_offset(const aexis_batch* bt, int seq, int layer) {
+    const auto& c = bt->d->cfg;
+    return (((size_t)layer * bt->max_batch + seq) * c.n_kv_heads) * bt->cap * c.head_dim;
+}
+
+AEXIS_API int aexis_cuda_batch_kv_export(aexis_batch* bt, int seq, int layer, int rows, float* k_out, float* v_out) {
+    if (!bt) return AEXIS_E_NULL;
+    int rc = batch_kv_args(bt, seq, layer, rows, k_out, v_out);
+    if (rc) return rc;
+    aexis_ctx* ctx = bt->d->ctx;
+    const int len = seq < bt->batch ? bt->host_pos[seq] : 0;
+    if (rows < len) return aexis_fail(ctx, AEXIS_E_SHAPE, "rows %d < sequence length %d", rows, len);
+    const auto& c = bt->d->cfg;
+    const size_t off = batch_kv_offset(bt, seq, layer);
+    return aexis_cuda_check(ctx, launch_kv_export(bt->kc + off, bt->vc + off, c.n_kv_heads, bt->cap, c.head_dim,
+                                                  bt->tc_attn ? 1 : 0, len, rows, k_out, v_out, ctx->stream),
+                            "kv export launch");
+}
+
+AEXIS_API int aexis_cuda_batch_kv_import(aexis_batch* bt, int seq, int layer, const float* k_in, const float* v_in,
+                                         int rows, int length) {
+    if (!bt) return AEXIS_E_NULL;
+    int rc = batch_kv_args(bt, seq, layer, rows, k_in, v_in);
+    if (rc) return rc;
+    aexis_ctx* ctx = bt->d->ctx;
+    if (length < 0 || length > rows || length >= bt->cap)
+        return aexis_fail(ctx, AEXIS_E_RANGE, "length %d outside [0, min(rows %d, capacity %d - 1)]", length, rows,
+                          bt->cap);
+    const auto& c = bt->d->cfg;
+    const size_t off = batch_kv_offset(bt, seq, layer);
+    return aexis_cuda_check(ctx, launch_kv_import(k_in, v_in, c.n_kv_heads, bt->cap, c.head_dim, bt->tc_attn ? 1 : 0,
+                                                  length, rows, bt->kc + off, bt->vc + off, ctx->stream),
+                            "kv import launch");
+}
+
 AEXIS_API int aexis_cuda_batch_generate(aexis_batch* bt, const int32_t* first_tokens, int steps, int32_t* out_tokens) {
     if (!bt) return AEXIS_E_NULL;
     aexis_ctx* ctx = bt->d->ctx;

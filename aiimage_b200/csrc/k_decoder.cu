@@ -737,6 +737,56 @@ AEXIS_API int aexis_cuda_decoder_position(const aexis_decoder* d, int32_t* out) 
     return AEXIS_OK;
 }
 
+AEXIS_API int aexis_cuda_decoder_set_position(aexis_decoder* d, int32_t position) {
+    if (!d) return AEXIS_E_NULL;
+    if (position < 0 || position > d->cfg.kv_capacity)
+        return aexis_fail(d->ctx, AEXIS_E_RANGE, "position %d outside [0, %d]", position, d->cfg.kv_capacity);
+    int rc = dbind(d);
+    if (rc) return rc;
+    const int ints[3] = {0, position, 0};
+    rc = aexis_cuda_check(d->ctx, cudaMemcpyAsync(d->ints, ints, sizeof(ints), cudaMemcpyHostToDevice, d->ctx->stream),
+                          "position upload");
+    if (!rc) rc = aexis_cuda_check(d->ctx, cudaStreamSynchronize(d->ctx->stream), "sync");
+    if (!rc) d->host_pos = position;
+    return rc;
+}
+
+static int kv_layer_args(aexis_decoder* d, int layer, int rows, const void* k, const void* v) {
+    if (!k || !v) return aexis_fail(d->ctx, AEXIS_E_NULL, "K/V buffer is null");
+    if (layer < 0 || layer >= d->cfg.n_layers)
+        return aexis_fail(d->ctx, AEXIS_E_RANGE, "layer %d outside [0, %d)", layer, d->cfg.n_layers);
+    if (rows <= 0) return aexis_fail(d->ctx, AEXIS_E_RANGE, "rows=%d", rows);
+    return dbind(d);
+}
+
+AEXIS_API int aexis_cuda_decoder_kv_export(aexis_decoder* d, int layer, int rows, float* k_out, float* v_out) {
+    if (!d) return AEXIS_E_NULL;
+    int rc = kv_layer_args(d, layer, rows, k_out, v_out);
+    if (rc) return rc;
+    if (rows < d->host_pos)
+        return aexis_fail(d->ctx, AEXIS_E_SHAPE, "rows %d < sequence length %d", rows, d->host_pos);
+    const auto& c = d->cfg;
+    const size_t per = (size_t)c.n_kv_heads * c.kv_capacity * c.head_dim;
+    return aexis_cuda_check(d->ctx, launch_kv_export(d->kcache + per * layer, d->vcache + per * layer, c.n_kv_heads,
+                                                     c.kv_capacity, c.head_dim, 0, d->host_pos, rows, k_out, v_out,
+                                                     d->ctx->stream), "kv export launch");
+}
+
+AEXIS_API int aexis_cuda_decoder_kv_import(aexis_decoder* d, int layer, const float* k_in, const float* v_in, int rows,
+                                           int length) {
+    if (!d) return AEXIS_E_NULL;
+    int rc = kv_layer_args(d, layer, rows, k_in, v_in);
+    if (rc) return rc;
+    const auto& c = d->cfg;
+    if (length < 0 || length > rows || length > c.kv_capacity)
+        return aexis_fail(d->ctx, AEXIS_E_RANGE, "length %d outside [0, min(rows %d, capacity %d)]", length, rows,
+                          c.kv_capacity);
+    const size_t per = (size_t)c.n_kv_heads * c.kv_capacity * c.head_dim;
+    return aexis_cuda_check(d->ctx, launch_kv_import(k_in, v_in, c.n_kv_heads, c.kv_capacity, c.head_dim, 0, length,
+                                                     rows, d->kcache + per * layer, d->vcache + per * layer,
+                                                     d->ctx->stream), "kv import launch");
+}
+
 AEXIS_API int aexis_cuda_decoder_prefill(aexis_decoder* d, const int32_t* tokens, int count, int32_t* next_token) {
     if (!d) return AEXIS_E_NULL;
     if (!tokens || !next_token) return aexis_fail(d->ctx, AEXIS_E_NULL, "tokens/next_token is null");

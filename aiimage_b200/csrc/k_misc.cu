@@ -304,6 +304,26 @@ __global__ void act_quant_i8_kernel(const void* a, int a_dtype, int lda, int m, 
     }
 }
 
+// A Pack4 texture-array activation (the inputPacked A of
+// AexisGemm2DPack4LinearTextureAFromPack4, HLSL Pack4Matmul:880-891,
+// 1106-1190) gathered into row-major [m][k] of the same dtype. Element
+// (row, kk) is lane kk & 3 of texel (x, row, slice) with pack = kk >> 2,
+// x = pack % width, slice = pack / width; the texel sits at
+// ((slice * height + row) * width + x) * 4. Packs past the last slice read 0
+// (the reference's loop stops there).
+template <typename T>
+__global__ void gather_pack4a_kernel(const T* a, int width, int height, int slices, int m, int k, T* out) {
+    const long long total = (long long)m * k;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+         i += (long long)gridDim.x * blockDim.x) {
+        const int r = (int)(i / k), kk = (int)(i - (long long)r * k);
+        const int pack = kk >> 2, x = pack % width, sl = pack / width;
+        T v = T(0.0f);
+        if (sl < slices) v = a[(((long long)sl * height + r) * width + x) * 4 + (kk & 3)];
+        out[i] = v;
+    }
+}
+
 // Bounded wait on a flag nothing sets: one thread polls it until
 // limit_cycles of SM clock pass, then records AEXIS_E_TIMEOUT in the status
 // word and returns (the path every bounded barrier wait takes when it gives up).
@@ -433,6 +453,16 @@ cudaError_t launch_act_quant_i8(const void* a, int a_dtype, int lda, int m, int 
                                 int is_unsigned, __half* out, cudaStream_t s) {
     act_quant_i8_kernel<<<grid_for((long long)m * k), kT, 0, s>>>(a, a_dtype, lda, m, k, scale, zero_point,
                                                                    is_unsigned, out);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_gather_pack4a(const void* a, int a_dtype, int width, int height, int slices, int m, int k,
+                                 void* out, cudaStream_t s) {
+    const int g = grid_for((long long)m * k);
+    if (a_dtype == AEXIS_F16)
+        gather_pack4a_kernel<__half><<<g, kT, 0, s>>>((const __half*)a, width, height, slices, m, k, (__half*)out);
+    else
+        gather_pack4a_kernel<float><<<g, kT, 0, s>>>((const float*)a, width, height, slices, m, k, (float*)out);
     return cudaGetLastError();
 }
 

@@ -9,7 +9,8 @@
 // aexis_cuda_argmax_static runs the same two-pass argmax with its keys in a
 // fixed array compiled into this library, needs no context, and allocates
 // nothing.
-#include <atomic>
+#include <cuda.h>
+
 #include <mutex>
 
 #include "aexis_internal.h"
@@ -22,24 +23,69 @@ namespace {
 // (AEXIS_ARGMAX_STATIC_MAX_ROWS * 8 bytes) until the process exits.
 __device__ __align__(256) unsigned long long g_static_keys[AEXIS_ARGMAX_STATIC_MAX_ROWS];
 
+// The array's device address belongs to one CUDA context: a host that makes
+// its own context current (cuCtxCreate) or resets the device gets a new copy
+// of the array at another address. The set-up below is therefore keyed by
+// the current context's ID (cuCtxGetId: unique over the process lifetime,
+// never reused), looked up through the runtime's driver entry point so the
+// library needs no link against the driver library.
 constexpr int kMaxDevices = 64;
-std::mutex g_setup_mutex;
-std::atomic<void*> g_keys_addr[kMaxDevices] = {};
-int g_sm_count[kMaxDevices] = {};
-
-// Per-device set-up, once, with that device current: the device address of
-// the key array (host code may not use g_static_keys itself; its host name
-// is only a stand-in) and the SM count used to size the grid.
-int setup_device(int dev) {
-    std::lock_guard<std::mutex> lock(g_setup_mutex);
-    if (g_keys_addr[dev].load()) return AEXIS_OK;
-    void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_static_keys) != cudaSuccess || !p) return AEXIS_E_CUDA;
+struct DeviceSetup {
+    unsigned long long ctx_id = 0;  // 0: not set up
+    void* keys = nullptr;
     int sms = 0;
-    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0)
-        return AEXIS_E_CUDA;
-    g_sm_count[dev] = sms;
-    g_keys_addr[dev].store(p);
+};
+std::mutex g_setup_mutex;
+DeviceSetup g_setup[kMaxDevices];
+
+typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
+typedef CUresult (*CtxGetIdFn)(CUcontext, unsigned long long*);
+CtxGetCurrentFn g_ctx_get_current = nullptr;
+CtxGetIdFn g_ctx_get_id = nullptr;
+
+// ID of the calling thread's current context, or 0 on failure. With no
+// context current yet (a caller that never used the runtime on this thread),
+// cudaSetDevice makes the device's primary context current first.
+unsigned long long current_context_id(int dev) {
+    if (!g_ctx_get_current || !g_ctx_get_id) {
+        void* f1 = nullptr;
+        void* f2 = nullptr;
+        cudaDriverEntryPointQueryResult q1 = cudaDriverEntryPointSymbolNotFound, q2 = q1;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f1, cudaEnableDefault, &q1) != cudaSuccess ||
+            cudaGetDriverEntryPoint("cuCtxGetId", &f2, cudaEnableDefault, &q2) != cudaSuccess ||
+            q1 != cudaDriverEntryPointSuccess || q2 != cudaDriverEntryPointSuccess || !f1 || !f2)
+            return 0;
+        g_ctx_get_current = reinterpret_cast<CtxGetCurrentFn>(f1);
+        g_ctx_get_id = reinterpret_cast<CtxGetIdFn>(f2);
+    }
+    CUcontext c = nullptr;
+    unsigned long long id = 0;
+    if (g_ctx_get_current(&c) != CUDA_SUCCESS) return 0;
+    if (!c && (cudaSetDevice(dev) != cudaSuccess || g_ctx_get_current(&c) != CUDA_SUCCESS || !c)) return 0;
+    if (g_ctx_get_id(c, &id) != CUDA_SUCCESS) return 0;
+    return id;
+}
+
+// Set-up for the current device and context, with that device current: the
+// device address of the key array (host code may not pass g_static_keys
+// itself to a kernel; its host name is only a stand-in) and the SM count used
+// to size the grid. Runs on the first call in each context.
+int setup_device(int dev, DeviceSetup* out) {
+    std::lock_guard<std::mutex> lock(g_setup_mutex);
+    const unsigned long long id = current_context_id(dev);
+    if (!id) return AEXIS_E_CUDA;
+    DeviceSetup& st = g_setup[dev];
+    if (st.ctx_id != id) {
+        void* p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_static_keys) != cudaSuccess || !p) return AEXIS_E_CUDA;
+        int sms = 0;
+        if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0)
+            return AEXIS_E_CUDA;
+        st.keys = p;
+        st.sms = sms;
+        st.ctx_id = id;
+    }
+    *out = st;
     return AEXIS_OK;
 }
 
@@ -53,16 +99,12 @@ AEXIS_API int aexis_cuda_argmax_static(const float* logits, int rows, int width,
     if (ld < width) return AEXIS_E_SHAPE;
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return AEXIS_E_CUDA;
-    void* keys = g_keys_addr[dev].load();
-    if (!keys) {
-        const int rc = setup_device(dev);
-        if (rc) return rc;
-        keys = g_keys_addr[dev].load();
-    }
+    DeviceSetup st;
+    const int rc = setup_device(dev, &st);
+    if (rc) return rc;
     // The same kernels as aexis_cuda_argmax: the keys are cleared on the
     // stream (cudaMemsetAsync allocates nothing), then max-reduced, decoded.
-    const cudaError_t e = launch_argmax(logits, rows, width, ld, out_idx,
-                                        static_cast<unsigned long long*>(keys), g_sm_count[dev],
-                                        static_cast<cudaStream_t>(cuda_stream));
+    const cudaError_t e = launch_argmax(logits, rows, width, ld, out_idx, static_cast<unsigned long long*>(st.keys),
+                                        st.sms, static_cast<cudaStream_t>(cuda_stream));
     return e == cudaSuccess ? AEXIS_OK : AEXIS_E_CUDA;
 }

@@ -117,6 +117,50 @@ class DecoderSession:
         self._check(lib().aexis_cuda_decoder_logits(self.h, _np(out)))
         return out
 
+    # -- state in the reference's layout (Qwen35DecoderState) -----------------
+    def kv_rows_floats(self, rows: int) -> int:
+        """Floats of one Pack4 CDHW cache texture [head_dim, rows, n_kv_heads]."""
+        c = self.cfg
+        return 4 * ((c.n_kv_heads + 3) // 4) * rows * c.head_dim
+
+    def kv_export(self, layer: int, k_out, v_out, rows: int):
+        """Layer `layer`'s K and V caches into device fp32 Pack4 CDHW tensors of `rows` rows
+        (aexis_cuda_decoder_kv_export); rows past the position are zero."""
+        self.ops._bind_stream()
+        self._check(lib().aexis_cuda_decoder_kv_export(self.h, int(layer), int(rows), k_out.data_ptr(),
+                                                       v_out.data_ptr()))
+
+    def kv_import(self, layer: int, k_in, v_in, rows: int, length: int):
+        """Positions [0, length) of layer `layer`'s caches from Pack4 CDHW tensors (rounded to fp16)."""
+        self.ops._bind_stream()
+        self._check(lib().aexis_cuda_decoder_kv_import(self.h, int(layer), k_in.data_ptr(), v_in.data_ptr(),
+                                                       int(rows), int(length)))
+
+    def set_position(self, position: int):
+        self.ops._bind_stream()
+        self._check(lib().aexis_cuda_decoder_set_position(self.h, int(position)))
+
+    def export_state(self, rows: int | None = None) -> dict:
+        """Qwen35DecoderState as the reference holds it: {"cache_k<i>", "cache_v<i>": Pack4 CDHW fp32
+        device tensors of `rows` (default: the position) rows, "sequence_length": the position}."""
+        import torch
+        pos = self.position
+        rows = max(pos, 1) if rows is None else int(rows)
+        state = {"sequence_length": pos, "rows": rows}
+        for layer in range(self.cfg.n_layers):
+            k = torch.empty(self.kv_rows_floats(rows), dtype=torch.float32, device=f"cuda:{self.ops.device}")
+            v = torch.empty_like(k)
+            self.kv_export(layer, k, v, rows)
+            state[f"cache_k{layer}"], state[f"cache_v{layer}"] = k, v
+        return state
+
+    def import_state(self, state: dict):
+        """Load a state of export_state's form; decoding continues at its sequence_length."""
+        length, rows = int(state["sequence_length"]), int(state["rows"])
+        for layer in range(self.cfg.n_layers):
+            self.kv_import(layer, state[f"cache_k{layer}"], state[f"cache_v{layer}"], rows, length)
+        self.set_position(length)
+
     def set_schedule(self, mode: int):
         """How generate runs its greedy steps: 0 (default) one CUDA graph per
         step, 1 one persistent kernel for the whole call, -1 1 where supported."""
@@ -176,6 +220,24 @@ class BatchSession:
         """As generate, without copying the tokens back (timing runs)."""
         t = np.ascontiguousarray(first_tokens, dtype=np.int32)
         self._check(lib().aexis_cuda_batch_generate(self.h, _np(t), int(steps), None))
+
+    def kv_export(self, seq: int, layer: int, k_out, v_out, rows: int):
+        """Sequence `seq`'s layer-`layer` K and V caches as Pack4 CDHW fp32 device tensors of `rows` rows."""
+        self.dec.ops._bind_stream()
+        self._check(lib().aexis_cuda_batch_kv_export(self.h, int(seq), int(layer), int(rows), k_out.data_ptr(),
+                                                     v_out.data_ptr()))
+
+    def kv_import(self, seq: int, layer: int, k_in, v_in, rows: int, length: int):
+        self.dec.ops._bind_stream()
+        self._check(lib().aexis_cuda_batch_kv_import(self.h, int(seq), int(layer), k_in.data_ptr(), v_in.data_ptr(),
+                                                     int(rows), int(length)))
+
+    def set_positions(self, positions):
+        """Sequences 0..len(positions)-1 become the batch, each continuing at positions[i]."""
+        p = np.ascontiguousarray(positions, dtype=np.int32)
+        self.dec.ops._bind_stream()
+        self._check(lib().aexis_cuda_batch_set_positions(self.h, p.size, _np(p)))
+        self.n = int(p.size)
 
     @property
     def positions(self) -> np.ndarray:

@@ -47,6 +47,7 @@ SIGNATURES = {
     "aexis_cuda_set_int8_activations": (i32, [vp, i32, f32, i32, i32]),
     "aexis_cuda_gemm": (i32, [vp, vp, i32, i32, i32, i32, vp, vp, f32, f32, vp, i32, i32, i32]),
     "aexis_cuda_gemm_tiled": (i32, [vp, vp, i32, i32, i32, i32, vp, vp, f32, f32, vp, i32, i32, i32]),
+    "aexis_cuda_gemm_pack4a": (i32, [vp, vp, i32, i32, i32, i32, i32, i32, vp, vp, f32, f32, vp, i32, i32, i32]),
     "aexis_cuda_rmsnorm": (i32, [vp, vp, i32, i32, i32, i32, vp, i32, f32, vp, i32]),
     "aexis_cuda_rope": (i32, [vp, vp, i32, i32, i32, vp, vp, i32, vp]),
     "aexis_cuda_kv_append": (i32, [vp, vp, i32, i32, i32, i32, vp, i32]),
@@ -77,6 +78,12 @@ SIGNATURES = {
     "aexis_cuda_decoder_generate": (i32, [vp, vp, i32, i32, vp]),
     "aexis_cuda_decoder_logits": (i32, [vp, vp]),
     "aexis_cuda_decoder_set_schedule": (i32, [vp, i32]),
+    "aexis_cuda_decoder_kv_export": (i32, [vp, i32, i32, vp, vp]),
+    "aexis_cuda_decoder_kv_import": (i32, [vp, i32, vp, vp, i32, i32]),
+    "aexis_cuda_decoder_set_position": (i32, [vp, C.c_int32]),
+    "aexis_cuda_batch_kv_export": (i32, [vp, i32, i32, i32, vp, vp]),
+    "aexis_cuda_batch_kv_import": (i32, [vp, i32, i32, vp, vp, i32, i32]),
+    "aexis_cuda_batch_set_positions": (i32, [vp, i32, vp]),
     "aexis_cuda_decoder_schedule": (i32, [vp, vp]),
     "aexis_cuda_selftest_wait": (i32, [vp, C.c_longlong]),
     "aexis_cuda_batch_create": (i32, [vp, i32, i32, i32, C.POINTER(vp)]),
@@ -95,6 +102,16 @@ def declared_functions() -> list[str]:
     text = open(HEADER).read()
     text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
     return sorted(set(re.findall(r"\b(aexis_(?:cuda_|quantize_)\w+)\s*\(", text)))
+
+
+def header_constant(name: str) -> int:
+    """An integer #define or enum value of include/aexis_cuda.h (e.g. AEXIS_E_RANGE)."""
+    text = re.sub(r"/\*.*?\*/", "", open(HEADER).read(), flags=re.S)
+    m = re.search(r"#define\s+" + name + r"\s+(-?\d+)\b", text) or re.search(r"\b" + name + r"\s*=\s*(-?\d+)\b",
+                                                                                text)
+    if not m:
+        raise KeyError(name)
+    return int(m.group(1))
 
 
 def lib():

@@ -210,7 +210,7 @@ class AexisOps:
         self._call(lib().aexis_cuda_weights_dequant, w.handle, _ptr(out))
 
     # -- linear -----------------------------------------------------------
-    def _gemm(self, fn, a, c, m, n, k, trans_b, alpha, beta, use_c, broadcast_type_c, output):
+    def _gemm_weights(self, a, c, trans_b, use_c, broadcast_type_c, output):
         if a is None:
             raise errors.ArgumentNullError("a")
         if output is None:
@@ -224,21 +224,54 @@ class AexisOps:
             raise errors.NotSupportedError("quantized Gemm weights are stored transB (output-channel major)")
         if use_c and broadcast_type_c != 4:
             raise errors.NotSupportedError("bias broadcast type 4 (per output column) only")
-        lda = a.stride(0) if a.dim() == 2 else k
+        return w
+
+    def _gemm(self, fn, a, c, m, n, k, trans_b, alpha, beta, use_c, broadcast_type_c, output, lda=None):
+        w = self._gemm_weights(a, c, trans_b, use_c, broadcast_type_c, output)
+        if lda is None:
+            lda = a.stride(0) if a.dim() == 2 else k
         ldy = output.stride(0) if output.dim() == 2 else n
         self._call(fn, _ptr(a), _dtype_code(a), lda, m, k, w.handle, _ptr(c) if use_c else None, alpha, beta,
                    _ptr(output), _dtype_code(output), ldy, n)
 
     def gemm2d_pack4_linear_texture_a(self, a, c, m, n, k, trans_b=True, alpha=1.0, beta=1.0, use_c=False,
-                                      broadcast_type_c=4, output=None):
-        """AexisOps.Gemm2DPack4LinearTextureA (:3649-3683)."""
-        self._gemm(lib().aexis_cuda_gemm, a, c, m, n, k, trans_b, alpha, beta, use_c, broadcast_type_c, output)
+                                      broadcast_type_c=4, output=None, input_packed=False, a_width=None,
+                                      a_height=None, a_slices=1):
+        """AexisOps.Gemm2DPack4LinearTextureA(a, inputPacked, ...) (:3649-3683).
+
+        input_packed=False: `a` is the linear [m, k] texture (row stride = its stride(0)).
+        input_packed=True: `a` is a Pack4 texture array of a_width texels x a_height rows x a_slices
+        slices stored flat ([slices][height][width][4], the CDHW layout); its K values run along the
+        texels of a row and continue in the next slice (AexisGemm2DPack4LinearTextureAFromPack4)."""
+        if not input_packed:
+            self._gemm(lib().aexis_cuda_gemm, a, c, m, n, k, trans_b, alpha, beta, use_c, broadcast_type_c, output)
+            return
+        w = self._gemm_weights(a, c, trans_b, use_c, broadcast_type_c, output)
+        if a_width is None:
+            raise errors.ArgumentNullError("a_width (texels per row of the packed input)")
+        a_height = m if a_height is None else a_height
+        ldy = output.stride(0) if output.dim() == 2 else n
+        self._call(lib().aexis_cuda_gemm_pack4a, _ptr(a), _dtype_code(a), int(a_width), int(a_height),
+                   int(a_slices), m, k, w.handle, _ptr(c) if use_c else None, alpha, beta, _ptr(output),
+                   _dtype_code(output), ldy, n)
 
     def gemm2d_pack4_tiled_texture_a(self, a, c, m, n, k, trans_b=True, alpha=1.0, beta=1.0, use_c=False,
                                      broadcast_type_c=4, output=None):
         """AexisOps.Gemm2DPack4TiledTextureAFromLinear (:3722-3752); output row stride = its tiled width."""
         self._gemm(lib().aexis_cuda_gemm_tiled, a, c, m, n, k, trans_b, alpha, beta, use_c, broadcast_type_c,
                    output)
+
+    def gemm2d_pack4_tiled_texture_a_from_pack4(self, a, c, m, n, k, trans_b=True, alpha=1.0, beta=1.0,
+                                                use_c=False, broadcast_type_c=4, output=None, a_width=None):
+        """AexisOps.Gemm2DPack4TiledTextureAFromPack4 (:3782-3826). The kernel reads slice 0 of the Pack4
+        input only (AexisGemm2DPack4TiledTextureAFromPack4_Impl, HLSL Pack4Matmul:2275-2300), so each row
+        is a run of a_width texels: the linear form with a row stride of 4 * a_width
+        (a_width defaults to ceil(k / 4), the width the reference sets)."""
+        a_width = (k + 3) // 4 if a_width is None else int(a_width)
+        if 4 * a_width < k:
+            raise errors.ArgumentError("a packed row of a_width texels holds fewer than k values")
+        self._gemm(lib().aexis_cuda_gemm_tiled, a, c, m, n, k, trans_b, alpha, beta, use_c, broadcast_type_c,
+                   output, lda=4 * a_width)
 
     # -- pointwise --------------------------------------------------------
     def rms_norm_pack4_linear_mat(self, x, rows, width, gamma, affine_size, affine, eps, output):

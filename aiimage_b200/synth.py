@@ -18,12 +18,24 @@ def rng(seed: int, *tag: int) -> np.random.Generator:
     return np.random.default_rng([int(seed), *[int(t) for t in tag]])
 
 
-def q4_weights(n: int, k: int, group: int, seed: int, tag=(0,), scale_lo=0.002, scale_hi=0.02):
+def q4_weights(n: int, k: int, group: int, seed: int, tag=(0,), scale_lo=0.002, scale_hi=0.02,
+               balanced: bool = False):
     """Symmetric int4 uniform in [-8, 7] packed two per byte along K; one fp16
-    scale per `group` consecutive K values (config 2)."""
+    scale per `group` consecutive K values (config 2).
+
+    balanced=True draws codes uniform in [-7, 7] instead, the range the
+    reference's own quantizer emits (maxAbs/7, clamp to [-7, 7]). The [-8, 7]
+    draw has mean -1/2, so every output row carries a bias of -scale/2 times
+    the sum of its inputs; through a 24-layer residual stack with unit norm
+    gains that common mode feeds itself and the greedy path collapses onto
+    one token. The balanced draw has mean zero."""
     assert (n * k) % 8 == 0 and k % group == 0
     r = rng(seed, 4, *tag)
-    packed = r.integers(0, 256, size=n * k // 2, dtype=np.uint8).view(np.uint32)
+    if balanced:
+        q = (r.integers(-7, 8, size=n * k, dtype=np.int8).astype(np.uint8) & 0xF).reshape(-1, 2)
+        packed = (q[:, 0] | (q[:, 1] << 4)).astype(np.uint8).view(np.uint32)
+    else:
+        packed = r.integers(0, 256, size=n * k // 2, dtype=np.uint8).view(np.uint32)
     scales = r.uniform(scale_lo, scale_hi, size=n * k // group).astype(np.float16)
     return packed, scales
 
@@ -110,11 +122,21 @@ class SyntheticDecoder:
 
     linear(layer, which) -> (packed uint32, scales fp16) with which 0..6 =
     q, k, v, o, gate, up, down (layer -1, which 7 = lm_head). Norm and
-    embedding weights are fp16 drawn from N(0, 0.02).
+    embedding weights are fp16 drawn from N(0, 0.02) (the measured configs).
+
+    norm_mean shifts the norm gains to N(norm_mean, 0.02). With the measured
+    configs' gains near zero every layer's output is tiny next to the
+    residual, attention scores are about 0.01 and the softmax is nearly
+    uniform, so the greedy path barely depends on the context. Gains near 1
+    (norm_mean=1, as a trained model has) give selective attention and
+    context-dependent tokens: a parity check on such a model fails on errors
+    in late-position attention or RoPE that the measured model hides.
+    balanced_q4 draws the Q4 codes from [-7, 7] (see q4_weights), which such
+    a model needs to keep its greedy path from collapsing.
     """
 
-    def __init__(self, cfg: DecoderCfg, seed: int = 3):
-        self.cfg, self.seed = cfg, seed
+    def __init__(self, cfg: DecoderCfg, seed: int = 3, norm_mean: float = 0.0, balanced_q4: bool = False):
+        self.cfg, self.seed, self.norm_mean, self.balanced_q4 = cfg, seed, float(norm_mean), bool(balanced_q4)
         self._lin = {}
         self._norm = {}
         c = cfg
@@ -122,18 +144,22 @@ class SyntheticDecoder:
             for which, (n, k) in enumerate(c.shapes()):
                 self._lin[(layer, which)] = self._make(c.bits, c.group, n, k, (layer, which))
             for which in range(2):
-                self._norm[(layer, which)] = self._normal(c.hidden, (100, layer, which))
+                self._norm[(layer, which)] = self._gain(c.hidden, (100, layer, which))
         self._lin[(-1, 7)] = self._make(c.lm_bits, c.lm_group, c.vocab, c.hidden, (999, 7))
-        self._norm[(-1, 0)] = self._normal(c.hidden, (100, 999, 0))
+        self._norm[(-1, 0)] = self._gain(c.hidden, (100, 999, 0))
         self.embedding = self._normal(c.vocab * c.hidden, (200,)).reshape(c.vocab, c.hidden)
 
     def _make(self, bits, group, n, k, tag):
         if bits == 4:
-            return q4_weights(n, k, group, self.seed, tag)
+            return q4_weights(n, k, group, self.seed, tag, balanced=self.balanced_q4)
         return q8_weights(n, k, self.seed, tag)
 
     def _normal(self, count, tag):
         return (rng(self.seed, 7, *tag).standard_normal(count, dtype=np.float32) * 0.02).astype(np.float16)
+
+    def _gain(self, count, tag):
+        g = rng(self.seed, 7, *tag).standard_normal(count, dtype=np.float32) * 0.02
+        return (g + np.float32(self.norm_mean)).astype(np.float16)
 
     def linear(self, layer: int, which: int):
         return self._lin[(layer, which)]

@@ -150,6 +150,24 @@ int aexis_cuda_gemm(aexis_ctx* ctx, const void* a, int a_dtype, int lda, int m, 
                     const aexis_weights* w, const float* bias, float alpha, float beta,
                     void* y, int y_dtype, int ldy, int n);
 
+/* Ops.Gemm2DPack4LinearTextureA with inputPacked = true (Ops:3649-3683),
+ * kernel AexisGemm2DPack4LinearTextureAFromPack4 (HLSL Pack4Matmul:1106-1190,
+ * A read as AexisGemm2DPack4LinearTextureAReadPack4, :880-891): the same
+ * product as aexis_cuda_gemm with A in a Pack4 texture array of a_width
+ * texels, a_height rows and a_slices slices, stored like a CDHW tensor
+ * (texel (x, row, slice) at ((slice * a_height + row) * a_width + x) * 4).
+ * Element (row, kk) is lane kk & 3 of texel (pack % a_width, row,
+ * pack / a_width) with pack = kk >> 2; values past the last slice count as 0.
+ * When 4 * a_width >= k the rows are read in place (row stride 4 * a_width);
+ * otherwise they are first gathered into a row-major context buffer.
+ * The tiled form (Gemm2DPack4TiledTextureAFromPack4, Ops:3782-3826) reads
+ * slice 0 only: it is aexis_cuda_gemm_tiled with lda = 4 * a_width.
+ * Errors: as aexis_cuda_gemm; a_width, a_slices <= 0 or a_height < m ->
+ * E_SHAPE. */
+int aexis_cuda_gemm_pack4a(aexis_ctx* ctx, const void* a, int a_dtype, int a_width, int a_height, int a_slices,
+                           int m, int k, const aexis_weights* w, const float* bias, float alpha, float beta,
+                           void* y, int y_dtype, int ldy, int n);
+
 /* Ops.SetInt8ActivationQuantization (Ops:741-785) with its plan resolved to
  * (scale, zero_point, unsigned): while enabled, aexis_cuda_gemm and
  * aexis_cuda_gemm_tiled fake-quantise every activation as the HLSL
@@ -437,6 +455,33 @@ int aexis_cuda_decoder_generate(aexis_decoder* dec, const int32_t* prompt, int n
  * greedy path (Qwen35DecoderSession.ProjectLogits :715-733). */
 int aexis_cuda_decoder_logits(aexis_decoder* dec, float* out_logits);
 
+/* ---- decoder state in the reference's layout ------------------------------
+ * Qwen35DecoderState (Samples/.../Qwen35DecoderSession.cs:48-100) carries one
+ * K and one V texture per attention layer ("cache_k<i>", "cache_v<i>") from
+ * step to step (:550-568), plus its SequenceLength / PositionId. These calls
+ * move that state across the ABI: a cache texture is a device fp32 Pack4 CDHW
+ * tensor [w = head_dim, h = rows, c = n_kv_heads], element (x = dim, y =
+ * position, c = kv head) at ((c/4 * rows + y) * head_dim + x) * 4 + (c & 3),
+ * the layout aexis_cuda_kv_append writes and aexis_cuda_sdpa reads (k/v with
+ * dst_len = the sequence length). The decoders keep fp16 caches, so an
+ * import rounds to fp16 (round to nearest even) and a round trip is exact for
+ * fp16-representable values. */
+
+/* Write layer `layer`'s K and V caches (device k_out, v_out, each
+ * 4 * ceil(n_kv_heads/4) * rows * head_dim floats): positions below the
+ * current position hold the cache, the rest of the rows are zero.
+ * Errors: rows < position -> E_SHAPE; layer outside [0, n_layers) -> E_RANGE. */
+int aexis_cuda_decoder_kv_export(aexis_decoder* dec, int layer, int rows, float* k_out, float* v_out);
+/* Load positions [0, length) of layer `layer`'s caches from Pack4 textures of
+ * `rows` rows (device). Does not move the position: after importing every
+ * layer, call aexis_cuda_decoder_set_position(dec, length). */
+int aexis_cuda_decoder_kv_import(aexis_decoder* dec, int layer, const float* k_in, const float* v_in, int rows,
+                                 int length);
+/* Set the next position (Qwen35DecoderState.PositionId / SequenceLength) to
+ * `position` in [0, kv_capacity]: the next token is written at that position
+ * and attends positions [0, position]. */
+int aexis_cuda_decoder_set_position(aexis_decoder* dec, int32_t position);
+
 /* How aexis_cuda_decoder_generate schedules its greedy steps (no reference
  * counterpart: the reference dispatches per layer). mode 0: one CUDA graph
  * per step (every kernel a programmatic dependent of the previous one);
@@ -487,6 +532,20 @@ int aexis_cuda_batch_fill_context(aexis_batch* batch, int n, const int32_t* ctx_
  * (host, may be NULL) receives [steps][n] step-major. Synchronous. E_RANGE
  * when a sequence would pass its capacity. */
 int aexis_cuda_batch_generate(aexis_batch* batch, const int32_t* first_tokens, int steps, int32_t* out_tokens);
+
+/* The batch's sequences in the reference's state layout (see the decoder
+ * state calls above; one Qwen35DecoderState per sequence). seq in
+ * [0, max_batch). Export: rows >= the sequence's position (E_SHAPE), rows
+ * past it zero; a sequence beyond the last fill / set_positions exports as
+ * empty. Import: positions [0, length) with length < kv_capacity. After the
+ * imports, aexis_cuda_batch_set_positions(batch, n, positions) makes
+ * sequences 0..n-1 the batch, each continuing at positions[i] (host, each in
+ * [0, kv_capacity)), as aexis_cuda_batch_fill_context does for synthetic
+ * contexts. */
+int aexis_cuda_batch_kv_export(aexis_batch* batch, int seq, int layer, int rows, float* k_out, float* v_out);
+int aexis_cuda_batch_kv_import(aexis_batch* batch, int seq, int layer, const float* k_in, const float* v_in, int rows,
+                               int length);
+int aexis_cuda_batch_set_positions(aexis_batch* batch, int n, const int32_t* positions);
 
 /* Next position of each sequence (host [n]). */
 int aexis_cuda_batch_positions(const aexis_batch* batch, int32_t* out);

@@ -172,6 +172,25 @@ ORACLE_API void oracle_gemm_tiled(const float* a, int lda, int m, int k, int bit
     gemm_impl<true>(a, lda, m, k, bits, P, S, blk, n, bias, alpha, beta, y, ldy);
 }
 
+// The A operand of AexisGemm2DPack4LinearTextureAFromPack4_Impl
+// (HLSL_MM:1106-1190, inputPacked = true in Ops.Gemm2DPack4LinearTextureA,
+// AexisOps.cs:3649-3683) as a row-major [m][k] matrix: the kernel walks
+// logicalPack = 0, 1, ... with packX = logicalPack % width, packSlice =
+// logicalPack / width, stops at the first packSlice >= slices, and uses lane
+// kk & 3 of texel (packX, row, packSlice) for kk = 4*logicalPack + lane < K
+// (AexisGemm2DPack4LinearTextureAReadPack4, HLSL_MM:880-891). A texture array
+// [slices][height][width] of float4 is stored flat as
+// ((slice*height + row)*width + x)*4 + lane. Values past the last slice are
+// never added; 0 stands in for them (acc + 0 = acc).
+ORACLE_API void oracle_read_pack4a(const float* a, int width, int height, int slices, int m, int k, float* out) {
+    for (int row = 0; row < m; ++row)
+        for (int kk = 0; kk < k; ++kk) {
+            const int pack = kk >> 2, x = pack % std::max(1, width), sl = pack / std::max(1, width);
+            out[(int64_t)row * k + kk] =
+                sl < slices ? a[(((int64_t)sl * height + row) * width + x) * 4 + (kk & 3)] : 0.0f;
+        }
+}
+
 // W8A8 activation fake-quantisation, AexisQuantizeGemmActivationForInt8
 // (HLSL_MM:792-800): q = clamp(round(v / scale) + zp), back to (q - zp)*scale.
 ORACLE_API void oracle_quantize_activation_int8(const float* x, int count, float scale, int zp,
@@ -586,6 +605,15 @@ ORACLE_API int oracle_decoder_fill_context(void* h, int ctx, uint64_t seed, int6
     return 0;
 }
 ORACLE_API void oracle_decoder_reset(void* h) { ((ODecoder*)h)->pos = 0; }
+// Layer `layer`'s cache (kind 0 = K, 1 = V) as [kv_heads][capacity][head_dim]
+// fp32 (the fp16-rounded values the decoder attends over).
+ORACLE_API void oracle_decoder_kv(void* h, int layer, int kind, float* out) {
+    ODecoder* d = (ODecoder*)h;
+    const auto& c = d->c;
+    const size_t per = (size_t)c.n_kv_heads * c.kv_capacity * c.head_dim;
+    const float* src = (kind == 0 ? d->kcache : d->vcache).data() + per * layer;
+    std::memcpy(out, src, per * sizeof(float));
+}
 ORACLE_API int oracle_decoder_position(void* h) { return ((ODecoder*)h)->pos; }
 
 // which: 0 q, 1 k, 2 v, 3 o, 4 gate, 5 up, 6 down; layer -1 = lm_head.

@@ -43,6 +43,7 @@ def lib():
         for name in ("oracle_gemm", "oracle_gemm_tiled"):
             getattr(L, name).argtypes = [F32P, C.c_int, C.c_int, C.c_int, C.c_int, U32P, F32P,
                                          C.c_int, C.c_int, vp, C.c_float, C.c_float, F32P, C.c_int]
+        L.oracle_read_pack4a.argtypes = [F32P, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, F32P]
         L.oracle_quantize_activation_int8.argtypes = [F32P, C.c_int, C.c_float, C.c_int, C.c_int, F32P]
         L.oracle_rmsnorm.argtypes = [F32P, C.c_int, C.c_int, C.c_int, vp, C.c_int, C.c_float, F32P, C.c_int]
         L.oracle_rope.argtypes = [F32P, C.c_int, C.c_int, C.c_int, F32P, F32P, C.c_int, F32P]
@@ -73,6 +74,7 @@ def lib():
         L.oracle_decoder_set_embedding.argtypes = [vp, F32P]
         L.oracle_decoder_step.argtypes = [vp, C.c_int, C.c_int, vp, vp]
         L.oracle_decoder_fill_context.argtypes = [vp, C.c_int, C.c_uint64, C.c_int64]
+        L.oracle_decoder_kv.argtypes = [vp, C.c_int, C.c_int, F32P]
         L.oracle_decoder_fill_context.restype = C.c_int
         L.oracle_num_threads.restype = C.c_int
         _lib = L
@@ -121,6 +123,16 @@ def gemm(a, bits: int, packed, scales, blk: int, n: int, bias=None, alpha: float
     fn(a, k, m, k, bits, np.ascontiguousarray(packed, dtype=np.uint32), _f32(scales), blk, n,
        _ptr(b), alpha, beta, y, n)
     return y
+
+
+def read_pack4a(a_flat, width: int, height: int, slices: int, m: int, k: int) -> np.ndarray:
+    """The row-major [m, k] A that AexisGemm2DPack4LinearTextureAFromPack4 reads from a flat Pack4 texture
+    array [slices][height][width][4] (see oracle_read_pack4a)."""
+    a = _f32(a_flat).reshape(-1)
+    assert a.size >= slices * height * width * 4
+    out = np.empty((m, k), dtype=np.float32)
+    lib().oracle_read_pack4a(a, width, height, slices, m, k, out)
+    return out
 
 
 def quantize_activation_int8(x, scale: float, zp: int = 0, unsigned: bool = False) -> np.ndarray:
@@ -342,6 +354,13 @@ class OracleDecoder:
         next position ctx."""
         if lib().oracle_decoder_fill_context(self._h, int(ctx), int(seed) & (2**64 - 1), int(seq_id)) != 0:
             raise ValueError("context must be in [0, kv_capacity)")
+
+    def kv(self, layer: int, kind: int) -> np.ndarray:
+        """Layer `layer`'s K (kind 0) or V (kind 1) cache, [kv_heads, capacity, head_dim] fp32."""
+        c = self._c
+        out = np.empty((c.n_kv_heads, c.kv_capacity, c.head_dim), dtype=np.float32)
+        lib().oracle_decoder_kv(self._h, int(layer), int(kind), out)
+        return out
 
     def step(self, token: int, want_logits: bool = True):
         logits = np.empty(self._c.vocab, dtype=np.float32) if want_logits else None

@@ -1,16 +1,42 @@
 """Generates the greedy-decode golden fixtures with the CPU oracle.
 
 Run from the repository root:  python tests/golden/make_golden.py
-Writes tests/golden/decoder_greedy.json: for each case the synthetic model
-(seeded, aiimage_b200.synth), the prompt seed and length, the 64 greedy token
-ids, the top-1/top-2 logit margin at every step (a near-tie would make a
-token flip a numerics question rather than a bug) and the 20 largest logits
-of the last step.
+(about six minutes on 8 cores). Writes two files next to this script:
+
+decoder_greedy.json, per case: the synthetic model (config name, seed, norm
+gain mean, Q4 code range), the prompt seed and length (or, for the batched
+cases, each sequence's synthetic context), the greedy token ids, the
+top-1/top-2 logit margin at every step (a near-tie makes a token flip a
+numerics question rather than a bug), the logit scale max|logit| per step,
+and the count of distinct tokens.
+
+decoder_steps.npz, per case `<case>.ids` / `<case>.logits`: the TOPN largest
+logits of every step (ids and fp32 values, descending, ties by index), so a
+test can feed the golden tokens (teacher forcing) and compare the logits of
+every position, not only the last one.
+
+Cases:
+  qwen35_08b_q4_prompt512       BASELINE config 3 as measured (norm gains
+                                N(0, 0.02), Q4 codes [-8, 7]). Its greedy
+                                path is nearly a fixed point: attention is
+                                almost uniform with such gains.
+  qwen35_08b_q4_selective       the same shapes with norm gains N(1, 0.02) and
+                                Q4 codes [-7, 7] (the reference quantizer's
+                                range): selective attention, a greedy path
+                                with many distinct tokens.
+  qwen35_08b_q8_prompt64        the Q8 per-row model, 64-token prompt.
+  config4_q8_batch              BASELINE config 4's 32 sequences (contexts
+                                U[256, 4096], synthetic caches); sequences
+                                SEQS of them over all 128 steps.
+  config4_q8_batch_selective    the same batch on the Q8 model with unit
+                                norm gains.
 """
 import json
 import os
 import sys
 import time
+
+import numpy as np
 
 ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 sys.path.insert(0, ROOT)
@@ -19,32 +45,120 @@ sys.path.insert(0, os.path.join(ROOT, "oracle"))
 import oracle as O  # noqa: E402
 from aiimage_b200 import synth  # noqa: E402
 
+TOPN = 20
+HERE = os.path.dirname(os.path.abspath(__file__))
+
 CASES = {
-    # 24-layer Q4 g32 decoder, 512-token prompt, 64 greedy tokens.
     "qwen35_08b_q4_prompt512": dict(cfg="QWEN35_08B_Q4", seed=3, prompt_len=512, prompt_seed=30, max_new=64),
-    # The Q8 per-row variant of the same model (config 4's weights), shorter prompt.
+    "qwen35_08b_q4_selective": dict(cfg="QWEN35_08B_Q4", seed=5, norm_mean=1.0, balanced_q4=True, prompt_len=512,
+                                    prompt_seed=50, max_new=64),
     "qwen35_08b_q8_prompt64": dict(cfg="QWEN35_08B_Q8", seed=4, prompt_len=64, prompt_seed=40, max_new=64),
 }
 
+# Config 4: the batch test draws ctx_lens and first tokens from this seed
+# sequence, 32 sequences, and decodes CONFIG4_STEPS greedy steps.
+CONFIG4 = dict(cfg="QWEN35_08B_Q8", seed=4, batch=32, rng=[4, 256, 4096], ctx_lo=256, ctx_hi=4096,
+               fill_seed=4, steps=128, kv_capacity=4096 + 128)
+BATCH_CASES = {
+    "config4_q8_batch": dict(CONFIG4),
+    "config4_q8_batch_selective": dict(CONFIG4, norm_mean=1.0),
+}
 
-def run(case):
+
+def model_of(case):
     cfg = getattr(synth, case["cfg"])
-    model = synth.SyntheticDecoder(cfg, seed=case["seed"])
+    if "kv_capacity" in case:
+        cfg = synth.DecoderCfg(**{**cfg.as_dict(), "kv_capacity": case["kv_capacity"]})
+    return synth.SyntheticDecoder(cfg, seed=case["seed"], norm_mean=case.get("norm_mean", 0.0),
+                                  balanced_q4=case.get("balanced_q4", False))
+
+
+def config4_batch(case, vocab):
+    """The batch's contexts and first tokens (drawn as the GPU test draws them)."""
+    r = np.random.default_rng(case["rng"])
+    ctx = r.integers(case["ctx_lo"], case["ctx_hi"] + 1, size=case["batch"]).astype(np.int32)
+    first = r.integers(0, vocab, size=case["batch"]).astype(np.int32)
+    return ctx, first
+
+
+def config4_pick(ctx):
+    """Four sequences: the shortest and longest contexts and two in between."""
+    order = np.argsort(ctx, kind="stable")
+    return sorted({int(order[0]), int(order[len(order) // 3]), int(order[2 * len(order) // 3]), int(order[-1])})
+
+
+def top(logits, n=TOPN):
+    idx = np.lexsort((np.arange(logits.size), -logits))[:n]
+    return idx.astype(np.int32), logits[idx].astype(np.float32)
+
+
+def greedy_trace(dec, first_token, steps):
+    """Greedy decoding from the current position: per step the token, the
+    margin, the logit scale and the TOPN logits."""
+    toks, margins, scales, ids, vals = [], [], [], [], []
+    tok = int(first_token)
+    for _ in range(steps):
+        tok, logits, margin = dec.step(tok)
+        toks.append(int(tok))
+        margins.append(float(margin))
+        scales.append(float(np.abs(logits).max()))
+        i, v = top(logits)
+        ids.append(i)
+        vals.append(v)
+    return toks, margins, scales, np.stack(ids), np.stack(vals)
+
+
+def run(case, arrays, name):
+    model = model_of(case)
     prompt = model.prompt(case["prompt_len"], seed=case["prompt_seed"])
     dec = O.OracleDecoder(model)
     t = time.time()
-    toks, margins = dec.generate(prompt, case["max_new"])
-    top = sorted(range(len(dec.last_logits)), key=lambda i: (-dec.last_logits[i], i))[:20]
-    return dict(case, tokens=toks, margins=[float(m) for m in margins], oracle_seconds=round(time.time() - t, 1),
-                oracle_threads=O.num_threads(), last_top20_ids=top,
-                last_top20_logits=[float(dec.last_logits[i]) for i in top])
+    for tk in prompt[:-1]:
+        dec.step(int(tk), want_logits=False)
+    toks, margins, scales, ids, vals = greedy_trace(dec, prompt[-1], case["max_new"])
+    arrays[name + ".ids"], arrays[name + ".logits"] = ids, vals
+    return dict(case, tokens=toks, margins=margins, logit_scale=scales, distinct=len(set(toks)),
+                oracle_seconds=round(time.time() - t, 1), oracle_threads=O.num_threads(),
+                last_top20_ids=[int(x) for x in ids[-1]], last_top20_logits=[float(x) for x in vals[-1]])
+
+
+def run_batch(case, arrays, name):
+    model = model_of(case)
+    ctx, first = config4_batch(case, model.cfg.vocab)
+    seqs = config4_pick(ctx)
+    t = time.time()
+    out = dict(case, seqs=seqs, ctx_lens=[int(ctx[i]) for i in seqs], first=[int(first[i]) for i in seqs],
+               tokens=[], margins=[], logit_scale=[], distinct=[])
+    all_ids, all_vals = [], []
+    for i in seqs:
+        dec = O.OracleDecoder(model)
+        dec.fill_context(int(ctx[i]), case["fill_seed"], i)
+        toks, margins, scales, ids, vals = greedy_trace(dec, first[i], case["steps"])
+        out["tokens"].append(toks)
+        out["margins"].append(margins)
+        out["logit_scale"].append(scales)
+        out["distinct"].append(len(set(toks)))
+        all_ids.append(ids[:, :8])
+        all_vals.append(vals[:, :8])
+    arrays[name + ".ids"], arrays[name + ".logits"] = np.stack(all_ids), np.stack(all_vals)
+    out["oracle_seconds"] = round(time.time() - t, 1)
+    out["oracle_threads"] = O.num_threads()
+    return out
 
 
 if __name__ == "__main__":
     O.build()
-    out = {name: run(c) for name, c in CASES.items()}
-    path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "decoder_greedy.json")
-    with open(path, "w") as f:
+    arrays = {}
+    out = {}
+    for name, c in CASES.items():
+        out[name] = run(c, arrays, name)
+        print(name, "distinct", out[name]["distinct"], "min margin %.3g" % min(out[name]["margins"]),
+              out[name]["oracle_seconds"], "s", flush=True)
+    for name, c in BATCH_CASES.items():
+        out[name] = run_batch(c, arrays, name)
+        print(name, "seqs", out[name]["seqs"], "distinct", out[name]["distinct"],
+              "min margin %.3g" % min(min(m) for m in out[name]["margins"]), out[name]["oracle_seconds"], "s",
+              flush=True)
+    with open(os.path.join(HERE, "decoder_greedy.json"), "w") as f:
         json.dump(out, f, indent=1)
-    for name, c in out.items():
-        print(name, c["tokens"][:8], "min margin", min(c["margins"]), c["oracle_seconds"], "s")
+    np.savez_compressed(os.path.join(HERE, "decoder_steps.npz"), **arrays)

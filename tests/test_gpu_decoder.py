@@ -11,6 +11,13 @@ from aiimage_b200 import synth
 pytestmark = pytest.mark.gpu
 
 GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "decoder_greedy.json")
+STEPS = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "decoder_steps.npz")
+TOL = 1e-3  # logits within TOL * max|logit| of the oracle's
+
+
+def golden_model(gold):
+    return synth.SyntheticDecoder(getattr(synth, gold["cfg"]), seed=gold["seed"], norm_mean=gold.get("norm_mean", 0.0),
+                                  balanced_q4=gold.get("balanced_q4", False))
 
 
 def make_session(ops, model):
@@ -73,13 +80,18 @@ def test_decoder_capacity_and_errors(ops):
 
 
 @pytest.mark.parametrize("case,schedule", [("qwen35_08b_q4_prompt512", 0), ("qwen35_08b_q4_prompt512", 1),
+                                           ("qwen35_08b_q4_selective", 0), ("qwen35_08b_q4_selective", 1),
                                            ("qwen35_08b_q8_prompt64", 0)])
 def test_full_decoder_matches_golden_tokens(ops, case, schedule):
     """BASELINE config 3 (and its Q8 variant): 64 greedy tokens identical to the
     oracle's, generated offline into tests/golden/decoder_greedy.json; the Q4
-    model under both schedules (per-step graphs, one persistent kernel)."""
+    models under both schedules (per-step graphs, one persistent kernel). The
+    selective model (unit norm gains) has a greedy path of 64 distinct tokens,
+    so a wrong attention or RoPE at any late position changes the tokens."""
     gold = json.load(open(GOLDEN))[case]
-    model = synth.SyntheticDecoder(getattr(synth, gold["cfg"]), seed=gold["seed"])
+    if case.endswith("selective"):
+        assert gold["distinct"] >= 16
+    model = golden_model(gold)
     prompt = model.prompt(gold["prompt_len"], seed=gold["prompt_seed"])
     sess = make_session(ops, model)
     sess.set_schedule(schedule)
@@ -90,6 +102,38 @@ def test_full_decoder_matches_golden_tokens(ops, case, schedule):
     ref = np.array(gold["last_top20_logits"], dtype=np.float32)
     got_top = logits[np.array(gold["last_top20_ids"])]
     assert np.max(np.abs(got_top - ref)) <= 1e-3 * np.abs(ref).max()
+
+
+@pytest.mark.parametrize("case", ["qwen35_08b_q4_prompt512", "qwen35_08b_q4_selective", "qwen35_08b_q8_prompt64"])
+def test_full_decoder_teacher_forced_logits_every_step(ops, case):
+    """Every one of the 64 steps, not only the last: the golden tokens are fed
+    back one at a time (aexis_cuda_decoder_step), and at each step the GPU's
+    logits at the oracle's 20 largest agree within TOL of the logit scale, and
+    the GPU's greedy token is the oracle's wherever the oracle's top-1/top-2
+    margin exceeds twice that tolerance."""
+    gold = json.load(open(GOLDEN))[case]
+    steps = np.load(STEPS)
+    ids, vals = steps[case + ".ids"], steps[case + ".logits"]
+    model = golden_model(gold)
+    prompt = model.prompt(gold["prompt_len"], seed=gold["prompt_seed"])
+    sess = make_session(ops, model)
+    toks = gold["tokens"]
+    got = sess.prefill(prompt)
+    exact = decided = 0
+    for s in range(gold["max_new"]):
+        if s:
+            got = sess.step(toks[s - 1])
+        logits = sess.logits()
+        scale = gold["logit_scale"][s]
+        err = np.max(np.abs(logits[ids[s]] - vals[s]))
+        assert err <= TOL * scale, (s, err, scale)
+        assert int(np.argmax(logits)) == got
+        if gold["margins"][s] > 2 * TOL * scale:
+            decided += 1
+            assert got == toks[s], (s, got, toks[s])
+        exact += got == toks[s]
+    assert sess.position == gold["prompt_len"] + gold["max_new"] - 1
+    assert exact >= decided and exact >= gold["max_new"] - 2, (exact, decided)
 
 
 # Decoders the persistent greedy loop takes: GQA groups of 4 and 2, partial

@@ -230,3 +230,89 @@ def test_argument_errors(ops):
         ops.new_int4_weight_only_upload(p, s, 64, 64, 48)  # group does not divide K
     with pytest.raises(errors.ArgumentError):
         ops.new_int8_weight_only_upload(p, s[:10], 64, 64)
+
+
+# inputPacked = true (AexisGemm2DPack4LinearTextureAFromPack4): A in a Pack4 texture array
+# [slices][height][width][4]. Cases: several slices with m > 1, a ragged last slice (K not a
+# multiple of 4*width), texture taller than m, slices beyond K (unused), too few slices (the
+# missing K values count as 0), a single slice read in place, and the tensor-core path (Q8, m >= 4).
+@pytest.mark.parametrize("bits,k,n,m,width,height,slices,a_f32", [
+    (4, 1024, 512, 3, 128, 3, 2, False),     # two slices, exactly full
+    (4, 1024, 3072, 2, 96, 5, 3, True),      # ragged last slice, taller texture, fp32 A
+    (8, 1024, 3584, 5, 64, 5, 4, False),     # Q8 tensor-core GEMM (m >= 4) behind the gather
+    (8, 4096, 96, 2, 200, 2, 6, True),       # more slices than K needs
+    (4, 512, 256, 2, 32, 2, 2, False),       # too few slices: K values 256.. read as 0
+    (8, 1024, 256, 3, 256, 4, 1, True),      # one slice: read in place, row stride 4 * width
+])
+def test_gemm_input_packed_pack4_array(ops, oracle, bits, k, n, m, width, height, slices, a_f32):
+    import torch
+    if bits == 4:
+        p, s = synth.q4_weights(n, k, 32, seed=9, tag=(k, n, m))
+        w = ops.new_int4_weight_only_upload(p, s, n, k, 32)
+        blk = 32
+    else:
+        p, s = synth.q8_weights(n, k, seed=9, tag=(k, n, m))
+        w = ops.new_int8_weight_only_upload(p, s, n, k)
+        blk = 0
+    rng = np.random.default_rng([k, n, m, width])
+    flat = rng.standard_normal(slices * height * width * 4).astype(np.float16)
+    bias = rng.standard_normal(n).astype(np.float32)
+    a_ref = oracle.read_pack4a(flat.astype(np.float32), width, height, slices, m, k)
+    ref = oracle.gemm(a_ref, bits, p, s.astype(np.float32), blk, n, bias=bias, alpha=0.75, beta=0.5)
+    a = torch.from_numpy(flat.astype(np.float32) if a_f32 else flat).cuda()
+    y = torch.zeros((m, n), dtype=torch.float32, device="cuda")
+    b = torch.from_numpy(bias).cuda()
+    ops.set_int4_gemm_weights(w if bits == 4 else None)
+    ops.set_int8_gemm_weights(w if bits == 8 else None)
+    ops.gemm2d_pack4_linear_texture_a(a, b, m, n, k, True, 0.75, 0.5, True, 4, y, input_packed=True,
+                                      a_width=width, a_height=height, a_slices=slices)
+    torch.cuda.synchronize()
+    assert_gemv_close(y.cpu().numpy(), ref)
+    if 4 * width < k:
+        # The gather must give the same numbers as the linear path on the gathered rows.
+        y2 = torch.zeros_like(y)
+        a_lin = torch.from_numpy(a_ref.astype(np.float32 if a_f32 else np.float16)).cuda()
+        ops.gemm2d_pack4_linear_texture_a(a_lin, b, m, n, k, True, 0.75, 0.5, True, 4, y2)
+        torch.cuda.synchronize()
+        assert torch.equal(y, y2)
+
+
+def test_gemm_input_packed_errors(ops):
+    import torch
+    p, s = synth.q4_weights(64, 256, 32, seed=1)
+    w = ops.new_int4_weight_only_upload(p, s, 64, 256, 32)
+    ops.set_int4_gemm_weights(w)
+    ops.set_int8_gemm_weights(None)
+    a = torch.zeros(4096, device="cuda")
+    y = torch.zeros((2, 64), device="cuda")
+    with pytest.raises(errors.ArgumentError):  # texture shorter than m
+        ops.gemm2d_pack4_linear_texture_a(a, None, 2, 64, 256, output=y, input_packed=True, a_width=16,
+                                          a_height=1, a_slices=4)
+    with pytest.raises(errors.ArgumentError):  # no slices
+        ops.gemm2d_pack4_linear_texture_a(a, None, 2, 64, 256, output=y, input_packed=True, a_width=16,
+                                          a_height=2, a_slices=0)
+    with pytest.raises(errors.ArgumentNullError):
+        ops.gemm2d_pack4_linear_texture_a(a, None, 2, 64, 256, output=y, input_packed=True)
+    with pytest.raises(errors.ArgumentError):  # weight shape mismatch is caught before the gather
+        ops.gemm2d_pack4_linear_texture_a(a, None, 2, 64, 512, output=y, input_packed=True, a_width=16,
+                                          a_height=2, a_slices=8)
+
+
+def test_tiled_from_pack4_matches_tiled_from_linear(ops, oracle):
+    """Gemm2DPack4TiledTextureAFromPack4 reads slice 0 of a texture ceil(k/4) (or more) texels wide."""
+    import torch
+    k, n, m, width = 1000, 300, 3, 260
+    p, s = synth.q8_weights(n, k, seed=12)
+    w = ops.new_int8_weight_only_upload(p, s, n, k)
+    ops.set_int8_gemm_weights(w)
+    ops.set_int4_gemm_weights(None)
+    rng = np.random.default_rng(12)
+    flat = rng.standard_normal(m * width * 4).astype(np.float32)
+    bias = rng.standard_normal(n).astype(np.float32)
+    ref = oracle.gemm(oracle.read_pack4a(flat, width, m, 1, m, k), 8, p, s.astype(np.float32), 0, n, bias=bias,
+                      alpha=1.5, beta=0.25, tiled=True)
+    y = torch.zeros((m, n), device="cuda")
+    ops.gemm2d_pack4_tiled_texture_a_from_pack4(torch.from_numpy(flat).cuda(), torch.from_numpy(bias).cuda(), m, n,
+                                                k, True, 1.5, 0.25, True, 4, y, a_width=width)
+    torch.cuda.synchronize()
+    assert_gemv_close(y.cpu().numpy(), ref)
