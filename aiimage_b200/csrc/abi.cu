@@ -755,10 +755,6 @@ AEXIS_API int aexis_cuda_sample(aexis_ctx* ctx, const float* logits, int rows, i
     if (!std::isfinite(temperature) || !std::isfinite(top_p))
         return aexis_fail(ctx, AEXIS_E_RANGE, "temperature %g top_p %g", (double)temperature, (double)top_p);
     const bool sample = temperature > 0.0f;
-    if (sample && (top_k < 1 || top_k > 64))
-        return aexis_fail(ctx, AEXIS_E_UNSUPPORTED,
-                          "top_k=%d: sampling keeps 1..64 candidates (top_k 0, the whole vocabulary, is not built)",
-                          top_k);
     if (sample && !uniforms) return aexis_fail(ctx, AEXIS_E_NULL, "uniform draws are null");
     int rc = bind(ctx);
     if (rc) return rc;
@@ -776,7 +772,7 @@ AEXIS_API int aexis_cuda_sample(aexis_ctx* ctx, const float* logits, int rows, i
         ctx->samp_bytes = need;
     }
     void* tk = nullptr;
-    if (sample) {
+    if (sample && top_k >= 1 && top_k <= 64) {
         rc = aexis_scratch(ctx, topk_scratch_bytes(rows, width, top_k < width ? top_k : width, ctx->sm_count), &tk);
         if (rc) return rc;
     }

@@ -21,6 +21,19 @@
 // Greedy rows (temperature <= 0) and rows whose sum is not finite and
 // positive take the first maximum of the penalised scores, as the reference's
 // ArgMax does.
+//
+// top_k <= 0 (the whole vocabulary) and top_k > 64 take sample_full_kernel
+// instead of steps 2-3: one CTA per row finds the nucleus cut and the drawn
+// token without sorting, by a mass-weighted radix select over the
+// probabilities' float bits (positive floats order like their bit patterns):
+// a question "the first position in descending-probability order whose
+// prefix mass reaches X" is answered with three histogram passes (12, 12 and
+// 8 bits of the key, each bin holding the count and the exact fixed-point
+// mass of its elements) and one pass over the elements equal to the found
+// value, in index order. The prefix masses are exact sums of the
+// probabilities in 2^-62 fixed point, where the reference sums them one by
+// one in fp64: the two differ by about n * 2^-53 of the kept mass, so a draw
+// closer than that to a cumulative boundary may pick the neighbouring token.
 #include "aexis_internal.h"
 
 #include <cfloat>
@@ -250,6 +263,265 @@ __global__ void sample_finish_kernel(const SamplePartial* __restrict__ parts, in
     out[row] = ix[keep - 1];
 }
 
+// ---------------------------------------------------------------------------
+// Whole-vocabulary selection (top_k <= 0 or > 64).
+constexpr int kFullThreads = 1024;
+constexpr int kFullBins = 4096;
+
+struct FullShared {
+    unsigned long long mass[kFullBins];  // fixed-point mass of the bin's elements
+    unsigned int cnt[kFullBins];         // their count
+    unsigned long long wm[32];           // per-warp scan partials
+    unsigned int wc[32];
+    int bin;                             // bin found by the current level (-1: none)
+    unsigned long long above_m;          // mass and count of the keys above the found ones
+    unsigned int above_c;
+    int idx;                             // index found by the tie pass
+    unsigned long long total;            // mass of the whole row (level 1)
+    float m;
+    double sum;
+    unsigned long long key;
+};
+
+// 2^62: probabilities in [0, 1] as fixed point (a float's 24-bit mantissa
+// times 2^62 is exact in double; the conversion truncates below 2^-62).
+__device__ __forceinline__ unsigned long long prob_fx(float p) {
+    return (unsigned long long)((double)p * 4611686018427387904.0);
+}
+
+// The reference's probability of one score: (float)(exp((s - max)/T) / sum).
+__device__ __forceinline__ float full_prob(float sc, float m, float temperature, double sum) {
+    return (float)((double)expf((sc - m) / temperature) / sum);
+}
+
+struct Found {
+    int ok;                    // 0: the target exceeds the row's mass (by_mass) or count
+    int pos;                   // 1-based position in descending-probability order
+    int idx;                   // token at that position
+    unsigned long long mass;   // prefix mass up to and including it
+};
+
+// The first position whose prefix mass (by_mass) or count (otherwise)
+// reaches `target` (>= 1), over the row's probabilities in descending order,
+// equal probabilities by ascending index. Called by every thread of the CTA.
+__device__ Found full_find(const float* __restrict__ srow, int width, float m, float temperature, double sum,
+                           unsigned long long target, bool by_mass, FullShared& sh) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    unsigned int prefix = 0, pmask = 0;
+    unsigned long long above_m = 0;
+    unsigned int above_c = 0;
+    const int shifts[3] = {20, 8, 0}, bits[3] = {12, 12, 8};
+    for (int lv = 0; lv < 3; ++lv) {
+        const int nb = 1 << bits[lv], sft = shifts[lv];
+        for (int b = tid; b < nb; b += kFullThreads) {
+            sh.mass[b] = 0;
+            sh.cnt[b] = 0;
+        }
+        __syncthreads();
+        // Warp-uniform tiles: lanes with the same bin add their masses with
+        // shuffles first, so a bin shared by a whole warp (a flat
+        // distribution) costs one shared atomic, not 32.
+        for (int base = 0; base < width; base += kFullThreads) {
+            const int i = base + tid;
+            int bin = -1;
+            unsigned long long fx = 0;
+            if (i < width) {
+                const float pr = full_prob(srow[i], m, temperature, sum);
+                const unsigned int key = __float_as_uint(pr);
+                if ((key & pmask) == prefix) {
+                    bin = (int)((key >> sft) & (unsigned)(nb - 1));
+                    fx = prob_fx(pr);
+                }
+            }
+            const unsigned grp = __match_any_sync(0xffffffffu, bin);
+            unsigned long long gsum = 0;
+#pragma unroll 8
+            for (int o = 0; o < 32; ++o) {
+                const unsigned long long v = __shfl_sync(0xffffffffu, fx, o);
+                if ((grp >> o) & 1u) gsum += v;
+            }
+            if (bin >= 0 && __ffs(grp) - 1 == lane) {
+                atomicAdd(&sh.mass[bin], gsum);
+                atomicAdd(&sh.cnt[bin], (unsigned)__popc(grp));
+            }
+        }
+        __syncthreads();
+        // Suffix sums over the bins in descending order: thread t owns bins
+        // [t*per, t*per + per); the threads are scanned from the top.
+        const int per = nb / kFullThreads > 0 ? nb / kFullThreads : 1;
+        unsigned long long tm = 0;
+        unsigned int tc = 0;
+        const int b0 = tid * per;
+        if (b0 < nb)
+            for (int b = b0; b < b0 + per; ++b) {
+                tm += sh.mass[b];
+                tc += sh.cnt[b];
+            }
+        unsigned long long sm = tm;  // inclusive suffix over the lanes >= this one
+        unsigned int sc = tc;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const unsigned long long vm = __shfl_down_sync(0xffffffffu, sm, o);
+            const unsigned int vc = __shfl_down_sync(0xffffffffu, sc, o);
+            if (lane + o < 32) {
+                sm += vm;
+                sc += vc;
+            }
+        }
+        if (lane == 0) {
+            sh.wm[warp] = sm;
+            sh.wc[warp] = sc;
+        }
+        if (tid == 0) sh.bin = -1;
+        __syncthreads();
+        unsigned long long later_m = 0;  // mass of the bins of later warps (above this thread's)
+        unsigned int later_c = 0;
+        for (int w = warp + 1; w < 32; ++w) {
+            later_m += sh.wm[w];
+            later_c += sh.wc[w];
+        }
+        unsigned long long run_m = above_m + later_m + (sm - tm);
+        unsigned int run_c = above_c + later_c + (sc - tc);
+        if (b0 < nb)
+            for (int b = b0 + per - 1; b >= b0; --b) {
+                const unsigned long long bm = sh.mass[b];
+                const unsigned int bc = sh.cnt[b];
+                const bool hit = by_mass ? (run_m < target && target <= run_m + bm)
+                                         : (run_c < target && target <= run_c + bc);
+                if (hit) {
+                    sh.bin = b;
+                    sh.above_m = run_m;
+                    sh.above_c = run_c;
+                }
+                run_m += bm;
+                run_c += bc;
+            }
+        if (lv == 0 && tid == 0) {
+            unsigned long long t = 0;
+            for (int w = 0; w < 32; ++w) t += sh.wm[w];
+            sh.total = t;
+        }
+        __syncthreads();
+        if (sh.bin < 0) return Found{0, 0, 0, 0};
+        prefix |= (unsigned)sh.bin << sft;
+        pmask |= (unsigned)(nb - 1) << sft;
+        above_m = sh.above_m;
+        above_c = sh.above_c;
+        __syncthreads();
+    }
+    // Every element left has the key `prefix`; the c-th of them by index is the answer.
+    const unsigned long long tau_fx = prob_fx(__uint_as_float(prefix));
+    unsigned int c;
+    if (by_mass) {
+        const unsigned long long need = target - above_m;  // > 0
+        c = (unsigned int)((need + tau_fx - 1) / tau_fx);
+    } else {
+        c = (unsigned int)(target - above_c);
+    }
+    unsigned int run = 0;
+    for (int base = 0; base < width; base += kFullThreads) {
+        const int i = base + tid;
+        bool match = false;
+        if (i < width) match = __float_as_uint(full_prob(srow[i], m, temperature, sum)) == prefix;
+        const int tile = __syncthreads_count(match);
+        if (run + (unsigned)tile >= c) {
+            const unsigned bal = __ballot_sync(0xffffffffu, match);
+            if (lane == 0) sh.wc[warp] = (unsigned)__popc(bal);
+            __syncthreads();
+            unsigned int before = run;
+            for (int w = 0; w < warp; ++w) before += sh.wc[w];
+            const unsigned int mine = before + (unsigned)__popc(bal & ((1u << lane) - 1u)) + 1u;
+            if (match && mine == c) sh.idx = i;
+            __syncthreads();
+            return Found{1, (int)(above_c + c), sh.idx, above_m + (unsigned long long)c * tau_fx};
+        }
+        run += (unsigned)tile;
+    }
+    return Found{0, 0, 0, 0};  // not reached: the bin held at least c elements
+}
+
+__global__ void __launch_bounds__(kFullThreads, 1)
+sample_full_kernel(const SamplePartial* __restrict__ parts, int segs, const float* __restrict__ scores, int ld,
+                   float temperature, int top_k, float top_p, int width, const double* __restrict__ uniforms,
+                   int32_t* __restrict__ out) {
+    extern __shared__ __align__(16) unsigned char full_smem[];
+    FullShared& sh = *reinterpret_cast<FullShared*>(full_smem);
+    const int row = blockIdx.x, tid = threadIdx.x;
+    const bool sample = temperature > 0.0f;
+    const float inv_t = sample ? 1.0f / temperature : 0.0f;
+    if (tid < 32) {
+        unsigned long long key = 0ull;
+        float m = -INFINITY;
+        double s = 0.0;
+        for (int i = tid; i < segs; i += 32) {
+            const SamplePartial p = parts[(long long)row * segs + i];
+            key = p.key > key ? p.key : key;
+            softmax_merge(m, s, p.m, p.sum, inv_t);
+        }
+#pragma unroll
+        for (int o = 16; o >= 1; o >>= 1) {
+            const unsigned long long k2 = __shfl_xor_sync(0xffffffffu, key, o);
+            const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
+            const double s2 = __shfl_xor_sync(0xffffffffu, s, o);
+            key = k2 > key ? k2 : key;
+            softmax_merge(m, s, m2, s2, inv_t);
+        }
+        if (tid == 0) {
+            sh.m = m;
+            sh.sum = s;
+            sh.key = key;
+        }
+    }
+    __syncthreads();
+    const float m = sh.m;
+    const double sum = sh.sum;
+    if (!sample || !(sum > 0.0 && sum <= DBL_MAX)) {
+        if (tid == 0) out[row] = aexis_argmax_index(sh.key);
+        return;
+    }
+    const float* srow = scores + (long long)row * ld;
+    // keep = min(top_k, V) (all when top_k <= 0); kept = its prefix mass.
+    int keep = width, keep_idx = -1;
+    unsigned long long kept = 0;
+    bool kept_known = false;
+    if (top_k > 0 && top_k < width) {
+        const Found f = full_find(srow, width, m, temperature, sum, (unsigned long long)top_k, false, sh);
+        keep = f.pos;
+        keep_idx = f.idx;
+        kept = f.mass;
+        kept_known = true;
+    }
+    if (top_p < 1.0f) {
+        // The nucleus: the first position whose cumulative reaches top_p, if within keep.
+        const double tp = top_p > 0.0f ? (double)top_p : 0.0;
+        unsigned long long target = (unsigned long long)ceil(tp * 4611686018427387904.0);
+        if (target < 1) target = 1;
+        const Found f = full_find(srow, width, m, temperature, sum, target, true, sh);
+        if (f.ok && f.pos <= keep) {
+            keep = f.pos;
+            keep_idx = f.idx;
+            kept = f.mass;
+            kept_known = true;
+        }
+    }
+    if (!kept_known) {
+        // keep = V: the whole row's mass (level 1 of any search sums it; a
+        // target above every mass stops the search there).
+        if (!(top_p < 1.0f)) full_find(srow, width, m, temperature, sum, ~0ull, true, sh);
+        kept = sh.total;
+    }
+    // The draw: the first position whose cumulative reaches u * kept.
+    unsigned long long x = (unsigned long long)(uniforms[row] * (double)kept);
+    if (x < 1) x = 1;
+    if (x > kept) x = kept;
+    const Found f = full_find(srow, width, m, temperature, sum, x, true, sh);
+    if (tid == 0) {
+        int pick = f.ok ? f.idx : -1;
+        if (!f.ok || f.pos > keep) pick = keep_idx >= 0 ? keep_idx : f.idx;
+        out[row] = pick >= 0 ? pick : aexis_argmax_index(sh.key);
+    }
+}
+
 __global__ void history_add_kernel(uint32_t* history, int rows, int hist_words, int width, const int32_t* tokens) {
     const int r = blockIdx.x * blockDim.x + threadIdx.x;
     if (r >= rows) return;
@@ -301,6 +573,16 @@ cudaError_t launch_sample(const float* logits, int rows, int width, int ld, cons
                                                                ld_s, parts);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
+    if (sample && (top_k <= 0 || top_k > 64)) {
+        // The whole vocabulary (or more candidates than the top-k kernels keep).
+        const size_t smem = sizeof(FullShared);
+        e = cudaFuncSetAttribute(sample_full_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+        sample_full_kernel<<<rows, kFullThreads, smem, s>>>(parts, segs, penalised ? scores : logits,
+                                                            penalised ? ld_s : ld, temperature, top_k, top_p, width,
+                                                            uniforms, out);
+        return cudaGetLastError();
+    }
     const int k = sample ? (top_k < width ? top_k : width) : 1;
     if (sample) {
         e = launch_topk(penalised ? scores : logits, rows, width, penalised ? ld_s : ld, k, cand_vals, cand_idx,

@@ -202,6 +202,19 @@ class Sweep:
         for i in range(len(SWEEP)):
             self.gemv(copy, i)
 
+    def graph_steps(self, fn, n: int):
+        """Capture n consecutive steps fn(i % copies), i = 0..n-1, into one graph."""
+        import torch
+        g = torch.cuda.CUDAGraph()
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            with torch.cuda.graph(g, stream=s):
+                for i in range(n):
+                    fn(i % self.copies)
+        torch.cuda.current_stream().wait_stream(s)
+        return g
+
     def graph(self, fn, reps: int):
         """Capture `reps` rotations of fn(copy) over all copies into one graph."""
         import torch
@@ -217,28 +230,52 @@ class Sweep:
         return g
 
 
-def time_graph_steps(graph_big, steps_per_big, graphs_single, copies, steps, warmup, world):
-    """Replay graphs for exactly `steps` steps after `warmup`; CUDA-event time."""
+class StepGraphs:
+    """Graphs that replay exactly n steps of fn(copy), copies rotating so no
+    two consecutive steps read the same weights: a chunk of C steps (C a
+    multiple of the copy count) replayed n // C times, then one graph of the
+    n % C remaining steps (copies 0.. again, after a chunk that ended on the
+    last copy)."""
+
+    def __init__(self, sw, fn, n: int, max_chunk: int = 240):
+        self.copies = sw.copies
+        c = self.copies * max(1, min(n, max_chunk) // self.copies)
+        self.chunk = c if n >= c else 0
+        self.reps = n // c if self.chunk else 0
+        rem = n - self.reps * c
+        self.g_chunk = sw.graph_steps(fn, c) if self.chunk else None
+        self.g_rem = sw.graph_steps(fn, rem) if rem else None
+        self.n = n
+
+    def replay(self):
+        for _ in range(self.reps):
+            self.g_chunk.replay()
+        if self.g_rem is not None:
+            self.g_rem.replay()
+
+
+def time_steps(graphs: StepGraphs, world: int) -> float:
+    """CUDA-event time of exactly graphs.n steps, barrier + synchronize on both sides."""
     import torch
-
-    def run(n):
-        done = 0
-        while n - done >= steps_per_big:
-            graph_big.replay()
-            done += steps_per_big
-        while done < n:
-            graphs_single[done % copies].replay()
-            done += 1
-
-    run(warmup)
     barrier(world)
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     start.record()
-    run(steps)
+    graphs.replay()
     end.record()
     end.synchronize()
     barrier(world)
     return start.elapsed_time(end) / 1e3
+
+
+def load_window(graphs: StepGraphs, seconds: float):
+    """Replays the same steps for about `seconds` (untimed): the clock
+    sampler's window around the timed region, so it holds many NVML samples
+    taken under the same load."""
+    import torch
+    t0 = time.perf_counter()
+    while time.perf_counter() - t0 < seconds:
+        graphs.replay()
+        torch.cuda.synchronize()
 
 
 def run_gpu(args):
@@ -253,13 +290,14 @@ def run_gpu(args):
     for c in range(copies):  # first calls outside capture (kernel attributes, occupancy)
         sw.step(c)
     torch.cuda.synchronize()
-    singles = [sw.graph(lambda c, cc=cc: sw.step(cc) if c == 0 else None, 1) for cc in range(copies)]
-    reps = max(1, 60 // copies)
-    big = sw.graph(sw.step, reps)
-    steps_per_big = reps * copies
-
+    timed = StepGraphs(sw, sw.step, args.steps)
+    warm = StepGraphs(sw, sw.step, args.warmup)
+    warm.replay()
+    torch.cuda.synchronize()
     with ClockSampler(local) as clk:
-        secs = time_graph_steps(big, steps_per_big, singles, copies, args.steps, args.warmup, world)
+        load_window(timed, 0.25)
+        secs = time_steps(timed, world)
+        load_window(timed, 0.1)
     secs = max_over_ranks(secs, world)
     value = world * args.steps * STEP_BYTES / secs / 1e9
 
@@ -382,10 +420,10 @@ def run_gpu(args):
             "vs_baseline": None,
             "dtype": "int4 weights, fp16 act/scales, fp32 accumulate",
             "data": "synthetic (seeded PCG64; BASELINE config 2 shapes and distributions)",
-            "config": {"workload": "config2_q4_g32_gemv_sweep_m1", "shapes_KxN": [list(s) for s in SWEEP],
-                       "bytes_per_step": STEP_BYTES, "weight_copies": copies,
-                       "l2": f"weights rotated over {copies} copies ({copies * STEP_BYTES / 2**20:.0f} MiB > 4x L2)",
-                       "parallelism": f"replicas x{world}"},
+            "config": sweep_config(world),
+            "timing": {"graphs": f"exactly {args.steps} steps: {timed.reps} replay(s) of a {timed.chunk}-step graph"
+                                 f" + one {args.steps - timed.reps * timed.chunk}-step graph",
+                       "events": "CUDA events on the launching stream, barrier + synchronize both sides"},
             "roofline": {"bound": "hbm", "kernel": "gemv_mma_kernel q4 g32 fp16-x int8-MMA path (1024x151936)",
                          "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": traffic,
@@ -404,13 +442,23 @@ def run_gpu(args):
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "path": "aexis_cuda_gemm via ctypes, pinned host x/y, sync per step"},
             "gpu_launches": args.steps * len(SWEEP),
-            "clocks": clk.summary(),
+            "clocks": {**clk.summary(), "window": "NVML every 5 ms over 0.25 s of the same step graphs, the"
+                                                  " timed region, then 0.1 s more"},
         }
         print(json.dumps(line), flush=True)
     ops.close()
     if world > 1:
         import torch.distributed as dist
         dist.destroy_process_group()
+
+
+def sweep_config(world: int) -> dict:
+    """The workload, identical in both arms (the reference arm rotates the same weight copies in host memory)."""
+    copies = max(2, -(-4 * L2_BYTES // STEP_BYTES))
+    return {"workload": "config2_q4_g32_gemv_sweep_m1", "shapes_KxN": [list(s) for s in SWEEP],
+            "bytes_per_step": STEP_BYTES, "weight_copies": copies,
+            "l2": f"weights rotated over {copies} copies ({copies * STEP_BYTES / 2**20:.0f} MiB > 4x L2)",
+            "parallelism": f"replicas x{world}"}
 
 
 def bench_q8(ops, peak):
@@ -794,24 +842,27 @@ def bench_config5(ops, world: int, rank: int, reps: int = 10):
 
 def cpu_baseline(budget_s: float = 12.0):
     """The CPU oracle (restated reference path) on the same sweep, all host
-    threads, bounded to ~budget_s of work."""
+    threads, bounded to ~budget_s of work, rotating the same weight copies as
+    the GPU arm (host memory)."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle as O
     O.build()
+    copies = sweep_config(1)["weight_copies"]
     host = [synth.q4_weights(n, k, GROUP, 1, tag=(k, n)) for (k, n) in SWEEP]
+    sets = [[(p.copy(), s.astype(np.float32)) for p, s in host] for _ in range(copies)]
     xs = [synth.activations(k, 1, tag=(k, n)).astype(np.float32) for (k, n) in SWEEP]
-    scales = [s.astype(np.float32) for _, s in host]
     passes, t0 = 0, time.perf_counter()
     while True:
-        for (p, _), s, x, (k, n) in zip(host, scales, xs, SWEEP):
+        for (p, s), x, (k, n) in zip(sets[passes % copies], xs, SWEEP):
             O.gemm(x, 4, p, s, GROUP, n)
         passes += 1
         el = time.perf_counter() - t0
-        if el >= budget_s or passes >= 50:
+        if el >= budget_s or passes >= 60:
             break
     return {"value": round(passes * STEP_BYTES / el / 1e9, 3), "unit": "GB/s", "cores": O.num_threads(),
             "kind": "port", "sample": f"{passes} full sweep pass(es) of config 2 through the C++ oracle "
-                                      f"(sequential fp32 per output, OpenMP over outputs), {el:.1f} s"}
+                                      f"(sequential fp32 per output, OpenMP over outputs), weights rotated over "
+                                      f"{copies} host copies, {el:.1f} s"}
 
 
 def run_only(args):
@@ -897,36 +948,42 @@ def run_only(args):
 def run_reference(args):
     """--impl reference: the reference's CPU path for this workload (the C++
     oracle restating AexisGemm2DPack4LinearTextureA / AexisGemm2DReadB) on all
-    host threads. Under torchrun only rank 0 runs."""
+    host threads, over the same weight copies the GPU arm rotates (host
+    memory, step i reads copy i % copies). Under torchrun only rank 0 runs."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
+    world = int(os.environ.get("WORLD_SIZE", "1"))
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle as O
     O.build()
+    cfg = sweep_config(world)
+    copies = cfg["weight_copies"]
     host = [synth.q4_weights(n, k, GROUP, 1, tag=(k, n)) for (k, n) in SWEEP]
+    sets = [[(p.copy(), s.astype(np.float32)) for p, s in host] for _ in range(copies)]
     xs = [synth.activations(k, 1, tag=(k, n)).astype(np.float32) for (k, n) in SWEEP]
-    scales = [s.astype(np.float32) for _, s in host]
 
-    def step():
-        for (p, _), s, x, (k, n) in zip(host, scales, xs, SWEEP):
+    def step(c):
+        for (p, s), x, (k, n) in zip(sets[c], xs, SWEEP):
             O.gemm(x, 4, p, s, GROUP, n)
 
-    for _ in range(args.warmup):
-        step()
+    for i in range(args.warmup):
+        step(i % copies)
     t0 = time.perf_counter()
-    for _ in range(args.steps):
-        step()
+    for i in range(args.steps):
+        step(i % copies)
     el = time.perf_counter() - t0
     value = args.steps * STEP_BYTES / el / 1e9
     line = {"impl": "reference", "metric": "Q4 g32 dequant-GEMV sweep, algorithmic HBM GB/s (batch 1)",
-            "value": round(value, 3), "unit": "GB/s", "n_gpus": int(os.environ.get("WORLD_SIZE", "1")),
+            "value": round(value, 3), "unit": "GB/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(el / args.steps * 1e3, 3),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "int4 weights, fp32 compute", "data": "synthetic (same seeded inputs as the GPU arm)",
-            "config": {"workload": "config2_q4_g32_gemv_sweep_m1", "shapes_KxN": [list(s) for s in SWEEP]},
+            "dtype": "int4 weights, fp16 act/scales, fp32 accumulate",
+            "data": "synthetic (seeded PCG64; BASELINE config 2 shapes and distributions)",
+            "config": cfg,
             "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": O.num_threads(), "kind": "port",
-                             "sample": f"{args.steps} full sweep passes through the C++ oracle"},
+                             "sample": f"{args.steps} full sweep passes through the C++ oracle (sequential fp32 per"
+                                       f" output, OpenMP over outputs), weights rotated over {copies} host copies"},
             "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 

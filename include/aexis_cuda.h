@@ -293,9 +293,12 @@ int aexis_cuda_topk(aexis_ctx* ctx, const float* logits, int rows, int width, in
  *       (s < 0 ? s * penalty : s / penalty);
  *   temperature <= 0: the first maximum of s (ArgMax, :1894-1900);
  *   else p = (float)(exp((s - max)/T) / sum) with the sum in double; the
- *   top_k most probable, then the smallest prefix whose cumulative reaches
- *   top_p (at least one); draw = uniforms[r] * kept mass; the first token
- *   whose cumulative reaches the draw. A sum that is not finite and positive
+ *   top_k most probable (top_k <= 0: the whole vocabulary), then the
+ *   smallest prefix whose cumulative reaches top_p (at least one); draw =
+ *   uniforms[r] * kept mass; the first token whose cumulative reaches the
+ *   draw. top_k 1..64 takes the top-k kernels; any other top_k a radix select
+ *   weighted by probability mass (no sort), whose prefix sums are exact in
+ *   2^-62 fixed point where the reference sums in fp64 one by one. A sum that is not finite and positive
  *   (a NaN score, no finite score) falls back to ArgMax, as the reference.
  * logits: device fp32 [rows, ld]; history: NULL or a device bitmap
  * [rows][ceil(width/32)] uint32 (bit t % 32 of word t / 32 = token t was
@@ -305,8 +308,7 @@ int aexis_cuda_topk(aexis_ctx* ctx, const float* logits, int rows, int width, in
  * (the reference's Array.Sort leaves exact ties unordered).
  * Errors: NULL logits/out -> E_NULL; rows, width <= 0, penalty <= 0 or a
  * non-finite temperature / top_p -> E_RANGE; ld < width -> E_SHAPE; when
- * sampling: top_k outside 1..64 -> E_UNSUPPORTED (top_k 0, sampling over the
- * whole vocabulary, is not built), uniforms NULL -> E_NULL. */
+ * sampling: uniforms NULL -> E_NULL. */
 int aexis_cuda_sample(aexis_ctx* ctx, const float* logits, int rows, int width, int ld,
                       const uint32_t* history, float repetition_penalty, float temperature, int top_k,
                       float top_p, const double* uniforms, int32_t* out_idx);

@@ -1,7 +1,8 @@
 """Generates the greedy-decode golden fixtures with the CPU oracle.
 
-Run from the repository root:  python tests/golden/make_golden.py
-(about six minutes on 8 cores). Writes two files next to this script:
+Run from the repository root:  python tests/golden/make_golden.py [case ...]
+(about twelve minutes on 8 cores for every case; naming cases regenerates
+only those and keeps the others). Writes two files next to this script:
 
 decoder_greedy.json, per case: the synthetic model (config name, seed, norm
 gain mean, Q4 code range), the prompt seed and length (or, for the batched
@@ -28,8 +29,17 @@ Cases:
   config4_q8_batch              BASELINE config 4's 32 sequences (contexts
                                 U[256, 4096], synthetic caches); sequences
                                 SEQS of them over all 128 steps.
-  config4_q8_batch_selective    the same batch on the Q8 model with unit
-                                norm gains.
+  config4_q8_batch_selective    the same batch on the Q8 model with norm
+                                gains N(1/8, 0.02). The Q8 weights are about
+                                8x the Q4 ones (std 0.4 against 0.05), so
+                                gains of 1/8 give the activation scale the Q4
+                                selective model has with gains of 1. With
+                                gains of 1 the attention scores reach a
+                                standard deviation near 160: one fp16 ulp of a
+                                cached key moves a score by about 0.4, and
+                                the softmax amplifies that rounding, so that
+                                model is too ill-conditioned for a parity
+                                check.
 """
 import json
 import os
@@ -61,7 +71,7 @@ CONFIG4 = dict(cfg="QWEN35_08B_Q8", seed=4, batch=32, rng=[4, 256, 4096], ctx_lo
                fill_seed=4, steps=128, kv_capacity=4096 + 128)
 BATCH_CASES = {
     "config4_q8_batch": dict(CONFIG4),
-    "config4_q8_batch_selective": dict(CONFIG4, norm_mean=1.0),
+    "config4_q8_batch_selective": dict(CONFIG4, norm_mean=0.125),
 }
 
 
@@ -148,17 +158,27 @@ def run_batch(case, arrays, name):
 
 if __name__ == "__main__":
     O.build()
-    arrays = {}
-    out = {}
+    only = set(sys.argv[1:])
+    json_path, npz_path = os.path.join(HERE, "decoder_greedy.json"), os.path.join(HERE, "decoder_steps.npz")
+    out, arrays = {}, {}
+    if only:  # keep the cases not asked for
+        out = json.load(open(json_path))
+        arrays = dict(np.load(npz_path))
+        unknown = only - set(CASES) - set(BATCH_CASES)
+        assert not unknown, unknown
     for name, c in CASES.items():
+        if only and name not in only:
+            continue
         out[name] = run(c, arrays, name)
         print(name, "distinct", out[name]["distinct"], "min margin %.3g" % min(out[name]["margins"]),
               out[name]["oracle_seconds"], "s", flush=True)
     for name, c in BATCH_CASES.items():
+        if only and name not in only:
+            continue
         out[name] = run_batch(c, arrays, name)
         print(name, "seqs", out[name]["seqs"], "distinct", out[name]["distinct"],
               "min margin %.3g" % min(min(m) for m in out[name]["margins"]), out[name]["oracle_seconds"], "s",
               flush=True)
-    with open(os.path.join(HERE, "decoder_greedy.json"), "w") as f:
+    with open(json_path, "w") as f:
         json.dump(out, f, indent=1)
-    np.savez_compressed(os.path.join(HERE, "decoder_steps.npz"), **arrays)
+    np.savez_compressed(npz_path, **arrays)

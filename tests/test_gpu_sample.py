@@ -130,15 +130,58 @@ def test_history_add_and_device_sampler(ops, oracle):
         logits = np.roll(logits, 1, axis=1)
 
 
+@pytest.mark.parametrize("temp,top_k,top_p,pen", [
+    (0.3, 0, 0.8, 1.1),      # whole vocabulary with the default temperature and nucleus
+    (1.0, 0, 1.0, 1.0),      # whole vocabulary, no nucleus: the draw walks the full distribution
+    (2.0, 0, 0.95, 1.1),     # a flat distribution: a nucleus of thousands of tokens
+    (0.7, -3, 0.9, 1.3),     # top_k <= 0 means the whole vocabulary, as in the reference
+    (0.8, 100, 0.97, 1.1),   # more candidates than the top-k kernels keep
+    (1.5, 5000, 1.0, 1.0),   # top-k only, thousands of candidates
+    (0.5, 0, 0.0, 1.1),      # top_p 0 keeps one token
+])
+@pytest.mark.parametrize("rows,width,scale", [(1, 151936, 4.0), (5, 151936, 2.0), (6, 3001, 1.0)])
+def test_whole_vocabulary_sampling_matches_oracle(ops, oracle, temp, top_k, top_p, pen, rows, width, scale):
+    """top_k <= 0 and top_k > 64 (the radix-select path) against the oracle's
+    full sort of every probability, same draws."""
+    logits, hist, u = make_case(int(temp * 10) + abs(top_k) + rows + width, rows, width, scale, 40)
+    got = run(ops, logits, hist, pen, temp, top_k, top_p, u)
+    ref, margin = oracle.sample(logits, hist, pen, temp, top_k, top_p, u)
+    sure = margin > 1e-5
+    assert sure.sum() >= max(1, rows - 2)
+    np.testing.assert_array_equal(got[sure], ref[sure])
+
+
+def test_whole_vocabulary_draw_sweep_and_ties(ops, oracle):
+    """One row under 64 draws spread over its whole distribution (top_k 0,
+    top_p 1); then rows of exactly equal scores, where every token has the
+    same probability and the draw picks by index (equal probabilities rank by
+    ascending index), and a row with half its scores at -inf."""
+    logits, hist, _ = make_case(77, 1, 151936, 1.5, 30)
+    one = np.repeat(logits, 64, axis=0)
+    h1 = np.repeat(hist, 64, axis=0)
+    u = (np.arange(64) + 0.5) / 64
+    got = run(ops, one, h1, 1.1, 1.0, 0, 1.0, u)
+    ref, margin = oracle.sample(one, h1, 1.1, 1.0, 0, 1.0, u)
+    sure = margin > 1e-6
+    assert sure.sum() >= 60
+    np.testing.assert_array_equal(got[sure], ref[sure])
+    assert len(set(got.tolist())) > 32
+    flat = np.zeros((8, 5000), dtype=np.float32)
+    flat[7, ::2] = -np.inf
+    uf = np.array([0.0, 0.1, 0.25, 0.5, 0.75, 0.9, 0.999, 0.5])
+    got = run(ops, flat, None, 1.0, 1.0, 0, 1.0, uf)
+    ref, _ = oracle.sample(flat, None, 1.0, 1.0, 0, 1.0, uf)
+    np.testing.assert_array_equal(got, ref)
+    got = run(ops, flat, None, 1.0, 1.0, 0, 0.3, uf)
+    ref, _ = oracle.sample(flat, None, 1.0, 1.0, 0, 0.3, uf)
+    np.testing.assert_array_equal(got, ref)
+
+
 def test_sample_argument_errors(ops):
     import torch
     x = torch.zeros((2, 100), dtype=torch.float32, device="cuda")
     out = torch.zeros(2, dtype=torch.int32, device="cuda")
     u = torch.zeros(2, dtype=torch.float64, device="cuda")
-    with pytest.raises(errors.NotSupportedError):
-        ops.sample(x, 2, 100, None, 1.0, 0.5, 0, 1.0, u, out)      # top_k 0: whole-vocabulary sampling
-    with pytest.raises(errors.NotSupportedError):
-        ops.sample(x, 2, 100, None, 1.0, 0.5, 65, 1.0, u, out)
     with pytest.raises(errors.ArgumentNullError):
         ops.sample(x, 2, 100, None, 1.0, 0.5, 10, 1.0, None, out)  # sampling needs draws
     with pytest.raises(errors.ArgumentOutOfRangeError):
