@@ -759,7 +759,8 @@ AEXIS_API int aexis_cuda_sample(aexis_ctx* ctx, const float* logits, int rows, i
     int rc = bind(ctx);
     if (rc) return rc;
     const bool penalised = history != nullptr && repetition_penalty != 1.0f;
-    const size_t need = sample_scratch_bytes(rows, width, ctx->sm_count, penalised);
+    const bool full = sample && (top_k <= 0 || top_k > 64);
+    const size_t need = sample_scratch_bytes(rows, width, ctx->sm_count, penalised, full);
     if (need > ctx->samp_bytes) {
         if (ctx->samp) {
             cudaStreamSynchronize(ctx->stream);

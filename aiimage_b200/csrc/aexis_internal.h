@@ -212,7 +212,8 @@ cudaError_t launch_act_quant_i8(const void* a, int a_dtype, int lda, int m, int 
 cudaError_t launch_gather_pack4a(const void* a, int a_dtype, int width, int height, int slices, int m, int k,
                                  void* out, cudaStream_t s);
 // Device sampler (k_sample.cu). `topk_scratch` holds topk_scratch_bytes(rows, width, min(top_k, width)).
-size_t sample_scratch_bytes(int rows, int width, int sm_count, bool scores);
+// `full`: room for the whole-vocabulary path's probabilities (top_k <= 0 or > 64).
+size_t sample_scratch_bytes(int rows, int width, int sm_count, bool scores, bool full);
 cudaError_t launch_sample(const float* logits, int rows, int width, int ld, const uint32_t* history, float pen,
                           float temperature, int top_k, float top_p, const double* uniforms, int32_t* out,
                           void* scratch, void* topk_scratch, int sm_count, cudaStream_t s);

@@ -269,15 +269,17 @@ constexpr int kFullThreads = 1024;
 constexpr int kFullBins = 4096;
 
 struct FullShared {
-    unsigned long long mass[kFullBins];  // fixed-point mass of the bin's elements
-    unsigned int cnt[kFullBins];         // their count
-    unsigned long long wm[32];           // per-warp scan partials
+    unsigned long long l1_mass[kFullBins];  // level 1 (key bits 31..20) of the whole row, kept for every query
+    unsigned int l1_cnt[kFullBins];
+    unsigned long long mass[kFullBins];     // levels 2 and 3 of the current query
+    unsigned int cnt[kFullBins];
+    unsigned long long wm[32];              // per-warp scan partials
     unsigned int wc[32];
-    int bin;                             // bin found by the current level (-1: none)
-    unsigned long long above_m;          // mass and count of the keys above the found ones
+    int bin;                                // bin found by the current level (-1: none)
+    unsigned long long above_m;             // mass and count of the keys above the found ones
     unsigned int above_c;
-    int idx;                             // index found by the tie pass
-    unsigned long long total;            // mass of the whole row (level 1)
+    int idx;                                // index found by the tie pass
+    unsigned long long total;               // mass of the whole row
     float m;
     double sum;
     unsigned long long key;
@@ -294,6 +296,26 @@ __device__ __forceinline__ float full_prob(float sc, float m, float temperature,
     return (float)((double)expf((sc - m) / temperature) / sum);
 }
 
+// Adds (fx, 1) to bin `bin` (>= 0; -1 adds nothing). When the whole warp
+// shares one bin (a flat distribution) it adds once, reduced by shuffles;
+// otherwise lane by lane.
+__device__ __forceinline__ void full_hist_add(unsigned long long* mass, unsigned int* cnt, int bin,
+                                              unsigned long long fx) {
+    const int b0 = __shfl_sync(0xffffffffu, bin, 0);
+    if (__all_sync(0xffffffffu, bin == b0)) {
+        if (b0 < 0) return;
+#pragma unroll
+        for (int o = 16; o >= 1; o >>= 1) fx += __shfl_xor_sync(0xffffffffu, fx, o);
+        if ((threadIdx.x & 31) == 0) {
+            atomicAdd(&mass[b0], fx);
+            atomicAdd(&cnt[b0], 32u);
+        }
+    } else if (bin >= 0) {
+        atomicAdd(&mass[bin], fx);
+        atomicAdd(&cnt[bin], 1u);
+    }
+}
+
 struct Found {
     int ok;                    // 0: the target exceeds the row's mass (by_mass) or count
     int pos;                   // 1-based position in descending-probability order
@@ -301,113 +323,104 @@ struct Found {
     unsigned long long mass;   // prefix mass up to and including it
 };
 
+// Scans the histogram `nb` bins (mass/cnt) from the top for the bin where the
+// prefix (starting at above_m / above_c) reaches `target`; sets sh.bin (-1
+// when none), sh.above_m, sh.above_c. Every thread calls it.
+__device__ void full_scan(const unsigned long long* mass, const unsigned int* cnt, int nb, unsigned long long above_m,
+                          unsigned int above_c, unsigned long long target, bool by_mass, FullShared& sh) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int per = nb / kFullThreads > 0 ? nb / kFullThreads : 1;
+    unsigned long long tm = 0;
+    unsigned int tc = 0;
+    const int b0 = tid * per;
+    if (b0 < nb)
+        for (int b = b0; b < b0 + per; ++b) {
+            tm += mass[b];
+            tc += cnt[b];
+        }
+    unsigned long long sm = tm;  // inclusive suffix over the lanes >= this one
+    unsigned int sc = tc;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const unsigned long long vm = __shfl_down_sync(0xffffffffu, sm, o);
+        const unsigned int vc = __shfl_down_sync(0xffffffffu, sc, o);
+        if (lane + o < 32) {
+            sm += vm;
+            sc += vc;
+        }
+    }
+    __syncthreads();  // the previous user of sh.wm / sh.bin is done
+    if (lane == 0) {
+        sh.wm[warp] = sm;
+        sh.wc[warp] = sc;
+    }
+    if (tid == 0) sh.bin = -1;
+    __syncthreads();
+    unsigned long long later_m = 0;  // the bins of later warps lie above this thread's
+    unsigned int later_c = 0;
+    for (int w = warp + 1; w < 32; ++w) {
+        later_m += sh.wm[w];
+        later_c += sh.wc[w];
+    }
+    unsigned long long run_m = above_m + later_m + (sm - tm);
+    unsigned int run_c = above_c + later_c + (sc - tc);
+    if (b0 < nb)
+        for (int b = b0 + per - 1; b >= b0; --b) {
+            const unsigned long long bm = mass[b];
+            const unsigned int bc = cnt[b];
+            const bool hit = by_mass ? (run_m < target && target <= run_m + bm)
+                                     : (run_c < target && target <= run_c + bc);
+            if (hit) {
+                sh.bin = b;
+                sh.above_m = run_m;
+                sh.above_c = run_c;
+            }
+            run_m += bm;
+            run_c += bc;
+        }
+    __syncthreads();
+}
+
 // The first position whose prefix mass (by_mass) or count (otherwise)
 // reaches `target` (>= 1), over the row's probabilities in descending order,
-// equal probabilities by ascending index. Called by every thread of the CTA.
-__device__ Found full_find(const float* __restrict__ srow, int width, float m, float temperature, double sum,
-                           unsigned long long target, bool by_mass, FullShared& sh) {
+// equal probabilities by ascending index. probs: the row's probabilities
+// (written by the first pass); level 1 comes from sh.l1_*. Every thread calls it.
+__device__ Found full_find(const float* __restrict__ probs, int width, unsigned long long target, bool by_mass,
+                           FullShared& sh) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    unsigned int prefix = 0, pmask = 0;
-    unsigned long long above_m = 0;
-    unsigned int above_c = 0;
-    const int shifts[3] = {20, 8, 0}, bits[3] = {12, 12, 8};
-    for (int lv = 0; lv < 3; ++lv) {
-        const int nb = 1 << bits[lv], sft = shifts[lv];
+    full_scan(sh.l1_mass, sh.l1_cnt, kFullBins, 0, 0, target, by_mass, sh);
+    if (sh.bin < 0) return Found{0, 0, 0, 0};
+    unsigned int prefix = (unsigned)sh.bin << 20, pmask = 0xFFFu << 20;
+    unsigned long long above_m = sh.above_m;
+    unsigned int above_c = sh.above_c;
+    const unsigned int* pbits = reinterpret_cast<const unsigned int*>(probs);
+    for (int lv = 1; lv < 3; ++lv) {
+        const int nb = lv == 1 ? 4096 : 256, sft = lv == 1 ? 8 : 0;
         for (int b = tid; b < nb; b += kFullThreads) {
             sh.mass[b] = 0;
             sh.cnt[b] = 0;
         }
         __syncthreads();
-        // Warp-uniform tiles: lanes with the same bin add their masses with
-        // shuffles first, so a bin shared by a whole warp (a flat
-        // distribution) costs one shared atomic, not 32.
         for (int base = 0; base < width; base += kFullThreads) {
             const int i = base + tid;
             int bin = -1;
             unsigned long long fx = 0;
             if (i < width) {
-                const float pr = full_prob(srow[i], m, temperature, sum);
-                const unsigned int key = __float_as_uint(pr);
+                const unsigned int key = pbits[i];
                 if ((key & pmask) == prefix) {
                     bin = (int)((key >> sft) & (unsigned)(nb - 1));
-                    fx = prob_fx(pr);
+                    fx = prob_fx(__uint_as_float(key));
                 }
             }
-            const unsigned grp = __match_any_sync(0xffffffffu, bin);
-            unsigned long long gsum = 0;
-#pragma unroll 8
-            for (int o = 0; o < 32; ++o) {
-                const unsigned long long v = __shfl_sync(0xffffffffu, fx, o);
-                if ((grp >> o) & 1u) gsum += v;
-            }
-            if (bin >= 0 && __ffs(grp) - 1 == lane) {
-                atomicAdd(&sh.mass[bin], gsum);
-                atomicAdd(&sh.cnt[bin], (unsigned)__popc(grp));
-            }
+            full_hist_add(sh.mass, sh.cnt, bin, fx);
         }
         __syncthreads();
-        // Suffix sums over the bins in descending order: thread t owns bins
-        // [t*per, t*per + per); the threads are scanned from the top.
-        const int per = nb / kFullThreads > 0 ? nb / kFullThreads : 1;
-        unsigned long long tm = 0;
-        unsigned int tc = 0;
-        const int b0 = tid * per;
-        if (b0 < nb)
-            for (int b = b0; b < b0 + per; ++b) {
-                tm += sh.mass[b];
-                tc += sh.cnt[b];
-            }
-        unsigned long long sm = tm;  // inclusive suffix over the lanes >= this one
-        unsigned int sc = tc;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const unsigned long long vm = __shfl_down_sync(0xffffffffu, sm, o);
-            const unsigned int vc = __shfl_down_sync(0xffffffffu, sc, o);
-            if (lane + o < 32) {
-                sm += vm;
-                sc += vc;
-            }
-        }
-        if (lane == 0) {
-            sh.wm[warp] = sm;
-            sh.wc[warp] = sc;
-        }
-        if (tid == 0) sh.bin = -1;
-        __syncthreads();
-        unsigned long long later_m = 0;  // mass of the bins of later warps (above this thread's)
-        unsigned int later_c = 0;
-        for (int w = warp + 1; w < 32; ++w) {
-            later_m += sh.wm[w];
-            later_c += sh.wc[w];
-        }
-        unsigned long long run_m = above_m + later_m + (sm - tm);
-        unsigned int run_c = above_c + later_c + (sc - tc);
-        if (b0 < nb)
-            for (int b = b0 + per - 1; b >= b0; --b) {
-                const unsigned long long bm = sh.mass[b];
-                const unsigned int bc = sh.cnt[b];
-                const bool hit = by_mass ? (run_m < target && target <= run_m + bm)
-                                         : (run_c < target && target <= run_c + bc);
-                if (hit) {
-                    sh.bin = b;
-                    sh.above_m = run_m;
-                    sh.above_c = run_c;
-                }
-                run_m += bm;
-                run_c += bc;
-            }
-        if (lv == 0 && tid == 0) {
-            unsigned long long t = 0;
-            for (int w = 0; w < 32; ++w) t += sh.wm[w];
-            sh.total = t;
-        }
-        __syncthreads();
-        if (sh.bin < 0) return Found{0, 0, 0, 0};
+        full_scan(sh.mass, sh.cnt, nb, above_m, above_c, target, by_mass, sh);
+        if (sh.bin < 0) return Found{0, 0, 0, 0};  // not reached: level 1 found the target's bin
         prefix |= (unsigned)sh.bin << sft;
         pmask |= (unsigned)(nb - 1) << sft;
         above_m = sh.above_m;
         above_c = sh.above_c;
-        __syncthreads();
     }
     // Every element left has the key `prefix`; the c-th of them by index is the answer.
     const unsigned long long tau_fx = prob_fx(__uint_as_float(prefix));
@@ -421,8 +434,7 @@ __device__ Found full_find(const float* __restrict__ srow, int width, float m, f
     unsigned int run = 0;
     for (int base = 0; base < width; base += kFullThreads) {
         const int i = base + tid;
-        bool match = false;
-        if (i < width) match = __float_as_uint(full_prob(srow[i], m, temperature, sum)) == prefix;
+        const bool match = i < width && pbits[i] == prefix;
         const int tile = __syncthreads_count(match);
         if (run + (unsigned)tile >= c) {
             const unsigned bal = __ballot_sync(0xffffffffu, match);
@@ -443,7 +455,7 @@ __device__ Found full_find(const float* __restrict__ srow, int width, float m, f
 __global__ void __launch_bounds__(kFullThreads, 1)
 sample_full_kernel(const SamplePartial* __restrict__ parts, int segs, const float* __restrict__ scores, int ld,
                    float temperature, int top_k, float top_p, int width, const double* __restrict__ uniforms,
-                   int32_t* __restrict__ out) {
+                   float* __restrict__ probs_all, int ld_p, int32_t* __restrict__ out) {
     extern __shared__ __align__(16) unsigned char full_smem[];
     FullShared& sh = *reinterpret_cast<FullShared*>(full_smem);
     const int row = blockIdx.x, tid = threadIdx.x;
@@ -472,6 +484,10 @@ sample_full_kernel(const SamplePartial* __restrict__ parts, int segs, const floa
             sh.key = key;
         }
     }
+    for (int b = tid; b < kFullBins; b += kFullThreads) {
+        sh.l1_mass[b] = 0;
+        sh.l1_cnt[b] = 0;
+    }
     __syncthreads();
     const float m = sh.m;
     const double sum = sh.sum;
@@ -479,42 +495,55 @@ sample_full_kernel(const SamplePartial* __restrict__ parts, int segs, const floa
         if (tid == 0) out[row] = aexis_argmax_index(sh.key);
         return;
     }
+    // One pass over the scores: the probabilities (kept for the later
+    // passes) and the level-1 histogram every query starts from.
     const float* srow = scores + (long long)row * ld;
+    float* probs = probs_all + (long long)row * ld_p;
+    for (int base = 0; base < width; base += kFullThreads) {
+        const int i = base + tid;
+        int bin = -1;
+        unsigned long long fx = 0;
+        if (i < width) {
+            const float pr = full_prob(srow[i], m, temperature, sum);
+            probs[i] = pr;
+            bin = (int)(__float_as_uint(pr) >> 20);
+            fx = prob_fx(pr);
+        }
+        full_hist_add(sh.l1_mass, sh.l1_cnt, bin, fx);
+    }
+    __syncthreads();
+    if (tid == 0) {
+        unsigned long long t = 0;
+        for (int b = 0; b < kFullBins; ++b) t += sh.l1_mass[b];
+        sh.total = t;
+    }
+    __syncthreads();
     // keep = min(top_k, V) (all when top_k <= 0); kept = its prefix mass.
     int keep = width, keep_idx = -1;
-    unsigned long long kept = 0;
-    bool kept_known = false;
+    unsigned long long kept = sh.total;
     if (top_k > 0 && top_k < width) {
-        const Found f = full_find(srow, width, m, temperature, sum, (unsigned long long)top_k, false, sh);
+        const Found f = full_find(probs, width, (unsigned long long)top_k, false, sh);
         keep = f.pos;
         keep_idx = f.idx;
         kept = f.mass;
-        kept_known = true;
     }
     if (top_p < 1.0f) {
         // The nucleus: the first position whose cumulative reaches top_p, if within keep.
         const double tp = top_p > 0.0f ? (double)top_p : 0.0;
         unsigned long long target = (unsigned long long)ceil(tp * 4611686018427387904.0);
         if (target < 1) target = 1;
-        const Found f = full_find(srow, width, m, temperature, sum, target, true, sh);
+        const Found f = full_find(probs, width, target, true, sh);
         if (f.ok && f.pos <= keep) {
             keep = f.pos;
             keep_idx = f.idx;
             kept = f.mass;
-            kept_known = true;
         }
-    }
-    if (!kept_known) {
-        // keep = V: the whole row's mass (level 1 of any search sums it; a
-        // target above every mass stops the search there).
-        if (!(top_p < 1.0f)) full_find(srow, width, m, temperature, sum, ~0ull, true, sh);
-        kept = sh.total;
     }
     // The draw: the first position whose cumulative reaches u * kept.
     unsigned long long x = (unsigned long long)(uniforms[row] * (double)kept);
     if (x < 1) x = 1;
     if (x > kept) x = kept;
-    const Found f = full_find(srow, width, m, temperature, sum, x, true, sh);
+    const Found f = full_find(probs, width, x, true, sh);
     if (tid == 0) {
         int pick = f.ok ? f.idx : -1;
         if (!f.ok || f.pos > keep) pick = keep_idx >= 0 ? keep_idx : f.idx;
@@ -541,13 +570,15 @@ int sample_segments(int rows, int width, int sm_count) {
     return segs < 1 ? 1 : segs;
 }
 
-size_t sample_scratch_bytes(int rows, int width, int sm_count, bool scores) {
+size_t sample_scratch_bytes(int rows, int width, int sm_count, bool scores, bool full) {
     const size_t ld_s = (size_t)((width + 3) & ~3);
     size_t b = (size_t)rows * sample_segments(rows, width, sm_count) * sizeof(SamplePartial);
     b = (b + 255) & ~(size_t)255;
     b += (size_t)rows * 64 * (sizeof(float) + sizeof(int32_t));
     b = (b + 255) & ~(size_t)255;
     if (scores) b += (size_t)rows * ld_s * sizeof(float);
+    b = (b + 255) & ~(size_t)255;
+    if (full) b += (size_t)rows * ld_s * sizeof(float);
     return b;
 }
 
@@ -578,9 +609,14 @@ cudaError_t launch_sample(const float* logits, int rows, int width, int ld, cons
         const size_t smem = sizeof(FullShared);
         e = cudaFuncSetAttribute(sample_full_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
+        size_t poff = ((size_t)rows * segs * sizeof(SamplePartial) + 255) & ~(size_t)255;
+        poff = (poff + (size_t)rows * 64 * 8 + 255) & ~(size_t)255;
+        if (penalised) poff += (size_t)rows * ld_s * sizeof(float);
+        poff = (poff + 255) & ~(size_t)255;
+        float* probs = reinterpret_cast<float*>(p + poff);
         sample_full_kernel<<<rows, kFullThreads, smem, s>>>(parts, segs, penalised ? scores : logits,
                                                             penalised ? ld_s : ld, temperature, top_k, top_p, width,
-                                                            uniforms, out);
+                                                            uniforms, probs, ld_s, out);
         return cudaGetLastError();
     }
     const int k = sample ? (top_k < width ? top_k : width) : 1;

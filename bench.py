@@ -687,7 +687,18 @@ def bench_sampler(ops, peak):
         t = e0.elapsed_time(e1) / 1e3 / n
         read = rows * vocab * 4
         out[f"rows{rows}"] = {"us_per_call": round(t * 1e6, 2), "logits_GB/s": round(read / t / 1e9, 1)}
-    out["workload"] = "Qwen35Sampler.Select defaults (T 0.3, top-k 50, top-p 0.8, penalty 1.1), vocab 151936"
+        # The whole vocabulary (top_k 0): the radix select by probability mass.
+        for _ in range(3):
+            ops.sample(logits, rows, vocab, hist, 1.1, 0.3, 0, 0.8, u, ids)
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(10):
+            ops.sample(logits, rows, vocab, hist, 1.1, 0.3, 0, 0.8, u, ids)
+        e1.record()
+        e1.synchronize()
+        out[f"rows{rows}_top_k0"] = {"us_per_call": round(e0.elapsed_time(e1) / 10 * 1e3, 2)}
+    out["workload"] = ("Qwen35Sampler.Select defaults (T 0.3, top-k 50, top-p 0.8, penalty 1.1), vocab 151936;"
+                       " *_top_k0: the same with top-k 0 (the whole vocabulary)")
     out["timing"] = "CUDA events over 50 back-to-back calls, logits resident"
     return out
 

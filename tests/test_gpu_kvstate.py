@@ -140,13 +140,22 @@ def test_batch_state_export_import(ops, oracle, head_dim):
     got_src = src.generate(first, 6)
     got_dst = dst.generate(first, 6)
     assert np.array_equal(got_src, got_dst)
-    assert np.array_equal(src.logits(), dst.logits())
-    # After decoding, both hold the same (longer) state.
+    # The batched GEMMs split K over CTAs and add with fp32 atomics, so two
+    # runs agree to rounding, not bit for bit.
+    ls, ld = src.logits(), dst.logits()
+    assert np.max(np.abs(ls - ld)) <= 1e-5 * np.abs(ls).max()
+    # After decoding, both hold the same (longer) state: the imported context
+    # bit for bit, the decoded positions within one fp16 rounding.
     k2, v2 = torch.empty_like(k), torch.empty_like(k)
     for i in range(ctx.size):
         src.kv_export(i, 1, k, v, rows)
         dst.kv_export(i, 1, k2, v2, rows)
-        assert torch.equal(k, k2) and torch.equal(v, v2)
+        for a, b in ((k, k2), (v, v2)):
+            la = unpack4_cdhw(a.cpu().numpy(), cfg.n_kv_heads, rows, cfg.head_dim)
+            lb = unpack4_cdhw(b.cpu().numpy(), cfg.n_kv_heads, rows, cfg.head_dim)
+            n = int(ctx[i])
+            assert np.array_equal(la[:, :n], lb[:, :n])
+            assert np.allclose(la[:, n:], lb[:, n:], rtol=1e-3, atol=1e-6)
     with pytest.raises(errors.ArgumentOutOfRangeError):
         dst.kv_import(0, 0, k, v, rows, 150)  # no room left for a token
     with pytest.raises(errors.ArgumentOutOfRangeError):
