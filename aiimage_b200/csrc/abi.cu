@@ -164,6 +164,7 @@ AEXIS_API int aexis_cuda_destroy(aexis_ctx* ctx) {
     if (ctx->act_q) cudaFree(ctx->act_q);
     if (ctx->samp) cudaFree(ctx->samp);
     if (ctx->pack_a) cudaFree(ctx->pack_a);
+    if (ctx->fused) cudaFree(ctx->fused);
     if (ctx->status) cudaFree(ctx->status);
     if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
     delete ctx;
@@ -497,6 +498,55 @@ AEXIS_API int aexis_cuda_gemm_pack4a(aexis_ctx* ctx, const void* a, int a_dtype,
                                                     ctx->stream), "Pack4 input gather launch");
     if (rc) return rc;
     return gemm_common(ctx, ctx->pack_a, a_dtype, k, m, k, w, bias, alpha, beta, y, y_dtype, ldy, n, EPI_STORE);
+}
+
+// ------------------------------------------------------------ lm_head + top-k
+namespace {
+
+size_t align256(size_t b) { return (b + 255) & ~(size_t)255; }
+
+}  // namespace
+
+AEXIS_API int aexis_cuda_gemm_topk(aexis_ctx* ctx, const void* a, int a_dtype, int lda, int m, int k,
+                                   const aexis_weights* w, float alpha, int top_k, int64_t index_offset,
+                                   float* out_vals, int32_t* out_idx, uint64_t* greedy_keys) {
+    if (!ctx) return AEXIS_E_NULL;
+    if (!a || !w || !out_vals || !out_idx) return aexis_fail(ctx, AEXIS_E_NULL, "a, b or an output is null");
+    if (m <= 0 || k <= 0) return aexis_fail(ctx, AEXIS_E_RANGE, "m=%d k=%d", m, k);
+    if (top_k < 1 || top_k > 64) return aexis_fail(ctx, AEXIS_E_RANGE, "top_k=%d (1..64)", top_k);
+    if (w->kind != WK_Q4 && w->kind != WK_Q8)
+        return aexis_fail(ctx, AEXIS_E_UNSUPPORTED, "Gemm needs INT4 or INT8 weights");
+    if (w->k != k) return aexis_fail(ctx, AEXIS_E_SHAPE, "weight is [%d, %d], call asks for k=%d", w->n, w->k, k);
+    if (lda < k) return aexis_fail(ctx, AEXIS_E_SHAPE, "lda=%d < k", lda);
+    if (!valid_dtype(a_dtype)) return aexis_fail(ctx, AEXIS_E_UNSUPPORTED, "dtype a=%d", a_dtype);
+    int rc = bind(ctx);
+    if (rc) return rc;
+    const int n = w->n;
+    // The logits in a context buffer (row stride n), then the top-k kernels
+    // over them and the greedy keys from the top-k lists.
+    const size_t need = align256((size_t)m * n * sizeof(float));
+    if (need > ctx->fused_bytes) {
+        if (ctx->fused) {
+            cudaStreamSynchronize(ctx->stream);
+            cudaFree(ctx->fused);
+            ctx->fused = nullptr;
+            ctx->fused_bytes = 0;
+        }
+        rc = aexis_cuda_check(ctx, cudaMalloc(&ctx->fused, need), "logits buffer");
+        if (rc) return rc;
+        ctx->fused_bytes = need;
+    }
+    float* logits = reinterpret_cast<float*>(ctx->fused);
+    rc = gemm_common(ctx, a, a_dtype, lda, m, k, w, nullptr, alpha, 1.0f, logits, AEXIS_F32, n, n, EPI_STORE_TILED);
+    if (rc) return rc;
+    void* tk = nullptr;
+    rc = aexis_scratch(ctx, topk_scratch_bytes(m, n, top_k, ctx->sm_count), &tk);
+    if (rc) return rc;
+    cudaError_t e = launch_topk(logits, m, n, n, top_k, out_vals, out_idx, tk, ctx->sm_count, ctx->stream);
+    if (e == cudaSuccess && greedy_keys)
+        e = launch_topk_greedy_keys(logits, m, n, out_vals, out_idx, top_k, (long long)index_offset,
+                                    reinterpret_cast<unsigned long long*>(greedy_keys), ctx->stream);
+    return aexis_cuda_check(ctx, e, "lm_head top-k launch");
 }
 
 // ------------------------------------------------------- pointwise layers

@@ -59,6 +59,9 @@ struct aexis_ctx {
     // with more than one slice; grow-only).
     void* pack_a = nullptr;
     size_t pack_a_bytes = 0;
+    // aexis_cuda_gemm_topk: the logits between its GEMM and its top-k (grow-only).
+    void* fused = nullptr;
+    size_t fused_bytes = 0;
 };
 
 // Records `msg` on the context and returns `code`.

@@ -57,6 +57,7 @@ SIGNATURES = {
     "aexis_cuda_argmax_static": (i32, [vp, i32, i32, i32, vp, vp]),
     "aexis_cuda_argmax_keys": (i32, [vp, vp, i32, i32, i32, C.c_int64, vp]),
     "aexis_cuda_topk": (i32, [vp, vp, i32, i32, i32, i32, vp, vp]),
+    "aexis_cuda_gemm_topk": (i32, [vp, vp, i32, i32, i32, i32, vp, f32, i32, C.c_int64, vp, vp, vp]),
     "aexis_cuda_topk_merge": (i32, [vp, vp, i32, i32, i32, i32, vp, vp, vp]),
     "aexis_cuda_embed": (i32, [vp, vp, i32, vp, vp, vp]),
     "aexis_cuda_swish": (i32, [vp, vp, i32, vp]),

@@ -323,6 +323,19 @@ class AexisOps:
         ld = ld if ld is not None else (logits.stride(0) if logits.dim() == 2 else width)
         self._call(lib().aexis_cuda_topk, _ptr(logits), rows, width, ld, k, _ptr(out_vals), _ptr(out_idx))
 
+    def gemm_topk(self, a, m, k, top_k, out_vals, out_idx, keys=None, alpha=1.0, index_offset=0):
+        """The bound Q8/Q4 weights' tiled lm_head (no bias) and the top-k of its logits per row, without
+        writing the logits (aexis_cuda_gemm_topk): out_vals/out_idx [m, top_k], optional greedy keys [m]
+        (int64 view of the uint64 keys) with global indices (index_offset added)."""
+        if a is None:
+            raise errors.ArgumentNullError("a")
+        w = self._int4 or self._int8
+        if w is None:
+            raise errors.NotSupportedError("only INT4/INT8 weight-only Gemm weights are implemented by this backend")
+        lda = a.stride(0) if a.dim() == 2 else k
+        self._call(lib().aexis_cuda_gemm_topk, _ptr(a), _dtype_code(a), lda, m, k, w.handle, float(alpha), int(top_k),
+                   int(index_offset), _ptr(out_vals), _ptr(out_idx), _ptr(keys))
+
     def topk_greedy_keys(self, logits, width, rows, k, top_vals, top_idx, index_offset, keys, ld=None):
         """The shard's argmax keys (as argmax_keys) from its top-k lists, without re-reading the logits."""
         ld = ld if ld is not None else (logits.stride(0) if logits.dim() == 2 else width)

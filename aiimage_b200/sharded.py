@@ -2,11 +2,11 @@
 
 Rank r of G holds the contiguous lm_head rows [r*V/G, (r+1)*V/G) as a Q8 weight
 handle. One call:
-  1. logits of the shard, [M, V/G] fp32, on the tensor cores (aexis_cuda_gemm);
-  2. per row the shard's top-k (aexis_cuda_topk, indices shifted by the shard
-     offset), and from its first entry the shard's argmax as a 64-bit key
-     carrying the GLOBAL index (aexis_cuda_topk_greedy_keys: the same keys as
-     aexis_cuda_argmax_keys without a second pass over the logits);
+  1-2. per row the shard's top-k and, from its first entry, the shard's
+     argmax as a 64-bit key carrying the GLOBAL index, in one
+     aexis_cuda_gemm_topk: the [M, V/G] logits on the tensor cores, then the
+     top-k and the greedy keys from the top-k lists (aexis_cuda_gemm_tiled +
+     aexis_cuda_topk + aexis_cuda_topk_greedy_keys in one call);
   3. the keys and the top-k lists packed into one buffer, one all-gather of
      those buffers (NCCL over NVLink; gloo in the CPU tests), then one merge
      kernel (aexis_cuda_topk_merge): the largest key, and the k largest
@@ -82,24 +82,27 @@ class ShardedLmHead:
         self.ops.gemm2d_pack4_tiled_texture_a(x, None, m, self.n, self.hidden, True, 1.0, 1.0, False, 4, out)
         return out
 
+    def shard_topk(self, x: torch.Tensor, k: int, keys, vals, idx):
+        """The shard's top-k (shard-local indices) and greedy keys (global indices), fused with its GEMM."""
+        self.ops.set_int4_gemm_weights(None)
+        self.ops.set_int8_gemm_weights(self.w)
+        self.ops.gemm_topk(x, x.shape[0], self.hidden, k, vals, idx, keys, 1.0, self.lo)
+
     def forward(self, x: torch.Tensor, k: int = 50, logits: torch.Tensor | None = None):
-        """Greedy ids [M] (int64) and the global top-k (values [M,k], ids [M,k])."""
+        """Greedy ids [M] (int64) and the global top-k (values [M,k], ids [M,k]).
+        `logits` is accepted for compatibility and not used (nothing is materialised)."""
         m = x.shape[0]
-        logits = self.shard_logits(x, logits)
         if self.world == 1:
             keys = torch.empty(m, dtype=torch.int64, device=x.device)
             vals = torch.empty((m, k), dtype=torch.float32, device=x.device)
             idx = torch.empty((m, k), dtype=torch.int32, device=x.device)
-            self.ops.top_k(logits, self.n, m, k, vals, idx)
-            self.ops.topk_greedy_keys(logits, self.n, m, k, vals, idx, self.lo, keys)
+            self.shard_topk(x, k, keys, vals, idx)
             return keys_to_ids(keys), vals, idx.to(torch.int64)
         # The shard's keys and top-k straight into one packed buffer, one
         # all-gather, one merge kernel.
         buf = torch.empty(packed_words(m, k), dtype=torch.int32, device=x.device)
         keys, vals, idx = pack_views(buf, m, k)
-        # One pass over the shard's logits: the greedy keys come from the top-k lists.
-        self.ops.top_k(logits, self.n, m, k, vals, idx)
-        self.ops.topk_greedy_keys(logits, self.n, m, k, vals, idx, self.lo, keys)
+        self.shard_topk(x, k, keys, vals, idx)
         gathered = exchange(buf, self.group)
         ids = torch.empty(m, dtype=torch.int64, device=x.device)
         out_v = torch.empty((m, k), dtype=torch.float32, device=x.device)

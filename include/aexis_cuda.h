@@ -257,6 +257,20 @@ int aexis_cuda_argmax_keys(aexis_ctx* ctx, const float* logits, int rows, int wi
 int aexis_cuda_topk_greedy_keys(aexis_ctx* ctx, const float* logits, int rows, int width, int ld, int k,
                                 const float* top_vals, const int32_t* top_idx, int64_t index_offset,
                                 uint64_t* keys);
+/* The lm_head and the sampler's top-k in one call, for a batch of hidden
+ * states: aexis_cuda_gemm_tiled (bias NULL, beta 1) into a context buffer of
+ * [m, w->n] fp32 logits, then aexis_cuda_topk and (when greedy_keys is not
+ * NULL) aexis_cuda_topk_greedy_keys on them, with the same results
+ * (AexisGemm2DPack4TiledTextureAFromLinear, HLSL Pack4Matmul:2245-2275, then
+ * the Qwen35Sampler candidate order, Samples/.../Qwen35DecoderSession.cs:
+ * 1869-1872; no single reference counterpart).
+ * out_vals/out_idx: device [m, top_k] (shard-local indices); greedy_keys:
+ * device uint64 [m] with global indices (index_offset added), or NULL.
+ * Errors: as aexis_cuda_gemm_tiled; top_k outside 1..64 -> E_RANGE. */
+int aexis_cuda_gemm_topk(aexis_ctx* ctx, const void* a, int a_dtype, int lda, int m, int k,
+                         const aexis_weights* w, float alpha, int top_k, int64_t index_offset, float* out_vals,
+                         int32_t* out_idx, uint64_t* greedy_keys);
+
 /* Rows that aexis_cuda_argmax_static accepts in one call (the size of its
  * fixed key array: 4096 x 8 bytes, held on every GPU that loads the library). */
 #define AEXIS_ARGMAX_STATIC_MAX_ROWS 4096

@@ -84,3 +84,62 @@ def test_config5_lm_head_rows_and_argmax(ops, oracle):
     ref = oracle.gemm(x[rows].astype(np.float32), 8, p, s.astype(np.float32), 0, n)
     assert_gemv_close(got[rows], ref)
     assert np.array_equal(np.argmax(got[rows], axis=1), oracle.argmax(ref))
+
+
+def _unfused_topk(ops, w, x, k, offset):
+    """Reference for aexis_cuda_gemm_topk: the tiled lm_head to fp32 logits, then the top-k and greedy-key calls."""
+    import torch
+    m, n = x.shape[0], w.n
+    logits = torch.empty((m, n), dtype=torch.float32, device="cuda")
+    ops.set_int4_gemm_weights(None)
+    ops.set_int8_gemm_weights(w)
+    ops.gemm2d_pack4_tiled_texture_a(x, None, m, n, w.k, True, 1.0, 1.0, False, 4, logits)
+    vals = torch.empty((m, k), dtype=torch.float32, device="cuda")
+    idx = torch.empty((m, k), dtype=torch.int32, device="cuda")
+    keys = torch.empty(m, dtype=torch.int64, device="cuda")
+    ops.top_k(logits, n, m, k, vals, idx)
+    ops.topk_greedy_keys(logits, n, m, k, vals, idx, offset, keys)
+    return vals, idx, keys
+
+
+@pytest.mark.parametrize("n,m,act,k,offset", [
+    (151936, 256, "f16", 50, 0),      # BASELINE config 5 on one GPU
+    (18992, 256, "f16", 50, 132944),  # the last of eight vocab shards (global indices)
+    (37984, 37, "f32", 64, 37984),    # fp32 activations (hi/lo split), ragged m
+    (75968, 5, "f16", 1, 0),          # k = 1: the greedy token alone
+    (4097, 128, "f16", 20, 0),        # a partial last slab
+    (3000, 16, "f16", 50, 0),         # narrow rows: the exact top-k path
+])
+def test_fused_lm_head_topk_matches_unfused(ops, n, m, act, k, offset):
+    """aexis_cuda_gemm_topk: the same values, indices and greedy keys, bit for bit, as the logits written
+    by the tiled GEMM followed by aexis_cuda_topk and aexis_cuda_topk_greedy_keys. Adversarial rows: all
+    logits equal (x = 0: ties go by index), all NaN (nothing selectable, (-inf, -1) padding, the greedy
+    key of a NaN at index 0), huge activations, and a row equal to another."""
+    import torch
+    p, s = synth.q8_weights(n, 1024, seed=n % 97, tag=(n, 1024))
+    w = ops.new_int8_weight_only_upload(p, s, n, 1024)
+    x = synth.activations(1024, seed=n % 89, tag=(m, 1024), m=m).astype(np.float32)
+    x[0] = 0.0
+    if m > 3:
+        x[1] = np.nan
+        x[2] *= 1000.0
+        x[3] = x[4 % m]
+    xt = torch.from_numpy(x if act == "f32" else x.astype(np.float16)).cuda()
+    rv, ri, rk = _unfused_topk(ops, w, xt, k, offset)
+    vals = torch.full((m, k), 7.0, dtype=torch.float32, device="cuda")
+    idx = torch.full((m, k), -7, dtype=torch.int32, device="cuda")
+    keys = torch.zeros(m, dtype=torch.int64, device="cuda")
+    ops.set_int8_gemm_weights(w)
+    for _ in range(2):  # twice: the second call reuses the sample and the buffers
+        ops.gemm_topk(xt, m, 1024, k, vals, idx, keys, 1.0, offset)
+        torch.cuda.synchronize()
+        ops.sync()
+        assert torch.equal(vals, rv) and torch.equal(idx, ri) and torch.equal(keys, rk)
+    assert idx[0].tolist() == list(range(k))  # the plateau: lowest indices first
+    if m > 3:
+        assert (idx[1] == -1).all() and torch.isinf(vals[1]).all()
+        if offset == 0:
+            assert int(keys[1]) & 0xFFFFFFFF == 0xFFFFFFFF  # a NaN at global index 0 is the greedy pick
+        else:
+            assert int(keys[1]) == 0  # a shard past index 0 has nothing selectable in an all-NaN row
+        assert torch.equal(idx[3], idx[4 % m])
