@@ -9,11 +9,24 @@ struct aexis_decoder {
     aexis_ctx* ctx = nullptr;
     aexis_decoder_config cfg = {};
     struct Layer {
+        // A linear-attention layer keeps in_proj in qkv and out_proj in o.
         aexis_weights qkv, o, gateup, down;
         float* norm[2] = {nullptr, nullptr};
-        int set_mask = 0;  // bit w set once linear w was loaded; bits 7,8 the norms
+        // bit w set once linear w was loaded (in_proj bit 0, out_proj bit 3,
+        // the linear-attention parameters bits 1 and 2); bits 7,8 the norms
+        int set_mask = 0;
+        int kind = AEXIS_LAYER_FULL_ATTENTION;
+        int attn_slot = -1;             // full attention: index of its KV cache
+        float* conv_w = nullptr;        // linear attention: [conv_kernel][channels]
+        float* lin_params = nullptr;    // a_log [heads], dt_bias [heads], gamma [vdim]
+        float* conv_state = nullptr;    // [conv_kernel][channels]
+        float* gdr_state = nullptr;     // [heads][kdim][vdim]
     };
     std::vector<Layer> layers;
+    int n_attn = 0;                 // full-attention layers (KV caches)
+    bool hybrid = false;            // some layer is linear attention
+    float* lin_proj = nullptr;      // in_proj output of the current linear-attention layer
+    float* lin_y = nullptr;         // its gated-norm output (out_proj input)
     aexis_weights lm;
     int lm_set = 0;
     float* final_norm = nullptr;
@@ -22,7 +35,7 @@ struct aexis_decoder {
     int* rope_map = nullptr;        // [qkv rows]
     float* rope_cos = nullptr;      // [cap][rot/2]
     float* rope_sin = nullptr;
-    __half* kcache = nullptr;       // [layers][kv][cap][D]
+    __half* kcache = nullptr;       // [full-attention layers][kv][cap][D]
     __half* vcache = nullptr;
     float *h = nullptr, *q = nullptr, *attn = nullptr, *act = nullptr, *logits = nullptr, *part = nullptr;
     unsigned int* counters = nullptr;
@@ -43,6 +56,25 @@ struct aexis_decoder {
     void* persist_off = nullptr;     // [sm_count + 1] unit offsets into persist_stream
     bool persist_packed = false;     // persist_stream matches the current weights
 };
+
+// One decode step of a linear-attention block after its in_proj GEMV
+// (k_recurrent.cu): ShortConv + SiLU, the Gated Delta Rule and the gated
+// per-head RMSNorm, one cluster of vdim/16 CTAs per head, launched as a
+// programmatic dependent of the previous kernel.
+struct LinAttnDecode {
+    const float* proj = nullptr;     // in_proj output [q k v z b a]
+    const float* conv_w = nullptr;   // [kernel][channels]
+    float* conv_state = nullptr;     // [kernel][channels], shifted in place
+    const float* a_log = nullptr;    // [heads]
+    const float* dt_bias = nullptr;  // [heads]
+    const float* gamma = nullptr;    // [vdim]
+    float* state = nullptr;          // [heads][kdim][vdim], updated in place
+    float* y = nullptr;              // [heads][vdim], the out_proj input
+    int heads = 0, kdim = 0, vdim = 0, kernel = 0;
+    float gdr_eps = 1e-6f, norm_eps = 1e-6f;
+};
+bool lin_attn_decode_supported(int heads, int kdim, int vdim, int kernel);
+cudaError_t launch_lin_attn_decode(const LinAttnDecode& a, cudaStream_t s);
 
 // One layer of one sequence's KV cache (fp16 [kvh][cap][D], rows swizzled
 // when swz) to and from Pack4 CDHW fp32 [w = D, h = rows, c = kvh]

@@ -658,6 +658,8 @@ AEXIS_API int aexis_cuda_batch_create(aexis_decoder* d, int max_batch, int kv_ca
         return aexis_fail(ctx, AEXIS_E_UNSUPPORTED, "batched decoding runs Q8 weights (bits=%d lm_bits=%d)", c.bits,
                           c.lm_bits);
     const int D = c.head_dim, qd = c.n_heads * D;
+    if (d->hybrid)
+        return aexis_fail(ctx, AEXIS_E_UNSUPPORTED, "batched decoding runs full-attention stacks only");
     if (c.hidden % 64 || qd % 64 || c.ffn % 64)
         return aexis_fail(ctx, AEXIS_E_UNSUPPORTED, "hidden, ffn and heads*head_dim must be multiples of 64");
     {

@@ -1,14 +1,22 @@
-// k_decoder.cu -- the fused batch-1 decode step of the synthetic full-attention
-// decoder (Qwen35DecoderSession.DecodeCore + SelectNextToken, greedy).
+// k_decoder.cu -- the fused batch-1 decode step of the synthetic decoder
+// (Qwen35DecoderSession.DecodeCore + SelectNextToken, greedy), all layers
+// full attention or Qwen3.5's hybrid stack of linear- and full-attention
+// blocks.
 //
 // One step is a chain of kernels captured once into a CUDA graph, every edge a
 // programmatic dependent launch (each kernel streams its weights while the
 // previous one drains, then waits for its activation input):
 //   embed      h = E[token] (fp16 table -> fp32), clear the argmax key
-//   per layer  qkv   RMSNorm prologue + Q4/Q8 GEMV + RoPE + fp16 KV append
+//   per full-attention layer
+//              qkv   RMSNorm prologue + Q4/Q8 GEMV + RoPE + fp16 KV append
 //              attn  split-K GQA decode attention, last CTA per KV head merges
 //              o     GEMV, residual add into h
-//              ffn1  RMSNorm prologue + fused gate|up GEMV + SiLU*up
+//   per linear-attention layer
+//              in    RMSNorm prologue + GEMV to [q k v z b a] (fp32)
+//              core  ShortConv + SiLU, Gated Delta Rule, gated per-head
+//                    RMSNorm (lin_attn_decode_kernel, k_recurrent.cu)
+//              out   GEMV, residual add into h
+//   per layer  ffn1  RMSNorm prologue + fused gate|up GEMV + SiLU*up
 //              ffn2  down GEMV, residual add into h
 //   lm_head    RMSNorm prologue + GEMV, logits + fused greedy argmax key
 //   finish     token = argmax, position += 1
@@ -35,6 +43,9 @@ constexpr int kMaxHeadDim = 256;
 constexpr int kMaxGroup = 8;      // query heads per KV head
 constexpr int kMinChunk = 32;     // fewest context positions per split
 constexpr int kMaxChunk = 64;     // chunk bound at the largest supported capacity
+// The Gated Delta Rule's norm eps (reference_ops.py gated_delta_rule default,
+// the value the reference's GatedDeltaRule layer is exported with).
+constexpr float kGdrEps = 1e-6f;
 
 // h = E[token], key = 0. token_src[token_idx ? *token_idx : 0].
 __global__ void dec_embed_kernel(const __half* table, int vocab, int hidden, const int* token,
@@ -300,6 +311,70 @@ cudaError_t launch_pdl(const void* fn, dim3 grid, dim3 block, size_t smem, cudaS
     return cudaLaunchKernelExC(&cfg, fn, args);
 }
 
+// h += down(SiLU(gate(xn)) * up(xn)), xn = RMSNorm(h) * norm[1].
+cudaError_t enqueue_ffn(aexis_decoder* d, aexis_decoder::Layer& L, cudaStream_t s) {
+    cudaError_t e;
+    GemvArgs f1;
+    f1.status = d->ctx->status;
+    f1.pdl = true;
+    f1.x = d->h;
+    f1.w = &L.gateup;
+    f1.y = d->act;
+    f1.epilogue = EPI_SWIGLU;
+    f1.norm_gamma = L.norm[1];
+    f1.norm_eps = d->cfg.eps;
+    if ((e = launch_gemv(f1, d->ctx->sm_count, s)) != cudaSuccess) return e;
+    GemvArgs f2;
+    f2.status = d->ctx->status;
+    f2.pdl = true;
+    f2.x = d->act;
+    f2.w = &L.down;
+    f2.y = d->h;
+    f2.epilogue = EPI_RESIDUAL;
+    return launch_gemv(f2, d->ctx->sm_count, s);
+}
+
+// A linear-attention block's mixer: in_proj (RMSNorm prologue, fp32 [q k v
+// z b a]), the fused conv + GDR + gated-norm kernel, out_proj added into h.
+cudaError_t enqueue_linear_attention(aexis_decoder* d, aexis_decoder::Layer& L, cudaStream_t s) {
+    const auto& c = d->cfg;
+    cudaError_t e;
+    GemvArgs in;
+    in.status = d->ctx->status;
+    in.pdl = true;
+    in.x = d->h;
+    in.w = &L.qkv;
+    in.y = d->lin_proj;
+    in.epilogue = EPI_STORE;
+    in.norm_gamma = L.norm[0];
+    in.norm_eps = c.eps;
+    if ((e = launch_gemv(in, d->ctx->sm_count, s)) != cudaSuccess) return e;
+    LinAttnDecode la;
+    la.proj = d->lin_proj;
+    la.conv_w = L.conv_w;
+    la.conv_state = L.conv_state;
+    la.a_log = L.lin_params;
+    la.dt_bias = L.lin_params + c.lin_heads;
+    la.gamma = L.lin_params + 2 * c.lin_heads;
+    la.state = L.gdr_state;
+    la.y = d->lin_y;
+    la.heads = c.lin_heads;
+    la.kdim = c.lin_kdim;
+    la.vdim = c.lin_vdim;
+    la.kernel = c.conv_kernel;
+    la.gdr_eps = kGdrEps;
+    la.norm_eps = c.eps;
+    if ((e = launch_lin_attn_decode(la, s)) != cudaSuccess) return e;
+    GemvArgs o;
+    o.status = d->ctx->status;
+    o.pdl = true;
+    o.x = d->lin_y;
+    o.w = &L.o;
+    o.y = d->h;
+    o.epilogue = EPI_RESIDUAL;
+    return launch_gemv(o, d->ctx->sm_count, s);
+}
+
 // Enqueue one decode step (emit = 1: lm_head + greedy token; 0: prompt token).
 cudaError_t enqueue_step(aexis_decoder* d, cudaStream_t s, int emit) {
     const auto& c = d->cfg;
@@ -320,8 +395,13 @@ cudaError_t enqueue_step(aexis_decoder* d, cudaStream_t s, int emit) {
     const float scale = 1.0f / sqrtf((float)D);
     for (int l = 0; l < c.n_layers; ++l) {
         auto& L = d->layers[l];
-        __half* kc = d->kcache + (size_t)l * c.n_kv_heads * c.kv_capacity * D;
-        __half* vc = d->vcache + (size_t)l * c.n_kv_heads * c.kv_capacity * D;
+        if (L.kind == AEXIS_LAYER_LINEAR_ATTENTION) {
+            if ((e = enqueue_linear_attention(d, L, s)) != cudaSuccess) return e;
+            if ((e = enqueue_ffn(d, L, s)) != cudaSuccess) return e;
+            continue;
+        }
+        __half* kc = d->kcache + (size_t)L.attn_slot * c.n_kv_heads * c.kv_capacity * D;
+        __half* vc = d->vcache + (size_t)L.attn_slot * c.n_kv_heads * c.kv_capacity * D;
         GemvArgs g;
         g.status = d->ctx->status;
         g.pdl = true;
@@ -367,24 +447,7 @@ cudaError_t enqueue_step(aexis_decoder* d, cudaStream_t s, int emit) {
         o.y = d->h;
         o.epilogue = EPI_RESIDUAL;
         if ((e = launch_gemv(o, d->ctx->sm_count, s)) != cudaSuccess) return e;
-        GemvArgs f1;
-        f1.status = d->ctx->status;
-        f1.pdl = true;
-        f1.x = d->h;
-        f1.w = &L.gateup;
-        f1.y = d->act;
-        f1.epilogue = EPI_SWIGLU;
-        f1.norm_gamma = L.norm[1];
-        f1.norm_eps = c.eps;
-        if ((e = launch_gemv(f1, d->ctx->sm_count, s)) != cudaSuccess) return e;
-        GemvArgs f2;
-        f2.status = d->ctx->status;
-        f2.pdl = true;
-        f2.x = d->act;
-        f2.w = &L.down;
-        f2.y = d->h;
-        f2.epilogue = EPI_RESIDUAL;
-        if ((e = launch_gemv(f2, d->ctx->sm_count, s)) != cudaSuccess) return e;
+        if ((e = enqueue_ffn(d, L, s)) != cudaSuccess) return e;
     }
     if (emit) {
         GemvArgs lm;
@@ -524,18 +587,56 @@ AEXIS_API int aexis_cuda_decoder_create(aexis_ctx* ctx, const aexis_decoder_conf
         return aexis_fail(ctx, AEXIS_E_SHAPE, "lm_group %d must divide hidden", c.lm_group);
     if ((long long)c.kv_capacity > (kAttnSplits * 64LL))
         return aexis_fail(ctx, AEXIS_E_RANGE, "kv_capacity %d > %d", c.kv_capacity, kAttnSplits * 64);
+    bool hybrid = false;
+    if (c.layer_types)
+        for (int l = 0; l < c.n_layers; ++l) {
+            if (c.layer_types[l] != AEXIS_LAYER_FULL_ATTENTION && c.layer_types[l] != AEXIS_LAYER_LINEAR_ATTENTION)
+                return aexis_fail(ctx, AEXIS_E_RANGE, "layer_types[%d] = %d", l, c.layer_types[l]);
+            hybrid |= c.layer_types[l] == AEXIS_LAYER_LINEAR_ATTENTION;
+        }
+    const long long lin_nv = (long long)c.lin_heads * c.lin_vdim;
+    const long long lin_ch = 2LL * c.lin_heads * c.lin_kdim + lin_nv;  // conv channels
+    const long long lin_rows = lin_ch + lin_nv + 2LL * c.lin_heads;    // in_proj rows
+    if (hybrid) {
+        if (!lin_attn_decode_supported(c.lin_heads, c.lin_kdim, c.lin_vdim, c.conv_kernel))
+            return aexis_fail(ctx, AEXIS_E_UNSUPPORTED,
+                              "linear attention heads=%d kdim=%d vdim=%d conv_kernel=%d (kdim a multiple of 4 up "
+                              "to 256, vdim a multiple of 16 up to 128, kernel 1..16)",
+                              c.lin_heads, c.lin_kdim, c.lin_vdim, c.conv_kernel);
+        if (lin_rows > (1LL << 30) || lin_nv % 32 || (c.bits == 4 && lin_nv % c.group))
+            return aexis_fail(ctx, AEXIS_E_SHAPE, "lin_heads*lin_vdim %lld must be a multiple of 32 and of the group",
+                              lin_nv);
+    }
     int rc = aexis_cuda_check(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
     if (rc) return rc;
     aexis_decoder* d = new (std::nothrow) aexis_decoder();
     if (!d) return aexis_fail(ctx, AEXIS_E_STATE, "out of host memory");
     d->ctx = ctx;
     d->cfg = c;
+    d->cfg.layer_types = nullptr;  // the kinds live in layers[]
+    d->hybrid = hybrid;
     d->layers.resize(c.n_layers);
+    for (int l = 0; l < c.n_layers; ++l) {
+        auto& L = d->layers[l];
+        L.kind = c.layer_types ? c.layer_types[l] : AEXIS_LAYER_FULL_ATTENTION;
+        if (L.kind == AEXIS_LAYER_FULL_ATTENTION) L.attn_slot = d->n_attn++;
+    }
     const int kvd = c.n_kv_heads * c.head_dim;
     const int sdt = c.scale_dtype;
     for (auto& L : d->layers) {
-        if (!rc) rc = alloc_weights(d, L.qkv, c.bits, c.group, sdt, qd + 2 * kvd, c.hidden);
-        if (!rc) rc = alloc_weights(d, L.o, c.bits, c.group, sdt, c.hidden, qd);
+        if (L.kind == AEXIS_LAYER_LINEAR_ATTENTION) {
+            const size_t gdr = (size_t)c.lin_heads * c.lin_kdim * c.lin_vdim;
+            if (!rc) rc = alloc_weights(d, L.qkv, c.bits, c.group, sdt, (int)lin_rows, c.hidden);
+            if (!rc) rc = alloc_weights(d, L.o, c.bits, c.group, sdt, c.hidden, (int)lin_nv);
+            if (!rc) rc = alloc(d, (void**)&L.conv_w, sizeof(float) * c.conv_kernel * lin_ch, "conv alloc");
+            if (!rc) rc = alloc(d, (void**)&L.conv_state, sizeof(float) * c.conv_kernel * lin_ch, "conv alloc");
+            if (!rc) rc = alloc(d, (void**)&L.gdr_state, sizeof(float) * gdr, "gdr alloc");
+            if (!rc)
+                rc = alloc(d, (void**)&L.lin_params, sizeof(float) * (2 * c.lin_heads + c.lin_vdim), "param alloc");
+        } else {
+            if (!rc) rc = alloc_weights(d, L.qkv, c.bits, c.group, sdt, qd + 2 * kvd, c.hidden);
+            if (!rc) rc = alloc_weights(d, L.o, c.bits, c.group, sdt, c.hidden, qd);
+        }
         if (!rc) rc = alloc_weights(d, L.gateup, c.bits, c.group, sdt, 2 * c.ffn, c.hidden);
         if (!rc) rc = alloc_weights(d, L.down, c.bits, c.group, sdt, c.hidden, c.ffn);
         if (!rc) rc = alloc(d, (void**)&L.norm[0], sizeof(float) * c.hidden, "norm alloc");
@@ -544,9 +645,11 @@ AEXIS_API int aexis_cuda_decoder_create(aexis_ctx* ctx, const aexis_decoder_conf
     if (!rc) rc = alloc_weights(d, d->lm, c.lm_bits, c.lm_group, sdt, c.vocab, c.hidden);
     if (!rc) rc = alloc(d, (void**)&d->final_norm, sizeof(float) * c.hidden, "norm alloc");
     if (!rc) rc = alloc(d, (void**)&d->embed, sizeof(__half) * (size_t)c.vocab * c.hidden, "embedding alloc");
-    const size_t kv = (size_t)c.n_layers * c.n_kv_heads * c.kv_capacity * c.head_dim;
+    const size_t kv = (size_t)(d->n_attn > 0 ? d->n_attn : 1) * c.n_kv_heads * c.kv_capacity * c.head_dim;
     if (!rc) rc = alloc(d, (void**)&d->kcache, sizeof(__half) * kv, "kv alloc");
     if (!rc) rc = alloc(d, (void**)&d->vcache, sizeof(__half) * kv, "kv alloc");
+    if (!rc && hybrid) rc = alloc(d, (void**)&d->lin_proj, sizeof(float) * lin_rows, "alloc");
+    if (!rc && hybrid) rc = alloc(d, (void**)&d->lin_y, sizeof(float) * lin_nv, "alloc");
     if (!rc) rc = alloc(d, (void**)&d->h, sizeof(float) * c.hidden, "alloc");
     if (!rc) rc = alloc(d, (void**)&d->q, sizeof(float) * qd, "alloc");
     if (!rc) rc = alloc(d, (void**)&d->attn, sizeof(float) * qd, "alloc");
@@ -622,13 +725,14 @@ AEXIS_API int aexis_cuda_decoder_destroy(aexis_decoder* d) {
         free_weights(L.o);
         free_weights(L.gateup);
         free_weights(L.down);
-        if (L.norm[0]) cudaFree(L.norm[0]);
-        if (L.norm[1]) cudaFree(L.norm[1]);
+        float* lbufs[] = {L.norm[0], L.norm[1], L.conv_w, L.conv_state, L.gdr_state, L.lin_params};
+        for (float* b : lbufs)
+            if (b) cudaFree(b);
     }
     free_weights(d->lm);
     void* bufs[] = {d->final_norm, d->embed, d->rope_map, d->rope_cos, d->rope_sin, d->kcache, d->vcache, d->h, d->q,
                     d->attn, d->act, d->logits, d->part, d->counters, d->key, d->ints, d->persist_phases,
-                    d->persist_sync, d->persist_stream, d->persist_off};
+                    d->persist_sync, d->persist_stream, d->persist_off, d->lin_proj, d->lin_y};
     for (void* b : bufs)
         if (b) cudaFree(b);
     delete d;
@@ -651,9 +755,13 @@ AEXIS_API int aexis_cuda_decoder_set_linear(aexis_decoder* d, int layer, int whi
         if (!rc) d->lm_set = 1;
         return rc;
     }
-    if (layer < 0 || layer >= c.n_layers || which < 0 || which > 6)
+    if (layer < 0 || layer >= c.n_layers || which < 0 || which > 9 || which == 7)
         return aexis_fail(d->ctx, AEXIS_E_RANGE, "layer=%d which=%d", layer, which);
     auto& L = d->layers[layer];
+    const bool lin = L.kind == AEXIS_LAYER_LINEAR_ATTENTION;
+    if (lin ? (which <= 3) : (which >= 8))
+        return aexis_fail(d->ctx, AEXIS_E_RANGE, "which=%d does not exist in %s layer %d", which,
+                          lin ? "linear-attention" : "full-attention", layer);
     const int D = c.head_dim, qd = c.n_heads * D, kvd = c.n_kv_heads * D;
     switch (which) {
         case 0:
@@ -675,13 +783,60 @@ AEXIS_API int aexis_cuda_decoder_set_linear(aexis_decoder* d, int layer, int whi
         case 4: rc = scatter_rows(d, L.gateup, packed, scales, scale_dtype, c.ffn, 0, 2, none); break;
         case 5: rc = scatter_rows(d, L.gateup, packed, scales, scale_dtype, c.ffn, 1, 2, none); break;
         case 6: rc = scatter_rows(d, L.down, packed, scales, scale_dtype, c.hidden, 0, 1, none); break;
+        case 8: rc = scatter_rows(d, L.qkv, packed, scales, scale_dtype, L.qkv.n, 0, 1, none); break;
+        case 9: rc = scatter_rows(d, L.o, packed, scales, scale_dtype, c.hidden, 0, 1, none); break;
     }
+    aexis_weights* w = which <= 2 || which == 8 ? &L.qkv : which == 3 || which == 9 ? &L.o
+                     : which <= 5 ? &L.gateup : &L.down;
     if (!rc) {
-        aexis_weights* w = which <= 2 ? &L.qkv : which == 3 ? &L.o : which <= 5 ? &L.gateup : &L.down;
         if (w->frag) rc = build_frag(d, *w);
         d->persist_packed = false;
     }
-    if (!rc) L.set_mask |= 1 << which;
+    if (!rc) L.set_mask |= 1 << (which == 8 ? 0 : which == 9 ? 3 : which);
+    return rc;
+}
+
+AEXIS_API int aexis_cuda_layer_types_interval(int32_t n_layers, int32_t interval, int32_t* out) {
+    if (!out) return AEXIS_E_NULL;
+    if (n_layers < 0) return AEXIS_E_RANGE;
+    for (int i = 0; i < n_layers; ++i)
+        out[i] = interval <= 0 || (i + 1) % interval == 0 ? AEXIS_LAYER_FULL_ATTENTION : AEXIS_LAYER_LINEAR_ATTENTION;
+    return AEXIS_OK;
+}
+
+AEXIS_API int aexis_cuda_decoder_set_linear_attention(aexis_decoder* d, int layer, const void* conv, const void* a_log,
+                                                      const void* dt_bias, const void* gamma, int dtype) {
+    if (!d) return AEXIS_E_NULL;
+    if (!conv || !a_log || !dt_bias || !gamma) return aexis_fail(d->ctx, AEXIS_E_NULL, "parameter array is null");
+    if (dtype != AEXIS_F16 && dtype != AEXIS_F32) return aexis_fail(d->ctx, AEXIS_E_UNSUPPORTED, "dtype %d", dtype);
+    const auto& c = d->cfg;
+    if (layer < 0 || layer >= c.n_layers || d->layers[layer].kind != AEXIS_LAYER_LINEAR_ATTENTION)
+        return aexis_fail(d->ctx, AEXIS_E_RANGE, "layer %d is not a linear-attention layer", layer);
+    int rc = dbind(d);
+    if (rc) return rc;
+    auto& L = d->layers[layer];
+    const size_t K = (size_t)c.conv_kernel;
+    const size_t ch = 2 * (size_t)c.lin_heads * c.lin_kdim + (size_t)c.lin_heads * c.lin_vdim;
+    auto at = [&](const void* p, size_t i) {
+        return dtype == AEXIS_F16 ? __half2float(((const __half*)p)[i]) : ((const float*)p)[i];
+    };
+    // [channels][kernel] -> tap-major [kernel][channels]: a warp reads
+    // consecutive channels of one tap.
+    std::vector<float> w(K * ch);
+    for (size_t g = 0; g < ch; ++g)
+        for (size_t k = 0; k < K; ++k) w[k * ch + g] = at(conv, g * K + k);
+    std::vector<float> prm(2 * (size_t)c.lin_heads + c.lin_vdim);
+    for (int i = 0; i < c.lin_heads; ++i) {
+        prm[i] = at(a_log, i);
+        prm[c.lin_heads + i] = at(dt_bias, i);
+    }
+    for (int i = 0; i < c.lin_vdim; ++i) prm[2 * c.lin_heads + i] = at(gamma, i);
+    rc = aexis_cuda_check(d->ctx, cudaMemcpy(L.conv_w, w.data(), sizeof(float) * w.size(), cudaMemcpyHostToDevice),
+                          "conv upload");
+    if (!rc)
+        rc = aexis_cuda_check(d->ctx, cudaMemcpy(L.lin_params, prm.data(), sizeof(float) * prm.size(),
+                                                 cudaMemcpyHostToDevice), "parameter upload");
+    if (!rc) L.set_mask |= (1 << 1) | (1 << 2);
     return rc;
 }
 
@@ -728,7 +883,16 @@ AEXIS_API int aexis_cuda_decoder_reset(aexis_decoder* d) {
     int rc = dbind(d);
     if (rc) return rc;
     d->host_pos = 0;
-    return aexis_cuda_check(d->ctx, cudaMemsetAsync(d->ints, 0, sizeof(int) * 3, d->ctx->stream), "reset");
+    const auto& c = d->cfg;
+    cudaError_t e = cudaMemsetAsync(d->ints, 0, sizeof(int) * 3, d->ctx->stream);
+    for (auto& L : d->layers) {
+        if (L.kind != AEXIS_LAYER_LINEAR_ATTENTION || e != cudaSuccess) continue;
+        const size_t ch = 2 * (size_t)c.lin_heads * c.lin_kdim + (size_t)c.lin_heads * c.lin_vdim;
+        e = cudaMemsetAsync(L.conv_state, 0, sizeof(float) * c.conv_kernel * ch, d->ctx->stream);
+        if (e == cudaSuccess)
+            e = cudaMemsetAsync(L.gdr_state, 0, sizeof(float) * c.lin_heads * c.lin_kdim * c.lin_vdim, d->ctx->stream);
+    }
+    return aexis_cuda_check(d->ctx, e, "reset");
 }
 
 AEXIS_API int aexis_cuda_decoder_position(const aexis_decoder* d, int32_t* out) {
@@ -755,8 +919,48 @@ static int kv_layer_args(aexis_decoder* d, int layer, int rows, const void* k, c
     if (!k || !v) return aexis_fail(d->ctx, AEXIS_E_NULL, "K/V buffer is null");
     if (layer < 0 || layer >= d->cfg.n_layers)
         return aexis_fail(d->ctx, AEXIS_E_RANGE, "layer %d outside [0, %d)", layer, d->cfg.n_layers);
+    if (d->layers[layer].kind != AEXIS_LAYER_FULL_ATTENTION)
+        return aexis_fail(d->ctx, AEXIS_E_RANGE, "layer %d is linear attention: it has no KV cache", layer);
     if (rows <= 0) return aexis_fail(d->ctx, AEXIS_E_RANGE, "rows=%d", rows);
     return dbind(d);
+}
+
+static int recurrent_layer_args(aexis_decoder* d, int layer) {
+    if (layer < 0 || layer >= d->cfg.n_layers || d->layers[layer].kind != AEXIS_LAYER_LINEAR_ATTENTION)
+        return aexis_fail(d->ctx, AEXIS_E_RANGE, "layer %d is not a linear-attention layer", layer);
+    return dbind(d);
+}
+
+// Both directions of the recurrent-cache copy (device to device, on the context stream).
+static int recurrent_copy(aexis_decoder* d, int layer, float* conv_dst, const float* conv_src, float* gdr_dst,
+                          const float* gdr_src) {
+    const auto& c = d->cfg;
+    const size_t ch = 2 * (size_t)c.lin_heads * c.lin_kdim + (size_t)c.lin_heads * c.lin_vdim;
+    cudaError_t e = cudaSuccess;
+    if (conv_dst && conv_src)
+        e = cudaMemcpyAsync(conv_dst, conv_src, sizeof(float) * c.conv_kernel * ch, cudaMemcpyDeviceToDevice,
+                            d->ctx->stream);
+    if (e == cudaSuccess && gdr_dst && gdr_src)
+        e = cudaMemcpyAsync(gdr_dst, gdr_src, sizeof(float) * c.lin_heads * c.lin_kdim * c.lin_vdim,
+                            cudaMemcpyDeviceToDevice, d->ctx->stream);
+    return aexis_cuda_check(d->ctx, e, "recurrent cache copy");
+}
+
+AEXIS_API int aexis_cuda_decoder_recurrent_export(aexis_decoder* d, int layer, float* conv_out, float* gdr_out) {
+    if (!d) return AEXIS_E_NULL;
+    int rc = recurrent_layer_args(d, layer);
+    if (rc) return rc;
+    const auto& L = d->layers[layer];
+    return recurrent_copy(d, layer, conv_out, L.conv_state, gdr_out, L.gdr_state);
+}
+
+AEXIS_API int aexis_cuda_decoder_recurrent_import(aexis_decoder* d, int layer, const float* conv_in,
+                                                  const float* gdr_in) {
+    if (!d) return AEXIS_E_NULL;
+    int rc = recurrent_layer_args(d, layer);
+    if (rc) return rc;
+    auto& L = d->layers[layer];
+    return recurrent_copy(d, layer, L.conv_state, conv_in, L.gdr_state, gdr_in);
 }
 
 AEXIS_API int aexis_cuda_decoder_kv_export(aexis_decoder* d, int layer, int rows, float* k_out, float* v_out) {
@@ -766,8 +970,8 @@ AEXIS_API int aexis_cuda_decoder_kv_export(aexis_decoder* d, int layer, int rows
     if (rows < d->host_pos)
         return aexis_fail(d->ctx, AEXIS_E_SHAPE, "rows %d < sequence length %d", rows, d->host_pos);
     const auto& c = d->cfg;
-    const size_t per = (size_t)c.n_kv_heads * c.kv_capacity * c.head_dim;
-    return aexis_cuda_check(d->ctx, launch_kv_export(d->kcache + per * layer, d->vcache + per * layer, c.n_kv_heads,
+    const size_t per = (size_t)c.n_kv_heads * c.kv_capacity * c.head_dim * d->layers[layer].attn_slot;
+    return aexis_cuda_check(d->ctx, launch_kv_export(d->kcache + per, d->vcache + per, c.n_kv_heads,
                                                      c.kv_capacity, c.head_dim, 0, d->host_pos, rows, k_out, v_out,
                                                      d->ctx->stream), "kv export launch");
 }
@@ -781,9 +985,9 @@ AEXIS_API int aexis_cuda_decoder_kv_import(aexis_decoder* d, int layer, const fl
     if (length < 0 || length > rows || length > c.kv_capacity)
         return aexis_fail(d->ctx, AEXIS_E_RANGE, "length %d outside [0, min(rows %d, capacity %d)]", length, rows,
                           c.kv_capacity);
-    const size_t per = (size_t)c.n_kv_heads * c.kv_capacity * c.head_dim;
+    const size_t per = (size_t)c.n_kv_heads * c.kv_capacity * c.head_dim * d->layers[layer].attn_slot;
     return aexis_cuda_check(d->ctx, launch_kv_import(k_in, v_in, c.n_kv_heads, c.kv_capacity, c.head_dim, 0, length,
-                                                     rows, d->kcache + per * layer, d->vcache + per * layer,
+                                                     rows, d->kcache + per, d->vcache + per,
                                                      d->ctx->stream), "kv import launch");
 }
 

@@ -765,6 +765,7 @@ size_t persist_smem_bytes() {
 // one CTA per SM resident (cooperative launch).
 bool decoder_persist_supported(const aexis_decoder* d, int sm_count) {
     const auto& c = d->cfg;
+    if (d->hybrid) return false;  // the phase table covers full-attention layers only
     if (c.bits != 4 || c.lm_bits != 4 || c.group != 32 || c.lm_group != 32 || c.scale_dtype != AEXIS_F16) return false;
     if (c.head_dim != kPHeadDim || c.n_heads % c.n_kv_heads || c.n_heads / c.n_kv_heads > kPMaxHpg) return false;
     if (c.kv_capacity > kPChunk * kPMaxSplits) return false;

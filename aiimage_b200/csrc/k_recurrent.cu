@@ -16,7 +16,9 @@
 // so the state crosses HBM once in and once out per call. For batch-1 decode
 // (one token) the kernel is bound by that 2 x heads x kdim x vdim x 4 bytes
 // and by launch latency.
-#include "aexis_internal.h"
+#include <cooperative_groups.h>
+
+#include "decoder_internal.h"
 
 namespace {
 
@@ -225,7 +227,239 @@ __global__ void __launch_bounds__(kGdrThreads) gdr_kernel(GdrArgs p) {
     }
 }
 
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;"); }
+
+// One decode step of a hybrid decoder's linear-attention block, after its
+// in_proj GEMV: ShortConv + SiLU on the step's q/k/v channels, the Gated
+// Delta Rule for one token, and the per-head gated RMSNorm, in one launch.
+//   proj  = [q k v z b a] of this token (in_proj output, fp32)
+//   q,k,v = silu(conv over [cache rows 1..K-1, proj]) (tap order as AexisShortConvPack4)
+//   o     = GDR(q, k, v, b, a) as gdr_kernel, one token
+//   y     = o * rsqrt(max(mean_head(o^2) + eps, 1e-20)) * gamma * silu(z)
+// Grid (vdim/16, heads), one cluster of vdim/16 CTAs per head: CTA (x, h)
+// owns columns 16x..16x+15 of head h's state (kept in registers as in
+// gdr_kernel) and recomputes the conv of the head's q and k rows it needs
+// (a few FMAs each) instead of reading them from another kernel. The
+// per-head norm sums o^2 over the cluster's CTAs through distributed shared
+// memory. The conv cache shifts in place after the first cluster barrier,
+// when every CTA of the head has read it: q/k rows by the cluster's CTA 0,
+// v columns by the CTA that owns them. The second barrier keeps every CTA's
+// shared memory alive until the others have read it.
+// Before griddepcontrol.wait the kernel reads only the state, the conv
+// cache and weights and the per-head parameters, which the previous kernel
+// (the in_proj GEMV) does not write; the sums over the cached conv taps are
+// done there too.
+template <int RPT>
+__global__ void __launch_bounds__(kGdrThreads) lin_attn_decode_kernel(LinAttnDecode p) {
+    namespace cg = cooperative_groups;
+    cg::cluster_group cluster = cg::this_cluster();
+    const int tid = threadIdx.x;
+    const int qd = tid & 3;
+    const int r = tid >> 2;
+    const int warp = tid >> 5, lane = tid & 31;
+    const int h = blockIdx.y;
+    const int heads = p.heads, kd = p.kdim, vd = p.vdim, K = p.kernel;
+    const long long nq = (long long)heads * kd;
+    const long long C = 2 * nq + (long long)heads * vd;  // conv channels
+    const int c0 = blockIdx.x * kGdrCols + qd * 4;      // vd is a multiple of 16: always < vd
+
+    __shared__ float red_a[4][4][6];
+    __shared__ float red_b[4][4][4];
+    __shared__ float ss_part;
+
+    // Conv over the K-1 cached taps of channel g (the newest tap comes from proj).
+    auto cached_taps = [&](long long g) {
+        float sum = 0.0f;
+        for (int k = 0; k + 1 < K; ++k) sum = fmaf(p.conv_state[(k + 1) * C + g], p.conv_w[k * C + g], sum);
+        return sum;
+    };
+    float S[RPT][4];
+    float cq[RPT], ck[RPT], wq[RPT], wk[RPT], cv[4], wv[4];
+#pragma unroll
+    for (int i = 0; i < RPT; ++i) {
+        const int j = r + 32 * i;
+        float4 st = make_float4(0.f, 0.f, 0.f, 0.f);
+        cq[i] = ck[i] = wq[i] = wk[i] = 0.0f;
+        if (j < kd) {
+            st = *reinterpret_cast<const float4*>(p.state + ((long long)h * kd + j) * vd + c0);
+            const long long gq = (long long)h * kd + j, gk = nq + gq;
+            cq[i] = cached_taps(gq);
+            ck[i] = cached_taps(gk);
+            wq[i] = p.conv_w[(K - 1) * C + gq];
+            wk[i] = p.conv_w[(K - 1) * C + gk];
+        }
+        S[i][0] = st.x; S[i][1] = st.y; S[i][2] = st.z; S[i][3] = st.w;
+    }
+    const long long gv0 = 2 * nq + (long long)h * vd + c0;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+        cv[c] = cached_taps(gv0 + c);
+        wv[c] = p.conv_w[(K - 1) * C + gv0 + c];
+    }
+    const float ealog = expf(p.a_log[h]);
+    const float dt = p.dt_bias[h];
+    const float inv_sqrt_k = rsqrtf((float)kd);
+
+    griddep_wait();
+    griddep_launch();
+
+    auto silu = [](float x) { return x / (1.0f + expf(-x)); };
+    float xq[RPT], xk[RPT], xv[4], qv[RPT], kv[RPT], vv[4];
+#pragma unroll
+    for (int i = 0; i < RPT; ++i) {
+        const int j = r + 32 * i;
+        xq[i] = xk[i] = qv[i] = kv[i] = 0.0f;
+        if (j < kd) {
+            xq[i] = p.proj[(long long)h * kd + j];
+            xk[i] = p.proj[nq + (long long)h * kd + j];
+            qv[i] = silu(fmaf(xq[i], wq[i], cq[i]));
+            kv[i] = silu(fmaf(xk[i], wk[i], ck[i]));
+        }
+    }
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+        xv[c] = p.proj[gv0 + c];
+        vv[c] = silu(fmaf(xv[c], wv[c], cv[c]));
+    }
+    const long long zo = C + (long long)h * vd;  // z of this head
+    const long long bo = C + (long long)heads * vd;
+    const float bb = p.proj[bo + h];
+    const float xa = p.proj[bo + heads + h] + dt;
+    const float beta = 1.0f / (1.0f + expf(-bb));
+    const float decay = expf(-ealog * (fmaxf(xa, 0.0f) + logf(1.0f + expf(-fabsf(xa)))));
+
+    float part[6] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int i = 0; i < RPT; ++i) {
+        part[0] = fmaf(qv[i], qv[i], part[0]);
+        part[1] = fmaf(kv[i], kv[i], part[1]);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            S[i][c] *= decay;
+            part[2 + c] = fmaf(kv[i], S[i][c], part[2 + c]);
+        }
+    }
+#pragma unroll
+    for (int m = 4; m < 32; m <<= 1)
+#pragma unroll
+        for (int e = 0; e < 6; ++e) part[e] += __shfl_xor_sync(0xffffffffu, part[e], m);
+    if (lane < 4) {
+#pragma unroll
+        for (int e = 0; e < 6; ++e) red_a[warp][qd][e] = part[e];
+    }
+    __syncthreads();
+    float tot[6];
+#pragma unroll
+    for (int e = 0; e < 6; ++e) tot[e] = (red_a[0][qd][e] + red_a[1][qd][e]) + (red_a[2][qd][e] + red_a[3][qd][e]);
+    const float qs = rsqrtf(tot[0] + p.gdr_eps);
+    const float ks = rsqrtf(tot[1] + p.gdr_eps);
+    float delta[4];
+#pragma unroll
+    for (int c = 0; c < 4; ++c) delta[c] = (vv[c] - tot[2 + c] * ks) * beta;
+    float o[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int i = 0; i < RPT; ++i) {
+        const float kn = kv[i] * ks;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            S[i][c] = fmaf(kn, delta[c], S[i][c]);
+            o[c] = fmaf(qv[i], S[i][c], o[c]);
+        }
+    }
+#pragma unroll
+    for (int m = 4; m < 32; m <<= 1)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) o[c] += __shfl_xor_sync(0xffffffffu, o[c], m);
+    if (lane < 4) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c) red_b[warp][qd][c] = o[c];
+    }
+    __syncthreads();
+    // Threads 0..3 (r == 0) finish the CTA's 16 columns and their sum of squares.
+    float ov[4] = {0.f, 0.f, 0.f, 0.f};
+    if (warp == 0) {
+        float ss = 0.0f;
+        if (r == 0) {
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                ov[c] = ((red_b[0][qd][c] + red_b[1][qd][c]) + (red_b[2][qd][c] + red_b[3][qd][c])) * qs * inv_sqrt_k;
+                ss = fmaf(ov[c], ov[c], ss);
+            }
+        }
+        ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+        ss += __shfl_xor_sync(0xffffffffu, ss, 2);
+        if (lane == 0) ss_part = ss;
+    }
+    cluster.sync();  // partial sums visible; every CTA of the head has read the conv cache
+    if (r == 0) {
+        float total = 0.0f;
+        const int nb = (int)cluster.num_blocks();
+        for (int b = 0; b < nb; ++b) total += *cluster.map_shared_rank(&ss_part, b);
+        const float inv = 1.0f / sqrtf(fmaxf(total / (float)vd + p.norm_eps, 1e-20f));
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            const float z = p.proj[zo + c0 + c];
+            p.y[(long long)h * vd + c0 + c] = ov[c] * inv * p.gamma[c0 + c] * silu(z);
+        }
+    }
+    cluster.barrier_arrive();
+    // Conv cache: drop the oldest row, append this token.
+    auto shift = [&](long long g, float x) {
+        for (int k = 0; k + 1 < K; ++k) p.conv_state[k * C + g] = p.conv_state[(k + 1) * C + g];
+        p.conv_state[(K - 1) * C + g] = x;
+    };
+    if (blockIdx.x == 0 && qd == 0) {
+#pragma unroll
+        for (int i = 0; i < RPT; ++i) {
+            const int j = r + 32 * i;
+            if (j < kd) {
+                shift((long long)h * kd + j, xq[i]);
+                shift(nq + (long long)h * kd + j, xk[i]);
+            }
+        }
+    }
+    if (r == 0) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c) shift(gv0 + c, xv[c]);
+    }
+#pragma unroll
+    for (int i = 0; i < RPT; ++i) {
+        const int j = r + 32 * i;
+        if (j < kd)
+            *reinterpret_cast<float4*>(p.state + ((long long)h * kd + j) * vd + c0) =
+                make_float4(S[i][0], S[i][1], S[i][2], S[i][3]);
+    }
+    cluster.barrier_wait();
+}
+
 }  // namespace
+
+bool lin_attn_decode_supported(int heads, int kdim, int vdim, int kernel) {
+    return heads > 0 && heads <= 65535 && kdim > 0 && kdim <= 256 && kdim % 4 == 0 && vdim % kGdrCols == 0 &&
+           vdim > 0 && vdim / kGdrCols <= 8 && kernel >= 1 && kernel <= 16;
+}
+
+cudaError_t launch_lin_attn_decode(const LinAttnDecode& a, cudaStream_t s) {
+    if (!lin_attn_decode_supported(a.heads, a.kdim, a.vdim, a.kernel)) return cudaErrorInvalidValue;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(a.vdim / kGdrCols, a.heads);
+    cfg.blockDim = dim3(kGdrThreads);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = a.vdim / kGdrCols;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    if (a.kdim <= 32) return cudaLaunchKernelEx(&cfg, lin_attn_decode_kernel<1>, a);
+    if (a.kdim <= 64) return cudaLaunchKernelEx(&cfg, lin_attn_decode_kernel<2>, a);
+    if (a.kdim <= 128) return cudaLaunchKernelEx(&cfg, lin_attn_decode_kernel<4>, a);
+    return cudaLaunchKernelEx(&cfg, lin_attn_decode_kernel<8>, a);
+}
 
 cudaError_t launch_short_conv(const float* weight, const float* mixed, const float* cache_in, float* out,
                               float* cache_out, int groups, int kernel, int seq, int cache_len, cudaStream_t s) {

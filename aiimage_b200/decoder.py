@@ -21,12 +21,21 @@ def _np(a):
 
 
 class DecoderSession:
+    """The decoder over a DecoderCfg: every layer full attention, or with
+    cfg.full_attention_interval > 0 the hybrid stack of linear-attention
+    (ShortConv + Gated Delta Rule) and full-attention layers."""
+
     def __init__(self, ops: AexisOps, cfg: DecoderCfg, scale_dtype: int = F16):
         self.ops, self.cfg = ops, cfg
         c = cfg
+        self.layer_types = c.layer_types()
+        self._types = np.ascontiguousarray(self.layer_types, dtype=np.int32)
+        hybrid = any(self.layer_types)
         self._cfg = DecoderConfig(c.n_layers, c.hidden, c.n_heads, c.n_kv_heads, c.head_dim, c.ffn, c.vocab,
                                   c.kv_capacity, c.rot_dim, c.bits, c.group, c.lm_bits, c.lm_group, scale_dtype,
-                                  c.rope_theta, c.eps)
+                                  c.rope_theta, c.eps,
+                                  self._types.ctypes.data_as(C.POINTER(C.c_int32)) if hybrid else None,
+                                  c.lin_heads, c.lin_kdim, c.lin_vdim, c.conv_kernel)
         self.h = C.c_void_p()
         check(lib().aexis_cuda_decoder_create(ops.ctx, C.byref(self._cfg), C.byref(self.h)), ops.ctx)
         self._scale_dtype = scale_dtype
@@ -64,6 +73,14 @@ class DecoderSession:
         g = g.astype(np.float16 if dt == F16 else np.float32, copy=False)
         self._check(lib().aexis_cuda_decoder_set_norm(self.h, layer, which, _np(g), dt))
 
+    def set_linear_attention(self, layer: int, conv: np.ndarray, a_log: np.ndarray, dt_bias: np.ndarray,
+                             gamma: np.ndarray):
+        """A linear-attention layer's conv [channels, kernel], a_log, dt_bias [lin_heads], gamma [lin_vdim]."""
+        dt = F16 if all(np.asarray(x).dtype == np.float16 for x in (conv, a_log, dt_bias, gamma)) else F32
+        arrs = [np.ascontiguousarray(x, dtype=np.float16 if dt == F16 else np.float32)
+                for x in (conv, a_log, dt_bias, gamma)]
+        self._check(lib().aexis_cuda_decoder_set_linear_attention(self.h, int(layer), *[_np(a) for a in arrs], dt))
+
     def set_embedding(self, table: np.ndarray):
         t = np.ascontiguousarray(table)
         dt = F16 if t.dtype == np.float16 else F32
@@ -75,8 +92,10 @@ class DecoderSession:
         same linear/norm/embedding accessors)."""
         c = self.cfg
         for layer in range(c.n_layers):
-            for which in range(7):
+            for which in c.linears(layer):
                 self.set_linear(layer, which, *model.linear(layer, which))
+            if self.layer_types[layer] == 1:
+                self.set_linear_attention(layer, *model.linear_attention(layer))
             for which in range(2):
                 self.set_norm(layer, which, model.norm(layer, which))
         self.set_linear(-1, 7, *model.linear(-1, 7))
@@ -140,25 +159,69 @@ class DecoderSession:
         self.ops._bind_stream()
         self._check(lib().aexis_cuda_decoder_set_position(self.h, int(position)))
 
+    def recurrent_shapes(self) -> tuple[int, int]:
+        """Floats of a linear-attention layer's (conv cache, GDR cache)."""
+        c = self.cfg
+        return c.conv_kernel * c.conv_channels(), c.lin_heads * c.lin_kdim * c.lin_vdim
+
+    def recurrent_export(self, layer: int, conv_out, gdr_out):
+        """A linear-attention layer's caches into device fp32 tensors (either may be None)
+        (aexis_cuda_decoder_recurrent_export): conv [conv_kernel, channels], GDR [heads, kdim, vdim]."""
+        self.ops._bind_stream()
+        self._check(lib().aexis_cuda_decoder_recurrent_export(
+            self.h, int(layer), None if conv_out is None else conv_out.data_ptr(),
+            None if gdr_out is None else gdr_out.data_ptr()))
+
+    def recurrent_import(self, layer: int, conv_in, gdr_in):
+        self.ops._bind_stream()
+        self._check(lib().aexis_cuda_decoder_recurrent_import(
+            self.h, int(layer), None if conv_in is None else conv_in.data_ptr(),
+            None if gdr_in is None else gdr_in.data_ptr()))
+
+    def _state_names(self):
+        """(layer, kind, ordinal): the reference numbers each cache kind on its own ("cache_k0".."cache_k5",
+        "cache_conv0".."cache_conv17" for Qwen3.5), in layer order."""
+        n_full = n_lin = 0
+        for layer, kind in enumerate(self.layer_types):
+            if kind == 1:
+                yield layer, kind, n_lin
+                n_lin += 1
+            else:
+                yield layer, kind, n_full
+                n_full += 1
+
     def export_state(self, rows: int | None = None) -> dict:
         """Qwen35DecoderState as the reference holds it: {"cache_k<i>", "cache_v<i>": Pack4 CDHW fp32
-        device tensors of `rows` (default: the position) rows, "sequence_length": the position}."""
+        device tensors of `rows` (default: the position) rows for the i-th full-attention layer,
+        "cache_conv<i>", "cache_gdr<i>": the i-th linear-attention layer's caches, "sequence_length": the
+        position}."""
         import torch
         pos = self.position
         rows = max(pos, 1) if rows is None else int(rows)
         state = {"sequence_length": pos, "rows": rows}
-        for layer in range(self.cfg.n_layers):
-            k = torch.empty(self.kv_rows_floats(rows), dtype=torch.float32, device=f"cuda:{self.ops.device}")
-            v = torch.empty_like(k)
-            self.kv_export(layer, k, v, rows)
-            state[f"cache_k{layer}"], state[f"cache_v{layer}"] = k, v
+        dev = f"cuda:{self.ops.device}"
+        nc, ng = self.recurrent_shapes()
+        for layer, kind, i in self._state_names():
+            if kind == 1:
+                conv = torch.empty(nc, dtype=torch.float32, device=dev)
+                gdr = torch.empty(ng, dtype=torch.float32, device=dev)
+                self.recurrent_export(layer, conv, gdr)
+                state[f"cache_conv{i}"], state[f"cache_gdr{i}"] = conv, gdr
+            else:
+                k = torch.empty(self.kv_rows_floats(rows), dtype=torch.float32, device=dev)
+                v = torch.empty_like(k)
+                self.kv_export(layer, k, v, rows)
+                state[f"cache_k{i}"], state[f"cache_v{i}"] = k, v
         return state
 
     def import_state(self, state: dict):
         """Load a state of export_state's form; decoding continues at its sequence_length."""
         length, rows = int(state["sequence_length"]), int(state["rows"])
-        for layer in range(self.cfg.n_layers):
-            self.kv_import(layer, state[f"cache_k{layer}"], state[f"cache_v{layer}"], rows, length)
+        for layer, kind, i in self._state_names():
+            if kind == 1:
+                self.recurrent_import(layer, state[f"cache_conv{i}"], state[f"cache_gdr{i}"])
+            else:
+                self.kv_import(layer, state[f"cache_k{i}"], state[f"cache_v{i}"], rows, length)
         self.set_position(length)
 
     def set_schedule(self, mode: int):

@@ -24,9 +24,11 @@ f32 = C.c_float
 
 class DecoderConfig(C.Structure):
     """aexis_decoder_config (field order is the ABI)."""
-    _fields_ = [(n, C.c_int32) for n in ("n_layers", "hidden", "n_heads", "n_kv_heads", "head_dim", "ffn", "vocab",
-                                         "kv_capacity", "rot_dim", "bits", "group", "lm_bits", "lm_group",
-                                         "scale_dtype")] + [("rope_theta", C.c_float), ("eps", C.c_float)]
+    _fields_ = ([(n, C.c_int32) for n in ("n_layers", "hidden", "n_heads", "n_kv_heads", "head_dim", "ffn", "vocab",
+                                          "kv_capacity", "rot_dim", "bits", "group", "lm_bits", "lm_group",
+                                          "scale_dtype")] + [("rope_theta", C.c_float), ("eps", C.c_float)]
+                + [("layer_types", C.POINTER(C.c_int32))]
+                + [(n, C.c_int32) for n in ("lin_heads", "lin_kdim", "lin_vdim", "conv_kernel")])
 
 
 # name -> (restype, argtypes)
@@ -82,6 +84,10 @@ SIGNATURES = {
     "aexis_cuda_decoder_kv_export": (i32, [vp, i32, i32, vp, vp]),
     "aexis_cuda_decoder_kv_import": (i32, [vp, i32, vp, vp, i32, i32]),
     "aexis_cuda_decoder_set_position": (i32, [vp, C.c_int32]),
+    "aexis_cuda_layer_types_interval": (i32, [i32, i32, vp]),
+    "aexis_cuda_decoder_set_linear_attention": (i32, [vp, i32, vp, vp, vp, vp, i32]),
+    "aexis_cuda_decoder_recurrent_export": (i32, [vp, i32, vp, vp]),
+    "aexis_cuda_decoder_recurrent_import": (i32, [vp, i32, vp, vp]),
     "aexis_cuda_batch_kv_export": (i32, [vp, i32, i32, i32, vp, vp]),
     "aexis_cuda_batch_kv_import": (i32, [vp, i32, i32, vp, vp, i32, i32]),
     "aexis_cuda_batch_set_positions": (i32, [vp, i32, vp]),

@@ -98,11 +98,42 @@ class DecoderCfg:
     lm_group: int = 32
     rope_theta: float = 1e6
     eps: float = 1e-6
+    # Hybrid stacks: 0 makes every layer full attention; n > 0 makes layer i
+    # full attention when (i + 1) % n == 0 and a linear-attention block
+    # (ShortConv + Gated Delta Rule) otherwise. Qwen3.5: 4, i.e. three linear
+    # blocks before each full-attention block, 18 + 6 of 24
+    # (Qwen35DecoderSession.cs:167-172).
+    full_attention_interval: int = 0
+    lin_heads: int = 16      # linear attention: heads of q, k, v, z, b and a
+    lin_kdim: int = 128      # per-head key dim (the GDR state's rows)
+    lin_vdim: int = 128      # per-head value dim (the GDR state's columns)
+    conv_kernel: int = 4     # ShortConv taps (cache rows)
 
     def shapes(self):
         qd, kvd = self.n_heads * self.head_dim, self.n_kv_heads * self.head_dim
         return [(qd, self.hidden), (kvd, self.hidden), (kvd, self.hidden), (self.hidden, qd),
                 (self.ffn, self.hidden), (self.ffn, self.hidden), (self.hidden, self.ffn)]
+
+    def layer_types(self) -> list[int]:
+        """Per layer 0 (full attention) or 1 (linear attention)."""
+        n = self.full_attention_interval
+        return [0 if n <= 0 or (i + 1) % n == 0 else 1 for i in range(self.n_layers)]
+
+    def conv_channels(self) -> int:
+        """ShortConv channels: q, k and v of every linear-attention head."""
+        return 2 * self.lin_heads * self.lin_kdim + self.lin_heads * self.lin_vdim
+
+    def lin_shapes(self):
+        """{which: (rows, k)} of a linear-attention layer: 8 in_proj with rows [q k v z b a], 9 out_proj, then
+        the FFN's 4, 5, 6."""
+        nv = self.lin_heads * self.lin_vdim
+        sh = self.shapes()
+        return {8: (self.conv_channels() + nv + 2 * self.lin_heads, self.hidden), 9: (self.hidden, nv),
+                4: sh[4], 5: sh[5], 6: sh[6]}
+
+    def linears(self, layer: int) -> tuple:
+        """The `which` ids a layer loads."""
+        return (8, 9, 4, 5, 6) if self.layer_types()[layer] == 1 else tuple(range(7))
 
     def as_dict(self):
         return asdict(self)
@@ -115,6 +146,14 @@ QWEN35_08B_Q8 = DecoderCfg(bits=8, group=0, lm_bits=8, lm_group=0)
 # A small model of the same structure for quick parity checks.
 TINY = DecoderCfg(n_layers=2, hidden=256, n_heads=4, n_kv_heads=2, head_dim=64, ffn=512, vocab=1000,
                   kv_capacity=96, rot_dim=64, group=32, lm_group=32)
+# The hybrid Qwen3.5-0.8B layout: 18 linear-attention blocks (16 heads,
+# key/value dims 128, conv kernel 4) and 6 full-attention blocks.
+QWEN35_08B_HYBRID_Q4 = DecoderCfg(full_attention_interval=4)
+QWEN35_08B_HYBRID_Q8 = DecoderCfg(full_attention_interval=4, bits=8, group=0, lm_bits=8, lm_group=0)
+# A small hybrid stack [linear, full, linear, full] with kdim != vdim.
+TINY_HYBRID = DecoderCfg(n_layers=4, hidden=256, n_heads=4, n_kv_heads=2, head_dim=64, ffn=512, vocab=1000,
+                         kv_capacity=96, rot_dim=64, group=32, lm_group=32, full_attention_interval=2,
+                         lin_heads=4, lin_kdim=64, lin_vdim=32, conv_kernel=4)
 
 
 class SyntheticDecoder:
@@ -139,12 +178,17 @@ class SyntheticDecoder:
         self.cfg, self.seed, self.norm_mean, self.balanced_q4 = cfg, seed, float(norm_mean), bool(balanced_q4)
         self._lin = {}
         self._norm = {}
+        self._lat = {}
         c = cfg
+        kinds = c.layer_types()
         for layer in range(c.n_layers):
-            for which, (n, k) in enumerate(c.shapes()):
+            shapes = c.lin_shapes() if kinds[layer] == 1 else dict(enumerate(c.shapes()))
+            for which, (n, k) in shapes.items():
                 self._lin[(layer, which)] = self._make(c.bits, c.group, n, k, (layer, which))
             for which in range(2):
                 self._norm[(layer, which)] = self._gain(c.hidden, (100, layer, which))
+            if kinds[layer] == 1:
+                self._lat[layer] = self._linear_attention_params(layer)
         self._lin[(-1, 7)] = self._make(c.lm_bits, c.lm_group, c.vocab, c.hidden, (999, 7))
         self._norm[(-1, 0)] = self._gain(c.hidden, (100, 999, 0))
         self.embedding = self._normal(c.vocab * c.hidden, (200,)).reshape(c.vocab, c.hidden)
@@ -161,8 +205,25 @@ class SyntheticDecoder:
         g = rng(self.seed, 7, *tag).standard_normal(count, dtype=np.float32) * 0.02
         return (g + np.float32(self.norm_mean)).astype(np.float16)
 
+    def _linear_attention_params(self, layer):
+        """fp16 (conv [channels, kernel] ~ U(-1/2, 1/2), the Conv1d default bound 1/sqrt(kernel) for kernel 4;
+        a_log = log(U(0.05, 2)), so the per-token decay exp(-exp(a_log) * softplus(a + dt_bias)) ranges from
+        nearly 1 to nearly 0 over the heads; dt_bias ~ N(0, 1/2); gamma ~ N(norm_mean, 0.02) like the other
+        gains)."""
+        c = self.cfg
+        r = rng(self.seed, 9, layer)
+        conv = r.uniform(-0.5, 0.5, size=(c.conv_channels(), c.conv_kernel)).astype(np.float16)
+        a_log = np.log(r.uniform(0.05, 2.0, size=c.lin_heads)).astype(np.float16)
+        dt_bias = (r.standard_normal(c.lin_heads) * 0.5).astype(np.float16)
+        gamma = self._gain(c.lin_vdim, (110, layer))
+        return conv, a_log, dt_bias, gamma
+
     def linear(self, layer: int, which: int):
         return self._lin[(layer, which)]
+
+    def linear_attention(self, layer: int):
+        """A linear-attention layer's (conv [channels, kernel], a_log [heads], dt_bias [heads], gamma [vdim])."""
+        return self._lat[layer]
 
     def norm(self, layer: int, which: int):
         return self._norm[(layer, which)]
@@ -177,7 +238,7 @@ class SyntheticDecoder:
         c = self.cfg
         tot = 0
         for layer in range(c.n_layers):
-            for which in range(7):
+            for which in c.linears(layer):
                 p, s = self.linear(layer, which)
                 tot += p.nbytes + s.nbytes
             tot += 2 * c.hidden * 4

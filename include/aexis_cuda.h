@@ -402,8 +402,27 @@ int aexis_cuda_gated_delta_rule(aexis_ctx* ctx, const float* a_log, const float*
 
 /* ------------------------------------------------------------------ decoder */
 
-/* Shape of the full-attention decoder stack driven by Qwen35DecoderSession
- * (Samples/.../Qwen35DecoderSession.cs:167-172 for the reference constants). */
+/* Layer kinds of a hybrid stack. Qwen3.5 (Qwen35DecoderSession.cs:167-172:
+ * AttentionCacheCount 6, ConvCacheCount 18, GdrCacheCount 18) repeats three
+ * linear-attention blocks (ShortConv + GatedDeltaRule) and one full-attention
+ * block six times: layer i is full attention when (i + 1) % 4 == 0. */
+#define AEXIS_LAYER_FULL_ATTENTION 0
+#define AEXIS_LAYER_LINEAR_ATTENTION 1
+#define AEXIS_QWEN35_FULL_ATTENTION_INTERVAL 4
+
+/* Shape of the decoder stack driven by Qwen35DecoderSession
+ * (Samples/.../Qwen35DecoderSession.cs:167-172 for the reference constants).
+ * With layer_types NULL every layer is full attention; otherwise
+ * layer_types[l] picks each layer's kind and the lin_* fields give the
+ * linear-attention blocks' shape:
+ *   xn = RMSNorm(h); [q k v z b a] = in_proj(xn)  (rows in that order:
+ *     lin_heads*lin_kdim q, as many k, lin_heads*lin_vdim v and z, lin_heads
+ *     b and a)
+ *   [q k v] = SiLU(ShortConv([q k v]))  (depthwise, conv_kernel taps over the
+ *     previous conv_kernel - 1 tokens and this one; cache of conv_kernel rows)
+ *   o = GatedDeltaRule(q, k, v, b, a)   (per head, state [kdim][vdim], eps 1e-6)
+ *   y = RMSNorm_per_head(o) * gamma * SiLU(z); h += out_proj(y)
+ *   then the same SwiGLU FFN as a full-attention layer. */
 typedef struct aexis_decoder_config {
     int32_t n_layers;
     int32_t hidden;
@@ -420,8 +439,20 @@ typedef struct aexis_decoder_config {
     int32_t lm_group;      /* Q4 group of the lm_head */
     int32_t scale_dtype;   /* AEXIS_F16 or AEXIS_F32: dtype of every weight scale */
     float rope_theta;
-    float eps;             /* RMSNorm eps */
+    float eps;             /* RMSNorm eps (also the gated per-head norm's) */
+    const int32_t* layer_types; /* host [n_layers] of AEXIS_LAYER_*, copied at create; NULL: all full attention */
+    int32_t lin_heads;     /* linear attention: heads (q, k, v, z, b, a, GDR state) */
+    int32_t lin_kdim;      /* key dim per head: multiple of 4, <= 256 */
+    int32_t lin_vdim;      /* value dim per head: multiple of 16, <= 128 */
+    int32_t conv_kernel;   /* ShortConv taps, 1..16 */
 } aexis_decoder_config;
+
+/* Fills out[0 .. n_layers) with the kinds of a stack whose every
+ * `interval`-th layer is full attention (layer i full when (i + 1) %
+ * interval == 0, else linear attention); interval AEXIS_QWEN35_FULL_-
+ * ATTENTION_INTERVAL gives Qwen3.5's 18 + 6 of 24. interval <= 0 makes
+ * every layer full attention. No device work. */
+int aexis_cuda_layer_types_interval(int32_t n_layers, int32_t interval, int32_t* out);
 
 /* Qwen35DecoderSession constructor (Qwen35DecoderSession.cs:1748-1766):
  * allocates the weights, fp16 KV cache and the per-step CUDA graph. */
@@ -431,11 +462,23 @@ int aexis_cuda_decoder_destroy(aexis_decoder* dec);
 
 /* Weight loading (AexisGemmLayer.LoadLayer -> NewInt{4,8}WeightOnlyUpload,
  * AexisGemmLayer.cs:15-160). layer in [0, n_layers) with which: 0 q_proj,
- * 1 k_proj, 2 v_proj, 3 o_proj, 4 gate_proj, 5 up_proj, 6 down_proj; or
- * layer -1, which 7 for the lm_head. Arrays are host arrays in the same
- * packed format as aexis_cuda_weights_q4 / _q8. */
+ * 1 k_proj, 2 v_proj, 3 o_proj (full-attention layers), 8 in_proj and
+ * 9 out_proj (linear-attention layers), 4 gate_proj, 5 up_proj,
+ * 6 down_proj (both); or layer -1, which 7 for the lm_head. Arrays are host
+ * arrays in the same packed format as aexis_cuda_weights_q4 / _q8. A `which`
+ * of the other layer kind -> E_RANGE. */
 int aexis_cuda_decoder_set_linear(aexis_decoder* dec, int layer, int which, const uint32_t* packed,
                                   const void* scales, int scale_dtype);
+
+/* A linear-attention layer's small parameters (host arrays of dtype): conv
+ * [channels][conv_kernel] with channels = 2*lin_heads*lin_kdim +
+ * lin_heads*lin_vdim in in_proj's q, k, v order (the ShortConv operator's
+ * weight = [groups, kernel], Tools/Qwen35NcnnBaseline/reference_ops.py:36-60),
+ * a_log and dt_bias [lin_heads] (GatedDeltaRule, reference_ops.py:88-152),
+ * gamma [lin_vdim] (the gated norm's gain, shared by the heads).
+ * A full-attention layer -> E_RANGE. */
+int aexis_cuda_decoder_set_linear_attention(aexis_decoder* dec, int layer, const void* conv, const void* a_log,
+                                            const void* dt_bias, const void* gamma, int dtype);
 
 /* RMSNorm gammas (AexisRMSNormLayer.LoadLayer, AexisRMSNormLayer.cs:16-45):
  * which 0 = input norm, 1 = post-attention norm; layer -1 = final norm.
@@ -447,7 +490,8 @@ int aexis_cuda_decoder_set_norm(aexis_decoder* dec, int layer, int which, const 
  * [vocab, hidden] of dtype. */
 int aexis_cuda_decoder_set_embedding(aexis_decoder* dec, const void* table, int dtype);
 
-/* Qwen35DecoderSession.CreateInitialState (:376-400): position back to 0. */
+/* Qwen35DecoderSession.CreateInitialState (:376-400): position back to 0,
+ * every conv and GDR cache zero. */
 int aexis_cuda_decoder_reset(aexis_decoder* dec);
 int aexis_cuda_decoder_position(const aexis_decoder* dec, int32_t* out_position);
 
@@ -495,8 +539,23 @@ int aexis_cuda_decoder_kv_import(aexis_decoder* dec, int layer, const float* k_i
                                  int length);
 /* Set the next position (Qwen35DecoderState.PositionId / SequenceLength) to
  * `position` in [0, kv_capacity]: the next token is written at that position
- * and attends positions [0, position]. */
+ * and attends positions [0, position]. The conv and GDR caches of a hybrid
+ * stack are not touched: import them with the position. */
 int aexis_cuda_decoder_set_position(aexis_decoder* dec, int32_t position);
+
+/* A linear-attention layer's recurrent caches as the reference's state holds
+ * them (CreateInitialState, Qwen35DecoderSession.cs:376-400): "cache_conv<i>"
+ * a Pack4 2D texture [w = channels/4, h = conv_kernel] (device fp32
+ * conv_kernel * channels floats, element (tap row, channel) at row *
+ * channels + channel, the oldest row first) and "cache_gdr<i>" a Pack4 2D
+ * array [w = lin_vdim/4, h = lin_kdim, slice = lin_heads] (lin_heads *
+ * lin_kdim * lin_vdim floats, element (head, key row, column) at (head *
+ * lin_kdim + row) * lin_vdim + column). Either pointer may be NULL to skip
+ * that cache. A full-attention layer -> E_RANGE (its state is the KV cache
+ * above; the KV calls take a full-attention layer and return E_RANGE for a
+ * linear-attention one). */
+int aexis_cuda_decoder_recurrent_export(aexis_decoder* dec, int layer, float* conv_out, float* gdr_out);
+int aexis_cuda_decoder_recurrent_import(aexis_decoder* dec, int layer, const float* conv_in, const float* gdr_in);
 
 /* How aexis_cuda_decoder_generate schedules its greedy steps (no reference
  * counterpart: the reference dispatches per layer). mode 0: one CUDA graph

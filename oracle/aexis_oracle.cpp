@@ -488,7 +488,9 @@ ORACLE_API void oracle_rope_tables(int positions, int rot_dim, float theta, floa
 
 // ---------------------------------------------------------------------------
 // Synthetic decoder (the Qwen3.5-0.8B-shaped full-attention stack used for
-// measurement), composed from the restated layers the way the reference's
+// measurement, or with layer_types the hybrid stack whose linear-attention
+// blocks are linear_attention_block below), composed from the restated
+// layers the way the reference's
 // decode loop drives them (DecodeCore DECODER:469-585, layer plugins
 // AexisRMSNormLayer / AexisGemmLayer / AexisRotaryEmbedLayer / AexisSdpaLayer):
 //   h = Embed(token)
@@ -504,11 +506,34 @@ struct OracleDecoderCfg {
     int32_t n_layers, hidden, n_heads, n_kv_heads, head_dim, ffn, vocab, kv_capacity;
     int32_t rot_dim, bits, group, lm_bits, lm_group;
     float theta, eps;
+    // Hybrid stacks (Qwen3.5: DECODER:167-172, 6 attention caches and 18
+    // conv/GDR caches). layer_types[l] = 1 makes layer l a linear-attention
+    // block; null or 0 everywhere is the all-full-attention stack.
+    int32_t lin_heads, lin_kdim, lin_vdim, conv_kernel;
+    const int32_t* layer_types;
 };
+
+// The linear-attention restatements further down (one token of each per
+// decode step here).
+ORACLE_API void oracle_short_conv(const float* weight, const float* mixed, const float* cache_in, float* out,
+                                  float* cache_out, int groups, int kernel, int seq, int cache_len);
+ORACLE_API void oracle_gated_delta_rule(const float* a_log, const float* dt_bias, const float* b, const float* a,
+                                        const float* q, const float* k, const float* v, const float* state_in,
+                                        float* out, float* state_out, int heads, int kdim, int vdim, int first,
+                                        int count, float eps);
 
 namespace {
 struct OLinear { const uint32_t* P = nullptr; const float* S = nullptr; int n = 0, k = 0, bits = 4, blk = 0; };
-struct OLayer { OLinear lin[7]; const float* norm[2] = {nullptr, nullptr}; };
+struct OLayer {
+    OLinear lin[7];  // a linear-attention layer uses lin[0] as in_proj, lin[3] as out_proj
+    const float* norm[2] = {nullptr, nullptr};
+    int kind = 0;    // 0 full attention, 1 linear attention
+    // Linear attention: ShortConv weight in its Pack4 layout, per-head a_log
+    // and dt_bias, the gated norm's gain, and the two recurrent caches.
+    std::vector<float> conv_w, a_log, dt_bias, gamma;
+    std::vector<float> conv_state;  // [conv_kernel][channels]
+    std::vector<float> gdr_state;   // [lin_heads][lin_kdim][lin_vdim]
+};
 struct ODecoder {
     OracleDecoderCfg c;
     std::vector<OLayer> layers;
@@ -544,13 +569,25 @@ ORACLE_API void* oracle_decoder_create(const OracleDecoderCfg* cfg) {
     const int q_n = c.n_heads * c.head_dim, kv_n = c.n_kv_heads * c.head_dim;
     const int shapes[7][2] = {{q_n, c.hidden}, {kv_n, c.hidden}, {kv_n, c.hidden}, {c.hidden, q_n},
                               {c.ffn, c.hidden}, {c.ffn, c.hidden}, {c.hidden, c.ffn}};
-    for (auto& L : d->layers)
+    const int l_nq = c.lin_heads * c.lin_kdim, l_nv = c.lin_heads * c.lin_vdim;
+    const int l_ch = 2 * l_nq + l_nv;
+    for (int l = 0; l < c.n_layers; ++l) {
+        OLayer& L = d->layers[l];
+        L.kind = c.layer_types ? c.layer_types[l] : 0;
         for (int w = 0; w < 7; ++w) {
-            L.lin[w].n = shapes[w][0];
-            L.lin[w].k = shapes[w][1];
+            int n = shapes[w][0], k = shapes[w][1];
+            if (L.kind == 1 && w == 0) n = l_ch + l_nv + 2 * c.lin_heads;  // [q k v z b a]
+            if (L.kind == 1 && w == 3) k = l_nv;
+            L.lin[w].n = n;
+            L.lin[w].k = k;
             L.lin[w].bits = c.bits;
-            L.lin[w].blk = c.bits == 4 ? (c.group > 0 ? c.group : shapes[w][1]) : 0;
+            L.lin[w].blk = c.bits == 4 ? (c.group > 0 ? c.group : k) : 0;
         }
+        if (L.kind == 1) {
+            L.conv_state.assign((size_t)c.conv_kernel * l_ch, 0.0f);
+            L.gdr_state.assign((size_t)c.lin_heads * c.lin_kdim * c.lin_vdim, 0.0f);
+        }
+    }
     d->lm.n = c.vocab;
     d->lm.k = c.hidden;
     d->lm.bits = c.lm_bits;
@@ -604,7 +641,15 @@ ORACLE_API int oracle_decoder_fill_context(void* h, int ctx, uint64_t seed, int6
     d->pos = ctx;
     return 0;
 }
-ORACLE_API void oracle_decoder_reset(void* h) { ((ODecoder*)h)->pos = 0; }
+// CreateInitialState (DECODER:376-400): position 0, conv and GDR caches zero.
+ORACLE_API void oracle_decoder_reset(void* h) {
+    ODecoder* d = (ODecoder*)h;
+    d->pos = 0;
+    for (auto& L : d->layers) {
+        std::fill(L.conv_state.begin(), L.conv_state.end(), 0.0f);
+        std::fill(L.gdr_state.begin(), L.gdr_state.end(), 0.0f);
+    }
+}
 // Layer `layer`'s cache (kind 0 = K, 1 = V) as [kv_heads][capacity][head_dim]
 // fp32 (the fp16-rounded values the decoder attends over).
 ORACLE_API void oracle_decoder_kv(void* h, int layer, int kind, float* out) {
@@ -616,14 +661,44 @@ ORACLE_API void oracle_decoder_kv(void* h, int layer, int kind, float* out) {
 }
 ORACLE_API int oracle_decoder_position(void* h) { return ((ODecoder*)h)->pos; }
 
-// which: 0 q, 1 k, 2 v, 3 o, 4 gate, 5 up, 6 down; layer -1 = lm_head.
-// The arrays are borrowed, not copied: the caller keeps them alive.
+// which: 0 q, 1 k, 2 v, 3 o, 4 gate, 5 up, 6 down; 8 in_proj and 9 out_proj
+// of a linear-attention layer; layer -1 = lm_head. The arrays are borrowed,
+// not copied: the caller keeps them alive.
 ORACLE_API void oracle_decoder_set_linear(void* h, int layer, int which, const uint32_t* P,
                                           const float* S) {
     ODecoder* d = (ODecoder*)h;
-    OLinear& L = layer < 0 ? d->lm : d->layers[layer].lin[which];
+    const int slot = which == 8 ? 0 : which == 9 ? 3 : which;
+    OLinear& L = layer < 0 ? d->lm : d->layers[layer].lin[slot];
     L.P = P;
     L.S = S;
+}
+
+// A linear-attention layer's small parameters (copied): conv [channels][kernel]
+// (the reference operator's weight=[groups, kernel], reference_ops.py:36-60),
+// a_log and dt_bias [lin_heads], gamma [lin_vdim] (the gated RMSNorm's gain,
+// shared by every head).
+ORACLE_API void oracle_decoder_set_linear_attention(void* h, int layer, const float* conv, const float* a_log,
+                                                    const float* dt_bias, const float* gamma) {
+    ODecoder* d = (ODecoder*)h;
+    const auto& c = d->c;
+    OLayer& L = d->layers[layer];
+    const int K = c.conv_kernel, ch = 2 * c.lin_heads * c.lin_kdim + c.lin_heads * c.lin_vdim;
+    // Pack4 CDHW [w = kernel, h = 1, c = channels] (RecurrentLoadShortConvWeight, COMMON:586-592).
+    L.conv_w.assign((size_t)((ch + 3) / 4) * 4 * K, 0.0f);
+    for (int g = 0; g < ch; ++g)
+        for (int k = 0; k < K; ++k) L.conv_w[((size_t)(g / 4) * K + k) * 4 + (g & 3)] = conv[(size_t)g * K + k];
+    L.a_log.assign(a_log, a_log + c.lin_heads);
+    L.dt_bias.assign(dt_bias, dt_bias + c.lin_heads);
+    L.gamma.assign(gamma, gamma + c.lin_vdim);
+}
+
+// A linear-attention layer's caches: conv [conv_kernel][channels] (the
+// reference's cache_conv texture, rows = taps) and GDR [heads][kdim][vdim]
+// (cache_gdr, texel x = column / 4, y = key row, slice = head).
+ORACLE_API void oracle_decoder_recurrent(void* h, int layer, float* conv_out, float* gdr_out) {
+    const OLayer& L = ((ODecoder*)h)->layers[layer];
+    if (conv_out) std::memcpy(conv_out, L.conv_state.data(), L.conv_state.size() * sizeof(float));
+    if (gdr_out) std::memcpy(gdr_out, L.gdr_state.data(), L.gdr_state.size() * sizeof(float));
 }
 
 // which: 0 attention norm, 1 ffn norm; layer -1 = final norm.
@@ -636,6 +711,57 @@ ORACLE_API void oracle_decoder_set_norm(void* h, int layer, int which, const flo
 ORACLE_API void oracle_decoder_set_embedding(void* h, const float* table) {
     ((ODecoder*)h)->embed = table;
 }
+
+namespace {
+// Qwen3.5's linear-attention decoder block for one token (the 18 blocks
+// `ShortConv + GatedDeltaRule` of the hybrid stack, UNITY_IMPLEMENTATION_PLAN
+// "topology": three of them before each cache-SDPA block), with the Qwen3-Next
+// GatedDeltaNet composition around the two custom operators:
+//   xn = RMSNorm(h); [q k v z b a] = Gemm_in(xn)
+//   [q k v] = ShortConv+SiLU([q k v]) (streaming cache of conv_kernel rows)
+//   o = GatedDeltaRule(q, k, v, b, a) per head (state [heads][kdim][vdim])
+//   y = RMSNorm_head(o) * gamma * SiLU(z); h += Gemm_out(y)
+//   xn = RMSNorm(h); h += Gemm_down(Swish(Gemm_gate(xn)) * Gemm_up(xn))
+// The operators are the restatements above (ShortConv COMMON:623-678, GDR
+// COMMON:680-753, eps 1e-6 as reference_ops.py:88); the norms are
+// oracle_rmsnorm with the model's eps.
+void linear_attention_block(ODecoder* d, OLayer& L, float* hs) {
+    const auto& c = d->c;
+    const int H = c.hidden, Hl = c.lin_heads, kd = c.lin_kdim, vd = c.lin_vdim, K = c.conv_kernel;
+    const int nq = Hl * kd, nv = Hl * vd, ch = 2 * nq + nv;
+    std::vector<float> xn(H), proj(L.lin[0].n), conv(ch), o(nv), y(nv), out(H);
+    oracle_rmsnorm(hs, 1, H, H, L.norm[0], H, c.eps, xn.data(), H);
+    run_linear(L.lin[0], xn.data(), proj.data());
+    oracle_short_conv(L.conv_w.data(), proj.data(), L.conv_state.data(), conv.data(), L.conv_state.data(), ch, K, 1,
+                      K);
+    // One token in the GDR's Pack4 CDHW layout (sequence packed by 4: lane 0).
+    std::vector<float> qp((size_t)nq * 4, 0.0f), kp((size_t)nq * 4, 0.0f), vp((size_t)nv * 4, 0.0f);
+    std::vector<float> op((size_t)nv * 4, 0.0f), st(L.gdr_state.size());
+    for (int i = 0; i < nq; ++i) {
+        qp[(size_t)i * 4] = conv[i];
+        kp[(size_t)i * 4] = conv[nq + i];
+    }
+    for (int i = 0; i < nv; ++i) vp[(size_t)i * 4] = conv[2 * nq + i];
+    const float* z = proj.data() + ch;
+    const float* b = z + nv;
+    const float* a = b + Hl;
+    oracle_gated_delta_rule(L.a_log.data(), L.dt_bias.data(), b, a, qp.data(), kp.data(), vp.data(),
+                            L.gdr_state.data(), op.data(), st.data(), Hl, kd, vd, 0, 1, 1e-6f);
+    L.gdr_state.swap(st);
+    for (int i = 0; i < nv; ++i) o[i] = op[(size_t)i * 4];
+    oracle_rmsnorm(o.data(), Hl, vd, vd, L.gamma.data(), vd, c.eps, y.data(), vd);
+    for (int i = 0; i < nv; ++i) y[i] = y[i] * (z[i] / (1.0f + std::exp(-z[i])));
+    run_linear(L.lin[3], y.data(), out.data());
+    for (int i = 0; i < H; ++i) hs[i] = hs[i] + out[i];
+    std::vector<float> g(c.ffn), u(c.ffn), act(c.ffn), dn(H);
+    oracle_rmsnorm(hs, 1, H, H, L.norm[1], H, c.eps, xn.data(), H);
+    run_linear(L.lin[4], xn.data(), g.data());
+    run_linear(L.lin[5], xn.data(), u.data());
+    oracle_swiglu(g.data(), u.data(), c.ffn, act.data());
+    run_linear(L.lin[6], act.data(), dn.data());
+    for (int i = 0; i < H; ++i) hs[i] = hs[i] + dn[i];
+}
+}  // namespace
 
 // One token at the current position. When want_logits is 0 the lm_head is
 // skipped (prompt tokens before the last) and -1 is returned; otherwise the
@@ -659,6 +785,10 @@ ORACLE_API int oracle_decoder_step(void* h, int token, int want_logits, float* l
     const int hpg = std::max(1, NH / KVH);
     for (int l = 0; l < c.n_layers; ++l) {
         OLayer& L = d->layers[l];
+        if (L.kind == 1) {
+            linear_attention_block(d, L, hs.data());
+            continue;
+        }
         oracle_rmsnorm(hs.data(), 1, H, H, L.norm[0], H, c.eps, xn.data(), H);
         run_linear(L.lin[0], xn.data(), q.data());
         run_linear(L.lin[1], xn.data(), k.data());

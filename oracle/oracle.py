@@ -75,6 +75,8 @@ def lib():
         L.oracle_decoder_step.argtypes = [vp, C.c_int, C.c_int, vp, vp]
         L.oracle_decoder_fill_context.argtypes = [vp, C.c_int, C.c_uint64, C.c_int64]
         L.oracle_decoder_kv.argtypes = [vp, C.c_int, C.c_int, F32P]
+        L.oracle_decoder_set_linear_attention.argtypes = [vp, C.c_int, F32P, F32P, F32P, F32P]
+        L.oracle_decoder_recurrent.argtypes = [vp, C.c_int, vp, vp]
         L.oracle_decoder_fill_context.restype = C.c_int
         L.oracle_num_threads.restype = C.c_int
         _lib = L
@@ -288,9 +290,11 @@ def rope_tables(positions: int, rot_dim: int, theta: float):
 
 # ---------------------------------------------------------------- decoder
 class _Cfg(C.Structure):
-    _fields_ = [(n, C.c_int32) for n in ("n_layers", "hidden", "n_heads", "n_kv_heads", "head_dim", "ffn",
-                                         "vocab", "kv_capacity", "rot_dim", "bits", "group", "lm_bits",
-                                         "lm_group")] + [("theta", C.c_float), ("eps", C.c_float)]
+    _fields_ = ([(n, C.c_int32) for n in ("n_layers", "hidden", "n_heads", "n_kv_heads", "head_dim", "ffn",
+                                          "vocab", "kv_capacity", "rot_dim", "bits", "group", "lm_bits",
+                                          "lm_group")] + [("theta", C.c_float), ("eps", C.c_float)]
+                + [(n, C.c_int32) for n in ("lin_heads", "lin_kdim", "lin_vdim", "conv_kernel")]
+                + [("layer_types", C.POINTER(C.c_int32))])
 
 
 class OracleDecoder:
@@ -303,18 +307,26 @@ class OracleDecoder:
     def __init__(self, model):
         cfg = model.cfg
         self._model = model
+        kinds = cfg.layer_types()
+        self._types = np.ascontiguousarray(kinds, dtype=np.int32)
         self._c = _Cfg(cfg.n_layers, cfg.hidden, cfg.n_heads, cfg.n_kv_heads, cfg.head_dim, cfg.ffn, cfg.vocab,
                        cfg.kv_capacity, cfg.rot_dim, cfg.bits, cfg.group, cfg.lm_bits, cfg.lm_group,
-                       cfg.rope_theta, cfg.eps)
+                       cfg.rope_theta, cfg.eps, cfg.lin_heads, cfg.lin_kdim, cfg.lin_vdim, cfg.conv_kernel,
+                       self._types.ctypes.data_as(C.POINTER(C.c_int32)))
         L = lib()
         self._h = L.oracle_decoder_create(C.byref(self._c))
         self._keep = []
         for layer in range(cfg.n_layers):
-            for which in range(7):
+            linear_attention = kinds[layer] == 1
+            for which in ((8, 9, 4, 5, 6) if linear_attention else range(7)):
                 p, s = model.linear(layer, which)
                 s32 = _f32(s)
                 self._keep.append(s32)
                 L.oracle_decoder_set_linear(self._h, layer, which, p, s32)
+            if linear_attention:
+                prm = [_f32(x) for x in model.linear_attention(layer)]
+                self._keep.extend(prm)
+                L.oracle_decoder_set_linear_attention(self._h, layer, *prm)
             for which in range(2):
                 g = _f32(model.norm(layer, which))
                 self._keep.append(g)
@@ -361,6 +373,15 @@ class OracleDecoder:
         out = np.empty((c.n_kv_heads, c.kv_capacity, c.head_dim), dtype=np.float32)
         lib().oracle_decoder_kv(self._h, int(layer), int(kind), out)
         return out
+
+    def recurrent(self, layer: int):
+        """A linear-attention layer's caches: (conv [conv_kernel, channels], gdr [heads, kdim, vdim]) fp32."""
+        c = self._c
+        ch = 2 * c.lin_heads * c.lin_kdim + c.lin_heads * c.lin_vdim
+        conv = np.empty((c.conv_kernel, ch), dtype=np.float32)
+        gdr = np.empty((c.lin_heads, c.lin_kdim, c.lin_vdim), dtype=np.float32)
+        lib().oracle_decoder_recurrent(self._h, int(layer), _ptr(conv), _ptr(gdr))
+        return conv, gdr
 
     def step(self, token: int, want_logits: bool = True):
         logits = np.empty(self._c.vocab, dtype=np.float32) if want_logits else None

@@ -26,6 +26,11 @@ Cases:
                                 range): selective attention, a greedy path
                                 with many distinct tokens.
   qwen35_08b_q8_prompt64        the Q8 per-row model, 64-token prompt.
+  qwen35_08b_hybrid_q4_selective
+                                the hybrid Qwen3.5 stack (18 linear-attention
+                                blocks, ShortConv + Gated Delta Rule, and 6
+                                full-attention blocks) with the selective
+                                model's gains and Q4 codes, 128-token prompt.
   config4_q8_batch              BASELINE config 4's 32 sequences (contexts
                                 U[256, 4096], synthetic caches); sequences
                                 SEQS of them over all 128 steps.
@@ -63,6 +68,8 @@ CASES = {
     "qwen35_08b_q4_selective": dict(cfg="QWEN35_08B_Q4", seed=5, norm_mean=1.0, balanced_q4=True, prompt_len=512,
                                     prompt_seed=50, max_new=64),
     "qwen35_08b_q8_prompt64": dict(cfg="QWEN35_08B_Q8", seed=4, prompt_len=64, prompt_seed=40, max_new=64),
+    "qwen35_08b_hybrid_q4_selective": dict(cfg="QWEN35_08B_HYBRID_Q4", seed=6, norm_mean=1.0, balanced_q4=True,
+                                           prompt_len=128, prompt_seed=60, max_new=64),
 }
 
 # Config 4: the batch test draws ctx_lens and first tokens from this seed
