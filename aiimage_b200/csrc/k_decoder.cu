@@ -601,7 +601,7 @@ AEXIS_API int aexis_cuda_decoder_create(aexis_ctx* ctx, const aexis_decoder_conf
         if (!lin_attn_decode_supported(c.lin_heads, c.lin_kdim, c.lin_vdim, c.conv_kernel))
             return aexis_fail(ctx, AEXIS_E_UNSUPPORTED,
                               "linear attention heads=%d kdim=%d vdim=%d conv_kernel=%d (kdim a multiple of 4 up "
-                              "to 256, vdim a multiple of 16 up to 128, kernel 1..16)",
+                              "to 256, vdim a multiple of 16 up to 128, kernel 1..8)",
                               c.lin_heads, c.lin_kdim, c.lin_vdim, c.conv_kernel);
         if (lin_rows > (1LL << 30) || lin_nv % 32 || (c.bits == 4 && lin_nv % c.group))
             return aexis_fail(ctx, AEXIS_E_SHAPE, "lin_heads*lin_vdim %lld must be a multiple of 32 and of the group",

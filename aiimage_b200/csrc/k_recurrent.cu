@@ -246,11 +246,12 @@ __device__ __forceinline__ void griddep_launch() { asm volatile("griddepcontrol.
 // when every CTA of the head has read it: q/k rows by the cluster's CTA 0,
 // v columns by the CTA that owns them. The second barrier keeps every CTA's
 // shared memory alive until the others have read it.
-// Before griddepcontrol.wait the kernel reads only the state, the conv
-// cache and weights and the per-head parameters, which the previous kernel
-// (the in_proj GEMV) does not write; the sums over the cached conv taps are
-// done there too.
-template <int RPT>
+// Global memory is read in two batches, every load of a batch in flight at
+// once: before griddepcontrol.wait the state, the conv cache rows and
+// weights and the per-head parameters (none written by the previous kernel,
+// the in_proj GEMV), after it the token's in_proj outputs. The cached conv
+// rows stay in registers for the shift (KT - 1 predicated taps, KT >= K).
+template <int RPT, int KT>
 __global__ void __launch_bounds__(kGdrThreads) lin_attn_decode_kernel(LinAttnDecode p) {
     namespace cg = cooperative_groups;
     cg::cluster_group cluster = cg::this_cluster();
@@ -260,74 +261,99 @@ __global__ void __launch_bounds__(kGdrThreads) lin_attn_decode_kernel(LinAttnDec
     const int warp = tid >> 5, lane = tid & 31;
     const int h = blockIdx.y;
     const int heads = p.heads, kd = p.kdim, vd = p.vdim, K = p.kernel;
-    const long long nq = (long long)heads * kd;
-    const long long C = 2 * nq + (long long)heads * vd;  // conv channels
-    const int c0 = blockIdx.x * kGdrCols + qd * 4;      // vd is a multiple of 16: always < vd
+    const int nq = heads * kd;
+    const int C = 2 * nq + heads * vd;                // conv channels
+    const int c0 = blockIdx.x * kGdrCols + qd * 4;   // vd is a multiple of 16: always < vd
+    constexpr int H = KT - 1;                         // cached taps held per channel
 
     __shared__ float red_a[4][4][6];
     __shared__ float red_b[4][4][4];
     __shared__ float ss_part;
 
-    // Conv over the K-1 cached taps of channel g (the newest tap comes from proj).
-    auto cached_taps = [&](long long g) {
-        float sum = 0.0f;
-        for (int k = 0; k + 1 < K; ++k) sum = fmaf(p.conv_state[(k + 1) * C + g], p.conv_w[k * C + g], sum);
-        return sum;
-    };
+    // Batch 1 (before the wait).
     float S[RPT][4];
-    float cq[RPT], ck[RPT], wq[RPT], wk[RPT], cv[4], wv[4];
+    float hq[RPT][H], hk[RPT][H], hv[4][H];            // cache rows 1..K-1
+    float wq[RPT][KT], wk[RPT][KT], wv[4][KT];          // conv taps 0..K-1
+    auto load_channel = [&](int g, float (&hist)[H], float (&w)[KT]) {
+#pragma unroll
+        for (int k = 0; k < KT; ++k) {
+            w[k] = k < K ? p.conv_w[k * C + g] : 0.0f;
+            if (k < H) hist[k] = k + 1 < K ? p.conv_state[(k + 1) * C + g] : 0.0f;
+        }
+    };
 #pragma unroll
     for (int i = 0; i < RPT; ++i) {
         const int j = r + 32 * i;
         float4 st = make_float4(0.f, 0.f, 0.f, 0.f);
-        cq[i] = ck[i] = wq[i] = wk[i] = 0.0f;
         if (j < kd) {
-            st = *reinterpret_cast<const float4*>(p.state + ((long long)h * kd + j) * vd + c0);
-            const long long gq = (long long)h * kd + j, gk = nq + gq;
-            cq[i] = cached_taps(gq);
-            ck[i] = cached_taps(gk);
-            wq[i] = p.conv_w[(K - 1) * C + gq];
-            wk[i] = p.conv_w[(K - 1) * C + gk];
+            st = *reinterpret_cast<const float4*>(p.state + (h * kd + j) * vd + c0);
+            load_channel(h * kd + j, hq[i], wq[i]);
+            load_channel(nq + h * kd + j, hk[i], wk[i]);
+        } else {
+#pragma unroll
+            for (int k = 0; k < KT; ++k) {
+                wq[i][k] = wk[i][k] = 0.0f;
+                if (k < H) hq[i][k] = hk[i][k] = 0.0f;
+            }
         }
         S[i][0] = st.x; S[i][1] = st.y; S[i][2] = st.z; S[i][3] = st.w;
     }
-    const long long gv0 = 2 * nq + (long long)h * vd + c0;
+    const int gv0 = 2 * nq + h * vd + c0;
+    float gm[4];
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
-        cv[c] = cached_taps(gv0 + c);
-        wv[c] = p.conv_w[(K - 1) * C + gv0 + c];
+        load_channel(gv0 + c, hv[c], wv[c]);
+        gm[c] = p.gamma[c0 + c];
     }
-    const float ealog = expf(p.a_log[h]);
+    const float alog = p.a_log[h];
     const float dt = p.dt_bias[h];
-    const float inv_sqrt_k = rsqrtf((float)kd);
 
     griddep_wait();
     griddep_launch();
 
-    auto silu = [](float x) { return x / (1.0f + expf(-x)); };
-    float xq[RPT], xk[RPT], xv[4], qv[RPT], kv[RPT], vv[4];
+    // Batch 2 (after the wait): this token's in_proj outputs.
+    float xq[RPT], xk[RPT], xv[4], zv[4];
 #pragma unroll
     for (int i = 0; i < RPT; ++i) {
         const int j = r + 32 * i;
-        xq[i] = xk[i] = qv[i] = kv[i] = 0.0f;
-        if (j < kd) {
-            xq[i] = p.proj[(long long)h * kd + j];
-            xk[i] = p.proj[nq + (long long)h * kd + j];
-            qv[i] = silu(fmaf(xq[i], wq[i], cq[i]));
-            kv[i] = silu(fmaf(xk[i], wk[i], ck[i]));
-        }
+        xq[i] = j < kd ? p.proj[h * kd + j] : 0.0f;
+        xk[i] = j < kd ? p.proj[nq + h * kd + j] : 0.0f;
     }
+    const int zo = C + h * vd;        // z of this head
+    const int bo = C + heads * vd;    // b, then a
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
         xv[c] = p.proj[gv0 + c];
-        vv[c] = silu(fmaf(xv[c], wv[c], cv[c]));
+        zv[c] = p.proj[zo + c0 + c];
     }
-    const long long zo = C + (long long)h * vd;  // z of this head
-    const long long bo = C + (long long)heads * vd;
     const float bb = p.proj[bo + h];
     const float xa = p.proj[bo + heads + h] + dt;
+
+    // conv: taps 0..K-2 over the cached rows, tap K-1 over this token, in order.
+    auto conv = [&](const float (&hist)[H], const float (&w)[KT], float x) {
+        float sum = 0.0f;
+#pragma unroll
+        for (int k = 0; k < H; ++k)
+            if (k + 1 < K) sum = fmaf(hist[k], w[k], sum);
+        float wl = w[0];
+#pragma unroll
+        for (int k = 1; k < KT; ++k)
+            if (k == K - 1) wl = w[k];
+        sum = fmaf(x, wl, sum);
+        return sum / (1.0f + expf(-sum));
+    };
+    float qv[RPT], kv[RPT], vv[4];
+#pragma unroll
+    for (int i = 0; i < RPT; ++i) {
+        const bool ok = r + 32 * i < kd;
+        qv[i] = ok ? conv(hq[i], wq[i], xq[i]) : 0.0f;
+        kv[i] = ok ? conv(hk[i], wk[i], xk[i]) : 0.0f;
+    }
+#pragma unroll
+    for (int c = 0; c < 4; ++c) vv[c] = conv(hv[c], wv[c], xv[c]);
     const float beta = 1.0f / (1.0f + expf(-bb));
-    const float decay = expf(-ealog * (fmaxf(xa, 0.0f) + logf(1.0f + expf(-fabsf(xa)))));
+    const float decay = expf(-expf(alog) * (fmaxf(xa, 0.0f) + logf(1.0f + expf(-fabsf(xa)))));
+    const float inv_sqrt_k = rsqrtf((float)kd);
 
     float part[6] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
@@ -398,15 +424,15 @@ __global__ void __launch_bounds__(kGdrThreads) lin_attn_decode_kernel(LinAttnDec
         for (int b = 0; b < nb; ++b) total += *cluster.map_shared_rank(&ss_part, b);
         const float inv = 1.0f / sqrtf(fmaxf(total / (float)vd + p.norm_eps, 1e-20f));
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-            const float z = p.proj[zo + c0 + c];
-            p.y[(long long)h * vd + c0 + c] = ov[c] * inv * p.gamma[c0 + c] * silu(z);
-        }
+        for (int c = 0; c < 4; ++c)
+            p.y[h * vd + c0 + c] = ov[c] * inv * gm[c] * (zv[c] / (1.0f + expf(-zv[c])));
     }
     cluster.barrier_arrive();
-    // Conv cache: drop the oldest row, append this token.
-    auto shift = [&](long long g, float x) {
-        for (int k = 0; k + 1 < K; ++k) p.conv_state[k * C + g] = p.conv_state[(k + 1) * C + g];
+    // Conv cache: drop the oldest row, append this token (from registers).
+    auto shift = [&](int g, const float (&hist)[H], float x) {
+#pragma unroll
+        for (int k = 0; k < H; ++k)
+            if (k + 1 < K) p.conv_state[k * C + g] = hist[k];
         p.conv_state[(K - 1) * C + g] = x;
     };
     if (blockIdx.x == 0 && qd == 0) {
@@ -414,20 +440,20 @@ __global__ void __launch_bounds__(kGdrThreads) lin_attn_decode_kernel(LinAttnDec
         for (int i = 0; i < RPT; ++i) {
             const int j = r + 32 * i;
             if (j < kd) {
-                shift((long long)h * kd + j, xq[i]);
-                shift(nq + (long long)h * kd + j, xk[i]);
+                shift(h * kd + j, hq[i], xq[i]);
+                shift(nq + h * kd + j, hk[i], xk[i]);
             }
         }
     }
     if (r == 0) {
 #pragma unroll
-        for (int c = 0; c < 4; ++c) shift(gv0 + c, xv[c]);
+        for (int c = 0; c < 4; ++c) shift(gv0 + c, hv[c], xv[c]);
     }
 #pragma unroll
     for (int i = 0; i < RPT; ++i) {
         const int j = r + 32 * i;
         if (j < kd)
-            *reinterpret_cast<float4*>(p.state + ((long long)h * kd + j) * vd + c0) =
+            *reinterpret_cast<float4*>(p.state + (h * kd + j) * vd + c0) =
                 make_float4(S[i][0], S[i][1], S[i][2], S[i][3]);
     }
     cluster.barrier_wait();
@@ -435,9 +461,20 @@ __global__ void __launch_bounds__(kGdrThreads) lin_attn_decode_kernel(LinAttnDec
 
 }  // namespace
 
+template <int KT>
+static cudaError_t launch_lin_attn_rpt(const cudaLaunchConfig_t& cfg, const LinAttnDecode& a) {
+    if (a.kdim <= 32) return cudaLaunchKernelEx(&cfg, lin_attn_decode_kernel<1, KT>, a);
+    if (a.kdim <= 64) return cudaLaunchKernelEx(&cfg, lin_attn_decode_kernel<2, KT>, a);
+    if (a.kdim <= 128) return cudaLaunchKernelEx(&cfg, lin_attn_decode_kernel<4, KT>, a);
+    return cudaLaunchKernelEx(&cfg, lin_attn_decode_kernel<8, KT>, a);
+}
+
 bool lin_attn_decode_supported(int heads, int kdim, int vdim, int kernel) {
+    // 32-bit indexing: the state and the in_proj rows stay below 2^30 elements.
     return heads > 0 && heads <= 65535 && kdim > 0 && kdim <= 256 && kdim % 4 == 0 && vdim % kGdrCols == 0 &&
-           vdim > 0 && vdim / kGdrCols <= 8 && kernel >= 1 && kernel <= 16;
+           vdim > 0 && vdim / kGdrCols <= 8 && kernel >= 1 && kernel <= 8 &&
+           (long long)heads * (2LL * kdim + 2LL * vdim + 2) < (1LL << 30) &&
+           (long long)heads * kdim * vdim < (1LL << 30);
 }
 
 cudaError_t launch_lin_attn_decode(const LinAttnDecode& a, cudaStream_t s) {
@@ -455,10 +492,8 @@ cudaError_t launch_lin_attn_decode(const LinAttnDecode& a, cudaStream_t s) {
     attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 2;
-    if (a.kdim <= 32) return cudaLaunchKernelEx(&cfg, lin_attn_decode_kernel<1>, a);
-    if (a.kdim <= 64) return cudaLaunchKernelEx(&cfg, lin_attn_decode_kernel<2>, a);
-    if (a.kdim <= 128) return cudaLaunchKernelEx(&cfg, lin_attn_decode_kernel<4>, a);
-    return cudaLaunchKernelEx(&cfg, lin_attn_decode_kernel<8>, a);
+    if (a.kernel <= 4) return launch_lin_attn_rpt<4>(cfg, a);
+    return launch_lin_attn_rpt<8>(cfg, a);
 }
 
 cudaError_t launch_short_conv(const float* weight, const float* mixed, const float* cache_in, float* out,

@@ -367,6 +367,13 @@ def run_gpu(args):
         except Exception as e:  # reported, never silently replaced
             decoder = {"error": f"{type(e).__name__}: {e}"}
 
+    hybrid = None
+    if not args.skip_decoder:
+        try:
+            hybrid = bench_hybrid_decoder(ops, peak)
+        except Exception as e:
+            hybrid = {"error": f"{type(e).__name__}: {e}"}
+
     config4 = None
     if not args.skip_config4:
         try:
@@ -432,6 +439,7 @@ def run_gpu(args):
             "per_shape": per_shape,
             "config1_q8": q8,
             "decoder": decoder,
+            "hybrid_decoder": hybrid,
             "config4": config4,
             "config5": config5,
             "linear_attention": linear_attn,
@@ -548,6 +556,41 @@ def bench_decoder(ops, peak, prompt_len: int = 512, new_tokens: int = 64):
             "frac": round(bytes_tok * n / gen_s / 1e9 / peak, 3), "first_tokens": toks[:8],
             "kernels_per_token": 2 + 5 * cfg.n_layers + 1, "schedule": "graph per step",
             "persistent_schedule": persist}
+
+
+def bench_hybrid_decoder(ops, peak, prompt_len: int = 512, new_tokens: int = 64):
+    """The hybrid Qwen3.5 stack (18 linear-attention blocks, ShortConv + Gated
+    Delta Rule, and 6 full-attention blocks; Q4 g32, vocab 151936): 512-token
+    prompt, then 64 greedy tokens through the graph-chained generate call.
+    Bytes per token: every weight once, the 6 KV caches at the mean context,
+    and per linear-attention layer the fp32 GDR state read and written
+    (2 x 16 x 128 x 128 x 4 bytes) plus the conv cache (3 rows read, 4
+    written, 6144 channels)."""
+    import torch
+    from aiimage_b200.decoder import DecoderSession
+    cfg = synth.QWEN35_08B_HYBRID_Q4
+    model = synth.SyntheticDecoder(cfg, seed=6, norm_mean=1.0, balanced_q4=True)
+    prompt = model.prompt(prompt_len, seed=60)
+    sess = DecoderSession(ops, cfg).load(model)
+    sess.prefill(prompt[:-1])
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    toks = sess.generate(prompt[-1:], new_tokens)
+    gen_s = time.perf_counter() - t0
+    sess.close()
+    kinds = cfg.layer_types()
+    n_full, n_lin = kinds.count(0), kinds.count(1)
+    kv_mean = n_full * 2 * cfg.n_kv_heads * cfg.head_dim * 2 * (prompt_len - 1 + new_tokens // 2)
+    state = n_lin * (2 * cfg.lin_heads * cfg.lin_kdim * cfg.lin_vdim * 4
+                     + (2 * cfg.conv_kernel - 1) * cfg.conv_channels() * 4)
+    bytes_tok = model.weight_bytes_per_token() + kv_mean + state
+    n = new_tokens
+    return {"workload": f"qwen35_hybrid_q4_decoder_prompt{prompt_len}_greedy{n} (18 linear + 6 full attention)",
+            "tokens_per_s": round(n / gen_s, 1), "ms_per_token": round(gen_s / n * 1e3, 4),
+            "bytes_per_token": bytes_tok, "recurrent_state_bytes_per_token": state,
+            "GB/s": round(bytes_tok * n / gen_s / 1e9, 1), "frac": round(bytes_tok * n / gen_s / 1e9 / peak, 3),
+            "first_tokens": toks[:8], "kernels_per_token": 2 + 5 * cfg.n_layers + 1,
+            "timing": "host clock around one generate call (one H2D token in, one D2H of the ids out)"}
 
 
 def bench_config4(ops, peak, world: int, rank: int, steps: int = 128, total_seqs: int = 256, per_batch: int = 32):
@@ -881,6 +924,7 @@ def run_only(args):
     --only dominant   W + K launches of the (1024, 151936) Q4 GEMV, rotating
                       over copies larger than L2, no graphs
     --only decoder    the config-3 decoder with --prompt-len / --new-tokens
+    --only hybrid     the hybrid Qwen3.5 decoder (18 linear + 6 full attention), same flags
     --only tcgemm     the config-5 lm_head GEMM alone (M=256, tensor cores)
     --only config4    one config-4 batch (32 sequences, --new-tokens steps)
     --only linear_attention  the Qwen3.5 GatedDeltaRule / ShortConv decode kernels
@@ -893,6 +937,8 @@ def run_only(args):
     peak, _ = measured_peak()
     if args.only == "decoder":
         out = bench_decoder(ops, peak, args.prompt_len, args.new_tokens)
+    elif args.only == "hybrid":
+        out = bench_hybrid_decoder(ops, peak, args.prompt_len, args.new_tokens)
     elif args.only == "linear_attention":
         out = bench_linear_attention(ops, peak)
     elif args.only == "sampler":
@@ -1014,7 +1060,7 @@ def main():
     ap.add_argument("--skip-linear-attention", action="store_true",
                     help="omit the GatedDeltaRule / ShortConv decode measurement")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
-    ap.add_argument("--only", choices=["dominant", "decoder", "tcgemm", "config4", "topk", "linear_attention", "sampler", "w8a8"], help="profiling mode (see run_only)")
+    ap.add_argument("--only", choices=["dominant", "decoder", "hybrid", "tcgemm", "config4", "topk", "linear_attention", "sampler", "w8a8"], help="profiling mode (see run_only)")
     ap.add_argument("--prompt-len", type=int, default=512)
     ap.add_argument("--new-tokens", type=int, default=64)
     args = ap.parse_args()

@@ -444,7 +444,7 @@ typedef struct aexis_decoder_config {
     int32_t lin_heads;     /* linear attention: heads (q, k, v, z, b, a, GDR state) */
     int32_t lin_kdim;      /* key dim per head: multiple of 4, <= 256 */
     int32_t lin_vdim;      /* value dim per head: multiple of 16, <= 128 */
-    int32_t conv_kernel;   /* ShortConv taps, 1..16 */
+    int32_t conv_kernel;   /* ShortConv taps, 1..8 */
 } aexis_decoder_config;
 
 /* Fills out[0 .. n_layers) with the kinds of a stack whose every

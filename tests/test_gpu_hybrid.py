@@ -160,7 +160,7 @@ def test_hybrid_argument_errors(ops):
         d.set_schedule(1)               # the persistent loop runs full-attention stacks only
     with pytest.raises(errors.NotSupportedError):
         BatchSession(d, max_batch=2, kv_capacity=32, max_steps=2)
-    for bad in (dict(lin_vdim=24), dict(lin_vdim=256), dict(lin_kdim=260), dict(conv_kernel=17)):
+    for bad in (dict(lin_vdim=24), dict(lin_vdim=256), dict(lin_kdim=260), dict(conv_kernel=9)):
         with pytest.raises((errors.NotSupportedError, errors.ArgumentError)):
             DecoderSession(ops, tiny(**bad))
 
