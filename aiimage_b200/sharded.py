@@ -103,10 +103,14 @@ class ShardedLmHead:
         buf = torch.empty(packed_words(m, k), dtype=torch.int32, device=x.device)
         keys, vals, idx = pack_views(buf, m, k)
         self.shard_topk(x, k, keys, vals, idx)
+        return self.merge(buf, m, k)
+
+    def merge(self, buf: torch.Tensor, m: int, k: int):
+        """The exchange step alone: all-gather every rank's packed buffer, then the merge kernel."""
         gathered = exchange(buf, self.group)
-        ids = torch.empty(m, dtype=torch.int64, device=x.device)
-        out_v = torch.empty((m, k), dtype=torch.float32, device=x.device)
-        out_i = torch.empty((m, k), dtype=torch.int32, device=x.device)
+        ids = torch.empty(m, dtype=torch.int64, device=buf.device)
+        out_v = torch.empty((m, k), dtype=torch.float32, device=buf.device)
+        out_i = torch.empty((m, k), dtype=torch.int32, device=buf.device)
         per = (self.vocab + self.world - 1) // self.world
         self.ops.topk_merge(gathered, self.world, m, k, per, ids, out_v, out_i)
         return ids, out_v, out_i.to(torch.int64)

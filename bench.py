@@ -139,16 +139,31 @@ def dist_setup(n_gpus: int):
         import datetime
         import torch.distributed as dist
         os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
-        # NCCL's version banner goes to stdout, where rank 0's one JSON line must stand
-        # alone; an explicit request for more (INFO, e.g. to see NVLS) is kept.
+        # NCCL's communicator set-up log (rank count, channels, NVLS) goes to
+        # stderr, so that rank 0's one JSON line stands alone on stdout; an
+        # explicit NCCL_DEBUG / NCCL_DEBUG_FILE request is kept.
         if os.environ.get("NCCL_DEBUG", "").upper() in ("", "VERSION"):
-            os.environ["NCCL_DEBUG"] = "WARN"
+            os.environ["NCCL_DEBUG"] = "INFO"
+            os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
+            os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
     else:
         torch.cuda.set_device(0)
     return world, rank, local
+
+
+def process_group_info(world: int):
+    """The communicator the timings ran over (None at N=1): backend, world size, NCCL version."""
+    if world == 1:
+        return None
+    import torch
+    import torch.distributed as dist
+    v = torch.cuda.nccl.version()
+    return {"backend": dist.get_backend(), "world_size": dist.get_world_size(),
+            "nccl": ".".join(str(x) for x in v) if isinstance(v, tuple) else str(v),
+            "log": "NCCL_DEBUG=INFO (subsystem INIT) on stderr"}
 
 
 def max_over_ranks(x: float, world: int) -> float:
@@ -449,6 +464,7 @@ def run_gpu(args):
             "e2e": {"value": round(e2e_steps * STEP_BYTES * world / e2e_s / 1e9, 2), "unit": "GB/s",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "path": "aexis_cuda_gemm via ctypes, pinned host x/y, sync per step"},
+            "process_group": process_group_info(world),
             "gpu_launches": args.steps * len(SWEEP),
             "clocks": {**clk.summary(), "window": "NVML every 5 ms over 0.25 s of the same step graphs, the"
                                                   " timed region, then 0.1 s more"},
@@ -874,6 +890,22 @@ def bench_config5(ops, world: int, rank: int, reps: int = 10):
     e1.record()
     e1.synchronize()
     argmax_s = e0.elapsed_time(e1) / 1e3 / reps
+    # The exchange alone (G > 1): all-gather of the packed keys + top-k lists and the merge kernel,
+    # on a buffer this rank's GEMM already filled; max over ranks, as the whole call.
+    exchange_s = None
+    if world > 1:
+        from aiimage_b200.sharded import pack_views, packed_words
+        buf = torch.empty(packed_words(m, k), dtype=torch.int32, device="cuda")
+        head.shard_topk(x, k, *pack_views(buf, m, k))
+        head.merge(buf, m, k)
+        torch.cuda.synchronize()
+        barrier(world)
+        e0.record()
+        for _ in range(reps):
+            head.merge(buf, m, k)
+        e1.record()
+        e1.synchronize()
+        exchange_s = max_over_ranks(e0.elapsed_time(e1) / 1e3 / reps, world)
     flops = 2.0 * m * vocab * hidden
     peak, kind = measured_tflops()
     out = {"workload": "config5_lm_head_q8_151936x1024_batch256_argmax_top50", "gpus": world,
@@ -884,6 +916,10 @@ def bench_config5(ops, world: int, rank: int, reps: int = 10):
            "gemm_frac_of_tensor_peak": round(2.0 * m * head.n * hidden / gemm_s / 1e12 / peak, 3),
            "tensor_peak": f"{peak} TFLOP/s ({kind}, MEASURED_PEAKS.json bf16_tflops)",
            "first_ids": ids[:6].tolist()}
+    if exchange_s is not None:
+        out["exchange_ms"] = round(exchange_s * 1e3, 4)
+        out["exchange"] = (f"NCCL all-gather of {packed_words(m, k) * 4} B per rank (keys + top-{k} values and"
+                           f" indices) + aexis_cuda_topk_merge, max over ranks")
     if world > 1 and rank == 0:
         full = ShardedLmHead(ops, p, s, vocab, hidden, 1, 0)
         ids1, _, idx1 = full.forward(x, k)
