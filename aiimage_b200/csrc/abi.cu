@@ -714,6 +714,84 @@ AEXIS_API int aexis_cuda_topk_merge(aexis_ctx* ctx, const int32_t* gathered, int
                                                          ctx->stream), "topk merge launch");
 }
 
+AEXIS_API int aexis_cuda_peer_buffer_bytes(int world, int rows, int k, size_t* out_bytes) {
+    if (!out_bytes) return AEXIS_E_NULL;
+    if (world < 1 || world > kPeerMaxRanks || rows <= 0 || k < 1 || k > 64) return AEXIS_E_RANGE;
+    *out_bytes = peer_recv_bytes(world, rows, k);
+    return AEXIS_OK;
+}
+
+AEXIS_API int aexis_cuda_peer_buffer_create(aexis_ctx* ctx, size_t bytes, void** out_ptr, uint8_t* out_handle) {
+    if (!ctx) return AEXIS_E_NULL;
+    if (!out_ptr || !out_handle) return aexis_fail(ctx, AEXIS_E_NULL, "null pointer");
+    if (bytes < kPeerHeaderBytes) return aexis_fail(ctx, AEXIS_E_RANGE, "bytes=%zu", bytes);
+    int rc = bind(ctx);
+    if (rc) return rc;
+    void* p = nullptr;
+    cudaError_t e = cudaMalloc(&p, bytes);
+    if (e == cudaSuccess) e = cudaMemset(p, 0, bytes);
+    cudaIpcMemHandle_t h;
+    if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, p);
+    if (e != cudaSuccess) {
+        if (p) cudaFree(p);
+        return aexis_cuda_check(ctx, e, "peer buffer create");
+    }
+    std::memcpy(out_handle, &h, sizeof(h));
+    *out_ptr = p;
+    return AEXIS_OK;
+}
+
+AEXIS_API int aexis_cuda_peer_buffer_open(aexis_ctx* ctx, const uint8_t* handle, void** out_ptr) {
+    if (!ctx) return AEXIS_E_NULL;
+    if (!handle || !out_ptr) return aexis_fail(ctx, AEXIS_E_NULL, "null pointer");
+    int rc = bind(ctx);
+    if (rc) return rc;
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, handle, sizeof(h));
+    return aexis_cuda_check(ctx, cudaIpcOpenMemHandle(out_ptr, h, cudaIpcMemLazyEnablePeerAccess), "peer buffer open");
+}
+
+AEXIS_API int aexis_cuda_peer_buffer_close(aexis_ctx* ctx, void* ptr, int imported) {
+    if (!ctx) return AEXIS_E_NULL;
+    if (!ptr) return aexis_fail(ctx, AEXIS_E_NULL, "null pointer");
+    int rc = bind(ctx);
+    if (rc) return rc;
+    cudaError_t e = cudaStreamSynchronize(ctx->stream);
+    if (e == cudaSuccess) e = imported ? cudaIpcCloseMemHandle(ptr) : cudaFree(ptr);
+    return aexis_cuda_check(ctx, e, "peer buffer close");
+}
+
+AEXIS_API int aexis_cuda_topk_push(aexis_ctx* ctx, const int32_t* packed, int rows, int k, void* const* peers,
+                                   int world, int rank) {
+    if (!ctx) return AEXIS_E_NULL;
+    if (!packed || !peers) return aexis_fail(ctx, AEXIS_E_NULL, "null pointer");
+    if (world < 1 || world > kPeerMaxRanks || rank < 0 || rank >= world || rows <= 0 || k < 1 || k > 64)
+        return aexis_fail(ctx, AEXIS_E_RANGE, "world=%d rank=%d rows=%d k=%d", world, rank, rows, k);
+    if (reinterpret_cast<uintptr_t>(packed) % 16)
+        return aexis_fail(ctx, AEXIS_E_SHAPE, "packed must be 16-byte aligned");
+    for (int p = 0; p < world; ++p)
+        if (!peers[p] || reinterpret_cast<uintptr_t>(peers[p]) % 256)
+            return aexis_fail(ctx, AEXIS_E_SHAPE, "peer buffer %d null or not 256-byte aligned", p);
+    int rc = bind(ctx);
+    if (rc) return rc;
+    return aexis_cuda_check(ctx, launch_topk_peer_push(packed, rows, k, peers, world, rank, ctx->stream),
+                            "topk push launch");
+}
+
+AEXIS_API int aexis_cuda_topk_merge_peers(aexis_ctx* ctx, const void* recv, int world, int rows, int k,
+                                          int shard_rows, int64_t* out_ids, float* out_vals, int32_t* out_idx) {
+    if (!ctx) return AEXIS_E_NULL;
+    if (!recv || !out_ids || !out_vals || !out_idx) return aexis_fail(ctx, AEXIS_E_NULL, "null pointer");
+    if (world < 1 || world > kPeerMaxRanks || rows <= 0 || shard_rows <= 0 || k < 1 || k > 64)
+        return aexis_fail(ctx, AEXIS_E_RANGE, "world=%d rows=%d shard_rows=%d k=%d", world, rows, shard_rows, k);
+    int rc = bind(ctx);
+    if (rc) return rc;
+    return aexis_cuda_check(ctx, launch_topk_peer_merge(recv, world, rows, k, shard_rows,
+                                                        reinterpret_cast<long long*>(out_ids), out_vals, out_idx,
+                                                        ctx->status, ctx->stream),
+                            "topk peer merge launch");
+}
+
 AEXIS_API int aexis_cuda_embed(aexis_ctx* ctx, const int32_t* words, int count, const aexis_weights* table,
                                const float* bias, float* out) {
     if (!ctx) return AEXIS_E_NULL;

@@ -198,6 +198,27 @@ size_t topk_scratch_bytes(int rows, int width, int k, int sm_count);
 // Merge of the shards' packed argmax keys and top-k lists (k_topk.cu).
 cudaError_t launch_topk_shard_merge(const int32_t* gathered, int lists, int rows, int k, int shard_rows, long long* ids,
                                     float* vals, int32_t* idx, cudaStream_t s);
+// The peer exchange of the same packed results (k_topk.cu). Every rank owns a
+// receive buffer, mapped into every other rank's process (CUDA IPC):
+//   u32 words [0, 16): flags [2][kPeerMaxRanks], flag[parity][s] = the epoch
+//                      of the last call whose result from shard s is in place;
+//   u32 word 16: the push kernel's CTA counter, word 17: the epoch of this
+//                rank's last push (both for its own buffer only);
+//   from byte 256: slots int32 [2][world][peer_slot_words], parity = epoch & 1.
+// The push takes the next epoch, writes rank's packed result into every
+// buffer's slot and releases the flags; the merge waits for all flags of the
+// epoch, then merges. Nothing of a call is on the host, so a call can be
+// captured in a CUDA graph.
+constexpr int kPeerMaxRanks = 8;
+constexpr int kPeerCounterWord = 16;
+constexpr int kPeerEpochWord = 17;
+constexpr size_t kPeerHeaderBytes = 256;
+int peer_slot_words(int rows, int k);
+size_t peer_recv_bytes(int world, int rows, int k);
+cudaError_t launch_topk_peer_push(const int32_t* packed, int rows, int k, void* const* peers, int world, int rank,
+                                  cudaStream_t s);
+cudaError_t launch_topk_peer_merge(const void* recv, int world, int rows, int k, int shard_rows, long long* ids,
+                                   float* vals, int32_t* idx, int* status, cudaStream_t s);
 // Greedy keys (aexis_argmax_key, global indices) from per-row top-k lists.
 cudaError_t launch_topk_greedy_keys(const float* logits, int rows, int ld, const float* vals, const int32_t* idx, int k,
                                     long long offset, unsigned long long* keys, cudaStream_t s);

@@ -48,6 +48,13 @@ constexpr int kTkMinSampledWidth = 32768;
 __device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;"); }
 
+// Bounded waits (the peer exchange's flags): about a second of SM clock,
+// then AEXIS_E_TIMEOUT in the context status word.
+constexpr long long kTkWaitLimitCycles = 2000000000LL;
+__device__ __forceinline__ void tk_report_timeout(int* status) {
+    if (status) atomicCAS(status, 0, (int)AEXIS_E_TIMEOUT);
+}
+
 __device__ __forceinline__ unsigned int tk_key32(float v) {
     return v != v ? 0u : aexis_orderable(v == 0.0f ? 0.0f : v);  // NaN below everything
 }
@@ -447,14 +454,50 @@ __global__ void __launch_bounds__(kTkThreads) topk_exact_kernel(const float* log
 // index i is global r * shard_rows + i. Per row: the largest key (the
 // greedy id, the scan's tie rule) and the k largest (value, global index)
 // keys of the shards' lists (warp r loads list r, then the tree merge).
+// With `flags` (the peer exchange: the receive buffer's header), the lists
+// arrive from the other ranks' push kernels: thread 0 first waits, bounded,
+// until every shard's flag of the call's parity holds the call's epoch (an
+// acquire at system scope: the pushes released it after their data); a wait
+// that runs out records AEXIS_E_TIMEOUT and the CTA writes nothing.
 __global__ void __launch_bounds__(kTkThreads) topk_shard_merge_kernel(const int32_t* gathered, int lists, int rows,
                                                                        int k, int shard_rows, long long* ids,
-                                                                       float* vals, int32_t* idx) {
+                                                                       float* vals, int32_t* idx,
+                                                                       int slot_words, const unsigned int* flags,
+                                                                       int* status) {
     __shared__ unsigned long long xch[kTkThreads];
     __shared__ unsigned long long best[kTkWarps];
+    __shared__ int arrived;
     const int row = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     griddep_wait();
-    const size_t per = (size_t)rows * 2 + (size_t)rows * k * 2;  // 32-bit words per shard
+    if (flags) {
+        // The call's epoch (this rank's push stored it) picks the slot parity.
+        const unsigned int e = *reinterpret_cast<const volatile unsigned int*>(flags + kPeerEpochWord);
+        flags += (e & 1u) * kPeerMaxRanks;
+        gathered += (size_t)(e & 1u) * lists * slot_words;
+        if (threadIdx.x == 0) {
+            int ok = 1;
+            const long long t0 = clock64();
+            for (int sh = 0; sh < lists && ok; ++sh) {
+                for (;;) {
+                    unsigned int f;
+                    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(f) : "l"(flags + sh) : "memory");
+                    if (f == e) break;
+                    if (clock64() - t0 > kTkWaitLimitCycles) {
+                        tk_report_timeout(status);
+                        ok = 0;
+                        break;
+                    }
+                }
+            }
+            arrived = ok;
+        }
+        __syncthreads();
+        if (!arrived) {
+            griddep_launch();
+            return;
+        }
+    }
+    const size_t per = (size_t)slot_words;  // 32-bit words per shard
     unsigned long long t[2] = {0ull, 0ull};
     unsigned long long kmax = 0ull;
     if (warp < lists) {
@@ -564,7 +607,86 @@ cudaError_t launch_topk(const float* logits, int rows, int width, int ld, int k,
 cudaError_t launch_topk_shard_merge(const int32_t* gathered, int lists, int rows, int k, int shard_rows, long long* ids,
                                     float* vals, int32_t* idx, cudaStream_t s) {
     if (lists < 1 || lists > kTkWarps || k < 1 || k > kTkMaxK) return cudaErrorInvalidValue;
-    return launch_pdl(topk_shard_merge_kernel, dim3(rows), s, gathered, lists, rows, k, shard_rows, ids, vals, idx);
+    const unsigned int* no_flags = nullptr;
+    int* no_status = nullptr;
+    return launch_pdl(topk_shard_merge_kernel, dim3(rows), s, gathered, lists, rows, k, shard_rows, ids, vals, idx,
+                      2 * rows + 2 * rows * k, no_flags, no_status);
+}
+
+namespace {
+
+// The peer exchange: each rank pushes its packed result (keys + top-k lists)
+// into slot `rank` of every rank's receive buffer (PeerRecv layout) with
+// plain stores over NVLink, then, once every CTA's stores are fenced at
+// system scope (the last CTA to arrive on the block counter knows), releases
+// the epoch into flag[parity][rank] of every receive buffer.
+struct PeerPtrs {
+    char* p[kPeerMaxRanks];
+};
+
+__global__ void __launch_bounds__(kTkThreads) topk_peer_push_kernel(const int32_t* __restrict__ src, int words,
+                                                                    PeerPtrs peers, int world, int rank,
+                                                                    int slot_words) {
+    griddep_wait();
+    // This call's epoch: one past the last call's, which this rank's
+    // previous push stored (every earlier kernel of the stream has finished).
+    unsigned int* own = reinterpret_cast<unsigned int*>(peers.p[rank]);
+    unsigned int* counter = own + kPeerCounterWord;
+    const unsigned int epoch = *reinterpret_cast<volatile unsigned int*>(own + kPeerEpochWord) + 1u;
+    const int parity = (int)(epoch & 1u);
+    const size_t slot = (size_t)(parity * world + rank) * (size_t)slot_words;  // in 32-bit words
+    const int n16 = words >> 2;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n16; i += gridDim.x * blockDim.x) {
+        const int4 v = __ldcg(reinterpret_cast<const int4*>(src) + i);
+        for (int p = 0; p < world; ++p)
+            reinterpret_cast<int4*>(reinterpret_cast<int32_t*>(peers.p[p] + kPeerHeaderBytes) + slot)[i] = v;
+    }
+    if (blockIdx.x == 0 && threadIdx.x < (words & 3)) {
+        const int i = (n16 << 2) + threadIdx.x;
+        const int32_t v = __ldcg(src + i);
+        for (int p = 0; p < world; ++p) (reinterpret_cast<int32_t*>(peers.p[p] + kPeerHeaderBytes) + slot)[i] = v;
+    }
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0 && atomicAdd(counter, 1u) == gridDim.x - 1) {
+        *counter = 0u;  // the next call's count
+        __threadfence_system();
+        for (int p = 0; p < world; ++p) {
+            unsigned int* flag = reinterpret_cast<unsigned int*>(peers.p[p]) + parity * kPeerMaxRanks + rank;
+            asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(flag), "r"(epoch) : "memory");
+        }
+        own[kPeerEpochWord] = epoch;  // read by this call's merge and the next push
+    }
+    griddep_launch();
+}
+
+}  // namespace
+
+int peer_slot_words(int rows, int k) { return ((2 * rows + 2 * rows * k) + 3) & ~3; }
+
+size_t peer_recv_bytes(int world, int rows, int k) {
+    return kPeerHeaderBytes + 2 * (size_t)world * (size_t)peer_slot_words(rows, k) * sizeof(int32_t);
+}
+
+cudaError_t launch_topk_peer_push(const int32_t* packed, int rows, int k, void* const* peers, int world, int rank,
+                                  cudaStream_t s) {
+    if (world < 1 || world > kPeerMaxRanks || rank < 0 || rank >= world) return cudaErrorInvalidValue;
+    PeerPtrs pp = {};
+    for (int p = 0; p < world; ++p) pp.p[p] = reinterpret_cast<char*>(peers[p]);
+    const int words = 2 * rows + 2 * rows * k;
+    const int blocks = ((words >> 2) + kTkThreads - 1) / kTkThreads;
+    return launch_pdl(topk_peer_push_kernel, dim3(blocks < 1 ? 1 : (blocks > 64 ? 64 : blocks)), s, packed, words, pp,
+                      world, rank, peer_slot_words(rows, k));
+}
+
+cudaError_t launch_topk_peer_merge(const void* recv, int world, int rows, int k, int shard_rows, long long* ids,
+                                   float* vals, int32_t* idx, int* status, cudaStream_t s) {
+    if (world < 1 || world > kPeerMaxRanks || k < 1 || k > kTkMaxK) return cudaErrorInvalidValue;
+    const char* base = reinterpret_cast<const char*>(recv);
+    const unsigned int* flags = reinterpret_cast<const unsigned int*>(base);
+    const int32_t* gathered = reinterpret_cast<const int32_t*>(base + kPeerHeaderBytes);
+    return launch_pdl(topk_shard_merge_kernel, dim3(rows), s, gathered, world, rows, k, shard_rows, ids, vals, idx,
+                      peer_slot_words(rows, k), flags, status);
 }
 
 namespace {

@@ -61,6 +61,12 @@ SIGNATURES = {
     "aexis_cuda_topk": (i32, [vp, vp, i32, i32, i32, i32, vp, vp]),
     "aexis_cuda_gemm_topk": (i32, [vp, vp, i32, i32, i32, i32, vp, f32, i32, C.c_int64, vp, vp, vp]),
     "aexis_cuda_topk_merge": (i32, [vp, vp, i32, i32, i32, i32, vp, vp, vp]),
+    "aexis_cuda_peer_buffer_bytes": (i32, [i32, i32, i32, C.POINTER(C.c_size_t)]),
+    "aexis_cuda_peer_buffer_create": (i32, [vp, C.c_size_t, C.POINTER(vp), vp]),
+    "aexis_cuda_peer_buffer_open": (i32, [vp, vp, C.POINTER(vp)]),
+    "aexis_cuda_peer_buffer_close": (i32, [vp, vp, i32]),
+    "aexis_cuda_topk_push": (i32, [vp, vp, i32, i32, C.POINTER(vp), i32, i32]),
+    "aexis_cuda_topk_merge_peers": (i32, [vp, vp, i32, i32, i32, i32, vp, vp, vp]),
     "aexis_cuda_embed": (i32, [vp, vp, i32, vp, vp, vp]),
     "aexis_cuda_swish": (i32, [vp, vp, i32, vp]),
     "aexis_cuda_swiglu": (i32, [vp, vp, vp, i32, vp]),

@@ -348,6 +348,37 @@ class AexisOps:
         self._call(lib().aexis_cuda_topk_merge, _ptr(gathered), lists, rows, k, shard_rows, _ptr(out_ids),
                    _ptr(out_vals), _ptr(out_idx))
 
+    # ---- the sharded lm_head's exchange over peer memory (aexis_cuda_peer_*)
+    @staticmethod
+    def peer_buffer_bytes(world, rows, k) -> int:
+        out = C.c_size_t(0)
+        check(lib().aexis_cuda_peer_buffer_bytes(world, rows, k, C.byref(out)), None)
+        return out.value
+
+    def peer_buffer_create(self, nbytes):
+        """A zeroed receive buffer of this device: (device pointer, 64-byte IPC handle)."""
+        ptr = C.c_void_p()
+        handle = (C.c_uint8 * 64)()
+        self._call(lib().aexis_cuda_peer_buffer_create, nbytes, C.byref(ptr), handle)
+        return ptr.value, bytes(handle)
+
+    def peer_buffer_open(self, handle: bytes) -> int:
+        """Another rank's receive buffer mapped into this process."""
+        ptr = C.c_void_p()
+        self._call(lib().aexis_cuda_peer_buffer_open, (C.c_uint8 * 64).from_buffer_copy(handle), C.byref(ptr))
+        return ptr.value
+
+    def peer_buffer_close(self, ptr: int, imported: bool):
+        self._call(lib().aexis_cuda_peer_buffer_close, ptr, int(imported))
+
+    def topk_push(self, packed, rows, k, peers, rank):
+        arr = (C.c_void_p * len(peers))(*peers)
+        self._call(lib().aexis_cuda_topk_push, _ptr(packed), rows, k, arr, len(peers), rank)
+
+    def topk_merge_peers(self, recv, world, rows, k, shard_rows, out_ids, out_vals, out_idx):
+        self._call(lib().aexis_cuda_topk_merge_peers, recv, world, rows, k, shard_rows, _ptr(out_ids),
+                   _ptr(out_vals), _ptr(out_idx))
+
     def embed_texture(self, words, count, table: Weights, bias, output):
         """AexisOps.EmbedTexture (:10764-10810)."""
         self._call(lib().aexis_cuda_embed, _ptr(words), count, table.handle, _ptr(bias), _ptr(output))

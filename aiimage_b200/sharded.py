@@ -7,10 +7,15 @@ handle. One call:
      aexis_cuda_gemm_topk: the [M, V/G] logits on the tensor cores, then the
      top-k and the greedy keys from the top-k lists (aexis_cuda_gemm_tiled +
      aexis_cuda_topk + aexis_cuda_topk_greedy_keys in one call);
-  3. the keys and the top-k lists packed into one buffer, one all-gather of
-     those buffers (NCCL over NVLink; gloo in the CPU tests), then one merge
-     kernel (aexis_cuda_topk_merge): the largest key, and the k largest
-     (value, global index) keys of the shards' sorted lists.
+  3. the keys and the top-k lists packed into one buffer, exchanged between
+     the ranks, then one merge kernel: the largest key, and the k largest
+     (value, global index) keys of the shards' sorted lists. With NCCL ranks
+     (one process per GPU of a node) the exchange goes over peer memory: each
+     rank's push kernel writes its buffer into every rank's receive buffer
+     over NVLink and releases an epoch flag, and the merge kernel waits for
+     all flags (aexis_cuda_topk_push / aexis_cuda_topk_merge_peers, buffers
+     mapped through CUDA IPC handles). exchange="collective" (and gloo, in
+     the CPU tests) uses one all-gather and aexis_cuda_topk_merge instead.
 Every logit is computed by exactly one rank with the same kernel and the same
 K order whatever G is, and the key's tie rule (lowest global index) matches
 the single-device scan (AexisArgMaxPack4LinearMat, HLSL Pack4Matmul:645-686),
@@ -60,11 +65,49 @@ def exchange(buf: torch.Tensor, group=None) -> torch.Tensor:
     return torch.cat(parts)
 
 
+class PeerExchange:
+    """Every rank's packed result through peer memory: one receive buffer per
+    rank (aexis_cuda_peer_buffer_create), the others' buffers mapped here by
+    their IPC handles (all-gathered once through torch.distributed), then per
+    call a push of this rank's buffer into every receive buffer and a merge
+    that waits for the call's epoch in this rank's own buffer (the epoch is a
+    device counter: a call can be captured in a CUDA graph)."""
+
+    def __init__(self, ops, rows: int, k: int, world: int, rank: int, group=None):
+        import torch.distributed as dist
+        self.ops, self.rows, self.k, self.world, self.rank, self.group = ops, rows, k, world, rank, group
+        self.own, handle = ops.peer_buffer_create(ops.peer_buffer_bytes(world, rows, k))
+        handles = [None] * world
+        dist.all_gather_object(handles, handle, group=group)
+        self.peers = [self.own if r == rank else ops.peer_buffer_open(h) for r, h in enumerate(handles)]
+        dist.barrier(group=group)  # every buffer mapped everywhere before the first push
+
+    def merge(self, buf: torch.Tensor, shard_rows: int, ids, vals, idx):
+        self.ops.topk_push(buf, self.rows, self.k, self.peers, self.rank)
+        self.ops.topk_merge_peers(self.own, self.world, self.rows, self.k, shard_rows, ids, vals, idx)
+
+    def close(self):
+        """Unmap the others' buffers and free this one, once every rank is past its last merge."""
+        import torch.distributed as dist
+        self.ops.sync()
+        dist.barrier(group=self.group)
+        for r, p in enumerate(self.peers):
+            if r != self.rank:
+                self.ops.peer_buffer_close(p, True)
+        dist.barrier(group=self.group)
+        self.ops.peer_buffer_close(self.own, False)
+        self.peers = []
+
+
 class ShardedLmHead:
     """One rank's shard of the lm_head (see module docstring)."""
 
-    def __init__(self, ops, packed, scales, vocab: int, hidden: int, world: int = 1, rank: int = 0, group=None):
+    def __init__(self, ops, packed, scales, vocab: int, hidden: int, world: int = 1, rank: int = 0, group=None,
+                 exchange: str = "auto"):
+        if exchange not in ("auto", "peer", "collective"):
+            raise ValueError(f"exchange={exchange!r} (auto, peer or collective)")
         self.ops, self.vocab, self.hidden, self.group = ops, vocab, hidden, group
+        self.rank, self.exchange_mode, self._peer = rank, exchange, None
         self.lo, self.hi = shard_range(vocab, world, rank)
         self.n = self.hi - self.lo
         import numpy as np
@@ -105,12 +148,38 @@ class ShardedLmHead:
         self.shard_topk(x, k, keys, vals, idx)
         return self.merge(buf, m, k)
 
+    def uses_peer_exchange(self) -> bool:
+        """Whether merge goes over peer memory (NCCL ranks, exchange "auto" or "peer")."""
+        if self.world == 1 or self.exchange_mode == "collective":
+            return False
+        import torch.distributed as dist
+        return dist.get_backend(self.group) == "nccl"
+
     def merge(self, buf: torch.Tensor, m: int, k: int):
-        """The exchange step alone: all-gather every rank's packed buffer, then the merge kernel."""
-        gathered = exchange(buf, self.group)
+        """The exchange step alone: every rank's packed buffer to every rank, then the merge kernel."""
         ids = torch.empty(m, dtype=torch.int64, device=buf.device)
         out_v = torch.empty((m, k), dtype=torch.float32, device=buf.device)
         out_i = torch.empty((m, k), dtype=torch.int32, device=buf.device)
-        per = (self.vocab + self.world - 1) // self.world
-        self.ops.topk_merge(gathered, self.world, m, k, per, ids, out_v, out_i)
+        self.merge_into(buf, m, k, ids, out_v, out_i)
         return ids, out_v, out_i.to(torch.int64)
+
+    def merge_into(self, buf: torch.Tensor, m: int, k: int, ids, out_v, out_i):
+        """merge into caller-owned outputs (ids int64 [m], values fp32 [m, k],
+        global indices int32 [m, k]). The peer path allocates nothing once its
+        buffers exist for (m, k), so a call can be captured in a CUDA graph."""
+        per = (self.vocab + self.world - 1) // self.world
+        if self.uses_peer_exchange():
+            if self._peer is None or (self._peer.rows, self._peer.k) != (m, k):
+                if self._peer is not None:
+                    self._peer.close()
+                self._peer = PeerExchange(self.ops, m, k, self.world, self.rank, self.group)
+            self._peer.merge(buf, per, ids, out_v, out_i)
+        else:
+            gathered = exchange(buf, self.group)
+            self.ops.topk_merge(gathered, self.world, m, k, per, ids, out_v, out_i)
+
+    def close(self):
+        """Release the peer exchange's buffers (collective: every rank calls it)."""
+        if self._peer is not None:
+            self._peer.close()
+            self._peer = None

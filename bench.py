@@ -851,6 +851,7 @@ def bench_config5(ops, world: int, rank: int, reps: int = 10):
     single-GPU run of the whole vocabulary."""
     import torch
     from aiimage_b200.sharded import ShardedLmHead
+    from aiimage_b200.sharded import keys_to_ids as sharded_ids
     vocab, hidden, m, k = 151936, 1024, 256, 50
     p, s = synth.q8_weights(vocab, hidden, seed=5, tag=(vocab, hidden))
     x = torch.from_numpy(synth.activations(hidden, seed=5, tag=(m, hidden), m=m)).cuda()
@@ -890,26 +891,80 @@ def bench_config5(ops, world: int, rank: int, reps: int = 10):
     e1.record()
     e1.synchronize()
     argmax_s = e0.elapsed_time(e1) / 1e3 / reps
-    # The exchange alone (G > 1): all-gather of the packed keys + top-k lists and the merge kernel,
-    # on a buffer this rank's GEMM already filled; max over ranks, as the whole call.
-    exchange_s = None
+    # The exchange alone (G > 1) on a buffer this rank's GEMM already filled, max over ranks as the whole
+    # call: the call's own path (peer memory: push + merge), then the collective path (one NCCL
+    # all-gather + aexis_cuda_topk_merge) for comparison.
+    exchange_s = collective_s = None
     if world > 1:
         from aiimage_b200.sharded import pack_views, packed_words
         buf = torch.empty(packed_words(m, k), dtype=torch.int32, device="cuda")
         head.shard_topk(x, k, *pack_views(buf, m, k))
-        head.merge(buf, m, k)
+
+        def time_merge():
+            head.merge(buf, m, k)
+            torch.cuda.synchronize()
+            barrier(world)
+            e0.record()
+            for _ in range(reps):
+                head.merge(buf, m, k)
+            e1.record()
+            e1.synchronize()
+            return max_over_ranks(e0.elapsed_time(e1) / 1e3 / reps, world)
+
+        peer = head.uses_peer_exchange()
+        exchange_s = time_merge()
+        head.exchange_mode = "collective"
+        collective_s = time_merge()
+        head.exchange_mode = "auto"
+    # The whole call as one CUDA graph (G = 1, or the peer exchange): the same kernels without the host's
+    # launch gaps, replayed `reps` times; its results are the ones checked against one GPU below.
+    graph_s = None
+    if world == 1 or head.uses_peer_exchange():
+        from aiimage_b200.sharded import pack_views, packed_words
+        gbuf = torch.empty(packed_words(m, k), dtype=torch.int32, device="cuda")
+        gk, gv, gi = pack_views(gbuf, m, k)
+        g_ids = torch.empty(m, dtype=torch.int64, device="cuda")
+        g_v = torch.empty((m, k), dtype=torch.float32, device="cuda")
+        g_i = torch.empty((m, k), dtype=torch.int32, device="cuda")
+
+        def one_call():
+            head.shard_topk(x, k, gk, gv, gi)
+            if world > 1:
+                head.merge_into(gbuf, m, k, g_ids, g_v, g_i)
+
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            for _ in range(3):
+                one_call()
+        torch.cuda.current_stream().wait_stream(side)
+        torch.cuda.synchronize()
+        barrier(world)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            one_call()
+        graph.replay()
         torch.cuda.synchronize()
         barrier(world)
         e0.record()
         for _ in range(reps):
-            head.merge(buf, m, k)
+            graph.replay()
         e1.record()
         e1.synchronize()
-        exchange_s = max_over_ranks(e0.elapsed_time(e1) / 1e3 / reps, world)
+        graph_s = max_over_ranks(e0.elapsed_time(e1) / 1e3 / reps, world)
+        if world > 1:
+            ids, vals, idx = g_ids, g_v, g_i.to(torch.int64)
+        else:
+            ids, vals, idx = sharded_ids(gk), gv, gi.to(torch.int64)
+        del graph
     flops = 2.0 * m * vocab * hidden
     peak, kind = measured_tflops()
+    best_s = graph_s if graph_s is not None else call_s
     out = {"workload": "config5_lm_head_q8_151936x1024_batch256_argmax_top50", "gpus": world,
-           "ms_per_call": round(call_s * 1e3, 4), "TFLOP/s": round(flops / call_s / 1e12, 1),
+           "ms_per_call": round(best_s * 1e3, 4), "TFLOP/s": round(flops / best_s / 1e12, 1),
+           "timing": ("one CUDA graph per call (top-k GEMM, and at G > 1 the peer push and merge), replayed"
+                      if graph_s is not None else "host loop of calls"),
+           "ms_per_call_host_loop": round(call_s * 1e3, 4),
            "gemm_rank_ms": round(gemm_s * 1e3, 4),
            "greedy_keys_from_topk_rank_ms": round(argmax_s * 1e3, 4), "topk_rank_ms": round(topk_s * 1e3, 4),
            "gemm_rank_TFLOP/s": round(2.0 * m * head.n * hidden / gemm_s / 1e12, 1),
@@ -918,14 +973,19 @@ def bench_config5(ops, world: int, rank: int, reps: int = 10):
            "first_ids": ids[:6].tolist()}
     if exchange_s is not None:
         out["exchange_ms"] = round(exchange_s * 1e3, 4)
-        out["exchange"] = (f"NCCL all-gather of {packed_words(m, k) * 4} B per rank (keys + top-{k} values and"
-                           f" indices) + aexis_cuda_topk_merge, max over ranks")
+        out["exchange"] = ((f"peer memory: aexis_cuda_topk_push of {packed_words(m, k) * 4} B (keys + top-{k} values"
+                            f" and indices) into every rank's receive buffer over NVLink + aexis_cuda_topk_merge_peers"
+                            f" (waits on the epoch flags)") if peer else
+                           f"NCCL all-gather of {packed_words(m, k) * 4} B per rank + aexis_cuda_topk_merge") + \
+            ", max over ranks"
+        out["exchange_collective_ms"] = round(collective_s * 1e3, 4)
     if world > 1 and rank == 0:
         full = ShardedLmHead(ops, p, s, vocab, hidden, 1, 0)
         ids1, _, idx1 = full.forward(x, k)
         out["ids_match_single_gpu"] = bool(torch.equal(ids1, ids))
         out["top50_match_single_gpu"] = bool(torch.equal(idx1, idx))
         full.w.free()
+    head.close()
     head.w.free()
     return out
 

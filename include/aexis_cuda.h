@@ -29,6 +29,7 @@
 #ifndef AEXIS_CUDA_H_
 #define AEXIS_CUDA_H_
 
+#include <stddef.h>
 #include <stdint.h>
 
 #ifdef __cplusplus
@@ -342,6 +343,41 @@ int aexis_cuda_sample_history_add(aexis_ctx* ctx, uint32_t* history, int rows, i
  * single-device calls on the whole vocabulary. */
 int aexis_cuda_topk_merge(aexis_ctx* ctx, const int32_t* gathered, int lists, int rows, int k,
                           int shard_rows, int64_t* out_ids, float* out_vals, int32_t* out_idx);
+
+/* No reference counterpart (the reference decodes on one device): the same
+ * exchange over peer memory instead of a collective, for ranks that are
+ * processes on GPUs of one node joined by NVLink.
+ *
+ * Every rank owns one receive buffer of aexis_cuda_peer_buffer_bytes(world,
+ * rows, k) bytes, made by aexis_cuda_peer_buffer_create (zeroed; out_handle:
+ * 64 bytes of CUDA IPC handle). The host hands the handles to the other
+ * ranks (any out-of-band channel), and each rank maps the others' buffers
+ * with aexis_cuda_peer_buffer_open. Per call (every rank makes the same
+ * calls in the same order):
+ *   aexis_cuda_topk_push copies this rank's packed result (the
+ *   aexis_cuda_topk_merge layout of one shard: rows uint64 greedy keys, rows
+ *   x k fp32 values, rows x k int32 shard-local indices; device, 16-byte
+ *   aligned) into slot `rank` of every receive buffer (`peers`: host array
+ *   of the world buffers as mapped in this process, peers[rank] its own),
+ *   then publishes the call's epoch in each buffer's flags;
+ *   aexis_cuda_topk_merge_peers waits on this rank's own buffer (`recv`)
+ *   until every shard's flag holds the epoch (bounded: AEXIS_E_TIMEOUT from
+ *   aexis_cuda_sync when a peer never arrives) and writes what
+ *   aexis_cuda_topk_merge writes.
+ * The epoch is a counter in the rank's own buffer (the push takes the next
+ * one), so the calls carry no host state and can be captured in a CUDA
+ * graph. Two parities of slots alternate by epoch, so a rank may push the
+ * next call while another still merges the current one.
+ * aexis_cuda_peer_buffer_close unmaps an opened buffer (imported = 1) or
+ * frees an own one (imported = 0), after every rank is past its last merge. */
+int aexis_cuda_peer_buffer_bytes(int world, int rows, int k, size_t* out_bytes);
+int aexis_cuda_peer_buffer_create(aexis_ctx* ctx, size_t bytes, void** out_ptr, uint8_t* out_handle);
+int aexis_cuda_peer_buffer_open(aexis_ctx* ctx, const uint8_t* handle, void** out_ptr);
+int aexis_cuda_peer_buffer_close(aexis_ctx* ctx, void* ptr, int imported);
+int aexis_cuda_topk_push(aexis_ctx* ctx, const int32_t* packed, int rows, int k, void* const* peers, int world,
+                         int rank);
+int aexis_cuda_topk_merge_peers(aexis_ctx* ctx, const void* recv, int world, int rows, int k, int shard_rows,
+                                int64_t* out_ids, float* out_vals, int32_t* out_idx);
 
 /* Ops.EmbedTexture (Ops:10764-10810; HLSL BufferTensor AexisEmbedValue:37-62):
  * out[q, p] = W(clamp(words[q], 0, vocab-1), p) (+ bias[p]) for a Q4 (group

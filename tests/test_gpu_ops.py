@@ -348,6 +348,61 @@ def test_topk_shard_merge_matches_full_vocab(ops, oracle, world):
     assert np.array_equal(host(ids), host(sharded.keys_to_ids(full_keys)))
 
 
+@pytest.mark.parametrize("world", [2, 3, 8])
+def test_topk_peer_exchange_matches_gathered_merge(ops, world):
+    """The sharded lm_head's exchange over peer memory with `world` ranks
+    simulated on one GPU (one receive buffer per rank; each rank's
+    aexis_cuda_topk_push writes every buffer, then each rank's
+    aexis_cuda_topk_merge_peers reads its own): every rank merges exactly
+    what aexis_cuda_topk_merge gives on the all-gathered buffers, over two
+    calls (both slot parities, other data in the second). The pushes finish
+    before any merge starts, so no kernel waits on another. An odd row count
+    leaves a packed result that is not a whole number of 16-byte units. When
+    one rank skips a push, the others' merges give up (AEXIS_E_TIMEOUT,
+    about a second) and the context keeps working."""
+    import torch
+    from aiimage_b200 import errors, sharded
+    rows, vocab, k = 7, 20003, 50
+    per = (vocab + world - 1) // world
+    w = sharded.packed_words(rows, k)
+    assert w % 4 != 0
+    recv = [ops.peer_buffer_create(ops.peer_buffer_bytes(world, rows, k))[0] for _ in range(world)]
+    try:
+        for call in (1, 2):
+            x = np.random.default_rng(40 + 10 * world + call).standard_normal((rows, vocab)).astype(np.float32)
+            x[0, 5] = x[0, vocab - 3] = x[0].max() + 1  # greedy tie across shards
+            x[1, per - 1] = x[1, per] = x[1].max() + 2  # tie at a shard boundary
+            xc = cuda(x)
+            bufs = [torch.zeros(w, dtype=torch.int32, device="cuda") for _ in range(world)]
+            for r in range(world):
+                lo, hi = sharded.shard_range(vocab, world, r)
+                keys, vals, idx = sharded.pack_views(bufs[r], rows, k)
+                ops.argmax_keys(xc[:, lo:hi], hi - lo, rows, lo, keys, ld=vocab)
+                ops.top_k(xc[:, lo:hi], hi - lo, rows, k, vals, idx, ld=vocab)
+            for r in range(world):
+                ops.topk_push(bufs[r], rows, k, recv, r)
+            ref = [torch.zeros(rows, dtype=torch.int64, device="cuda"),
+                   torch.zeros((rows, k), dtype=torch.float32, device="cuda"),
+                   torch.zeros((rows, k), dtype=torch.int32, device="cuda")]
+            ops.topk_merge(torch.cat(bufs), world, rows, k, per, *ref)
+            for r in range(world):
+                got = [torch.full_like(t, -7) for t in ref]
+                ops.topk_merge_peers(recv[r], world, rows, k, per, *got)
+                for g, e in zip(got, ref):
+                    assert np.array_equal(host(g), host(e)), (call, r)
+        ops.sync()
+        for r in range(1, world):  # rank 0 does not push the third call
+            ops.topk_push(bufs[r], rows, k, recv, r)
+        got = [torch.zeros_like(t) for t in ref]
+        ops.topk_merge_peers(recv[1], world, rows, k, per, *got)
+        with pytest.raises(errors.DeviceTimeoutError):
+            ops.sync()
+        ops.sync()
+    finally:
+        for p in recv:
+            ops.peer_buffer_close(p, False)
+
+
 @pytest.mark.parametrize("world", [1, 3, 8])
 def test_topk_greedy_keys_match_argmax_keys(ops, world):
     """aexis_cuda_topk_greedy_keys (the shard's argmax key from its top-k list) against aexis_cuda_argmax_keys
