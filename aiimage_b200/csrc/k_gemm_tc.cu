@@ -329,43 +329,73 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_q8_tc_kernel(TcParams p) {
         griddep_wait();
         griddep_launch();
         if (lane == 0) {
+            // tcgen05.mma issue blocks this thread about as long as the MMA
+            // runs, so the tensor pipe idles during whatever the thread does
+            // between k-blocks: that bookkeeping is kept to increments.
+            // Stage / phase counters advance by one; the smem descriptors of
+            // stage 0 are built once and advanced by the stage stride and by
+            // 32 bytes (2 units of the 16-byte start field) per K=16 step.
             const uint32_t idesc = idesc_f16_f32(kTM, p.nb);
-            int it = 0;
-            for (int t = 0; t < my_tiles && !*abort_flag; ++t) {
+            const uint64_t adesc0 = sw128_desc(smem_u32(base + L.a_off));
+            const uint64_t bdesc0 = sw128_desc(smem_u32(base + L.b_off));
+            const uint64_t a_step = (uint64_t)(L.a_stage >> 4), b_step = (uint64_t)(L.b_stage >> 4);
+            const uint64_t slab_step = (uint64_t)(kATileBytes >> 4);
+            int sa = 0, sb = 0;
+            uint32_t pa = 0, pb = 0;
+            uint64_t adesc = adesc0, bdesc = bdesc0;
+            bool ok = true;
+            for (int t = 0; t < my_tiles && ok; ++t) {
                 const TcTile T = tc_tile(p, s_lo, s_hi, t, nkb);
                 const int ns = T.ns;
                 const uint32_t acc = tmem + (uint32_t)((t & 1) * acc_cols);
                 // Buffer t & 1 was last drained by the epilogue of tile t - 2.
                 if (t >= 2 && !mbar_wait(acc_empty + (t & 1), ((t >> 1) + 1) & 1)) {
-                    report_timeout(p.status);
-                    *abort_flag = 1;
+                    ok = false;
                     break;
                 }
                 tc_fence_after();
-                for (int kb = T.kb0; kb < T.kb1; ++kb, ++it) {
-                    const int sa = it % kADepth, sb = it % BD;
-                    if (!mbar_wait(a_ready + sa, (it / kADepth) & 1) || !mbar_wait(b_full + sb, (it / BD) & 1)) {
-                        report_timeout(p.status);
-                        *abort_flag = 1;
+                for (int kb = T.kb0; kb < T.kb1; ++kb) {
+                    if (!mbar_wait(a_ready + sa, pa) || !mbar_wait(b_full + sb, pb)) {
+                        ok = false;
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t a0 = smem_u32(base + L.a_off + sa * L.a_stage);
-                    const uint32_t b0 = smem_u32(base + L.b_off + sb * L.b_stage);
+                    const int first = kb == T.kb0;
 #pragma unroll
-                    for (int j = 0; j < 2; ++j) {
-                        if (j < ns) {
+                    for (int kk = 0; kk < kKB / 16; ++kk)
+                        mma_f16(acc, adesc + 2 * kk, bdesc + 2 * kk, idesc, (first && kk == 0) ? 0 : 1);
+                    if (ns > 1) {
 #pragma unroll
-                            for (int kk = 0; kk < kKB / 16; ++kk)
-                                mma_f16(acc + (uint32_t)(j * p.nb), sw128_desc(a0 + j * kATileBytes + kk * 32),
-                                        sw128_desc(b0 + kk * 32), idesc, (kb > T.kb0 || kk > 0) ? 1 : 0);
-                        }
+                        for (int kk = 0; kk < kKB / 16; ++kk)
+                            mma_f16(acc + (uint32_t)p.nb, adesc + slab_step + 2 * kk, bdesc + 2 * kk, idesc,
+                                    (first && kk == 0) ? 0 : 1);
                     }
                     mma_commit(a_empty + sa);
                     mma_commit(b_empty + sb);
+                    if (++sa == kADepth) {
+                        sa = 0;
+                        pa ^= 1u;
+                        adesc = adesc0;
+                    } else {
+                        adesc += a_step;
+                    }
+                    if (++sb == BD) {
+                        sb = 0;
+                        pb ^= 1u;
+                        bdesc = bdesc0;
+                    } else {
+                        bdesc += b_step;
+                    }
                 }
-                if (*abort_flag) break;
+                if (!ok || *abort_flag) {
+                    ok = false;
+                    break;
+                }
                 mma_commit(acc_full + (t & 1));
+            }
+            if (!ok) {
+                report_timeout(p.status);
+                *abort_flag = 1;
             }
             // Every MMA this thread issued has completed before TMEM is freed.
             mma_commit(drain);
