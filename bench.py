@@ -269,11 +269,28 @@ class StepGraphs:
             self.g_rem.replay()
 
 
+# SM cycles of the spin queued ahead of a timed region (about 1 ms at 1.9 GHz).
+LAUNCH_COVER_CYCLES = 2_000_000
+
+
+def cover_launches():
+    """Queue a short device-side spin ahead of a start event. The host then
+    submits the timed graphs while the stream is still busy, so the events
+    bracket the steps' device time rather than the host's launch latency (a
+    20-step region lasts well under a millisecond; with idle streams its first
+    graph submission, slower still with several ranks sharing the host, would
+    count as GPU time)."""
+    import torch
+    torch.cuda._sleep(LAUNCH_COVER_CYCLES)
+
+
 def time_steps(graphs: StepGraphs, world: int) -> float:
     """CUDA-event time of exactly graphs.n steps, barrier + synchronize on both sides."""
     import torch
     barrier(world)
+    torch.cuda.synchronize()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    cover_launches()
     start.record()
     graphs.replay()
     end.record()
@@ -325,6 +342,7 @@ def run_gpu(args):
     torch.cuda.synchronize()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     n_rep = 5
+    cover_launches()
     ev0.record()
     for _ in range(n_rep):
         g_dom.replay()
@@ -342,6 +360,7 @@ def run_gpu(args):
         g = sw.graph(lambda c, i=i: sw.gemv(c, i), max(1, 120 // copies))
         g.replay()
         torch.cuda.synchronize()
+        cover_launches()
         ev0.record()
         g.replay()
         ev1.record()
@@ -514,6 +533,7 @@ def bench_q8(ops, peak):
     g.replay()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    cover_launches()
     e0.record()
     for _ in range(3):
         g.replay()
@@ -704,6 +724,7 @@ def bench_w8a8(ops, peak):
             g.replay()
             torch.cuda.synchronize()
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            cover_launches()
             e0.record()
             for _ in range(3):
                 g.replay()
@@ -813,6 +834,7 @@ def bench_linear_attention(ops, peak, prefill: int = 512):
         g.replay()
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        cover_launches()
         e0.record()
         for _ in range(3):
             g.replay()
@@ -946,6 +968,7 @@ def bench_config5(ops, world: int, rank: int, reps: int = 10):
         graph.replay()
         torch.cuda.synchronize()
         barrier(world)
+        cover_launches()
         e0.record()
         for _ in range(reps):
             graph.replay()
