@@ -428,6 +428,8 @@ __global__ void __launch_bounds__(kTaD) bat_attn_merge_prep_kernel(const float* 
     __shared__ int ps[kTaMaxB];
     __shared__ float wsm[kTaSlots];
     __shared__ float red[kTaD / 32];
+    __shared__ int vlist[kTaSlots];       // the valid slots, in increasing order
+    __shared__ int wcount[kTaD / 32];
     griddep_wait();
     griddep_launch();
     const int b = blockIdx.x, h = blockIdx.y, d = threadIdx.x, lane = d & 31, warp = d >> 5;
@@ -445,13 +447,28 @@ __global__ void __launch_bounds__(kTaD) bat_attn_merge_prep_kernel(const float* 
             mc = __ldcg(ph + (size_t)d * kTaStride + kTaD);
             lc = __ldcg(ph + (size_t)d * kTaStride + kTaD + 1);
         }
+        // The valid slots, compacted in increasing order, so that their
+        // partial rows can be loaded together (they need no weights yet).
+        const unsigned int bal = __ballot_sync(0xffffffffu, valid);
+        if (lane == 0) wcount[warp] = __popc(bal);
         float M = mc;
 #pragma unroll
         for (int o = 16; o >= 1; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
         if (lane == 0) red[warp] = M;
         __syncthreads();
+        int off = 0, nval = 0;
+#pragma unroll
+        for (int w = 0; w < kTaD / 32; ++w) {
+            off += w < warp ? wcount[w] : 0;
+            nval += wcount[w];
+        }
+        if (valid) vlist[off + __popc(bal & ((1u << lane) - 1u))] = d;
         M = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
         __syncthreads();
+        constexpr int kBatch = 8;
+        float ov[kBatch];
+#pragma unroll
+        for (int j = 0; j < kBatch; ++j) ov[j] = j < nval ? __ldcg(ph + (size_t)vlist[j] * kTaStride + d) : 0.0f;
         const float e = valid ? expf(mc - M) : 0.0f;
         float L = lc * e;
 #pragma unroll
@@ -460,9 +477,22 @@ __global__ void __launch_bounds__(kTaD) bat_attn_merge_prep_kernel(const float* 
         wsm[d] = e;
         __syncthreads();
         L = red[0] + red[1] + red[2] + red[3];
+        // Same terms in the same order as a walk over every slot: the valid
+        // slots by increasing index, skipping weights that underflow to 0.
         float acc = 0.0f;
-        for (int c = 0; c < n; ++c)
-            if (wsm[c] != 0.0f) acc = fmaf(wsm[c], __ldcg(ph + (size_t)c * kTaStride + d), acc);
+        for (int i0 = 0; i0 < nval; i0 += kBatch) {
+            if (i0 > 0)
+#pragma unroll
+                for (int j = 0; j < kBatch; ++j)
+                    ov[j] = i0 + j < nval ? __ldcg(ph + (size_t)vlist[i0 + j] * kTaStride + d) : 0.0f;
+#pragma unroll
+            for (int j = 0; j < kBatch; ++j) {
+                if (i0 + j < nval) {
+                    const float w = wsm[vlist[i0 + j]];
+                    if (w != 0.0f) acc = fmaf(w, ov[j], acc);
+                }
+            }
+        }
         v = acc / fmaxf(L, 1e-20f);
     }
     const int col = h * kTaD + d, kb = col >> 6, cc = col & 63;
