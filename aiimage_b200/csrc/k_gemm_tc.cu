@@ -759,14 +759,16 @@ cudaError_t launch_gemm_tc_prepared(const TcLaunch& a, cudaStream_t s) {
     p.bulk_out = (reinterpret_cast<uintptr_t>(a.y) & 15) == 0 && (((size_t)a.ldy * esz) & 15) == 0;
     p.accumulate = a.accumulate;
     // Split K only when accumulating and the slabs alone would leave SMs idle.
-    // The automatic split keeps at least two k-blocks per K range: a range's
-    // fixed cost (prologue, epilogue, atomics) outweighs one k-block's work
-    // (config 4: 1.525 -> 1.498 ms per step against one k-block per range).
+    // The automatic split aims at about two thirds of the SMs (rounded up per
+    // slab) and keeps at least two k-blocks per K range: a range's fixed cost
+    // (prologue, epilogue, atomics) outweighs a k-block's work. Config 4:
+    // 1.525 ms per step with one range per SM, 1.498 with the two-block cap,
+    // 1.425 with both.
     const int nkb = w->k / kKB;
     int ks = 1;
     if (a.accumulate && p.n_slabs < a.sm_count) {
         const int cap = a.k_splits > 0 ? nkb : (nkb / 2 > 1 ? nkb / 2 : 1);
-        ks = a.k_splits > 0 ? a.k_splits : a.sm_count / p.n_slabs;
+        ks = a.k_splits > 0 ? a.k_splits : (a.sm_count * 2 / 3 + p.n_slabs - 1) / p.n_slabs;
         ks = ks > cap ? cap : (ks < 1 ? 1 : ks);
     }
     p.k_splits = ks;
