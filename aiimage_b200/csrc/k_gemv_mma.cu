@@ -338,13 +338,19 @@ __global__ void __launch_bounds__(kMmaThreads, 2) gemv_mma_kernel(MmaParams mp) 
     const int xstep = lane < 4 ? 8 : 0;  // uint4 per four blocks
     unsigned long long best_key = 0ull;
 
-    int local = 0;
+    // This group's local-th unit sits in its private stage grp + NG * (local % SPG),
+    // fill local / SPG: the group waits for fill f of a stage only after it
+    // consumed fill f - 1. Slot and fill parity advance by one per unit.
+    int slot = 0, local = 0;
+    uint32_t fill_par = 0;
     for (int it = grp; it < my_units; it += NG, ++local) {
-        // This group's local-th unit sits in its private stage grp + NG * (local % SPG):
-        // the group waits for fill f of a stage only after it consumed fill f - 1.
-        const int s = grp + NG * (local % SPG);
+        const int s = grp + NG * slot;
         // Warp-uniform, so that the MMAs and shuffles below see the whole warp.
-        const bool ready = __all_sync(0xffffffffu, mbar_wait(full + s, (local / SPG) & 1));
+        const bool ready = __all_sync(0xffffffffu, mbar_wait(full + s, fill_par));
+        if (++slot == SPG) {
+            slot = 0;
+            fill_par ^= 1u;
+        }
         if (!ready) {
             report_timeout(p.status);
             *abort_flag = 1;
